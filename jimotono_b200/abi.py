@@ -1,0 +1,41 @@
+"""ctypes prototypes of every symbol declared in include/jimotono_b200.h.
+
+PROTOTYPES is also the list the CPU test suite checks against the header and
+the library's dynamic symbol table."""
+from __future__ import annotations
+
+import ctypes as C
+
+P = C.c_void_p
+I = C.c_int
+SZ = C.c_size_t
+F = C.c_float
+D = C.c_double
+
+# name: (restype, [argtypes])
+PROTOTYPES = {
+    # ---- reference-compatible W8A8 (w8a8.h) ----
+    "jt_w8a8_set_enabled": (I, [I]),
+    "jt_w8a8_get_enabled": (I, [P]),
+    "jt_w8a8_is_enabled": (I, []),
+    "jt_w8a8_quant_per_tensor": (I, [P, SZ, P, P]),
+    "jt_w8a8_dequant_per_tensor": (I, [P, F, SZ, P]),
+    "jt_w8a8_quant_per_channel": (I, [P, SZ, SZ, P, P]),
+    "jt_w8a8_dequant_per_channel": (I, [P, P, SZ, SZ, P]),
+    "jt_w8a8_gemm_per_tensor": (I, [P, P, F, F, P, I, I, I]),
+    "jt_w8a8_gemm_per_channel": (I, [P, P, F, P, P, I, I, I]),
+    "jt_w8a8_fakequant_per_tensor": (I, [P, SZ, P]),
+    "jt_w8a8_fakequant_per_channel": (I, [P, SZ, SZ, P]),
+    # ---- device entry points ----
+    "jt_b200_w8a8_gemm": (I, [P, I, P, P, I, P, P, I, I, I, I, P]),
+    "jt_b200_w8a8_gemm_i32": (I, [P, I, P, I, P, I, I, I, I, P]),
+    "jt_b200_sync": (I, []),
+    "jt_b200_version": (C.c_char_p, []),
+}
+
+
+def declare(handle: C.CDLL) -> None:
+    for name, (res, args) in PROTOTYPES.items():
+        fn = getattr(handle, name)
+        fn.restype = res
+        fn.argtypes = args

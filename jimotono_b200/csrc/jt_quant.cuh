@@ -1,0 +1,53 @@
+// jt_quant.cuh - device form of the reference's symmetric int8 quantizer
+// (w8a8.c:688-747): scale_d = maxabs / 127 (double), q = clamp(round(x /
+// scale_d), -127, 127) with round() = half away from zero, zero block ->
+// scale 1, q 0.  Codes are bit-identical to the reference.
+//
+// The division is done in fp32 first (x * (float)(127/maxabs)); that
+// estimate is within 2^-23 * 127 < 2e-5 of the exact quotient, so whenever
+// its fractional part is farther than 1e-3 from one half the rounded code is
+// already exact.  Only the rare near-tie case runs the double division the
+// reference uses.
+#pragma once
+#include <cstdint>
+
+namespace jt {
+
+struct QuantBlock {
+    double scale_d;   // maxabs / 127 (0 when maxabs == 0)
+    float inv;        // (float)(127 / maxabs), fast-path multiplier
+    float scale_f;    // stored scale: (float)scale_d, or 1.0f for a zero block
+};
+
+__device__ __forceinline__ QuantBlock quant_block(float maxabs) {
+    QuantBlock b;
+    if (maxabs == 0.0f) {
+        b.scale_d = 0.0;
+        b.inv = 0.0f;
+        b.scale_f = 1.0f;
+    } else {
+        b.scale_d = __ddiv_rn((double)maxabs, 127.0);
+        b.inv = __double2float_rn(__ddiv_rn(127.0, (double)maxabs));
+        b.scale_f = __double2float_rn(b.scale_d);
+    }
+    return b;
+}
+
+__device__ __forceinline__ int quant_code(float x, const QuantBlock &b) {
+    if (b.scale_d == 0.0) return 0;
+    const float y = __fmul_rn(x, b.inv);
+    const float ay = fabsf(y);
+    const float fr = __fsub_rn(ay, floorf(ay));
+    int q;
+    if (fabsf(__fsub_rn(fr, 0.5f)) > 1e-3f) {
+        q = static_cast<int>(floorf(__fadd_rn(ay, 0.5f)));
+        if (y < 0.0f) q = -q;
+    } else {
+        q = static_cast<int>(round(__ddiv_rn((double)x, b.scale_d)));
+    }
+    q = q > 127 ? 127 : q;
+    q = q < -127 ? -127 : q;
+    return q;
+}
+
+}  // namespace jt
