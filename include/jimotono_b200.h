@@ -100,6 +100,73 @@ int jt_b200_w8a8_gemm(const int8_t *X, int ldx, const float *sx, const int8_t *W
 int jt_b200_w8a8_gemm_i32(const int8_t *X, int ldx, const int8_t *W, int ldw, int32_t *C32,
                           int ldc, int M, int N, int K, void *stream);
 
+/* ---- quantized MoE layer (prepared weights) ----
+ *
+ * The layer of jt_moe_fwd_batch (moe_layer.c:980-1614; moe_layer.h:230-246)
+ * with the B200 precision policy: int8 per-token activations, routed
+ * gate/up INT2 and down INT4 with one fp16 scale per 64 K (group 64),
+ * shared experts int8 with per-channel scales, SwiGLU between the
+ * projections and h requantized to int8 per (row, 64 channels).  Routing
+ * (top-k, softmax, capacity sort, drop, renormalization) follows the
+ * reference bit for bit.  Dimension names follow the reference: d = n
+ * (model dim), f = h (expert ffn); the shared ffn fs may differ from f.
+ * Packed weights are little-endian along K: INT2 element k at bits
+ * 2*(k%4) of byte k/4, INT4 element k in the low (k even) or high (k odd)
+ * nibble of byte k/2; code li maps to (2*li - (2^bits-1)) * scale, the
+ * odd-symmetric levels of lowbit.c:41-45. */
+typedef struct jt_b200_moe_dims {
+    int T;            /* largest token count a forward call may pass */
+    int d;            /* model dim, multiple of 128 */
+    int f;            /* routed expert ffn, multiple of 128 */
+    int E;            /* routed experts, 1..4096 */
+    int k;            /* top-k, 1..min(E, 64) */
+    int S;            /* shared experts, 0..8 */
+    int fs;           /* shared expert ffn, multiple of 128 when S > 0 */
+    float cap_factor; /* capacity factor in [1.0, 1.5] (moe_layer.c:913-917) */
+} jt_b200_moe_dims;
+
+typedef struct jt_b200_moe_weights { /* device pointers */
+    const uint8_t *wg, *wu;  /* INT2 [E][f][d/4] */
+    const uint16_t *sg, *su; /* fp16 [E][f][d/64] */
+    const uint8_t *wd;       /* INT4 [E][d][f/2] */
+    const uint16_t *sd;      /* fp16 [E][d][f/64] */
+    const int8_t *wsg, *wsu; /* int8 [S][fs][d] */
+    const float *ssg, *ssu;  /* fp32 [S][fs] per-channel scales */
+    const int8_t *wsd;       /* int8 [S][d][fs] */
+    const float *ssd;        /* fp32 [S][d] */
+} jt_b200_moe_weights;
+
+typedef struct jt_b200_moe_plan jt_b200_moe_plan;
+
+/* Allocate the device workspace for one layer shape (the only allocation;
+ * forward calls allocate nothing). */
+int jt_b200_moe_plan_create(const jt_b200_moe_dims *dims, jt_b200_moe_plan **out);
+int jt_b200_moe_plan_destroy(jt_b200_moe_plan *plan);
+size_t jt_b200_moe_plan_bytes(const jt_b200_moe_plan *plan);
+
+/* Y[T][d] = sum over kept slots of w * expert(x) + sum of shared experts.
+ * x fp32 [T][d], logits fp32 [T][E] (router output), bias fp32 [E] or NULL
+ * (added to the logits before selection), y fp32 [T][d] or bf16 when
+ * y_bf16 != 0.  T <= dims.T; no 4096 cap on T.  Asynchronous on stream. */
+int jt_b200_moe_forward(jt_b200_moe_plan *plan, const jt_b200_moe_weights *w, const float *x,
+                        const float *logits, const float *bias, int T, void *y, int y_bf16,
+                        void *stream);
+
+/* Copy an intermediate of the last forward to host memory (synchronizes). */
+enum {
+    JT_B200_DBG_IDS = 0,     /* int32 [T][k] selected experts */
+    JT_B200_DBG_WEIGHTS = 1, /* fp32 [T][k] weights after renormalization */
+    JT_B200_DBG_PERM = 2,    /* int32 [kept] flattened (t*k+p) indices in expert order */
+    JT_B200_DBG_OFF = 3,     /* int32 [E+1] expert boundaries in perm */
+    JT_B200_DBG_DROP = 4,    /* uint8 [T][k] dropped flags */
+    JT_B200_DBG_XQ = 5,      /* int8 [T][d] per-token codes */
+    JT_B200_DBG_XS = 6,      /* fp32 [T] per-token scales */
+    JT_B200_DBG_HQ = 7,      /* int8 [kept][f] requantized SwiGLU output, perm order */
+    JT_B200_DBG_HS = 8,      /* fp32 [kept][f/64] its scales */
+    JT_B200_DBG_META = 9     /* int32 [4]: kept, token tiles, max kept per expert */
+};
+int jt_b200_moe_debug_copy(jt_b200_moe_plan *plan, int what, void *host_dst, size_t bytes);
+
 /* Synchronize the current device and fold any kernel-reported fault into
  * the return code (JT_OK or JT_ERR_CUDA). */
 int jt_b200_sync(void);

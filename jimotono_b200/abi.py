@@ -29,6 +29,11 @@ PROTOTYPES = {
     # ---- device entry points ----
     "jt_b200_w8a8_gemm": (I, [P, I, P, P, I, P, P, I, I, I, I, P]),
     "jt_b200_w8a8_gemm_i32": (I, [P, I, P, I, P, I, I, I, I, P]),
+    "jt_b200_moe_plan_create": (I, [P, P]),
+    "jt_b200_moe_plan_destroy": (I, [P]),
+    "jt_b200_moe_plan_bytes": (SZ, [P]),
+    "jt_b200_moe_forward": (I, [P, P, P, P, P, I, P, I, P]),
+    "jt_b200_moe_debug_copy": (I, [P, I, P, SZ]),
     "jt_b200_sync": (I, []),
     "jt_b200_version": (C.c_char_p, []),
 }

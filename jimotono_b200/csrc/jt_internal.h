@@ -46,6 +46,41 @@ int jtk_quant_tensor(const float *x, size_t n, int mode, int8_t *q, float *scale
 int jtk_dequant_rows(const int8_t *src, const float *scales, size_t rows, size_t cols,
                      float *dst, int *bad, cudaStream_t stream);
 
+/* fp32 -> bf16 (round to nearest even). */
+int jtk_f32_to_bf16(const float *src, uint16_t *dst, size_t n, cudaStream_t stream);
+
+int jtk_fill_single_range(int32_t *row_off, int32_t *tile_off, int T, int bn,
+                          cudaStream_t stream);
+
+/* MoE routing (jt_route.cu). */
+int jtk_route_topk(const float *logits, const float *bias, int T, int E, int k, int32_t *ids,
+                   float *w, cudaStream_t stream);
+int jtk_sort_chunks(int T);
+int jtk_moe_sort(const int32_t *ids, const float *w_in, int T, int k, int E, int cap, int bn,
+                 int32_t *hist, int32_t *off, int32_t *tile_off, int32_t *meta, int32_t *perm,
+                 int32_t *pos, uint8_t *drop, float *w_out, cudaStream_t stream);
+int jtk_quant_dispatch(const float *x, int T, int d, int k, const int32_t *pos,
+                       const float *wfin, int8_t *xq, float *xs, int8_t *xd, float *xs_d,
+                       float *w_d, int32_t *tok_d, cudaStream_t stream);
+
+/* Expert GEMMs (jt_moe_gemm.cu).  Token tile = 64 rows. */
+#define JTK_MOE_BN 64
+int jtk_moe_gateup_routed(const uint8_t *wg, const uint8_t *wu, const void *gs, const void *us,
+                          int E, int f, int d, const int8_t *xd, int rows_cap, const float *xs_d,
+                          const int32_t *row_off, const int32_t *tile_off, int8_t *hq, float *hs,
+                          int max_tiles_hint, cudaStream_t stream);
+int jtk_moe_down_routed(const uint8_t *wd, const void *ds, int E, int d, int f, const int8_t *hq,
+                        int rows_cap, const float *hs, const int32_t *row_off,
+                        const int32_t *tile_off, const int32_t *row_tok, const float *row_w,
+                        float *y, int max_tiles_hint, cudaStream_t stream);
+int jtk_moe_gateup_shared(const int8_t *wsg, const int8_t *wsu, const float *ssg,
+                          const float *ssu, int fs, int d, const int8_t *xq, int T,
+                          const float *xs, const int32_t *row_off, const int32_t *tile_off,
+                          int8_t *hq, float *hs, cudaStream_t stream);
+int jtk_moe_down_shared(const int8_t *wsd, const float *ssd, int d, int fs, const int8_t *hq,
+                        int T, const float *hs, const int32_t *row_off, const int32_t *tile_off,
+                        float *y, int accumulate, cudaStream_t stream);
+
 /* Device error word shared by all kernels of the library (0 = clean). */
 int jtk_read_and_clear_error(int *out_code);
 int *jtk_error_word(void);

@@ -1,0 +1,228 @@
+/* jt_moe.c - C11 host runtime of the quantized MoE layer on the B200.
+ *
+ * A plan owns the device workspace of one layer shape (allocated once, so a
+ * forward call allocates nothing) and enqueues the layer as a fixed chain of
+ * kernels on the caller's stream:
+ *
+ *   1. top-k + softmax over the router logits        (routing.c:16-76)
+ *   2. stable capacity sort, drop, renormalization   (moe_layer.c:895-978, :1171-1201)
+ *   3. per-token int8 quantization + dispatch of each kept (token, slot)
+ *      row into expert order                         (w8a8.c:688-747, moe_layer.c:1283-1288)
+ *   4. shared experts: gate/up + SwiGLU + requant, down (stores, then adds)
+ *                                                     (moe_layer.c:1469-1560)
+ *   5. routed experts: grouped gate/up + SwiGLU + requant, grouped down
+ *      with the weighted combine fused into its epilogue
+ *                                                     (moe_layer.c:1265-1463)
+ *   6. optional fp32 -> bf16 of the layer output.
+ *
+ * Every kernel is sized from device-side counts (kept pairs, per-expert token
+ * tiles), so the host never waits for the routing result. */
+#include <errno.h>
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "../../include/jimotono_b200.h"
+#include "jt_internal.h"
+
+struct jt_b200_moe_plan {
+    jt_b200_moe_dims dm;
+    int dev;
+    void *arena;
+    size_t arena_bytes;
+    int32_t *ids, *perm, *pos, *hist, *off, *tile_off, *meta, *tok_d;
+    int32_t *sh_row_off, *sh_tile_off;
+    float *w_raw, *w_fin, *xs, *xs_d, *w_d, *hs, *hs_s, *y32;
+    uint8_t *drop;
+    int8_t *xq, *xd, *hq, *hq_s;
+};
+
+static size_t align_up(size_t v) { return (v + 255u) & ~(size_t)255u; }
+
+static int dims_valid(const jt_b200_moe_dims *d) {
+    if (d->T <= 0 || d->d <= 0 || d->f <= 0) return 0;
+    if (d->d % 128 || d->f % 128 || d->f > 4096) return 0;
+    if (d->E <= 0 || d->E > 4096 || d->k <= 0 || d->k > d->E || d->k > 64) return 0;
+    if (d->S < 0 || d->S > 8) return 0;
+    if (d->S > 0 && (d->fs <= 0 || d->fs % 128 || d->fs > 4096)) return 0;
+    if (!(d->cap_factor >= 1.0f) || !(d->cap_factor <= 1.5f) || !isfinite((double)d->cap_factor))
+        return 0;
+    return 1;
+}
+
+int jt_b200_moe_plan_create(const jt_b200_moe_dims *dims, jt_b200_moe_plan **out) {
+    if (dims == NULL || out == NULL || !dims_valid(dims)) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    jt_b200_moe_plan *p = (jt_b200_moe_plan *)calloc(1, sizeof(*p));
+    if (!p) {
+        errno = ENOMEM;
+        return JT_ERR_NOMEM;
+    }
+    p->dm = *dims;
+    const size_t T = (size_t)dims->T, k = (size_t)dims->k, E = (size_t)dims->E;
+    const size_t d = (size_t)dims->d, f = (size_t)dims->f;
+    const size_t fs = dims->S > 0 ? (size_t)dims->fs : 64;
+    const size_t Tk = T * k;
+    const size_t nch = (size_t)jtk_sort_chunks(dims->T);
+    struct {
+        void **dst;
+        size_t bytes;
+    } parts[] = {
+        {(void **)&p->ids, Tk * 4},        {(void **)&p->perm, Tk * 4},
+        {(void **)&p->pos, Tk * 4},        {(void **)&p->hist, nch * E * 4},
+        {(void **)&p->off, (E + 1) * 4},   {(void **)&p->tile_off, (E + 1) * 4},
+        {(void **)&p->meta, 64},           {(void **)&p->tok_d, Tk * 4},
+        {(void **)&p->sh_row_off, 64},     {(void **)&p->sh_tile_off, 64},
+        {(void **)&p->w_raw, Tk * 4},      {(void **)&p->w_fin, Tk * 4},
+        {(void **)&p->xs, T * 4},          {(void **)&p->xs_d, Tk * 4},
+        {(void **)&p->w_d, Tk * 4},        {(void **)&p->hs, Tk * (f / 64) * 4},
+        {(void **)&p->hs_s, T * (fs / 64) * 4},
+        {(void **)&p->y32, T * d * 4},     {(void **)&p->drop, Tk},
+        {(void **)&p->xq, T * d},          {(void **)&p->xd, Tk * d},
+        {(void **)&p->hq, Tk * f},         {(void **)&p->hq_s, T * fs},
+    };
+    const size_t nparts = sizeof(parts) / sizeof(parts[0]);
+    size_t total = 0;
+    for (size_t i = 0; i < nparts; i++) total += align_up(parts[i].bytes);
+    if (cudaGetDevice(&p->dev) != cudaSuccess || cudaMalloc(&p->arena, total) != cudaSuccess) {
+        cudaGetLastError();
+        free(p);
+        errno = ENOMEM;
+        return JT_ERR_NOMEM;
+    }
+    /* Zero once: rows past the kept count are read by full token tiles. */
+    if (cudaMemset(p->arena, 0, total) != cudaSuccess) {
+        cudaFree(p->arena);
+        free(p);
+        errno = EIO;
+        return JT_ERR_CUDA;
+    }
+    p->arena_bytes = total;
+    size_t offb = 0;
+    for (size_t i = 0; i < nparts; i++) {
+        *parts[i].dst = (char *)p->arena + offb;
+        offb += align_up(parts[i].bytes);
+    }
+    *out = p;
+    return JT_OK;
+}
+
+int jt_b200_moe_plan_destroy(jt_b200_moe_plan *plan) {
+    if (plan == NULL) return JT_OK;
+    if (plan->arena) cudaFree(plan->arena);
+    free(plan);
+    return JT_OK;
+}
+
+size_t jt_b200_moe_plan_bytes(const jt_b200_moe_plan *plan) {
+    return plan ? plan->arena_bytes : 0;
+}
+
+static int weights_valid(const jt_b200_moe_weights *w, int S) {
+    if (!w->wg || !w->wu || !w->sg || !w->su || !w->wd || !w->sd) return 0;
+    if (S > 0 && (!w->wsg || !w->wsu || !w->ssg || !w->ssu || !w->wsd || !w->ssd)) return 0;
+    return 1;
+}
+
+#define LAUNCH(expr)                 \
+    do {                             \
+        int _r = (expr);             \
+        if (_r != 0) {               \
+            errno = _r == -1 ? EINVAL : EIO; \
+            return _r == -1 ? JT_ERR_INVAL : JT_ERR_CUDA; \
+        }                            \
+    } while (0)
+
+int jt_b200_moe_forward(jt_b200_moe_plan *plan, const jt_b200_moe_weights *w, const float *x,
+                        const float *logits, const float *bias, int T, void *y, int y_bf16,
+                        void *stream) {
+    if (plan == NULL || w == NULL || x == NULL || logits == NULL || y == NULL) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    const jt_b200_moe_dims *dm = &plan->dm;
+    if (T <= 0 || T > dm->T || !weights_valid(w, dm->S)) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    cudaStream_t st = (cudaStream_t)stream;
+    const int k = dm->k, E = dm->E, d = dm->d, f = dm->f, S = dm->S, fs = dm->fs;
+    const int rows_cap = dm->T * k;
+    /* capacity of moe_layer.c:931-943 (double arithmetic on the host) */
+    const double capd = ceil((double)dm->cap_factor * (double)((size_t)T * k) / (double)E);
+    if (!isfinite(capd) || capd < 1.0 || capd > 2147483647.0) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    const int cap = (int)capd;
+    float *yf = y_bf16 ? plan->y32 : (float *)y;
+
+    LAUNCH(jtk_route_topk(logits, bias, T, E, k, plan->ids, plan->w_raw, st));
+    LAUNCH(jtk_moe_sort(plan->ids, plan->w_raw, T, k, E, cap, JTK_MOE_BN, plan->hist, plan->off,
+                        plan->tile_off, plan->meta, plan->perm, plan->pos, plan->drop,
+                        plan->w_fin, st));
+    LAUNCH(jtk_quant_dispatch(x, T, d, k, plan->pos, plan->w_fin, plan->xq, plan->xs, plan->xd,
+                              plan->xs_d, plan->w_d, plan->tok_d, st));
+    if (S > 0) {
+        LAUNCH(jtk_fill_single_range(plan->sh_row_off, plan->sh_tile_off, T, JTK_MOE_BN, st));
+        for (int s = 0; s < S; s++) {
+            LAUNCH(jtk_moe_gateup_shared(w->wsg + (size_t)s * fs * d, w->wsu + (size_t)s * fs * d,
+                                         w->ssg + (size_t)s * fs, w->ssu + (size_t)s * fs, fs, d,
+                                         plan->xq, T, plan->xs, plan->sh_row_off,
+                                         plan->sh_tile_off, plan->hq_s, plan->hs_s, st));
+            LAUNCH(jtk_moe_down_shared(w->wsd + (size_t)s * d * fs, w->ssd + (size_t)s * d, d, fs,
+                                       plan->hq_s, T, plan->hs_s, plan->sh_row_off,
+                                       plan->sh_tile_off, yf, s > 0, st));
+        }
+    } else {
+        if (cudaMemsetAsync(yf, 0, (size_t)T * d * sizeof(float), st) != cudaSuccess) {
+            errno = EIO;
+            return JT_ERR_CUDA;
+        }
+    }
+    LAUNCH(jtk_moe_gateup_routed(w->wg, w->wu, w->sg, w->su, E, f, d, plan->xd, rows_cap,
+                                 plan->xs_d, plan->off, plan->tile_off, plan->hq, plan->hs, 0, st));
+    LAUNCH(jtk_moe_down_routed(w->wd, w->sd, E, d, f, plan->hq, rows_cap, plan->hs, plan->off,
+                               plan->tile_off, plan->tok_d, plan->w_d, yf, 0, st));
+    if (y_bf16) LAUNCH(jtk_f32_to_bf16(yf, (uint16_t *)y, (size_t)T * d, st));
+    return JT_OK;
+}
+
+int jt_b200_moe_debug_copy(jt_b200_moe_plan *plan, int what, void *host_dst, size_t bytes) {
+    if (plan == NULL || host_dst == NULL) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    const size_t T = (size_t)plan->dm.T, k = (size_t)plan->dm.k, E = (size_t)plan->dm.E;
+    const size_t d = (size_t)plan->dm.d, f = (size_t)plan->dm.f;
+    const void *src = NULL;
+    size_t cap = 0;
+    switch (what) {
+        case JT_B200_DBG_IDS: src = plan->ids; cap = T * k * 4; break;
+        case JT_B200_DBG_WEIGHTS: src = plan->w_fin; cap = T * k * 4; break;
+        case JT_B200_DBG_PERM: src = plan->perm; cap = T * k * 4; break;
+        case JT_B200_DBG_OFF: src = plan->off; cap = (E + 1) * 4; break;
+        case JT_B200_DBG_DROP: src = plan->drop; cap = T * k; break;
+        case JT_B200_DBG_XQ: src = plan->xq; cap = T * d; break;
+        case JT_B200_DBG_XS: src = plan->xs; cap = T * 4; break;
+        case JT_B200_DBG_HQ: src = plan->hq; cap = T * k * f; break;
+        case JT_B200_DBG_HS: src = plan->hs; cap = T * k * (f / 64) * 4; break;
+        case JT_B200_DBG_META: src = plan->meta; cap = 16; break;
+        default:
+            errno = EINVAL;
+            return JT_ERR_INVAL;
+    }
+    if (bytes > cap) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    if (cudaDeviceSynchronize() != cudaSuccess ||
+        cudaMemcpy(host_dst, src, bytes, cudaMemcpyDeviceToHost) != cudaSuccess) {
+        errno = EIO;
+        return JT_ERR_CUDA;
+    }
+    return JT_OK;
+}

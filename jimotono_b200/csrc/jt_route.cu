@@ -1,0 +1,386 @@
+// jt_route.cu - MoE routing on the GPU: top-k + softmax, the stable
+// capacity sort with drop, the conditional renormalization, and the fused
+// per-token quantization + dispatch that feeds the expert GEMMs.
+//
+//   k_route_topk     routing.c:16-76      (one warp per token)
+//   k_sort_count     moe_layer.c:944-946  (per-chunk expert histograms)
+//   k_sort_scan      moe_layer.c:931-954  (capacity, kept counts, offsets, GEMM tiles)
+//   k_sort_scatter   moe_layer.c:955-970  (stable placement / drop) fused with
+//                    the renormalization of moe_layer.c:1171-1201
+//   k_quant_dispatch w8a8.c:688-747 per token + copy of each token's codes to
+//                    its kept (token, slot) rows in expert order
+//
+// Integer results (ids, perm, off, drop) are bit-identical to the reference;
+// the softmax uses double exp like routing.c:59-70.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "jt_internal.h"
+#include "jt_quant.cuh"
+
+namespace {
+
+constexpr int kChunkTok = 64;  // tokens per sort chunk (chunks are token aligned)
+
+// ------------------------------------------------------------------ top-k
+// One warp per token.  Lane l holds logits l, l+32, ...  Each of the k
+// passes takes the maximum of (taken ? -inf : logit) with ties to the lowest
+// index, exactly the strict '>' scan of routing.c:38-52 (including its
+// behaviour when only -inf values remain).
+__global__ void k_route_topk(const float *__restrict__ logits, const float *__restrict__ bias,
+                             int T, int E, int k, int32_t *__restrict__ ids,
+                             float *__restrict__ w, int *err) {
+    const int warps = blockDim.x >> 5;
+    const int t = blockIdx.x * warps + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (t >= T) return;
+    extern __shared__ uint32_t taken_all[];  // warps * ceil(E/32) words
+    const int nw = (E + 31) / 32;
+    uint32_t *taken = taken_all + (threadIdx.x >> 5) * nw;
+    for (int i = lane; i < nw; i += 32) taken[i] = 0;
+    __syncwarp();
+    const float *row = logits + (size_t)t * E;
+    int nan_seen = 0;
+    for (int i = lane; i < E; i += 32) {
+        float v = row[i];
+        if (bias) v = __fadd_rn(v, bias[i]);
+        nan_seen |= (v != v);
+    }
+    if (__any_sync(0xffffffffu, nan_seen)) {
+        if (lane == 0) atomicExch(err, 0x81);
+        return;
+    }
+    int32_t sel[64];
+    float selv[64];
+    for (int p = 0; p < k; ++p) {
+        float best = 0.0f;
+        int bi = E;  // sentinel: "not set", like best == n in routing.c:40
+        for (int i = lane; i < E; i += 32) {
+            float v = row[i];
+            if (bias) v = __fadd_rn(v, bias[i]);
+            if ((taken[i >> 5] >> (i & 31)) & 1u) v = -INFINITY;
+            if (bi == E || v > best) {
+                best = v;
+                bi = i;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            // candidate with lower index wins unless the other is strictly larger
+            bool take;
+            if (oi == E) take = false;
+            else if (bi == E) take = true;
+            else if (oi < bi) take = !(best > ov);
+            else take = ov > best;
+            if (take) {
+                best = ov;
+                bi = oi;
+            }
+        }
+        sel[p] = bi;
+        if (lane == 0) atomicOr(&taken[bi >> 5], 1u << (bi & 31));
+        __syncwarp();
+        float lv = row[bi];
+        if (bias) lv = __fadd_rn(lv, bias[bi]);
+        selv[p] = lv;
+    }
+    if (lane == 0) {
+        float mx = selv[0];
+        for (int p = 1; p < k; ++p) mx = (selv[p] > mx) ? selv[p] : mx;
+        double sum = 0.0;
+        float ew[64];
+        for (int p = 0; p < k; ++p) {
+            const double e = exp((double)selv[p] - (double)mx);
+            sum += e;
+            ew[p] = (float)e;
+        }
+        if (!(sum > 0.0) || !isfinite(sum)) {
+            atomicExch(err, 0x82);
+            return;
+        }
+        const float inv = (float)(1.0 / sum);
+        for (int p = 0; p < k; ++p) {
+            ids[(size_t)t * k + p] = sel[p];
+            w[(size_t)t * k + p] = __fmul_rn(ew[p], inv);
+        }
+    }
+}
+
+// ------------------------------------------------------------------ sort
+// hist[c][e] = number of pairs of chunk c routed to expert e.
+__global__ void k_sort_count(const int32_t *__restrict__ ids, int T, int k, int E,
+                             int32_t *__restrict__ hist, int *err) {
+    extern __shared__ int32_t cnt[];
+    const int c = blockIdx.x;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    const int t0 = c * kChunkTok;
+    const int t1 = min(T, t0 + kChunkTok);
+    for (int q = t0 * k + threadIdx.x; q < t1 * k; q += blockDim.x) {
+        const int e = ids[q];
+        if (e < 0 || e >= E) {
+            atomicExch(err, 0x83);
+            continue;
+        }
+        atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) hist[(size_t)c * E + e] = cnt[e];
+}
+
+// One CTA.  base[c][e] = pairs of expert e in chunks < c; kept[e] =
+// min(count, cap); off = exclusive scan of kept; tiles: per expert
+// ceil(kept/bn) token tiles, tile_off = exclusive scan (GEMM scheduler).
+// meta[0] = kept total, meta[1] = total token tiles, meta[2] = max kept.
+__global__ void k_sort_scan(int32_t *__restrict__ hist_base, int nchunks, int E, int cap,
+                            int bn, int32_t *__restrict__ off, int32_t *__restrict__ tile_off,
+                            int32_t *__restrict__ meta) {
+    extern __shared__ int32_t sm[];  // 2 * blockDim.x
+    const int tid = threadIdx.x, nt = blockDim.x;
+    const int per = (E + nt - 1) / nt;
+    int kept_local[8], tiles_local[8];
+    int ks = 0, ts = 0, mx = 0;
+    for (int j = 0; j < per; ++j) {
+        const int e = tid * per + j;
+        int kc = 0, tc = 0;
+        if (e < E) {
+            int run = 0;
+            for (int c = 0; c < nchunks; ++c) {
+                const int h = hist_base[(size_t)c * E + e];
+                hist_base[(size_t)c * E + e] = run;  // becomes base[c][e]
+                run += h;
+            }
+            kc = run < cap ? run : cap;
+            tc = (kc + bn - 1) / bn;
+        }
+        kept_local[j] = kc;
+        tiles_local[j] = tc;
+        ks += kc;
+        ts += tc;
+        mx = kc > mx ? kc : mx;
+    }
+    sm[tid] = ks;
+    sm[nt + tid] = ts;
+    __syncthreads();
+    // inclusive Hillis-Steele scan over threads (nt <= 1024)
+    for (int o = 1; o < nt; o <<= 1) {
+        int a = 0, b = 0;
+        if (tid >= o) {
+            a = sm[tid - o];
+            b = sm[nt + tid - o];
+        }
+        __syncthreads();
+        sm[tid] += a;
+        sm[nt + tid] += b;
+        __syncthreads();
+    }
+    int run_k = sm[tid] - ks, run_t = sm[nt + tid] - ts;
+    for (int j = 0; j < per; ++j) {
+        const int e = tid * per + j;
+        if (e < E) {
+            off[e] = run_k;
+            tile_off[e] = run_t;
+        }
+        run_k += kept_local[j];
+        run_t += tiles_local[j];
+    }
+    if (tid == nt - 1) {
+        off[E] = sm[tid];
+        tile_off[E] = sm[nt + tid];
+        meta[0] = sm[tid];
+        meta[1] = sm[nt + tid];
+    }
+    // max kept per expert
+    __syncthreads();
+    sm[tid] = mx;
+    __syncthreads();
+    for (int o = nt / 2; o > 0; o >>= 1) {
+        if (tid < o) sm[tid] = max(sm[tid], sm[tid + o]);
+        __syncthreads();
+    }
+    if (tid == 0) meta[2] = sm[0];
+}
+
+// One warp per chunk, pairs visited in q order 32 at a time; lanes routed
+// to the same expert are ranked by __match_any_sync, so placement is the
+// sequential scan of moe_layer.c:955-970.  Then renormalization of the
+// chunk's tokens (moe_layer.c:1171-1201) with the final weights in wout.
+__global__ void k_sort_scatter(const int32_t *__restrict__ ids, const float *__restrict__ win,
+                               int T, int k, int E, int cap,
+                               const int32_t *__restrict__ base, const int32_t *__restrict__ off,
+                               int32_t *__restrict__ perm, int32_t *__restrict__ pos,
+                               uint8_t *__restrict__ drop, float *__restrict__ wout, int *err) {
+    extern __shared__ int32_t run[];  // E
+    const int c = blockIdx.x, lane = threadIdx.x;
+    for (int e = lane; e < E; e += 32) run[e] = 0;
+    __syncwarp();
+    const int t0 = c * kChunkTok, t1 = min(T, t0 + kChunkTok);
+    const int q0 = t0 * k, q1 = t1 * k;
+    for (int qb = q0; qb < q1; qb += 32) {
+        const int q = qb + lane;
+        const bool act = q < q1;
+        int e = act ? ids[q] : -1 - lane;  // unique negative keys for idle lanes
+        if (act && (e < 0 || e >= E)) {        // counted as an error by k_sort_count
+            e = -1 - lane;
+            if (act) {
+                pos[q] = -1;
+                drop[q] = 1;
+            }
+        }
+        const bool valid = act && e >= 0;
+        const unsigned same = __match_any_sync(0xffffffffu, e);
+        const unsigned lt = (1u << lane) - 1u;
+        int rank = 0;
+        if (valid) rank = run[e] + __popc(same & lt);
+        __syncwarp();
+        if (valid && (same & lt) == 0) run[e] += __popc(same);  // group leader
+        __syncwarp();
+        if (valid) {
+            const int g = base[(size_t)c * E + e] + rank;
+            if (g < cap) {
+                const int p = off[e] + g;
+                perm[p] = q;
+                pos[q] = p;
+                drop[q] = 0;
+            } else {
+                pos[q] = -1;
+                drop[q] = 1;
+            }
+        }
+    }
+    __syncwarp();
+    for (int t = t0 + lane; t < t1; t += 32) {
+        double s = 0.0;
+        int nd = 0;
+        for (int p = 0; p < k; ++p) {
+            const size_t q = (size_t)t * k + p;
+            if (drop[q]) nd++;
+            else s += (double)win[q];
+        }
+        const bool rn = nd > 0 && s > 0.0;
+        if (rn && !isfinite(s)) atomicExch(err, 0x84);
+        for (int p = 0; p < k; ++p) {
+            const size_t q = (size_t)t * k + p;
+            float v = win[q];
+            if (rn && !drop[q]) v = __double2float_rn(__ddiv_rn((double)v, s));
+            wout[q] = v;
+        }
+    }
+}
+
+// ------------------------------------------------------------------ quant + dispatch
+// One CTA per token: per-token int8 quantization of x (w8a8.c:688-747),
+// written to xq[t] (shared experts) and to every kept (t, p) row of the
+// expert-ordered activation matrix xd, with that row's metadata.
+__global__ void __launch_bounds__(256)
+    k_quant_dispatch(const float *__restrict__ x, int T, int d, int k,
+                     const int32_t *__restrict__ pos, const float *__restrict__ wfin,
+                     int8_t *__restrict__ xq, float *__restrict__ xs, int8_t *__restrict__ xd,
+                     float *__restrict__ xs_d, float *__restrict__ w_d,
+                     int32_t *__restrict__ tok_d, int *err) {
+    const int t = blockIdx.x;
+    if (t >= T) return;
+    const float *row = x + (size_t)t * d;
+    __shared__ float wm[8];
+    __shared__ int wb[8];
+    float m = 0.0f;
+    int bad = 0;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        const float v = row[i];
+        bad |= !isfinite(v);
+        m = fmaxf(m, fabsf(v));
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+    }
+    if ((threadIdx.x & 31) == 0) {
+        wm[threadIdx.x >> 5] = m;
+        wb[threadIdx.x >> 5] = bad;
+    }
+    __syncthreads();
+    m = 0.0f;
+    bad = 0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) {
+        m = fmaxf(m, wm[i]);
+        bad |= wb[i];
+    }
+    const jt::QuantBlock qb = jt::quant_block(bad ? 0.0f : m);
+    // Row metadata first: even on a rejected (non-finite) token every kept
+    // row must name this token, so later kernels never index a stale token.
+    int dst[64];
+    int nd = 0;
+    if (pos) {
+        for (int p = 0; p < k; ++p) {
+            const int ps = pos[(size_t)t * k + p];
+            if (ps >= 0) dst[nd++] = ps;
+        }
+        if (threadIdx.x < k) {
+            const int ps = pos[(size_t)t * k + threadIdx.x];
+            if (ps >= 0) {
+                xs_d[ps] = qb.scale_f;
+                w_d[ps] = wfin[(size_t)t * k + threadIdx.x];
+                tok_d[ps] = t;
+            }
+        }
+    }
+    if (threadIdx.x == 0) xs[t] = qb.scale_f;
+    if (bad) {
+        if (threadIdx.x == 0) atomicExch(err, 0x85);
+        return;
+    }
+    // 4 codes per thread per step, written as one 32-bit word
+    for (int i = threadIdx.x * 4; i < d; i += blockDim.x * 4) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int c = jt::quant_code(row[i + j], qb);
+            word |= (uint32_t)(uint8_t)(int8_t)c << (8 * j);
+        }
+        *reinterpret_cast<uint32_t *>(xq + (size_t)t * d + i) = word;
+        for (int j = 0; j < nd; ++j)
+            *reinterpret_cast<uint32_t *>(xd + (size_t)dst[j] * d + i) = word;
+    }
+}
+
+}  // namespace
+
+extern "C" int jtk_route_topk(const float *logits, const float *bias, int T, int E, int k,
+                              int32_t *ids, float *w, cudaStream_t stream) {
+    if (T <= 0 || E <= 0 || k <= 0 || k > E || k > 64) return -1;
+    const int warps = 4;
+    const size_t sm = (size_t)warps * ((E + 31) / 32) * sizeof(uint32_t);
+    k_route_topk<<<(T + warps - 1) / warps, warps * 32, sm, stream>>>(logits, bias, T, E, k, ids,
+                                                                      w, jtk_error_word());
+    return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
+extern "C" int jtk_sort_chunks(int T) { return (T + kChunkTok - 1) / kChunkTok; }
+
+extern "C" int jtk_moe_sort(const int32_t *ids, const float *w_in, int T, int k, int E, int cap,
+                            int bn, int32_t *hist, int32_t *off, int32_t *tile_off,
+                            int32_t *meta, int32_t *perm, int32_t *pos, uint8_t *drop,
+                            float *w_out, cudaStream_t stream) {
+    if (T <= 0 || k <= 0 || E <= 0 || E > 4096 || cap <= 0 || bn <= 0) return -1;
+    const int nch = jtk_sort_chunks(T);
+    int *err = jtk_error_word();
+    k_sort_count<<<nch, 256, (size_t)E * sizeof(int32_t), stream>>>(ids, T, k, E, hist, err);
+    int nt = 1024;
+    while (nt / 2 >= E && nt > 32) nt /= 2;
+    k_sort_scan<<<1, nt, 2 * nt * sizeof(int32_t), stream>>>(hist, nch, E, cap, bn, off,
+                                                             tile_off, meta);
+    k_sort_scatter<<<nch, 32, (size_t)E * sizeof(int32_t), stream>>>(
+        ids, w_in, T, k, E, cap, hist, off, perm, pos, drop, w_out, err);
+    return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
+extern "C" int jtk_quant_dispatch(const float *x, int T, int d, int k, const int32_t *pos,
+                                  const float *wfin, int8_t *xq, float *xs, int8_t *xd,
+                                  float *xs_d, float *w_d, int32_t *tok_d, cudaStream_t stream) {
+    if (T <= 0 || d <= 0 || (d % 4) != 0 || k > 64) return -1;
+    k_quant_dispatch<<<T, 256, 0, stream>>>(x, T, d, k, pos, wfin, xq, xs, xd, xs_d, w_d, tok_d,
+                                            jtk_error_word());
+    return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}

@@ -101,3 +101,45 @@ extern "C" int jtk_check_finite_f32(const float *p, size_t n, int *bad, cudaStre
     k_check_finite_f32<<<grid_for(n), 256, 0, stream>>>(p, n, bad);
     return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
+
+namespace {
+// fp32 -> bf16, round to nearest even (the rounding a bf16 output of the
+// layer gets; the reference commits Y = (float)yacc, moe_layer.c:1568-1574).
+__global__ void k_f32_to_bf16(const float *__restrict__ src, uint16_t *__restrict__ dst, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const uint32_t b = __float_as_uint(src[i]);
+        uint16_t h;
+        if ((b & 0x7fffffffu) > 0x7f800000u) h = (uint16_t)((b >> 16) | 0x40u);  // quiet NaN
+        else h = (uint16_t)((b + 0x7fffu + ((b >> 16) & 1u)) >> 16);
+        dst[i] = h;
+    }
+}
+}  // namespace
+
+extern "C" int jtk_f32_to_bf16(const float *src, uint16_t *dst, size_t n, cudaStream_t stream) {
+    size_t g = (n + 255) / 256;
+    const size_t cap = (size_t)jtk_num_sms() * 8;
+    if (g > cap) g = cap;
+    if (g < 1) g = 1;
+    k_f32_to_bf16<<<(int)g, 256, 0, stream>>>(src, dst, n);
+    return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
+namespace {
+// Row/tile ranges of a single "expert" covering rows [0, T) (shared experts).
+__global__ void k_fill_single_range(int32_t *row_off, int32_t *tile_off, int T, int bn) {
+    if (threadIdx.x == 0) {
+        row_off[0] = 0;
+        row_off[1] = T;
+        tile_off[0] = 0;
+        tile_off[1] = (T + bn - 1) / bn;
+    }
+}
+}  // namespace
+
+extern "C" int jtk_fill_single_range(int32_t *row_off, int32_t *tile_off, int T, int bn,
+                                     cudaStream_t stream) {
+    k_fill_single_range<<<1, 32, 0, stream>>>(row_off, tile_off, T, bn);
+    return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}

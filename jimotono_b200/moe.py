@@ -1,0 +1,120 @@
+"""Host-side view of the MoE device API (jt_b200_moe_* in jimotono_b200.h)
+plus seeded synthetic inputs in the layouts the kernels consume.
+
+The synthetic generators stand in for the benchmark configurations (there
+are no checkpoints): packed INT2/INT4 codes uniform over their levels, fp16
+group scales ~U[0.01, 0.05] as the configurations state, int8 shared-expert
+weights uniform over [-127, 127] with per-channel scales of the size int8
+quantization of N(0, 0.02) weights produces, activations and router logits
+~N(0, 1), and for the skewed-routing configuration a per-expert bias
+log(Zipf(s) pmf) over a seeded expert permutation.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import check, lib
+
+
+class MoeDims(C.Structure):
+    _fields_ = [("T", C.c_int), ("d", C.c_int), ("f", C.c_int), ("E", C.c_int), ("k", C.c_int),
+                ("S", C.c_int), ("fs", C.c_int), ("cap_factor", C.c_float)]
+
+
+class MoeWeights(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("wg", "wu", "sg", "su", "wd", "sd", "wsg", "wsu", "ssg",
+                                          "ssu", "wsd", "ssd")]
+
+
+WEIGHT_FIELDS = ("wg", "wu", "sg", "su", "wd", "sd", "wsg", "wsu", "ssg", "ssu", "wsd", "ssd")
+
+DBG_IDS, DBG_WEIGHTS, DBG_PERM, DBG_OFF, DBG_DROP, DBG_XQ, DBG_XS, DBG_HQ, DBG_HS, DBG_META = range(10)
+
+
+@dataclass
+class Dims:
+    T: int
+    d: int
+    f: int
+    E: int
+    k: int
+    S: int
+    fs: int
+    cap_factor: float = 1.5
+
+    def c(self) -> MoeDims:
+        return MoeDims(self.T, self.d, self.f, self.E, self.k, self.S, self.fs, self.cap_factor)
+
+
+def synth_weights(dm: Dims, seed: int) -> dict:
+    rng = np.random.default_rng(seed)
+    E, d, f, S, fs = dm.E, dm.d, dm.f, dm.S, max(dm.fs, 64)
+    w = {
+        "wg": rng.integers(0, 256, (E, f, d // 4), dtype=np.uint8),
+        "wu": rng.integers(0, 256, (E, f, d // 4), dtype=np.uint8),
+        "sg": rng.uniform(0.01, 0.05, (E, f, d // 64)).astype(np.float16),
+        "su": rng.uniform(0.01, 0.05, (E, f, d // 64)).astype(np.float16),
+        "wd": rng.integers(0, 256, (E, d, f // 2), dtype=np.uint8),
+        "sd": rng.uniform(0.01, 0.05, (E, d, f // 64)).astype(np.float16),
+        "wsg": rng.integers(-127, 128, (max(S, 1), fs, d), dtype=np.int8),
+        "wsu": rng.integers(-127, 128, (max(S, 1), fs, d), dtype=np.int8),
+        "ssg": rng.uniform(4e-4, 8e-4, (max(S, 1), fs)).astype(np.float32),
+        "ssu": rng.uniform(4e-4, 8e-4, (max(S, 1), fs)).astype(np.float32),
+        "wsd": rng.integers(-127, 128, (max(S, 1), d, fs), dtype=np.int8),
+        "ssd": rng.uniform(4e-4, 8e-4, (max(S, 1), d)).astype(np.float32),
+    }
+    return w
+
+
+def synth_inputs(dm: Dims, T: int, seed: int, zipf_s: float | None = None):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((T, dm.d), dtype=np.float32)
+    logits = rng.standard_normal((T, dm.E), dtype=np.float32)
+    bias = None
+    if zipf_s is not None:
+        ranks = rng.permutation(dm.E) + 1
+        pmf = 1.0 / ranks.astype(np.float64) ** zipf_s
+        pmf /= pmf.sum()
+        bias = np.log(pmf).astype(np.float32)
+    return x, logits, bias
+
+
+class Plan:
+    """Owns a jt_b200_moe_plan (device workspace of one layer shape)."""
+
+    def __init__(self, dm: Dims):
+        self.dm = dm
+        self._c = dm.c()
+        self.handle = C.c_void_p()
+        check(lib().jt_b200_moe_plan_create(C.byref(self._c), C.byref(self.handle)),
+              "jt_b200_moe_plan_create")
+
+    def forward(self, wptrs: MoeWeights, x_ptr: int, logits_ptr: int, bias_ptr, T: int,
+                y_ptr: int, y_bf16: bool, stream: int) -> None:
+        check(lib().jt_b200_moe_forward(self.handle, C.byref(wptrs), x_ptr, logits_ptr,
+                                        bias_ptr, T, y_ptr, int(y_bf16), stream),
+              "jt_b200_moe_forward")
+
+    def debug(self, what: int, dtype, count: int) -> np.ndarray:
+        out = np.empty(count, dtype=dtype)
+        if count:
+            check(lib().jt_b200_moe_debug_copy(self.handle, what, out.ctypes.data, out.nbytes),
+                  "jt_b200_moe_debug_copy")
+        return out
+
+    def bytes(self) -> int:
+        return lib().jt_b200_moe_plan_bytes(self.handle)
+
+    def close(self) -> None:
+        if self.handle:
+            lib().jt_b200_moe_plan_destroy(self.handle)
+            self.handle = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -350,9 +350,8 @@ void jto_lowbit_gemv(const int8_t *a, float sa, const uint8_t *packed, const uin
 
 /* Routed expert e on one quantized token row:
  *   gate/up: fold over 64-groups of fmaf((float)P, s_g, r), then * sa
- *   h = SwiGLU(gate, up); requantize h per 128-channel block (w8a8.c:688-747)
- *   down: per 128-block b: t = (float)P_{2b} * s_{2b}; t = fmaf((float)P_{2b+1}, s_{2b+1}, t);
- *         r = fmaf(t, hs_b, r). */
+ *   h = SwiGLU(gate, up); requantize h per 64-channel group (w8a8.c:688-747)
+ *   down: per 64-group g: t = (float)P_g * s_g; r = fmaf(t, hs_g, r). */
 static void routed_expert(const jto_moe_dims *dm, const jto_moe_weights *w, int e,
                           const int8_t *xq, float xs, int8_t *hq, float *hs, float *yout,
                           float *gbuf, float *ubuf, float *hbuf) {
@@ -375,14 +374,13 @@ static void routed_expert(const jto_moe_dims *dm, const jto_moe_weights *w, int 
         ubuf[c] = r * xs;
         hbuf[c] = jto_swiglu(gbuf[c], ubuf[c]);
     }
-    jto_quant_blocks(hbuf, 1, f, 128, hq, hs);
+    jto_quant_blocks(hbuf, 1, f, 64, hq, hs);
     for (int o = 0; o < d; o++) {
         jto_lowbit_partials(hq, wd + (size_t)o * (f / 2), 1, f, 4, P);
         float r = 0.0f;
-        for (int b = 0; b < f / 128; b++) {
-            float t = (float)P[2 * b] * jto_half_to_float(sd[(size_t)o * gf + 2 * b]);
-            t = fmaf((float)P[2 * b + 1], jto_half_to_float(sd[(size_t)o * gf + 2 * b + 1]), t);
-            r = fmaf(t, hs[b], r);
+        for (int g = 0; g < gf; g++) {
+            const float t = (float)P[g] * jto_half_to_float(sd[(size_t)o * gf + g]);
+            r = fmaf(t, hs[g], r);
         }
         yout[o] = r;
     }
@@ -390,8 +388,8 @@ static void routed_expert(const jto_moe_dims *dm, const jto_moe_weights *w, int 
 
 /* Shared expert s on token t:
  *   gate = ((float)acc * xs) * ssg[c]; up likewise; h = SwiGLU;
- *   requantize per 128-block; down: r = fmaf((float)P_b, hs_b, r) over
- *   128-blocks, y = r * ssd[o]. */
+ *   requantize per 64-channel group; down: r = fmaf((float)P_g, hs_g, r)
+ *   over 64-groups, y = r * ssd[o]. */
 static void shared_expert(const jto_moe_dims *dm, const jto_moe_weights *w, int s,
                           const int8_t *xq, float xs, float *yout, float *hbuf, int8_t *hq,
                           float *hs) {
@@ -409,13 +407,13 @@ static void shared_expert(const jto_moe_dims *dm, const jto_moe_weights *w, int 
         float u = ((float)au * xs) * w->ssu[(size_t)s * fs + c];
         hbuf[c] = jto_swiglu(g, u);
     }
-    jto_quant_blocks(hbuf, 1, fs, 128, hq, hs);
+    jto_quant_blocks(hbuf, 1, fs, 64, hq, hs);
     for (int o = 0; o < d; o++) {
         float r = 0.0f;
-        for (int b = 0; b < fs / 128; b++) {
+        for (int b = 0; b < fs / 64; b++) {
             int32_t P = 0;
-            for (int i = 0; i < 128; i++) {
-                const int k = b * 128 + i;
+            for (int i = 0; i < 64; i++) {
+                const int k = b * 64 + i;
                 P += (int32_t)hq[k] * (int32_t)wsd[(size_t)o * fs + k];
             }
             r = fmaf((float)P, hs[b], r);
@@ -443,7 +441,7 @@ int jto_moe_forward(const jto_moe_dims *dm, const jto_moe_weights *w, const floa
     float *ubuf = malloc((size_t)fmax_ * sizeof(float));
     float *hbuf = malloc((size_t)fmax_ * sizeof(float));
     int8_t *hqtmp = malloc((size_t)fmax_);
-    float *hstmp = malloc((size_t)(fmax_ / 128 + 1) * sizeof(float));
+    float *hstmp = malloc((size_t)(fmax_ / 64 + 1) * sizeof(float));
     float *ypair = malloc(Tk * (size_t)d * sizeof(float));
     float *ys = malloc((size_t)(S > 0 ? S : 1) * T * (size_t)d * sizeof(float));
     double *yacc = calloc((size_t)T * d, sizeof(double));
@@ -462,7 +460,7 @@ int jto_moe_forward(const jto_moe_dims *dm, const jto_moe_weights *w, const floa
         routed_expert(dm, w, e, xq + (size_t)t * d, xs[t], hqtmp, hstmp,
                       ypair + (size_t)i * d, gbuf, ubuf, hbuf);
         if (tr && tr->hq) memcpy(tr->hq + (size_t)i * f, hqtmp, (size_t)f);
-        if (tr && tr->hs) memcpy(tr->hs + (size_t)i * (f / 128), hstmp, (size_t)(f / 128) * sizeof(float));
+        if (tr && tr->hs) memcpy(tr->hs + (size_t)i * (f / 64), hstmp, (size_t)(f / 64) * sizeof(float));
     }
     for (int s = 0; s < S; s++)
         for (int t = 0; t < T; t++)

@@ -101,7 +101,7 @@ typedef struct jto_moe_trace {
     int8_t *xq;       /* [T][d] */
     float *xs;        /* [T] */
     int8_t *hq;       /* [kept][f]   (perm order) */
-    float *hs;        /* [kept][f/128] */
+    float *hs;        /* [kept][f/64] */
     float *ypair;     /* [kept][d]  expert output before weighting */
     float *yshared;   /* [T][d]     sum of shared experts */
     int kept;
