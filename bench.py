@@ -1,0 +1,384 @@
+"""Benchmark of the B200 quantized-MoE hot path (one JSON line on rank 0).
+
+Headline (`value`): MoE-layer tokens/s of the expert-parallel configuration
+(T=16384 tokens, d=2048, 1024 routed experts of ffn 1536
+top-8 with INT2 gate/up + INT4 down group-64, 2 shared INT8 experts of ffn
+4096) on N GPUs, device-resident inputs, whole-job throughput.  `parts`
+adds the other configurations' metrics on GPU 0: W8A8 TOPS (config 1),
+batch-1 decode HBM GB/s (config 2), prefill tokens/s (config 3).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+N > 1 runs under torchrun, one rank per GPU.  Until the NCCL dispatch /
+combine path lands every rank runs an independent replica of the layer on
+its own token slice ("replicas" in config.parallelism).
+
+`--impl reference` times the reference's own CPU implementation
+(oracle/_ref, the reference sources compiled unmodified) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG5 = dict(T=16384, d=2048, f=1536, E=1024, k=8, S=2, fs=4096, cap=1.5)
+CFG3 = dict(T=4096, d=2048, f=1024, E=256, k=8, S=2, fs=2048, cap=1.5)
+CFG2 = dict(T=1, d=1024, f=256, E=64, k=8, S=2, fs=512, cap=1.5)
+METRIC = "MoE-layer tokens/s at 1/2/4/8 B200; W8A8 TOPS; decode HBM GB/s vs peak"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            p = json.load(fh)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------- device helpers
+def dev_weights(torch, w: dict):
+    from jimotono_b200.moe import WEIGHT_FIELDS, MoeWeights
+    dw = {}
+    for n in WEIGHT_FIELDS:
+        a = w[n]
+        if a.dtype == np.float16:
+            a = a.view(np.int16)
+        dw[n] = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    return dw, MoeWeights(*[dw[n].data_ptr() for n in WEIGHT_FIELDS])
+
+
+def synth_weights_dev(torch, dm, seed):
+    """Random packed weights generated on the device (same distributions as
+    jimotono_b200.moe.synth_weights; large configurations would take minutes
+    to generate with numpy)."""
+    from jimotono_b200.moe import WEIGHT_FIELDS, MoeWeights
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    E, d, f, S, fs = dm.E, dm.d, dm.f, max(dm.S, 1), max(dm.fs, 64)
+
+    def u8(*shape):
+        return torch.randint(0, 256, shape, dtype=torch.uint8, device="cuda", generator=g)
+
+    def s8(*shape):
+        return torch.randint(-127, 128, shape, dtype=torch.int8, device="cuda", generator=g)
+
+    def uni(lo, hi, *shape, dtype=torch.float32):
+        return (torch.rand(shape, device="cuda", generator=g) * (hi - lo) + lo).to(dtype)
+
+    dw = {
+        "wg": u8(E, f, d // 4), "wu": u8(E, f, d // 4),
+        "sg": uni(0.01, 0.05, E, d // 64, f, dtype=torch.float16),
+        "su": uni(0.01, 0.05, E, d // 64, f, dtype=torch.float16),
+        "wd": u8(E, d, f // 2), "sd": uni(0.01, 0.05, E, f // 64, d, dtype=torch.float16),
+        "wsg": s8(S, fs, d), "wsu": s8(S, fs, d), "ssg": uni(4e-4, 8e-4, S, fs),
+        "ssu": uni(4e-4, 8e-4, S, fs), "wsd": s8(S, d, fs), "ssd": uni(4e-4, 8e-4, S, d),
+    }
+    return dw, MoeWeights(*[dw[n].data_ptr() for n in WEIGHT_FIELDS])
+
+
+def weight_bytes(dm) -> int:
+    routed = dm.E * (2 * dm.f * (dm.d // 4 + dm.d // 64 * 2) + dm.d * (dm.f // 2 + dm.f // 64 * 2))
+    shared = dm.S * (2 * dm.fs * (dm.d + 4) + dm.d * (dm.fs + 4))
+    return routed + shared
+
+
+# ----------------------------------------------------------------- MoE layer timing
+def time_layer(torch, cfg, rank, world, steps, warmup, seed, zipf=None, bf16=False, nrot=1,
+               profile=True):
+    from jimotono_b200 import lib
+    from jimotono_b200.moe import Dims, Plan
+    T = cfg["T"] // world if world > 1 else cfg["T"]
+    dm = Dims(T, cfg["d"], cfg["f"], cfg["E"], cfg["k"], cfg["S"], cfg["fs"], cfg["cap"])
+    rots = [synth_weights_dev(torch, dm, seed + 17 * r) for r in range(nrot)]
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed + 1000 * rank)
+    x = torch.randn((T, dm.d), device="cuda", generator=g)
+    logits = torch.randn((T, dm.E), device="cuda", generator=g)
+    bias = None
+    if zipf is not None:
+        rng = np.random.default_rng(seed)
+        ranks = rng.permutation(dm.E) + 1
+        pmf = 1.0 / ranks.astype(np.float64) ** zipf
+        pmf /= pmf.sum()
+        bias = torch.from_numpy(np.log(pmf).astype(np.float32)).cuda()
+    y = torch.empty((T, dm.d), dtype=torch.bfloat16 if bf16 else torch.float32, device="cuda")
+    plan = Plan(dm)
+    stream = torch.cuda.current_stream().cuda_stream
+    bp = bias.data_ptr() if bias is not None else None
+
+    def step(i):
+        plan.forward(rots[i % nrot][1], x.data_ptr(), logits.data_ptr(), bp, T, y.data_ptr(),
+                     bf16, stream)
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if lib().jt_b200_sync() != 0:
+        raise RuntimeError("kernel fault during warm-up")
+    if profile:
+        assert lib().jt_b200_moe_profile_begin(plan.handle, steps) == 0
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    stage = None
+    if profile:
+        arr = (C.c_float * 7)()
+        nsteps = C.c_int(0)
+        assert lib().jt_b200_moe_profile_end(plan.handle, arr, 7, C.byref(nsteps)) == 0
+        stage = [v / max(nsteps.value, 1) for v in arr]
+    if lib().jt_b200_sync() != 0:
+        raise RuntimeError("kernel fault during the timed region")
+    meta = plan.debug(9, np.int32, 4)
+    out = dict(T=T, ms_per_step=ms / steps, stage_ms=stage, kept=int(meta[0]), dims=dm, plan=plan,
+               x=x, logits=logits, y=y, rots=rots, bias=bias, bf16=bf16)
+    return out
+
+
+def e2e_layer(torch, st, steps, warmup):
+    """Same layer through the public API with host buffers: H2D of x and the
+    router logits from pinned memory, forward, D2H of the output, per step."""
+    dm, plan = st["dims"], st["plan"]
+    T = st["T"]
+    hx = torch.empty_like(st["x"], device="cpu").pin_memory()
+    hl = torch.empty_like(st["logits"], device="cpu").pin_memory()
+    hx.copy_(st["x"].cpu())
+    hl.copy_(st["logits"].cpu())
+    dx, dl = torch.empty_like(st["x"]), torch.empty_like(st["logits"])
+    y = st["y"]
+    hy = torch.empty(y.shape, dtype=y.dtype, device="cpu").pin_memory()
+    stream = torch.cuda.current_stream().cuda_stream
+    bp = st["bias"].data_ptr() if st["bias"] is not None else None
+    wp = st["rots"][0][1]
+
+    def step():
+        dx.copy_(hx, non_blocking=True)
+        dl.copy_(hl, non_blocking=True)
+        plan.forward(wp, dx.data_ptr(), dl.data_ptr(), bp, T, y.data_ptr(), st["bf16"], stream)
+        hy.copy_(y, non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    h2d = hx.numel() * hx.element_size() + hl.numel() * hl.element_size()
+    d2h = hy.numel() * hy.element_size()
+    return ms, h2d, d2h
+
+
+# ----------------------------------------------------------------- parts
+def part_w8a8(torch, steps=200):
+    from jimotono_b200 import lib
+    L = lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    res = {}
+    for (M, N, K, rot) in [(64, 4096, 1024, 32), (4096, 4096, 4096, 4)]:
+        bufs = []
+        for _ in range(rot):
+            X = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda")
+            W = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda")
+            sx = torch.rand(M, device="cuda") * 0.015 + 0.005
+            sw = torch.rand(N, device="cuda") * 0.009 + 0.001
+            Cm = torch.empty((M, N), device="cuda")
+            bufs.append((X, W, sx, sw, Cm))
+
+        def call(b):
+            X, W, sx, sw, Cm = b
+            return L.jt_b200_w8a8_gemm(X.data_ptr(), K, sx.data_ptr(), W.data_ptr(), K,
+                                       sw.data_ptr(), Cm.data_ptr(), N, M, N, K, stream)
+        for i in range(10):
+            call(bufs[i % rot])
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(steps):
+            call(bufs[i % rot])
+        e1.record()
+        torch.cuda.synchronize()
+        assert L.jt_b200_sync() == 0
+        us = e0.elapsed_time(e1) / steps * 1e3
+        byts = M * K + N * K + 4 * M * N + 4 * (M + N)
+        res[f"{M}x{N}x{K}"] = {"us": round(us, 3), "TOPS": round(2 * M * N * K / us / 1e6, 2),
+                               "GBs": round(byts / us / 1e3, 1)}
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-parts", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        from oracle.cpu_baseline import reference_arm
+        if rank == 0:
+            print(json.dumps(reference_arm(args.steps, args.warmup, METRIC)), flush=True)
+        return
+
+    import torch
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    hbm_peak, peak_kind = peaks()
+
+    with ClockSampler(local) as clk:
+        st = time_layer(torch, CFG5, rank, world, args.steps, args.warmup, seed=5)
+    ms = st["ms_per_step"]
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    tokens = CFG5["T"] if world > 1 else st["T"]
+    value = tokens / (ms / 1e3)
+    dm = st["dims"]
+    # dominant kernel: routed gate/up (int ops of the kept pairs)
+    stage = st["stage_ms"]
+    kept = st["kept"]
+    ops_gu = 2.0 * kept * dm.d * (2 * dm.f)
+    ops_dn = 2.0 * kept * dm.f * dm.d
+    ops_sh = 2.0 * st["T"] * dm.S * (2 * dm.fs * dm.d + dm.d * dm.fs)
+    e2e_ms, h2d, d2h = e2e_layer(torch, st, max(2, args.steps // 2), 2)
+    parts = {}
+    if rank == 0 and not args.no_parts:
+        st3 = time_layer(torch, CFG3, 0, 1, args.steps, args.warmup, seed=3, zipf=1.1, bf16=True)
+        parts["cfg3_prefill"] = {
+            "tokens_per_s": round(CFG3["T"] / (st3["ms_per_step"] / 1e3), 1),
+            "ms_per_step": round(st3["ms_per_step"], 4),
+            "stage_ms": [round(v, 4) for v in st3["stage_ms"]], "kept": st3["kept"],
+            "routed_TOPS": round(2.0 * st3["kept"] * CFG3["d"] * 3 * CFG3["f"] /
+                                 ((st3["stage_ms"][4] + st3["stage_ms"][5]) / 1e3) / 1e12, 1)}
+        del st3
+        st2 = time_layer(torch, CFG2, 0, 1, 200, 20, seed=2, nrot=8)
+        dm2 = st2["dims"]
+        per_tok = (dm2.k * (2 * dm2.f * (dm2.d // 4 + dm2.d // 64 * 2) + dm2.d * (dm2.f // 2 + dm2.f // 64 * 2))
+                   + dm2.S * (2 * dm2.fs * (dm2.d + 4) + dm2.d * (dm2.fs + 4)) + dm2.d * 8)
+        parts["cfg2_decode"] = {
+            "us_per_token": round(st2["ms_per_step"] * 1e3, 2), "bytes_per_token": per_tok,
+            "GBs": round(per_tok / (st2["ms_per_step"] / 1e3) / 1e9, 1),
+            "frac_hbm": round(per_tok / (st2["ms_per_step"] / 1e3) / 1e9 / hbm_peak, 4),
+            "stage_us": [round(v * 1e3, 2) for v in st2["stage_ms"]], "l2": "8 rotating weight copies (172 MB > L2)"}
+        del st2
+        parts["cfg1_w8a8"] = part_w8a8(torch)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        from oracle.cpu_baseline import cpu_baseline
+        cpu = cpu_baseline(seconds=20.0)
+    clocks = clk.summary()
+    if rank == 0:
+        gu_ms = stage[4]
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded; random-init packed weights)",
+            "config": {"workload": "cfg5 EP MoE layer: T=16384 d=2048 E=1024 f=1536 top-8 INT2/INT4 g64 + 2 shared INT8 f=4096, cap 1.5",
+                       "tokens": tokens, "parallelism": f"replicas{world}" if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (3.6 GB weights, 134 MB activations)"},
+            "e2e": {"value": round(tokens / (e2e_ms / 1e3) if world == 1 else st["T"] / (e2e_ms / 1e3), 1),
+                    "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": args.steps * (9 + 2 * dm.S),
+            "stage_ms": {n: round(v, 4) for n, v in zip(
+                ["route", "sort", "dispatch", "shared", "gateup", "down", "output"], stage)},
+            "kept_pairs": kept,
+            "roofline": {"bound": "tensor", "kernel": "routed gate/up (k_moe_gemm GU_ROUTED)",
+                         "achieved": round(ops_gu / (gu_ms / 1e3) / 1e12, 2), "peak": 4500.0,
+                         "unit": "TOPS", "frac": round(ops_gu / (gu_ms / 1e3) / 1e12 / 4500.0, 4),
+                         "peak_kind": "nominal dense int8 (no measured int8 peak in MEASURED_PEAKS)",
+                         "traffic": None},
+            "layer_TOPS": round((ops_gu + ops_dn + ops_sh) / (ms / 1e3) / 1e12, 1),
+            "clocks": clocks, "hbm_peak_gbs": hbm_peak, "hbm_peak_kind": peak_kind,
+            "parts": parts, "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    del st
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

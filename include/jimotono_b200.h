@@ -127,9 +127,9 @@ typedef struct jt_b200_moe_dims {
 
 typedef struct jt_b200_moe_weights { /* device pointers */
     const uint8_t *wg, *wu;  /* INT2 [E][f][d/4] */
-    const uint16_t *sg, *su; /* fp16 [E][f][d/64] */
+    const uint16_t *sg, *su; /* fp16 [E][d/64][f] (group-major) */
     const uint8_t *wd;       /* INT4 [E][d][f/2] */
-    const uint16_t *sd;      /* fp16 [E][d][f/64] */
+    const uint16_t *sd;      /* fp16 [E][f/64][d] (group-major) */
     const int8_t *wsg, *wsu; /* int8 [S][fs][d] */
     const float *ssg, *ssu;  /* fp32 [S][fs] per-channel scales */
     const int8_t *wsd;       /* int8 [S][d][fs] */
@@ -152,6 +152,23 @@ int jt_b200_moe_forward(jt_b200_moe_plan *plan, const jt_b200_moe_weights *w, co
                         const float *logits, const float *bias, int T, void *y, int y_bf16,
                         void *stream);
 
+/* Per-stage device timing of forward calls (CUDA events recorded on the
+ * forward's stream around each stage): begin() arms it for up to max_steps
+ * calls, end() waits for them and returns the summed milliseconds per
+ * stage (stage_ms[JT_B200_MOE_NSTAGE]) and the number of timed calls. */
+enum {
+    JT_B200_STAGE_ROUTE = 0,    /* top-k + softmax */
+    JT_B200_STAGE_SORT = 1,     /* capacity sort, drop, renormalization */
+    JT_B200_STAGE_DISPATCH = 2, /* per-token quantization + dispatch */
+    JT_B200_STAGE_SHARED = 3,   /* shared experts */
+    JT_B200_STAGE_GATEUP = 4,   /* routed gate/up + SwiGLU + requant */
+    JT_B200_STAGE_DOWN = 5,     /* routed down + weighted combine */
+    JT_B200_STAGE_OUTPUT = 6,   /* bf16 conversion */
+    JT_B200_MOE_NSTAGE = 7
+};
+int jt_b200_moe_profile_begin(jt_b200_moe_plan *plan, int max_steps);
+int jt_b200_moe_profile_end(jt_b200_moe_plan *plan, float *stage_ms, int nstage, int *steps);
+
 /* Copy an intermediate of the last forward to host memory (synchronizes). */
 enum {
     JT_B200_DBG_IDS = 0,     /* int32 [T][k] selected experts */
@@ -170,6 +187,9 @@ int jt_b200_moe_debug_copy(jt_b200_moe_plan *plan, int what, void *host_dst, siz
 /* Synchronize the current device and fold any kernel-reported fault into
  * the return code (JT_OK or JT_ERR_CUDA). */
 int jt_b200_sync(void);
+
+/* Human-readable description of the last failed launch on this thread. */
+const char *jt_b200_last_error(void);
 
 /* Library version string. */
 const char *jt_b200_version(void);

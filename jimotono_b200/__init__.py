@@ -45,4 +45,5 @@ class JtError(RuntimeError):
 
 def check(rc: int, what: str) -> None:
     if rc != JT_OK:
-        raise JtError(rc, what)
+        detail = lib().jt_b200_last_error().decode(errors="replace")
+        raise JtError(rc, f"{what} [{detail}]")

@@ -34,7 +34,10 @@ PROTOTYPES = {
     "jt_b200_moe_plan_bytes": (SZ, [P]),
     "jt_b200_moe_forward": (I, [P, P, P, P, P, I, P, I, P]),
     "jt_b200_moe_debug_copy": (I, [P, I, P, SZ]),
+    "jt_b200_moe_profile_begin": (I, [P, I]),
+    "jt_b200_moe_profile_end": (I, [P, P, I, P]),
     "jt_b200_sync": (I, []),
+    "jt_b200_last_error": (C.c_char_p, []),
     "jt_b200_version": (C.c_char_p, []),
 }
 

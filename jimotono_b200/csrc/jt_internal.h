@@ -49,37 +49,44 @@ int jtk_dequant_rows(const int8_t *src, const float *scales, size_t rows, size_t
 /* fp32 -> bf16 (round to nearest even). */
 int jtk_f32_to_bf16(const float *src, uint16_t *dst, size_t n, cudaStream_t stream);
 
-int jtk_fill_single_range(int32_t *row_off, int32_t *tile_off, int T, int bn,
-                          cudaStream_t stream);
+/* Shared-expert tile table: tiles[j] = {0, 64 j, T, 0}, ntiles[0] = ceil(T/64). */
+int jtk_fill_single_tiles(int4 *tiles, int32_t *ntiles, int T, cudaStream_t stream);
 
 /* MoE routing (jt_route.cu). */
 int jtk_route_topk(const float *logits, const float *bias, int T, int E, int k, int32_t *ids,
                    float *w, cudaStream_t stream);
 int jtk_sort_chunks(int T);
-int jtk_moe_sort(const int32_t *ids, const float *w_in, int T, int k, int E, int cap, int bn,
-                 int32_t *hist, int32_t *off, int32_t *tile_off, int32_t *meta, int32_t *perm,
-                 int32_t *pos, uint8_t *drop, float *w_out, cudaStream_t stream);
-int jtk_quant_dispatch(const float *x, int T, int d, int k, const int32_t *pos,
-                       const float *wfin, int8_t *xq, float *xs, int8_t *xd, float *xs_d,
-                       float *w_d, int32_t *tok_d, cudaStream_t stream);
 
-/* Expert GEMMs (jt_moe_gemm.cu).  Token tile = 64 rows. */
-#define JTK_MOE_BN 64
+/* Capacity sort.  tile_off [E+1]: 64-row token tiles per expert (scan);
+ * tiles: table of {expert, row0, row_end, 0} per token tile; meta[0] kept,
+ * meta[1] token tiles (= tile_off[E]), meta[2] max kept per expert. */
+int jtk_moe_sort(const int32_t *ids, const float *w_in, int T, int k, int E, int cap,
+                 int32_t *hist, int32_t *off, int32_t *tile_off, int4 *tiles, int32_t *meta,
+                 int32_t *perm, int32_t *pos, uint8_t *drop, float *w_out, cudaStream_t stream);
+/* Per-token quantization + dispatch; row_meta[row] = {scale, weight, token bits, 0}
+ * for every kept row, sh_meta[t] = {scale, 1, t bits, 0} (may be NULL). */
+int jtk_quant_dispatch(const float *x, int T, int d, int k, const int32_t *pos,
+                       const float *wfin, int8_t *xq, float *xs, int8_t *xd, float4 *row_meta,
+                       float4 *sh_meta, cudaStream_t stream);
+
+/* Expert GEMMs (jt_moe_gemm.cu), 64-row token tiles.  tiles / ntiles: tile
+ * table and its length (device).  row_meta [rows]: float4 records above.
+ * Group scales fp16 [E][K/64][n_ch]; h scales hs [rows][hs_ld] with
+ * hs_ld = round_up(n_ch/64, 4). */
 int jtk_moe_gateup_routed(const uint8_t *wg, const uint8_t *wu, const void *gs, const void *us,
-                          int E, int f, int d, const int8_t *xd, int rows_cap, const float *xs_d,
-                          const int32_t *row_off, const int32_t *tile_off, int8_t *hq, float *hs,
-                          int max_tiles_hint, cudaStream_t stream);
+                          int E, int f, int d, const int8_t *xd, int rows_cap,
+                          const float4 *row_meta, const int4 *tiles, const int32_t *ntiles,
+                          int8_t *hq, float *hs, int max_tiles_hint, cudaStream_t stream);
 int jtk_moe_down_routed(const uint8_t *wd, const void *ds, int E, int d, int f, const int8_t *hq,
-                        int rows_cap, const float *hs, const int32_t *row_off,
-                        const int32_t *tile_off, const int32_t *row_tok, const float *row_w,
-                        float *y, int max_tiles_hint, cudaStream_t stream);
+                        int rows_cap, const float *hs, const float4 *row_meta, const int4 *tiles,
+                        const int32_t *ntiles, float *y, int max_tiles_hint, cudaStream_t stream);
 int jtk_moe_gateup_shared(const int8_t *wsg, const int8_t *wsu, const float *ssg,
                           const float *ssu, int fs, int d, const int8_t *xq, int T,
-                          const float *xs, const int32_t *row_off, const int32_t *tile_off,
+                          const float4 *sh_meta, const int4 *tiles, const int32_t *ntiles,
                           int8_t *hq, float *hs, cudaStream_t stream);
 int jtk_moe_down_shared(const int8_t *wsd, const float *ssd, int d, int fs, const int8_t *hq,
-                        int T, const float *hs, const int32_t *row_off, const int32_t *tile_off,
-                        float *y, int accumulate, cudaStream_t stream);
+                        int T, const float *hs, const float4 *sh_meta, const int4 *tiles,
+                        const int32_t *ntiles, float *y, int accumulate, cudaStream_t stream);
 
 /* Device error word shared by all kernels of the library (0 = clean). */
 int jtk_read_and_clear_error(int *out_code);

@@ -21,22 +21,43 @@
 #include <math.h>
 #include <stdint.h>
 #include <stdlib.h>
+#include <stdio.h>
 #include <string.h>
 
 #include "../../include/jimotono_b200.h"
 #include "jt_internal.h"
+
+/* Description of the last failed launch (per thread): which launcher and
+ * the CUDA runtime's message. */
+static _Thread_local char g_last_error[512];
+
+void jt_set_last_error(const char *what, int code) {
+    const cudaError_t e = cudaPeekAtLastError();
+    snprintf(g_last_error, sizeof(g_last_error), "%.300s -> %d (%s)", what, code,
+             cudaGetErrorString(e));
+}
+
+const char *jt_b200_last_error(void) { return g_last_error; }
 
 struct jt_b200_moe_plan {
     jt_b200_moe_dims dm;
     int dev;
     void *arena;
     size_t arena_bytes;
-    int32_t *ids, *perm, *pos, *hist, *off, *tile_off, *meta, *tok_d;
-    int32_t *sh_row_off, *sh_tile_off;
-    float *w_raw, *w_fin, *xs, *xs_d, *w_d, *hs, *hs_s, *y32;
+    int32_t *ids, *perm, *pos, *hist, *off, *tile_off, *meta, *sh_ntiles;
+    int4 *tiles, *sh_tiles;
+    float4 *row_meta, *sh_meta;
+    float *w_raw, *w_fin, *xs, *hs, *hs_s, *y32;
     uint8_t *drop;
     int8_t *xq, *xd, *hq, *hq_s;
+    /* optional per-stage profiling: events[step][JT_B200_MOE_NSTAGE + 1] */
+    cudaEvent_t *prof_ev;
+    int prof_max, prof_used;
 };
+
+/* Row stride (floats) of the per-(row, 64-channel group) h scales: padded to
+ * 16 bytes so a token tile's scales are one TMA box. */
+static int hs_ld(int n_ch) { return ((n_ch / 64) + 3) & ~3; }
 
 static size_t align_up(size_t v) { return (v + 255u) & ~(size_t)255u; }
 
@@ -67,22 +88,23 @@ int jt_b200_moe_plan_create(const jt_b200_moe_dims *dims, jt_b200_moe_plan **out
     const size_t fs = dims->S > 0 ? (size_t)dims->fs : 64;
     const size_t Tk = T * k;
     const size_t nch = (size_t)jtk_sort_chunks(dims->T);
+    const size_t max_tiles = Tk / 64 + E + 1;
     struct {
         void **dst;
         size_t bytes;
     } parts[] = {
-        {(void **)&p->ids, Tk * 4},        {(void **)&p->perm, Tk * 4},
-        {(void **)&p->pos, Tk * 4},        {(void **)&p->hist, nch * E * 4},
-        {(void **)&p->off, (E + 1) * 4},   {(void **)&p->tile_off, (E + 1) * 4},
-        {(void **)&p->meta, 64},           {(void **)&p->tok_d, Tk * 4},
-        {(void **)&p->sh_row_off, 64},     {(void **)&p->sh_tile_off, 64},
-        {(void **)&p->w_raw, Tk * 4},      {(void **)&p->w_fin, Tk * 4},
-        {(void **)&p->xs, T * 4},          {(void **)&p->xs_d, Tk * 4},
-        {(void **)&p->w_d, Tk * 4},        {(void **)&p->hs, Tk * (f / 64) * 4},
-        {(void **)&p->hs_s, T * (fs / 64) * 4},
-        {(void **)&p->y32, T * d * 4},     {(void **)&p->drop, Tk},
-        {(void **)&p->xq, T * d},          {(void **)&p->xd, Tk * d},
-        {(void **)&p->hq, Tk * f},         {(void **)&p->hq_s, T * fs},
+        {(void **)&p->ids, Tk * 4},          {(void **)&p->perm, Tk * 4},
+        {(void **)&p->pos, Tk * 4},          {(void **)&p->hist, nch * E * 4},
+        {(void **)&p->off, (E + 1) * 4},     {(void **)&p->tile_off, (E + 1) * 4},
+        {(void **)&p->meta, 64},             {(void **)&p->sh_ntiles, 64},
+        {(void **)&p->tiles, max_tiles * 16}, {(void **)&p->sh_tiles, (T / 64 + 1) * 16},
+        {(void **)&p->row_meta, Tk * 16},    {(void **)&p->sh_meta, T * 16},
+        {(void **)&p->w_raw, Tk * 4},        {(void **)&p->w_fin, Tk * 4},
+        {(void **)&p->xs, T * 4},            {(void **)&p->hs, Tk * (size_t)hs_ld((int)f) * 4},
+        {(void **)&p->hs_s, T * (size_t)hs_ld((int)fs) * 4},
+        {(void **)&p->y32, T * d * 4},       {(void **)&p->drop, Tk},
+        {(void **)&p->xq, T * d},            {(void **)&p->xd, Tk * d},
+        {(void **)&p->hq, Tk * f},           {(void **)&p->hq_s, T * fs},
     };
     const size_t nparts = sizeof(parts) / sizeof(parts[0]);
     size_t total = 0;
@@ -110,8 +132,70 @@ int jt_b200_moe_plan_create(const jt_b200_moe_dims *dims, jt_b200_moe_plan **out
     return JT_OK;
 }
 
+static void prof_free(jt_b200_moe_plan *p) {
+    if (!p->prof_ev) return;
+    for (int i = 0; i < p->prof_max * (JT_B200_MOE_NSTAGE + 1); i++) cudaEventDestroy(p->prof_ev[i]);
+    free(p->prof_ev);
+    p->prof_ev = NULL;
+    p->prof_max = p->prof_used = 0;
+}
+
+int jt_b200_moe_profile_begin(jt_b200_moe_plan *plan, int max_steps) {
+    if (plan == NULL || max_steps <= 0 || max_steps > 4096) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    prof_free(plan);
+    const int n = max_steps * (JT_B200_MOE_NSTAGE + 1);
+    plan->prof_ev = (cudaEvent_t *)calloc((size_t)n, sizeof(cudaEvent_t));
+    if (!plan->prof_ev) {
+        errno = ENOMEM;
+        return JT_ERR_NOMEM;
+    }
+    for (int i = 0; i < n; i++) {
+        if (cudaEventCreate(&plan->prof_ev[i]) != cudaSuccess) {
+            plan->prof_max = i / (JT_B200_MOE_NSTAGE + 1);
+            prof_free(plan);
+            errno = EIO;
+            return JT_ERR_CUDA;
+        }
+    }
+    plan->prof_max = max_steps;
+    plan->prof_used = 0;
+    return JT_OK;
+}
+
+int jt_b200_moe_profile_end(jt_b200_moe_plan *plan, float *stage_ms, int nstage, int *steps) {
+    if (plan == NULL || stage_ms == NULL || nstage < JT_B200_MOE_NSTAGE || !plan->prof_ev) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    for (int s = 0; s < JT_B200_MOE_NSTAGE; s++) stage_ms[s] = 0.0f;
+    int rc = JT_OK;
+    for (int i = 0; i < plan->prof_used && rc == JT_OK; i++) {
+        cudaEvent_t *ev = plan->prof_ev + (size_t)i * (JT_B200_MOE_NSTAGE + 1);
+        if (cudaEventSynchronize(ev[JT_B200_MOE_NSTAGE]) != cudaSuccess) {
+            rc = JT_ERR_CUDA;
+            break;
+        }
+        for (int s = 0; s < JT_B200_MOE_NSTAGE; s++) {
+            float ms = 0.0f;
+            if (cudaEventElapsedTime(&ms, ev[s], ev[s + 1]) != cudaSuccess) {
+                rc = JT_ERR_CUDA;
+                break;
+            }
+            stage_ms[s] += ms;
+        }
+    }
+    if (steps) *steps = plan->prof_used;
+    prof_free(plan);
+    if (rc != JT_OK) errno = EIO;
+    return rc;
+}
+
 int jt_b200_moe_plan_destroy(jt_b200_moe_plan *plan) {
     if (plan == NULL) return JT_OK;
+    prof_free(plan);
     if (plan->arena) cudaFree(plan->arena);
     free(plan);
     return JT_OK;
@@ -127,13 +211,14 @@ static int weights_valid(const jt_b200_moe_weights *w, int S) {
     return 1;
 }
 
-#define LAUNCH(expr)                 \
-    do {                             \
-        int _r = (expr);             \
-        if (_r != 0) {               \
-            errno = _r == -1 ? EINVAL : EIO; \
-            return _r == -1 ? JT_ERR_INVAL : JT_ERR_CUDA; \
-        }                            \
+#define LAUNCH(expr)                                                          \
+    do {                                                                      \
+        int _r = (expr);                                                      \
+        if (_r != 0) {                                                        \
+            jt_set_last_error(#expr, _r);                                     \
+            errno = _r == -1 ? EINVAL : EIO;                                  \
+            return _r == -1 ? JT_ERR_INVAL : JT_ERR_CUDA;                     \
+        }                                                                     \
     } while (0)
 
 int jt_b200_moe_forward(jt_b200_moe_plan *plan, const jt_b200_moe_weights *w, const float *x,
@@ -158,24 +243,36 @@ int jt_b200_moe_forward(jt_b200_moe_plan *plan, const jt_b200_moe_weights *w, co
         return JT_ERR_INVAL;
     }
     const int cap = (int)capd;
+    int gu_hint = 0, dn_hint = 0;
     float *yf = y_bf16 ? plan->y32 : (float *)y;
+    cudaEvent_t *ev = NULL;
+    if (plan->prof_ev && plan->prof_used < plan->prof_max)
+        ev = plan->prof_ev + (size_t)(plan->prof_used++) * (JT_B200_MOE_NSTAGE + 1);
+#define MARK(i) \
+    do { \
+        if (ev) cudaEventRecord(ev[(i)], st); \
+    } while (0)
 
+    MARK(JT_B200_STAGE_ROUTE);
     LAUNCH(jtk_route_topk(logits, bias, T, E, k, plan->ids, plan->w_raw, st));
-    LAUNCH(jtk_moe_sort(plan->ids, plan->w_raw, T, k, E, cap, JTK_MOE_BN, plan->hist, plan->off,
-                        plan->tile_off, plan->meta, plan->perm, plan->pos, plan->drop,
+    MARK(JT_B200_STAGE_SORT);
+    LAUNCH(jtk_moe_sort(plan->ids, plan->w_raw, T, k, E, cap, plan->hist, plan->off,
+                        plan->tile_off, plan->tiles, plan->meta, plan->perm, plan->pos, plan->drop,
                         plan->w_fin, st));
+    MARK(JT_B200_STAGE_DISPATCH);
     LAUNCH(jtk_quant_dispatch(x, T, d, k, plan->pos, plan->w_fin, plan->xq, plan->xs, plan->xd,
-                              plan->xs_d, plan->w_d, plan->tok_d, st));
+                              plan->row_meta, S > 0 ? plan->sh_meta : NULL, st));
+    MARK(JT_B200_STAGE_SHARED);
     if (S > 0) {
-        LAUNCH(jtk_fill_single_range(plan->sh_row_off, plan->sh_tile_off, T, JTK_MOE_BN, st));
+        LAUNCH(jtk_fill_single_tiles(plan->sh_tiles, plan->sh_ntiles, T, st));
         for (int s = 0; s < S; s++) {
             LAUNCH(jtk_moe_gateup_shared(w->wsg + (size_t)s * fs * d, w->wsu + (size_t)s * fs * d,
                                          w->ssg + (size_t)s * fs, w->ssu + (size_t)s * fs, fs, d,
-                                         plan->xq, T, plan->xs, plan->sh_row_off,
-                                         plan->sh_tile_off, plan->hq_s, plan->hs_s, st));
+                                         plan->xq, T, plan->sh_meta, plan->sh_tiles,
+                                         plan->sh_ntiles, plan->hq_s, plan->hs_s, st));
             LAUNCH(jtk_moe_down_shared(w->wsd + (size_t)s * d * fs, w->ssd + (size_t)s * d, d, fs,
-                                       plan->hq_s, T, plan->hs_s, plan->sh_row_off,
-                                       plan->sh_tile_off, yf, s > 0, st));
+                                       plan->hq_s, T, plan->hs_s, plan->sh_meta, plan->sh_tiles,
+                                       plan->sh_ntiles, yf, s > 0, st));
         }
     } else {
         if (cudaMemsetAsync(yf, 0, (size_t)T * d * sizeof(float), st) != cudaSuccess) {
@@ -183,11 +280,26 @@ int jt_b200_moe_forward(jt_b200_moe_plan *plan, const jt_b200_moe_weights *w, co
             return JT_ERR_CUDA;
         }
     }
+    /* Upper bound of the device-side token-tile count: every non-empty
+     * expert adds at most one partial tile to (kept pairs)/64 full ones. */
+    {
+        const long long pairs = (long long)T * k;
+        const long long ne = pairs < E ? pairs : E;
+        const long long tl = ne + pairs / 64;
+        gu_hint = tl * (f / 64) > 0x7fffffffLL ? 0 : (int)(tl * (f / 64));
+        dn_hint = tl * (d / 128) > 0x7fffffffLL ? 0 : (int)(tl * (d / 128));
+    }
+    MARK(JT_B200_STAGE_GATEUP);
     LAUNCH(jtk_moe_gateup_routed(w->wg, w->wu, w->sg, w->su, E, f, d, plan->xd, rows_cap,
-                                 plan->xs_d, plan->off, plan->tile_off, plan->hq, plan->hs, 0, st));
-    LAUNCH(jtk_moe_down_routed(w->wd, w->sd, E, d, f, plan->hq, rows_cap, plan->hs, plan->off,
-                               plan->tile_off, plan->tok_d, plan->w_d, yf, 0, st));
+                                 plan->row_meta, plan->tiles, plan->tile_off + E, plan->hq,
+                                 plan->hs, gu_hint, st));
+    MARK(JT_B200_STAGE_DOWN);
+    LAUNCH(jtk_moe_down_routed(w->wd, w->sd, E, d, f, plan->hq, rows_cap, plan->hs,
+                               plan->row_meta, plan->tiles, plan->tile_off + E, yf, dn_hint, st));
+    MARK(JT_B200_STAGE_OUTPUT);
     if (y_bf16) LAUNCH(jtk_f32_to_bf16(yf, (uint16_t *)y, (size_t)T * d, st));
+    MARK(JT_B200_MOE_NSTAGE);
+#undef MARK
     return JT_OK;
 }
 
@@ -209,7 +321,22 @@ int jt_b200_moe_debug_copy(jt_b200_moe_plan *plan, int what, void *host_dst, siz
         case JT_B200_DBG_XQ: src = plan->xq; cap = T * d; break;
         case JT_B200_DBG_XS: src = plan->xs; cap = T * 4; break;
         case JT_B200_DBG_HQ: src = plan->hq; cap = T * k * f; break;
-        case JT_B200_DBG_HS: src = plan->hs; cap = T * k * (f / 64) * 4; break;
+        case JT_B200_DBG_HS: {
+            /* stored with a padded row stride; return [rows][f/64] */
+            const size_t G = f / 64, ld = (size_t)hs_ld((int)f);
+            if (bytes % (G * 4) || bytes / (G * 4) > T * k) {
+                errno = EINVAL;
+                return JT_ERR_INVAL;
+            }
+            const size_t rows = bytes / (G * 4);
+            if (cudaDeviceSynchronize() != cudaSuccess ||
+                cudaMemcpy2D(host_dst, G * 4, plan->hs, ld * 4, G * 4, rows,
+                             cudaMemcpyDeviceToHost) != cudaSuccess) {
+                errno = EIO;
+                return JT_ERR_CUDA;
+            }
+            return JT_OK;
+        }
         case JT_B200_DBG_META: src = plan->meta; cap = 16; break;
         default:
             errno = EINVAL;

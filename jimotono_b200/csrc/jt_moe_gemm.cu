@@ -16,18 +16,36 @@
 //   DN_SHARED  down projection of a shared expert (int8, per-channel), added
 //              into the layer output (moe_layer.c:1549-1559).
 //
-// Orientation: the MMA M side is 128 weight channels (TMEM lane = output
-// channel, so per-channel and per-group scales are per-thread scalars); the
-// MMA N side is a tile of kBN token rows.  Ragged experts are handled by a
-// device-side tile list (expert e owns token tiles tile_off[e]..tile_off[e+1]
-// over its rows row_off[e]..row_off[e+1]), so one persistent launch covers
-// every expert whatever the routing produced.
+// Orientation: the MMA M side is 128 weight rows (TMEM lane = weight row, so
+// per-channel and per-group weight scales are per-thread scalars); the MMA N
+// side is a tile of BN token rows.  Gate/up tiles stack 64 gate rows over the
+// same 64 up rows, so one MMA produces both halves of the SwiGLU input.
+// Ragged experts use a device-side tile list (expert e owns token tiles
+// tile_off[e]..tile_off[e+1] over rows row_off[e]..row_off[e+1]), so one
+// persistent launch covers every expert whatever the routing produced.
 //
-// Warp roles (10 warps): w0 TMA producer, w1 TMEM allocator + MMA issuer,
-// w2-5 unpack (packed INT2/INT4 bytes in SMEM -> int8 codes in the
-// 128-byte-swizzled K-major operand layout), w6-9 epilogue.  Group scales
-// force the int32 accumulator to be drained every 64 K: two TMEM slots let
-// the epilogue drain slot s while the MMAs fill slot s^1.
+// Warp roles (14 warps): w0 TMA producer (operands every 128 K, the tile's
+// fp16 group scales once per tile), w1 TMEM allocator + MMA issuer, w2-5
+// unpack (packed INT2/INT4 bytes -> int8 codes in the 128-byte-swizzled
+// K-major layout), w6-13 epilogue (two warps per TMEM lane quarter, one per
+// half of the token columns).
+//
+// Group scales force a drain of the int32 accumulator every 64 K.  The drain
+// is kept cheap and off the tensor core's critical path:
+//   * a ring of 512/BN TMEM accumulators lets the MMAs run several groups
+//     ahead of the epilogue;
+//   * every accumulator is pre-set to the float bit pattern 0x4B400000
+//     (= 12582912.0f) and the MMAs only accumulate, so each drained word is
+//     the exact float 12582912 + P (|P| <= 64*127*127 < 2^22): one packed
+//     subtract recovers P as a float, and the fold runs as packed f32x2 FMAs
+//     with the same IEEE results as the scalar restatement;
+//   * everything the epilogue needs per tile (the tile's expert and rows, the
+//     per-row metadata, the fp16 group scales, the activation group scales
+//     of the down projection) is fetched by the producer warp, which runs
+//     stages ahead, into a double-buffered SMEM tile slot - the epilogue
+//     never waits on global memory;
+//   * the drain takes two 64-K units per pass (one TMEM load wait, one store
+//     wait and one slot release round per pair).
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -42,88 +60,76 @@ namespace {
 
 constexpr int kBM = 128;  // MMA M: weight rows per tile
 constexpr int kBN = 64;   // MMA N: token rows per tile
+constexpr int kBH = 32;   // token columns per epilogue warp
 constexpr int kBK = 128;  // K per pipeline stage
-constexpr int kThreads = 320;
-constexpr int kEpiWarp0 = 6;
+constexpr int kThreads = 448;  // 14 warps
+constexpr int kEpiWarp0 = 6;   // warps 6..13: epilogue
+constexpr int kEpiThreads = 256;
+constexpr uint32_t kMagicU = 0x4B400000u;
+constexpr float kMagicF = 12582912.0f;
+constexpr int kMaxGroups = 64;  // K <= 4096
+constexpr size_t kSmemLimit = 232448;
 
 enum Mode { GU_ROUTED = 0, GU_SHARED = 1, DN_ROUTED = 2, DN_SHARED = 3 };
+
+__host__ __device__ constexpr uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
 template <int MODE>
 struct Cfg {
     static constexpr bool kGateUp = (MODE == GU_ROUTED || MODE == GU_SHARED);
     static constexpr bool kPacked = (MODE == GU_ROUTED || MODE == DN_ROUTED);
-    // gate/up tiles stack 64 gate rows over the same 64 up rows
-    static constexpr int kChTile = kGateUp ? 64 : 128;  // output channels per tile
+    static constexpr bool kDown = !kGateUp;
+    static constexpr bool kMagic = (MODE != GU_SHARED);  // 64-K drain units
+    static constexpr int kUB = kMagic ? 2 : 1;           // units per drain pass
+    static constexpr int kChTile = kGateUp ? 64 : 128;   // output channels per tile
     static constexpr int kBits = MODE == GU_ROUTED ? 2 : (MODE == DN_ROUTED ? 4 : 8);
     static constexpr uint32_t kPackedRow = kPacked ? (kBK * kBits / 8) : 0;  // bytes/row/stage
     static constexpr uint32_t kAU = kBM * kBK;  // unpacked operand, 16 KB
     static constexpr uint32_t kX = kBN * kBK;   // token rows, 8 KB
     static constexpr uint32_t kAP = kBM * kPackedRow;
     static constexpr uint32_t kStage = kAU + kX + kAP;
-    static constexpr uint32_t kHTile = kBN * 64 * 4;  // gate/up: g then h [row][64 ch];
-                                                      // down: hs [group][row]
-    static constexpr int kStagesRaw = (int)((200 * 1024 - kHTile) / kStage);
+    // per-tile slot: info | row meta [kBN] float4 | group scales fp16 [G][128] |
+    //                activation group scales [kBN][hs_ld] (down)
+    static constexpr uint32_t kOffMeta = 128;
+    static constexpr uint32_t kOffScale = kOffMeta + kBN * 16;
+    static constexpr uint32_t kOffBlk = kOffScale + (kPacked ? kMaxGroups * kBM * 2 : 0);
+    static constexpr uint32_t kSlot = align_up(kOffBlk + (kDown ? kBN * kMaxGroups * 4 : 0), 1024);
+    static constexpr uint32_t kHTile = kGateUp ? 2 * kBN * 64 * 4 : 0;  // g then u [row][64]
+    static constexpr size_t kFixed = 1024 + 2 * (size_t)kSlot + kHTile + 1024;
+    static constexpr int kStagesRaw = (int)((kSmemLimit - kFixed) / kStage);
     static constexpr int kStages = kStagesRaw > 6 ? 6 : kStagesRaw;
-    // K per drain: group-64 weights and the 64-channel activation blocks
-    // both drain every 64 K; the shared gate/up accumulates a whole tile.
-    static constexpr int kUnitK = (MODE == GU_SHARED) ? 0 : 64;
-    static constexpr uint32_t kTmemCols = 2 * kBN;
-    static constexpr size_t kSmem = 1024 + (size_t)kStages * kStage + kHTile + 1024;
+    static constexpr int kUnitK = kMagic ? 64 : 0;  // 0: one unit per tile
+    static constexpr int kSlots = 512 / kBN;        // TMEM accumulators
+    static constexpr uint32_t kTmemCols = 512;
+    static constexpr size_t kSmem = kFixed + (size_t)kStages * kStage;
+    static_assert(kStages >= 2, "pipeline depth");
+    static_assert(kSmem <= kSmemLimit, "shared memory");
+    static_assert(kSlots % 2 == 0, "unit pairs never wrap the slot ring");
 };
 
 struct MoeGemmParams {
     CUtensorMap tmA0;  // gate (or down) weights: packed bytes or int8 rows
     CUtensorMap tmA1;  // up weights (gate/up modes)
     CUtensorMap tmX;   // token rows [rows][K] int8
-    const int32_t *row_off;   // [E+1] token-row range per expert
-    const int32_t *tile_off;  // [E+1] token-tile range per expert (tile_off[E] = total)
-    int E;
-    int n_ch;  // output channels per expert (f for gate/up, d for down)
-    int K;     // reduction length (d for gate/up, f for down)
-    const __half *gs0;  // group scales [E][n_ch][K/64] (routed)
-    const __half *gs1;
+    CUtensorMap tmS0;  // group scales of A0, fp16 [E][K/64][n_ch] as bytes (routed)
+    CUtensorMap tmS1;  // group scales of A1
+    CUtensorMap tmM;   // row metadata [rows][16 B]
+    CUtensorMap tmH;   // activation group scales [rows][hs_ld] fp32 (down)
+    const int4 *tiles;       // token-tile table {e, row0, row_end, 0}
+    const int32_t *ntiles;   // its length
+    int n_ch;   // output channels per expert (f for gate/up, d for down)
+    int K;      // reduction length (d for gate/up, f for down)
+    int hs_ld;  // row stride of the activation group scales (down) / of hs (gate/up out)
     const float *cs0;  // per-channel scales [n_ch] (shared)
     const float *cs1;
-    const float *row_scale;  // gate/up: per-row activation scale [rows]
-    const float *blk_scale;  // down: per-(row, 64-K group) activation scale [rows][K/64]
-    int8_t *hq;              // gate/up out: codes [rows][n_ch]
-    float *hs;               // gate/up out: scales [rows][n_ch/64]
-    float *y;                // down out: [T][n_ch] fp32
-    const int32_t *row_tok;  // down: token of each row (routed)
-    const float *row_w;      // down: weight of each row (routed)
-    int y_accumulate;        // down: 0 store, 1 atomic add
+    int8_t *hq;        // gate/up out: codes [rows][n_ch]
+    float *hs;         // gate/up out: scales [rows][hs_ld]
+    float *y;          // down out: [T][n_ch] fp32
+    int y_accumulate;  // down: 0 store, 1 atomic add
     int *err;
 };
 
-__device__ __forceinline__ void named_bar_epi() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-
-// Expert owning token tile v (tile_off ascending, tile_off[E] = total).
-__device__ __forceinline__ int find_expert(const int32_t *tile_off, int E, int v) {
-    int lo = 0, hi = E;  // invariant tile_off[lo] <= v < tile_off[hi]
-    while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (__ldg(&tile_off[mid]) <= v) lo = mid;
-        else hi = mid;
-    }
-    return lo;
-}
-
-struct TileInfo {
-    int e, c0, r0, r_end;
-};
-
-template <int CH_TILE>
-__device__ __forceinline__ TileInfo tile_info(const MoeGemmParams &p, int u, int nch_tiles) {
-    TileInfo ti;
-    const int c = u % nch_tiles;
-    const int v = u / nch_tiles;
-    ti.e = find_expert(p.tile_off, p.E, v);
-    const int j = v - __ldg(&p.tile_off[ti.e]);
-    ti.c0 = c * CH_TILE;
-    ti.r0 = __ldg(&p.row_off[ti.e]) + j * kBN;
-    ti.r_end = __ldg(&p.row_off[ti.e + 1]);
-    return ti;
-}
+__device__ __forceinline__ void named_bar_epi() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 // ---------------------------------------------------------------- unpack
 // 16 INT2 codes (one 32-bit packed word, little-endian along K) -> 16 int8
@@ -167,19 +173,58 @@ template <int BITS>
 __device__ __forceinline__ void unpack_row(const uint8_t *src, uint8_t *dst_tile, int r) {
     uint8_t *row = dst_tile + r * 128;
     if (BITS == 2) {
-        const uint4 a = *reinterpret_cast<const uint4 *>(src);
-        const uint4 b = *reinterpret_cast<const uint4 *>(src + 16);
-        const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {  // 16 packed bytes -> 64 codes per pass
+            const uint4 a = *reinterpret_cast<const uint4 *>(src + 16 * h);
+            const uint32_t w[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-            *reinterpret_cast<uint4 *>(row + ((i ^ (r & 7)) << 4)) = unpack_int2_x16(w[i]);
+            for (int i = 0; i < 4; ++i) {
+                const int chunk = 4 * h + i;
+                *reinterpret_cast<uint4 *>(row + ((chunk ^ (r & 7)) << 4)) = unpack_int2_x16(w[i]);
+            }
+        }
     } else {
+#pragma unroll 1
+        for (int h = 0; h < 4; ++h) {  // 16 packed bytes -> 32 codes per pass
+            const uint4 a = *reinterpret_cast<const uint4 *>(src + 16 * h);
+            const uint2 l0 = unpack_int4_x8(a.x), h0 = unpack_int4_x8(a.y);
+            const uint2 l1 = unpack_int4_x8(a.z), h1 = unpack_int4_x8(a.w);
+            *reinterpret_cast<uint4 *>(row + (((2 * h) ^ (r & 7)) << 4)) = make_uint4(l0.x, l0.y, h0.x, h0.y);
+            *reinterpret_cast<uint4 *>(row + (((2 * h + 1) ^ (r & 7)) << 4)) = make_uint4(l1.x, l1.y, h1.x, h1.y);
+        }
+    }
+}
+
+__device__ __forceinline__ float2 as_f2(uint32_t a, uint32_t b) {
+    return make_float2(__uint_as_float(a), __uint_as_float(b));
+}
+
+__device__ __forceinline__ void st_shared_v4(void *p, int4 v) {
+    asm volatile("st.shared.v4.s32 [%0], {%1, %2, %3, %4};" ::"r"(jt::smem_u32(p)), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+// Fold one drained 32-column chunk of one 64-K unit into the running sums.
+template <int MODE>
+__device__ __forceinline__ void fold_chunk(float2 (&r2)[kBH / 2], const uint32_t (&a)[32], float s,
+                                           const float *blk, int hs_ld, int g) {
+    const float2 s2 = make_float2(s, s);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint2 a = *reinterpret_cast<const uint2 *>(src + 8 * i);
-            const uint2 lo = unpack_int4_x8(a.x), hi = unpack_int4_x8(a.y);
-            *reinterpret_cast<uint4 *>(row + ((i ^ (r & 7)) << 4)) =
-                make_uint4(lo.x, lo.y, hi.x, hi.y);
+    for (int j = 0; j < 32; j += 2) {
+        float2 &rr = r2[j / 2];
+        if (MODE == GU_SHARED) {
+            rr = make_float2(__int2float_rn((int32_t)a[j]), __int2float_rn((int32_t)a[j + 1]));
+        } else {
+            const float2 pf = __fadd2_rn(as_f2(a[j], a[j + 1]), make_float2(-kMagicF, -kMagicF));
+            if (MODE == GU_ROUTED) {
+                rr = __ffma2_rn(pf, s2, rr);
+            } else {
+                // activation group scale of columns j, j+1 (SMEM broadcast)
+                const float2 hv = make_float2(blk[j * hs_ld + g], blk[(j + 1) * hs_ld + g]);
+                const float2 t = (MODE == DN_ROUTED) ? __fmul2_rn(pf, s2) : pf;
+                rr = __ffma2_rn(t, hv, rr);
+            }
         }
     }
 }
@@ -188,26 +233,30 @@ template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant__ MoeGemmParams p) {
     using C = Cfg<MODE>;
     constexpr int S = C::kStages;
+    constexpr int NS = C::kSlots;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    float *h_tile = reinterpret_cast<float *>(smem + S * C::kStage);
-    uint8_t *tail = smem + S * C::kStage + C::kHTile;
+    uint8_t *slot_base = smem + S * C::kStage;  // 2 tile slots
+    float *h_tile = reinterpret_cast<float *>(slot_base + 2 * C::kSlot);
+    uint8_t *tail = reinterpret_cast<uint8_t *>(h_tile) + C::kHTile;
     uint64_t *full = reinterpret_cast<uint64_t *>(tail);  // TMA landed
-    uint64_t *ready = full + S;    // operands unpacked (packed modes)
-    uint64_t *empty = ready + S;   // MMAs finished reading the stage
-    uint64_t *tfull = empty + S;   // drain slot filled
-    uint64_t *tempty = tfull + 2;  // drain slot drained
-    uint64_t *drain = tempty + 2;
+    uint64_t *ready = full + S;      // operands unpacked (packed modes)
+    uint64_t *empty = ready + S;     // MMAs finished reading the stage
+    uint64_t *tfull = empty + S;     // drain slot filled
+    uint64_t *tempty = tfull + NS;   // drain slot drained and re-armed
+    uint64_t *pfull = tempty + NS;   // tile slot filled (producer)
+    uint64_t *pempty = pfull + 2;    // tile slot released (epilogue)
+    uint64_t *drain = pempty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-    float *s_rowa = reinterpret_cast<float *>(tail + 512);        // [kBN]
-    int *s_rowt = reinterpret_cast<int *>(tail + 512 + 4 * kBN);  // [kBN]
+    static_assert((3 * S + 2 * NS + 5) * 8 + 8 <= 1024, "barrier area");
 
     const int warp = jt::warp_id(), lane = jt::lane_id();
     const int nch_tiles = p.n_ch / C::kChTile;
     const int nk = p.K / kBK;
-    const int total = __ldg(&p.tile_off[p.E]) * nch_tiles;
+    const int ngroups = p.K / 64;
+    const int total = __ldg(p.ntiles) * nch_tiles;
     int *err = p.err;
     // stage layout: [A unpacked 128 x 128 | X 64 x 128 | A packed 128 x kPackedRow]
     auto stage_ptr = [&](int s) { return smem + s * C::kStage; };
@@ -218,9 +267,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
             jt::mbar_init(&ready[s], 4);
             jt::mbar_init(&empty[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < NS; ++b) {
             jt::mbar_init(&tfull[b], 1);
-            jt::mbar_init(&tempty[b], 4);
+            jt::mbar_init(&tempty[b], 8);  // one arrival per epilogue warp
+        }
+        for (int b = 0; b < 2; ++b) {
+            jt::mbar_init(&pfull[b], 1);
+            jt::mbar_init(&pempty[b], 8);
         }
         jt::mbar_init(drain, 1);
         *abort_flag = 0;
@@ -230,6 +283,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
         jt::prefetch_tmap(&p.tmA0);
         if (C::kGateUp) jt::prefetch_tmap(&p.tmA1);
         jt::prefetch_tmap(&p.tmX);
+        jt::prefetch_tmap(&p.tmM);
+        if (C::kPacked) {
+            jt::prefetch_tmap(&p.tmS0);
+            if (C::kGateUp) jt::prefetch_tmap(&p.tmS1);
+        }
+        if (C::kDown) jt::prefetch_tmap(&p.tmH);
     }
     if (warp == 1) {
         jt::tmem_alloc(tmem_slot, C::kTmemCols);
@@ -244,11 +303,39 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
             uint32_t stage = 0, phase = 0, issued_mask = 0, issued_phase = 0;
+            uint32_t ts = 0, tphase = 0, t_issued = 0, t_phase = 0;
             bool ok = true;
             constexpr uint32_t kTx = C::kX + (C::kPacked ? C::kAP : C::kAU);
+            const uint32_t scale_box = ngroups * (C::kGateUp ? 64 * 2 : 128 * 2);
+            const uint32_t slot_tx = kBN * 16 + (C::kPacked ? (C::kGateUp ? 2 : 1) * scale_box : 0) +
+                                     (C::kDown ? kBN * p.hs_ld * 4 : 0);
             for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
-                const TileInfo ti = tile_info<C::kChTile>(p, u, nch_tiles);
-                const int wrow = ti.e * p.n_ch + ti.c0;  // first weight row of the tile
+                const int4 te = __ldg(&p.tiles[u / nch_tiles]);  // {e, row0, row_end, 0}
+                const int c0 = (u % nch_tiles) * C::kChTile;
+                const int wrow = te.x * p.n_ch + c0;  // first weight row of the tile
+                // ---- per-tile slot: info, row meta, group scales, activation scales
+                if (!jt::mbar_wait(&pempty[ts], tphase ^ 1u, abort_flag, err)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t *sl = slot_base + ts * C::kSlot;
+                st_shared_v4(sl, make_int4(te.x, te.y, te.z, c0));
+                jt::mbar_arrive_expect_tx(&pfull[ts], slot_tx);
+                jt::tma_load_2d(sl + C::kOffMeta, &p.tmM, &pfull[ts], 0, te.y);
+                if (C::kPacked) {
+                    jt::tma_load_2d(sl + C::kOffScale, &p.tmS0, &pfull[ts], c0 * 2, te.x * ngroups);
+                    if (C::kGateUp)
+                        jt::tma_load_2d(sl + C::kOffScale + scale_box, &p.tmS1, &pfull[ts], c0 * 2,
+                                        te.x * ngroups);
+                }
+                if (C::kDown) jt::tma_load_2d(sl + C::kOffBlk, &p.tmH, &pfull[ts], 0, te.y);
+                t_issued |= 1u << ts;
+                t_phase = (t_phase & ~(1u << ts)) | (tphase << ts);
+                if (++ts == 2) {
+                    ts = 0;
+                    tphase ^= 1u;
+                }
+                // ---- operand stages
                 for (int kb = 0; kb < nk; ++kb) {
                     if (!jt::mbar_wait(&empty[stage], phase ^ 1u, abort_flag, err)) {
                         ok = false;
@@ -273,7 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                             jt::tma_load_2d(st, &p.tmA0, &full[stage], kb * kBK, wrow);
                         }
                     }
-                    jt::tma_load_2d(xs, &p.tmX, &full[stage], kb * kBK, ti.r0);
+                    jt::tma_load_2d(xs, &p.tmX, &full[stage], kb * kBK, te.y);
                     issued_mask |= 1u << stage;
                     issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
                     if (++stage == S) {
@@ -282,12 +369,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                     }
                 }
             }
-            if (!ok) {
+            if (!ok) {  // every issued TMA box must land before the CTA exits
                 for (int s = 0; s < S; ++s) {
                     if (!(issued_mask & (1u << s))) continue;
-                    const uint32_t par = (issued_phase >> s) & 1u;
                     const long long t0 = clock64();
-                    while (!jt::mbar_try_wait(&full[s], par) && clock64() - t0 < JT_SPIN_CYCLES / 16) {
+                    while (!jt::mbar_try_wait(&full[s], (issued_phase >> s) & 1u) &&
+                           clock64() - t0 < JT_SPIN_CYCLES / 16) {
+                    }
+                }
+                for (int s = 0; s < 2; ++s) {
+                    if (!(t_issued & (1u << s))) continue;
+                    const long long t0 = clock64();
+                    while (!jt::mbar_try_wait(&pfull[s], (t_phase >> s) & 1u) &&
+                           clock64() - t0 < JT_SPIN_CYCLES / 16) {
                     }
                 }
             }
@@ -319,18 +413,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                                                   ? (kb == nk - 1 && ks == kBK / 32 - 1)
                                                   : (ks % kStepsPerUnit == kStepsPerUnit - 1);
                         if (unit_start) {
-                            if (!jt::mbar_wait(&tempty[slot], slot_phase ^ 1u, abort_flag, err)) {
+                            // the epilogue arms (and re-arms) every slot
+                            if (!jt::mbar_wait(&tempty[slot], slot_phase, abort_flag, err)) {
                                 ok = false;
                                 break;
                             }
                             jt::tc_fence_after();
                         }
-                        jt::mma_i8(tmem_base + slot * kBN, dA + 2u * ks, dX + 2u * ks, kIdesc,
-                                   unit_start ? 0u : 1u);
+                        // magic-armed slots always accumulate onto 0x4B400000
+                        const uint32_t acc = C::kMagic ? 1u : (unit_start ? 0u : 1u);
+                        jt::mma_i8(tmem_base + slot * kBN, dA + 2u * ks, dX + 2u * ks, kIdesc, acc);
                         if (unit_end) {
                             jt::mma_commit(&tfull[slot]);
-                            slot ^= 1u;
-                            if (slot == 0) slot_phase ^= 1u;
+                            if (++slot == (uint32_t)NS) {
+                                slot = 0;
+                                slot_phase ^= 1u;
+                            }
                         }
                     }
                     if (!ok) break;
@@ -341,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                     }
                 }
             }
-            if (!ok) {
+            if (!ok) {  // already-issued MMAs retire before TMEM is released
                 jt::mma_commit(drain);
                 const long long t0 = clock64();
                 while (!jt::mbar_try_wait(drain, 0) && clock64() - t0 < JT_SPIN_CYCLES / 16) {
@@ -374,162 +472,163 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
         }
     } else {
         // ------------------------------------------------ epilogue warps
+        // Two warps per TMEM lane quarter: warp w reads lanes 32*(w%4)..+31
+        // and owns token-column half (w-6)/4 of every accumulator.
         const int q = warp & 3;                         // TMEM lane quarter
+        const int half = (warp - kEpiWarp0) >> 2;       // column half
         const int lr = q * 32 + lane;                   // operand row = TMEM lane
-        const int etid = threadIdx.x - kEpiWarp0 * 32;  // 0..127
+        const int etid = threadIdx.x - kEpiWarp0 * 32;  // 0..255
         // gate/up: rows 0..63 gate of channel lr, rows 64..127 up of channel lr-64
         const bool is_up = C::kGateUp && lr >= 64;
         const int lch = C::kGateUp ? (lr & 63) : lr;
-        uint32_t slot = 0, slot_phase = 0;
-        const int ngroups = p.K / 64;
-        for (int u = blockIdx.x; u < total; u += gridDim.x) {
-            const TileInfo ti = tile_info<C::kChTile>(p, u, nch_tiles);
-            const int ch = ti.c0 + lch;  // output channel within the expert
-            named_bar_epi();  // previous tile done with the SMEM scratch
-            if (etid < kBN) {
-                const int row = ti.r0 + etid;
-                const bool valid = row < ti.r_end;
-                if (C::kGateUp) {
-                    s_rowa[etid] = valid ? __ldg(&p.row_scale[row]) : 0.0f;
-                } else {
-                    s_rowa[etid] = (MODE == DN_ROUTED && valid) ? __ldg(&p.row_w[row]) : 0.0f;
-                    s_rowt[etid] = valid ? (MODE == DN_ROUTED ? __ldg(&p.row_tok[row]) : row) : -1;
-                }
+        const int j0 = half * kBH;  // first token column owned
+        const uint32_t tlane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + j0;
+        // arm every accumulator slot: magic pattern (64-K units) or nothing
+        if (C::kMagic) {
+            for (int b = 0; b < NS; ++b) jt::tmem_st32_fill(tlane + b * kBN, kMagicU);
+            jt::tmem_wait_st();
+        }
+        jt::tc_fence_before();
+        __syncwarp();
+        if (lane == 0)
+            for (int b = 0; b < NS; ++b) jt::mbar_arrive(&tempty[b]);
+        uint32_t slot = 0, slot_phase = 0, ts = 0, tphase = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+            if (!jt::mbar_wait(&pfull[ts], tphase, abort_flag, err)) {
+                ok = false;
+                break;
             }
-            if (!C::kGateUp) {
-                // activation group scales of the tile as [group][row] (zero for rows
-                // outside the expert; their results are never written)
-                for (int i = etid; i < ngroups * kBN; i += 128) {
-                    const int g = i / kBN, j = i % kBN, row = ti.r0 + j;
-                    h_tile[i] = row < ti.r_end ? __ldg(&p.blk_scale[(size_t)row * ngroups + g]) : 0.0f;
-                }
-            }
-            named_bar_epi();
-            float r[kBN];
+            const uint8_t *sl = slot_base + ts * C::kSlot;
+            const int4 info = *reinterpret_cast<const int4 *>(sl);  // {e, row0, row_end, c0}
+            const float4 *meta = reinterpret_cast<const float4 *>(sl + C::kOffMeta);
+            const __half *sc = reinterpret_cast<const __half *>(sl + C::kOffScale) +
+                               (C::kGateUp ? ((is_up ? ngroups * 64 : 0) + lch) : lr);
+            const float *blk = reinterpret_cast<const float *>(sl + C::kOffBlk) + j0 * p.hs_ld;
+            const int sc_stride = C::kGateUp ? 64 : 128;
+            const int ch = info.w + lch;  // output channel within the expert
+            float2 r2[kBH / 2];
 #pragma unroll
-            for (int j = 0; j < kBN; ++j) r[j] = 0.0f;
-            const __half *gsrow = nullptr;
-            if (C::kPacked)
-                gsrow = (is_up ? p.gs1 : p.gs0) + ((size_t)ti.e * p.n_ch + ch) * ngroups;
+            for (int j = 0; j < kBH / 2; ++j) r2[j] = make_float2(0.0f, 0.0f);
             const int nunits = C::kUnitK == 0 ? 1 : p.K / C::kUnitK;
-            bool ok = true;
-            float s_next = C::kPacked ? __half2float(gsrow[0]) : 1.0f;
-            for (int un = 0; un < nunits; ++un) {
-                const float s = s_next;
-                if (C::kPacked && un + 1 < nunits) s_next = __half2float(gsrow[un + 1]);
+            for (int un = 0; un < nunits; un += C::kUB) {
                 if (!jt::mbar_wait(&tfull[slot], slot_phase, abort_flag, err)) {
                     ok = false;
                     break;
                 }
-                jt::tc_fence_after();
-                const uint32_t trow = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + slot * kBN;
-                uint32_t a[kBN];
-                {
-                    uint32_t (&a0)[32] = *reinterpret_cast<uint32_t (*)[32]>(&a[0]);
-                    uint32_t (&a1)[32] = *reinterpret_cast<uint32_t (*)[32]>(&a[32]);
-                    jt::tmem_ld32(trow, a0);
-                    jt::tmem_ld32(trow + 32, a1);
-                    jt::tmem_wait_ld();
+                if (C::kUB == 2 && !jt::mbar_wait(&tfull[slot + 1], slot_phase, abort_flag, err)) {
+                    ok = false;
+                    break;
                 }
+                jt::tc_fence_after();
+                const uint32_t trow = tlane + slot * kBN;
+                uint32_t a0[32], a1[32];
+                jt::tmem_ld32(trow, a0);
+                if (C::kUB == 2) jt::tmem_ld32(trow + kBN, a1);
+                jt::tmem_wait_ld();
+                if (C::kMagic) {
+                    jt::tmem_st32_fill(trow, kMagicU);
+                    if (C::kUB == 2) jt::tmem_st32_fill(trow + kBN, kMagicU);
+                }
+                const float s0 = C::kPacked ? __half2float(sc[un * sc_stride]) : 1.0f;
+                fold_chunk<MODE>(r2, a0, s0, blk, p.hs_ld, un);
+                if (C::kUB == 2) {
+                    const float s1 = C::kPacked ? __half2float(sc[(un + 1) * sc_stride]) : 1.0f;
+                    fold_chunk<MODE>(r2, a1, s1, blk, p.hs_ld, un + 1);
+                }
+                if (C::kMagic) jt::tmem_wait_st();
                 jt::tc_fence_before();
                 __syncwarp();
-                if (lane == 0) jt::mbar_arrive(&tempty[slot]);
-                slot ^= 1u;
-                if (slot == 0) slot_phase ^= 1u;
-                if (MODE == GU_ROUTED) {
-#pragma unroll
-                    for (int j = 0; j < kBN; ++j)
-                        r[j] = __fmaf_rn(__int2float_rn((int32_t)a[j]), s, r[j]);
-                } else if (MODE == GU_SHARED) {
-#pragma unroll
-                    for (int j = 0; j < kBN; ++j) r[j] = __int2float_rn((int32_t)a[j]);
-                } else {
-                    const float *hsg = h_tile + un * kBN;
-#pragma unroll
-                    for (int j = 0; j < kBN; j += 4) {
-                        const float4 h4 = *reinterpret_cast<const float4 *>(hsg + j);
-                        const float hv[4] = {h4.x, h4.y, h4.z, h4.w};
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const float pf = __int2float_rn((int32_t)a[j + i]);
-                            const float t = (MODE == DN_ROUTED) ? __fmul_rn(pf, s) : pf;
-                            r[j + i] = __fmaf_rn(t, hv[i], r[j + i]);
-                        }
-                    }
+                if (lane == 0) {
+                    jt::mbar_arrive(&tempty[slot]);
+                    if (C::kUB == 2) jt::mbar_arrive(&tempty[slot + 1]);
+                }
+                slot += C::kUB;
+                if (slot == (uint32_t)NS) {
+                    slot = 0;
+                    slot_phase ^= 1u;
                 }
             }
             if (!ok) break;
             if constexpr (C::kGateUp) {
                 float cscale = 1.0f;
                 if (MODE == GU_SHARED) cscale = __ldg(is_up ? &p.cs1[ch] : &p.cs0[ch]);
-                // pass 1: gate rows publish g[row][ch]
-                if (!is_up) {
+                // pass 1: stage g and u (activation- and channel-scaled) in SMEM
+                float *dst_tile = h_tile + (is_up ? kBN * 64 : 0);
 #pragma unroll
-                    for (int j = 0; j < kBN; ++j) {
-                        const float xs = s_rowa[j];
-                        h_tile[j * 64 + lch] = (MODE == GU_ROUTED)
-                                                   ? __fmul_rn(r[j], xs)
-                                                   : __fmul_rn(__fmul_rn(r[j], xs), cscale);
-                    }
+                for (int j = 0; j < kBH; ++j) {
+                    const float xs = meta[j0 + j].x;
+                    const float rv = (j & 1) ? r2[j / 2].y : r2[j / 2].x;
+                    dst_tile[(j0 + j) * 64 + lch] = (MODE == GU_ROUTED)
+                                                        ? __fmul_rn(rv, xs)
+                                                        : __fmul_rn(__fmul_rn(rv, xs), cscale);
                 }
                 named_bar_epi();
-                // pass 2: up rows combine into h = SwiGLU(g, u) in place
-                if (is_up) {
-#pragma unroll
-                    for (int j = 0; j < kBN; ++j) {
-                        const float xs = s_rowa[j];
-                        const float uv = (MODE == GU_ROUTED)
-                                             ? __fmul_rn(r[j], xs)
-                                             : __fmul_rn(__fmul_rn(r[j], xs), cscale);
-                        h_tile[j * 64 + lch] = jt::swiglu(h_tile[j * 64 + lch], uv);
-                    }
-                }
+                // pass 2: h = SwiGLU(g, u) (moe_layer.c:146-148) over all epilogue
+                // threads, written over g
+#pragma unroll 2
+                for (int i = etid; i < kBN * 64; i += kEpiThreads)
+                    h_tile[i] = jt::swiglu(h_tile[i], h_tile[kBN * 64 + i]);
                 named_bar_epi();
-                // pass 3: two threads per row, 32 channels each -> codes + scale
-                const int j = etid >> 1, half = etid & 1;
-                const float *hr = h_tile + j * 64 + half * 32;
+                // pass 3: requantize each row's 64 channels (4 threads x 16) -> codes + scale
+                const int j = etid >> 2, part = etid & 3;
+                const float *hr = h_tile + j * 64 + part * 16;
                 float m = 0.0f;
                 int nf = 0;
 #pragma unroll
-                for (int i = 0; i < 32; i += 4) {
+                for (int i = 0; i < 16; i += 4) {
                     const float4 v4 = *reinterpret_cast<const float4 *>(hr + i);
                     nf |= !isfinite(v4.x) | !isfinite(v4.y) | !isfinite(v4.z) | !isfinite(v4.w);
                     m = fmaxf(m, fmaxf(fmaxf(fabsf(v4.x), fabsf(v4.y)), fmaxf(fabsf(v4.z), fabsf(v4.w))));
                 }
-                m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-                nf |= __shfl_xor_sync(0xffffffffu, nf, 1);
-                const int row = ti.r0 + j;
-                if (row < ti.r_end) {
+#pragma unroll
+                for (int o = 1; o < 4; o <<= 1) {
+                    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                    nf |= __shfl_xor_sync(0xffffffffu, nf, o);
+                }
+                const int row = info.y + j;
+                if (row < info.z) {
                     if (nf) atomicExch(err, JT_KERR_NONFINITE);
                     const jt::QuantBlock qb = jt::quant_block(m);
-                    uint32_t words[8];
+                    uint32_t words[4];
 #pragma unroll
-                    for (int w = 0; w < 8; ++w) {
+                    for (int b4 = 0; b4 < 4; ++b4) {
                         uint32_t word = 0;
 #pragma unroll
                         for (int b2 = 0; b2 < 4; ++b2) {
-                            const int c = jt::quant_code(hr[4 * w + b2], qb);
+                            const int c = jt::quant_code(hr[4 * b4 + b2], qb);
                             word |= (uint32_t)(uint8_t)(int8_t)c << (8 * b2);
                         }
-                        words[w] = word;
+                        words[b4] = word;
                     }
-                    int8_t *dst = p.hq + (size_t)row * p.n_ch + ti.c0 + half * 32;
-                    *reinterpret_cast<uint4 *>(dst) = make_uint4(words[0], words[1], words[2], words[3]);
-                    *reinterpret_cast<uint4 *>(dst + 16) = make_uint4(words[4], words[5], words[6], words[7]);
-                    if (half == 0) p.hs[(size_t)row * (p.n_ch / 64) + ti.c0 / 64] = qb.scale_f;
+                    *reinterpret_cast<uint4 *>(p.hq + (size_t)row * p.n_ch + info.w + part * 16) =
+                        make_uint4(words[0], words[1], words[2], words[3]);
+                    if (part == 0) p.hs[(size_t)row * p.hs_ld + info.w / 64] = qb.scale_f;
                 }
+                // all slot reads (meta) done before the slot is released
+                __syncwarp();
+                if (lane == 0) jt::mbar_arrive(&pempty[ts]);
+                named_bar_epi();  // h_tile free for the next tile
             } else {
                 float cs = 1.0f;
                 if (MODE == DN_SHARED) cs = __ldg(&p.cs0[ch]);
 #pragma unroll
-                for (int j = 0; j < kBN; ++j) {
-                    const int tok = s_rowt[j];
-                    if (tok < 0) continue;
-                    const float v = (MODE == DN_ROUTED) ? __fmul_rn(s_rowa[j], r[j]) : __fmul_rn(r[j], cs);
-                    float *dst = p.y + (size_t)tok * p.n_ch + ch;
+                for (int j = 0; j < kBH; ++j) {
+                    const int row = info.y + j0 + j;
+                    if (row >= info.z) continue;
+                    const float4 mt = meta[j0 + j];
+                    const float rv = (j & 1) ? r2[j / 2].y : r2[j / 2].x;
+                    const float v = (MODE == DN_ROUTED) ? __fmul_rn(mt.y, rv) : __fmul_rn(rv, cs);
+                    float *dst = p.y + (size_t)__float_as_int(mt.z) * p.n_ch + ch;
                     if (p.y_accumulate) atomicAdd(dst, v);
                     else *dst = v;
                 }
+                __syncwarp();
+                if (lane == 0) jt::mbar_arrive(&pempty[ts]);
+            }
+            if (++ts == 2) {
+                ts = 0;
+                tphase ^= 1u;
             }
         }
     }
@@ -558,111 +657,123 @@ int launch(MoeGemmParams &p, int max_tiles_hint, cudaStream_t stream) {
     return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 
+int hs_stride(int n_ch) { return ((n_ch / 64) + 3) & ~3; }
+
+bool meta_map(CUtensorMap *m, const float4 *row_meta, int rows) {
+    return jt::make_tmap_2d_u8(m, row_meta, 16, rows, 16, 16, kBN, false);
+}
+
 }  // namespace
 
-// Routed gate/up: wg, wu packed INT2 [E][f][d/4]; gs, us fp16 [E][f][d/64];
-// xd int8 [rows][d] in expert order with xs_d [rows]; writes hq [rows][f],
-// hs [rows][f/64].  max_tiles_hint bounds the grid (0 = all SMs).
+// Routed gate/up: wg, wu packed INT2 [E][f][d/4]; gs, us fp16 [E][d/64][f];
+// xd int8 [rows][d] in expert order; writes hq [rows][f] and hs
+// [rows][round_up(f/64, 4)].
 extern "C" int jtk_moe_gateup_routed(const uint8_t *wg, const uint8_t *wu, const void *gs,
                                      const void *us, int E, int f, int d, const int8_t *xd,
-                                     int rows_cap, const float *xs_d, const int32_t *row_off,
-                                     const int32_t *tile_off, int8_t *hq, float *hs,
+                                     int rows_cap, const float4 *row_meta, const int4 *tiles,
+                                     const int32_t *ntiles, int8_t *hq, float *hs,
                                      int max_tiles_hint, cudaStream_t stream) {
-    if (f % 64 || d % kBK || E <= 0 || rows_cap <= 0) return -1;
+    if (f % 64 || d % kBK || d / 64 > kMaxGroups || E <= 0 || rows_cap <= 0) return -1;
     MoeGemmParams p{};
-    const uint32_t prow = d / 4;
-    if (!jt::make_tmap_2d_u8(&p.tmA0, wg, prow, (uint64_t)E * f, prow, Cfg<GU_ROUTED>::kPackedRow, 64, false) ||
-        !jt::make_tmap_2d_u8(&p.tmA1, wu, prow, (uint64_t)E * f, prow, Cfg<GU_ROUTED>::kPackedRow, 64, false) ||
-        !jt::make_tmap_2d_u8(&p.tmX, xd, d, rows_cap, d, kBK, kBN, true))
+    const uint32_t prow = d / 4, G = d / 64;
+    if (!jt::make_tmap_2d_u8(&p.tmA0, wg, prow, (uint64_t)E * f, prow, 32, 64, false) ||
+        !jt::make_tmap_2d_u8(&p.tmA1, wu, prow, (uint64_t)E * f, prow, 32, 64, false) ||
+        !jt::make_tmap_2d_u8(&p.tmX, xd, d, rows_cap, d, kBK, kBN, true) ||
+        !jt::make_tmap_2d_u8(&p.tmS0, gs, (uint64_t)f * 2, (uint64_t)E * G, (uint64_t)f * 2, 128, G, false) ||
+        !jt::make_tmap_2d_u8(&p.tmS1, us, (uint64_t)f * 2, (uint64_t)E * G, (uint64_t)f * 2, 128, G, false) ||
+        !meta_map(&p.tmM, row_meta, rows_cap))
         return -2;
-    p.row_off = row_off;
-    p.tile_off = tile_off;
-    p.E = E;
+    p.tmH = p.tmM;
+    p.tiles = tiles;
+    p.ntiles = ntiles;
     p.n_ch = f;
     p.K = d;
-    p.gs0 = static_cast<const __half *>(gs);
-    p.gs1 = static_cast<const __half *>(us);
-    p.row_scale = xs_d;
+    p.hs_ld = hs_stride(f);
     p.hq = hq;
     p.hs = hs;
     return launch<GU_ROUTED>(p, max_tiles_hint, stream);
 }
 
-// Routed down: wd packed INT4 [E][d][f/2], ds fp16 [E][d][f/64]; hq [rows][f]
-// with hs [rows][f/64]; y[tok][d] += w_row * y_pair (atomic).
+// Routed down: wd packed INT4 [E][d][f/2], ds fp16 [E][f/64][d]; hq [rows][f]
+// with hs [rows][round_up(f/64, 4)]; y[tok][d] += w_row * y_pair (atomic).
 extern "C" int jtk_moe_down_routed(const uint8_t *wd, const void *ds, int E, int d, int f,
                                    const int8_t *hq, int rows_cap, const float *hs,
-                                   const int32_t *row_off, const int32_t *tile_off,
-                                   const int32_t *row_tok, const float *row_w, float *y,
-                                   int max_tiles_hint, cudaStream_t stream) {
-    // the tile's activation group scales are staged in SMEM: K <= 4096
-    if (d % kBM || f % kBK || f > 4096 || E <= 0 || rows_cap <= 0) return -1;
+                                   const float4 *row_meta, const int4 *tiles,
+                                   const int32_t *ntiles, float *y, int max_tiles_hint,
+                                   cudaStream_t stream) {
+    if (d % kBM || f % kBK || f / 64 > kMaxGroups || E <= 0 || rows_cap <= 0) return -1;
     MoeGemmParams p{};
-    const uint32_t prow = f / 2;
-    if (!jt::make_tmap_2d_u8(&p.tmA0, wd, prow, (uint64_t)E * d, prow, Cfg<DN_ROUTED>::kPackedRow, kBM, false) ||
-        !jt::make_tmap_2d_u8(&p.tmX, hq, f, rows_cap, f, kBK, kBN, true))
+    const uint32_t prow = f / 2, G = f / 64;
+    const int hs_ld = hs_stride(f);
+    if (!jt::make_tmap_2d_u8(&p.tmA0, wd, prow, (uint64_t)E * d, prow, 64, kBM, false) ||
+        !jt::make_tmap_2d_u8(&p.tmX, hq, f, rows_cap, f, kBK, kBN, true) ||
+        !jt::make_tmap_2d_u8(&p.tmS0, ds, (uint64_t)d * 2, (uint64_t)E * G, (uint64_t)d * 2, 256, G, false) ||
+        !meta_map(&p.tmM, row_meta, rows_cap) ||
+        !jt::make_tmap_2d_u8(&p.tmH, hs, (uint64_t)hs_ld * 4, rows_cap, (uint64_t)hs_ld * 4, hs_ld * 4, kBN, false))
         return -2;
     p.tmA1 = p.tmA0;
-    p.row_off = row_off;
-    p.tile_off = tile_off;
-    p.E = E;
+    p.tmS1 = p.tmS0;
+    p.tiles = tiles;
+    p.ntiles = ntiles;
     p.n_ch = d;
     p.K = f;
-    p.gs0 = static_cast<const __half *>(ds);
-    p.blk_scale = hs;
+    p.hs_ld = hs_ld;
     p.y = y;
-    p.row_tok = row_tok;
-    p.row_w = row_w;
     p.y_accumulate = 1;
     return launch<DN_ROUTED>(p, max_tiles_hint, stream);
 }
 
 // Shared gate/up (one shared expert): wsg, wsu int8 [fs][d] with per-channel
-// ssg, ssu; x int8 [T][d], xs [T]; writes hq [T][fs], hs [T][fs/64].
-// row_off = {0, T}, tile_off = {0, ceil(T/64)} (device, 2 entries each).
+// ssg, ssu; x int8 [T][d], sh_meta [T]; writes hq [T][fs] and hs [T][round_up(fs/64, 4)].
 extern "C" int jtk_moe_gateup_shared(const int8_t *wsg, const int8_t *wsu, const float *ssg,
                                      const float *ssu, int fs, int d, const int8_t *xq, int T,
-                                     const float *xs, const int32_t *row_off,
-                                     const int32_t *tile_off, int8_t *hq, float *hs,
+                                     const float4 *sh_meta, const int4 *tiles,
+                                     const int32_t *ntiles, int8_t *hq, float *hs,
                                      cudaStream_t stream) {
     if (fs % 64 || d % kBK || T <= 0) return -1;
     MoeGemmParams p{};
     if (!jt::make_tmap_2d_u8(&p.tmA0, wsg, d, fs, d, kBK, 64, true) ||
         !jt::make_tmap_2d_u8(&p.tmA1, wsu, d, fs, d, kBK, 64, true) ||
-        !jt::make_tmap_2d_u8(&p.tmX, xq, d, T, d, kBK, kBN, true))
+        !jt::make_tmap_2d_u8(&p.tmX, xq, d, T, d, kBK, kBN, true) || !meta_map(&p.tmM, sh_meta, T))
         return -2;
-    p.row_off = row_off;
-    p.tile_off = tile_off;
-    p.E = 1;
+    p.tmS0 = p.tmA0;
+    p.tmS1 = p.tmA0;
+    p.tmH = p.tmM;
+    p.tiles = tiles;
+    p.ntiles = ntiles;
     p.n_ch = fs;
     p.K = d;
+    p.hs_ld = hs_stride(fs);
     p.cs0 = ssg;
     p.cs1 = ssu;
-    p.row_scale = xs;
     p.hq = hq;
     p.hs = hs;
     return launch<GU_SHARED>(p, ((T + kBN - 1) / kBN) * (fs / 64), stream);
 }
 
-// Shared down: wsd int8 [d][fs] with per-channel ssd; hq [T][fs], hs [T][fs/64];
+// Shared down: wsd int8 [d][fs] with per-channel ssd; hq [T][fs], hs [T][round_up(fs/64, 4)];
 // y[t][d] = (accumulate ? y + v : v).
 extern "C" int jtk_moe_down_shared(const int8_t *wsd, const float *ssd, int d, int fs,
                                    const int8_t *hq, int T, const float *hs,
-                                   const int32_t *row_off, const int32_t *tile_off, float *y,
-                                   int accumulate, cudaStream_t stream) {
-    if (d % kBM || fs % kBK || fs > 4096 || T <= 0) return -1;
+                                   const float4 *sh_meta, const int4 *tiles,
+                                   const int32_t *ntiles, float *y, int accumulate,
+                                   cudaStream_t stream) {
+    if (d % kBM || fs % kBK || fs / 64 > kMaxGroups || T <= 0) return -1;
     MoeGemmParams p{};
+    const int hs_ld = hs_stride(fs);
     if (!jt::make_tmap_2d_u8(&p.tmA0, wsd, fs, d, fs, kBK, kBM, true) ||
-        !jt::make_tmap_2d_u8(&p.tmX, hq, fs, T, fs, kBK, kBN, true))
+        !jt::make_tmap_2d_u8(&p.tmX, hq, fs, T, fs, kBK, kBN, true) || !meta_map(&p.tmM, sh_meta, T) ||
+        !jt::make_tmap_2d_u8(&p.tmH, hs, (uint64_t)hs_ld * 4, T, (uint64_t)hs_ld * 4, hs_ld * 4, kBN, false))
         return -2;
     p.tmA1 = p.tmA0;
-    p.row_off = row_off;
-    p.tile_off = tile_off;
-    p.E = 1;
+    p.tmS0 = p.tmA0;
+    p.tmS1 = p.tmA0;
+    p.tiles = tiles;
+    p.ntiles = ntiles;
     p.n_ch = d;
     p.K = fs;
+    p.hs_ld = hs_ld;
     p.cs0 = ssd;
-    p.blk_scale = hs;
     p.y = y;
     p.y_accumulate = accumulate;
     return launch<DN_SHARED>(p, ((T + kBN - 1) / kBN) * (d / kBM), stream);

@@ -181,6 +181,20 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         : "r"(taddr));
 }
 
+// Store one 32-bit value into 32 consecutive columns of this warp's 32 lanes.
+__device__ __forceinline__ void tmem_st32_fill(uint32_t taddr, uint32_t v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+        "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
+        "r"(v)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // UMMA shared-memory descriptor for a K-major operand stored with the 128-byte
 // swizzle: rows of 128 bytes, 8-row core groups 1024 bytes apart.
 //   bits  0-13 start address >> 4

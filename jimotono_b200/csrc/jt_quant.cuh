@@ -33,6 +33,12 @@ __device__ __forceinline__ QuantBlock quant_block(float maxabs) {
     return b;
 }
 
+// Exact reference rounding, used only near a rounding tie (kept out of line
+// so callers do not carry the double-division code and its registers).
+static __device__ __noinline__ int quant_code_exact(float x, double scale_d) {
+    return static_cast<int>(round(__ddiv_rn((double)x, scale_d)));
+}
+
 __device__ __forceinline__ int quant_code(float x, const QuantBlock &b) {
     if (b.scale_d == 0.0) return 0;
     const float y = __fmul_rn(x, b.inv);
@@ -43,7 +49,7 @@ __device__ __forceinline__ int quant_code(float x, const QuantBlock &b) {
         q = static_cast<int>(floorf(__fadd_rn(ay, 0.5f)));
         if (y < 0.0f) q = -q;
     } else {
-        q = static_cast<int>(round(__ddiv_rn((double)x, b.scale_d)));
+        q = quant_code_exact(x, b.scale_d);
     }
     q = q > 127 ? 127 : q;
     q = q < -127 ? -127 : q;

@@ -131,20 +131,20 @@ __global__ void k_sort_count(const int32_t *__restrict__ ids, int T, int k, int 
 }
 
 // One CTA.  base[c][e] = pairs of expert e in chunks < c; kept[e] =
-// min(count, cap); off = exclusive scan of kept; tiles: per expert
-// ceil(kept/bn) token tiles, tile_off = exclusive scan (GEMM scheduler).
+// min(count, cap); off = exclusive scan of kept; tile_off = exclusive scan
+// of ceil(kept/64) (64-row token tiles of the expert GEMMs).
 // meta[0] = kept total, meta[1] = total token tiles, meta[2] = max kept.
 __global__ void k_sort_scan(int32_t *__restrict__ hist_base, int nchunks, int E, int cap,
-                            int bn, int32_t *__restrict__ off, int32_t *__restrict__ tile_off,
+                            int32_t *__restrict__ off, int32_t *__restrict__ tile_off,
                             int32_t *__restrict__ meta) {
     extern __shared__ int32_t sm[];  // 2 * blockDim.x
     const int tid = threadIdx.x, nt = blockDim.x;
     const int per = (E + nt - 1) / nt;
-    int kept_local[8], tiles_local[8];
+    int kept_local[8];
     int ks = 0, ts = 0, mx = 0;
     for (int j = 0; j < per; ++j) {
         const int e = tid * per + j;
-        int kc = 0, tc = 0;
+        int kc = 0;
         if (e < E) {
             int run = 0;
             for (int c = 0; c < nchunks; ++c) {
@@ -153,18 +153,16 @@ __global__ void k_sort_scan(int32_t *__restrict__ hist_base, int nchunks, int E,
                 run += h;
             }
             kc = run < cap ? run : cap;
-            tc = (kc + bn - 1) / bn;
         }
         kept_local[j] = kc;
-        tiles_local[j] = tc;
         ks += kc;
-        ts += tc;
+        ts += (kc + 63) / 64;
         mx = kc > mx ? kc : mx;
     }
     sm[tid] = ks;
     sm[nt + tid] = ts;
     __syncthreads();
-    // inclusive Hillis-Steele scan over threads (nt <= 1024)
+    // inclusive Hillis-Steele scans over threads (nt <= 1024)
     for (int o = 1; o < nt; o <<= 1) {
         int a = 0, b = 0;
         if (tid >= o) {
@@ -184,7 +182,7 @@ __global__ void k_sort_scan(int32_t *__restrict__ hist_base, int nchunks, int E,
             tile_off[e] = run_t;
         }
         run_k += kept_local[j];
-        run_t += tiles_local[j];
+        run_t += (kept_local[j] + 63) / 64;
     }
     if (tid == nt - 1) {
         off[E] = sm[tid];
@@ -201,6 +199,17 @@ __global__ void k_sort_scan(int32_t *__restrict__ hist_base, int nchunks, int E,
         __syncthreads();
     }
     if (tid == 0) meta[2] = sm[0];
+}
+
+// Token-tile table of the expert GEMMs: entry v = {expert, first row,
+// expert's end row, 0} for the 64-row tiles of every expert in order, so a
+// GEMM CTA finds its tile with one load instead of a search.
+__global__ void k_build_tiles(const int32_t *__restrict__ off, const int32_t *__restrict__ tile_off,
+                              int E, int4 *__restrict__ tiles) {
+    for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < E; e += gridDim.x * blockDim.x) {
+        const int r0 = off[e], r1 = off[e + 1], t0 = tile_off[e];
+        for (int j = 0; r0 + 64 * j < r1; ++j) tiles[t0 + j] = make_int4(e, r0 + 64 * j, r1, 0);
+    }
 }
 
 // One warp per chunk, pairs visited in q order 32 at a time; lanes routed
@@ -274,12 +283,13 @@ __global__ void k_sort_scatter(const int32_t *__restrict__ ids, const float *__r
 // One CTA per token: per-token int8 quantization of x (w8a8.c:688-747),
 // written to xq[t] (shared experts) and to every kept (t, p) row of the
 // expert-ordered activation matrix xd, with that row's metadata.
+// Row metadata of the expert GEMMs, one 16-byte record per row:
+// {activation scale, combine weight, token index (as bits), 0}.
 __global__ void __launch_bounds__(256)
     k_quant_dispatch(const float *__restrict__ x, int T, int d, int k,
                      const int32_t *__restrict__ pos, const float *__restrict__ wfin,
                      int8_t *__restrict__ xq, float *__restrict__ xs, int8_t *__restrict__ xd,
-                     float *__restrict__ xs_d, float *__restrict__ w_d,
-                     int32_t *__restrict__ tok_d, int *err) {
+                     float4 *__restrict__ row_meta, float4 *__restrict__ sh_meta, int *err) {
     const int t = blockIdx.x;
     if (t >= T) return;
     const float *row = x + (size_t)t * d;
@@ -319,14 +329,15 @@ __global__ void __launch_bounds__(256)
         }
         if (threadIdx.x < k) {
             const int ps = pos[(size_t)t * k + threadIdx.x];
-            if (ps >= 0) {
-                xs_d[ps] = qb.scale_f;
-                w_d[ps] = wfin[(size_t)t * k + threadIdx.x];
-                tok_d[ps] = t;
-            }
+            if (ps >= 0)
+                row_meta[ps] = make_float4(qb.scale_f, wfin[(size_t)t * k + threadIdx.x],
+                                           __int_as_float(t), 0.0f);
         }
     }
-    if (threadIdx.x == 0) xs[t] = qb.scale_f;
+    if (threadIdx.x == 0) {
+        xs[t] = qb.scale_f;
+        if (sh_meta) sh_meta[t] = make_float4(qb.scale_f, 1.0f, __int_as_float(t), 0.0f);
+    }
     if (bad) {
         if (threadIdx.x == 0) atomicExch(err, 0x85);
         return;
@@ -360,17 +371,18 @@ extern "C" int jtk_route_topk(const float *logits, const float *bias, int T, int
 extern "C" int jtk_sort_chunks(int T) { return (T + kChunkTok - 1) / kChunkTok; }
 
 extern "C" int jtk_moe_sort(const int32_t *ids, const float *w_in, int T, int k, int E, int cap,
-                            int bn, int32_t *hist, int32_t *off, int32_t *tile_off,
+                            int32_t *hist, int32_t *off, int32_t *tile_off, int4 *tiles,
                             int32_t *meta, int32_t *perm, int32_t *pos, uint8_t *drop,
                             float *w_out, cudaStream_t stream) {
-    if (T <= 0 || k <= 0 || E <= 0 || E > 4096 || cap <= 0 || bn <= 0) return -1;
+    if (T <= 0 || k <= 0 || E <= 0 || E > 4096 || cap <= 0) return -1;
     const int nch = jtk_sort_chunks(T);
     int *err = jtk_error_word();
     k_sort_count<<<nch, 256, (size_t)E * sizeof(int32_t), stream>>>(ids, T, k, E, hist, err);
     int nt = 1024;
     while (nt / 2 >= E && nt > 32) nt /= 2;
-    k_sort_scan<<<1, nt, 2 * nt * sizeof(int32_t), stream>>>(hist, nch, E, cap, bn, off,
-                                                             tile_off, meta);
+    k_sort_scan<<<1, nt, 2 * nt * sizeof(int32_t), stream>>>(hist, nch, E, cap, off, tile_off,
+                                                             meta);
+    k_build_tiles<<<(E + 255) / 256, 256, 0, stream>>>(off, tile_off, E, tiles);
     k_sort_scatter<<<nch, 32, (size_t)E * sizeof(int32_t), stream>>>(
         ids, w_in, T, k, E, cap, hist, off, perm, pos, drop, w_out, err);
     return cudaGetLastError() == cudaSuccess ? 0 : -4;
@@ -378,9 +390,9 @@ extern "C" int jtk_moe_sort(const int32_t *ids, const float *w_in, int T, int k,
 
 extern "C" int jtk_quant_dispatch(const float *x, int T, int d, int k, const int32_t *pos,
                                   const float *wfin, int8_t *xq, float *xs, int8_t *xd,
-                                  float *xs_d, float *w_d, int32_t *tok_d, cudaStream_t stream) {
+                                  float4 *row_meta, float4 *sh_meta, cudaStream_t stream) {
     if (T <= 0 || d <= 0 || (d % 4) != 0 || k > 64) return -1;
-    k_quant_dispatch<<<T, 256, 0, stream>>>(x, T, d, k, pos, wfin, xq, xs, xd, xs_d, w_d, tok_d,
+    k_quant_dispatch<<<T, 256, 0, stream>>>(x, T, d, k, pos, wfin, xq, xs, xd, row_meta, sh_meta,
                                             jtk_error_word());
     return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }

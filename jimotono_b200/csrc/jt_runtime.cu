@@ -53,9 +53,16 @@ bool make_tmap_2d_u8(CUtensorMap *map, const void *base, uint64_t inner, uint64_
 
 }  // namespace jt
 
+// Device address of the error word, looked up once per device (the host
+// symbol g_jt_err_word is not a device address; cudaGetSymbolAddress is).
 extern "C" int *jtk_error_word(void) {
+    static int *cache[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return nullptr;
+    if (dev < 64 && cache[dev]) return cache[dev];
     void *p = nullptr;
     if (cudaGetSymbolAddress(&p, g_jt_err_word) != cudaSuccess) return nullptr;
+    if (dev < 64) cache[dev] = static_cast<int *>(p);
     return static_cast<int *>(p);
 }
 
@@ -71,10 +78,13 @@ extern "C" int jtk_read_and_clear_error(int *out_code) {
 }
 
 extern "C" int jtk_num_sms(void) {
+    static int cache[64] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (dev >= 0 && dev < 64 && cache[dev]) return cache[dev];
     int n = 0;
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
         return 148;
+    if (dev >= 0 && dev < 64) cache[dev] = n;
     return n;
 }

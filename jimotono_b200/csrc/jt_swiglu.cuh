@@ -35,12 +35,15 @@ __device__ __forceinline__ float det_expf(float x) {
     return __fmul_rn(__fmul_rn(p, s1), s2);
 }
 
-__device__ __forceinline__ float swiglu(float g, float u) {
+// silu(g) = g * sig with sig = 1/(1 + exp(-g)); the reciprocal is the
+// correctly rounded 1/den, identical to the IEEE division 1.0f / den.
+__device__ __forceinline__ float silu(float g) {
     const float e = det_expf(-g);
     const float den = __fadd_rn(1.0f, e);
-    const float sig = __fdiv_rn(1.0f, den);
-    const float silu = __fmul_rn(g, sig);
-    return __fmul_rn(silu, u);
+    const float sig = __frcp_rn(den);
+    return __fmul_rn(g, sig);
 }
+
+__device__ __forceinline__ float swiglu(float g, float u) { return __fmul_rn(silu(g), u); }
 
 }  // namespace jt

@@ -127,19 +127,17 @@ extern "C" int jtk_f32_to_bf16(const float *src, uint16_t *dst, size_t n, cudaSt
 }
 
 namespace {
-// Row/tile ranges of a single "expert" covering rows [0, T) (shared experts).
-__global__ void k_fill_single_range(int32_t *row_off, int32_t *tile_off, int T, int bn) {
-    if (threadIdx.x == 0) {
-        row_off[0] = 0;
-        row_off[1] = T;
-        tile_off[0] = 0;
-        tile_off[1] = (T + bn - 1) / bn;
-    }
+// Tile table of a single "expert" covering rows [0, T) (shared experts):
+// entry j = {0, 64 j, T, 0}; ntiles[0] = ceil(T / 64).
+__global__ void k_fill_single_tiles(int4 *tiles, int32_t *ntiles, int T) {
+    const int n = (T + 63) / 64;
+    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x)
+        tiles[j] = make_int4(0, 64 * j, T, 0);
+    if (blockIdx.x == 0 && threadIdx.x == 0) ntiles[0] = n;
 }
 }  // namespace
 
-extern "C" int jtk_fill_single_range(int32_t *row_off, int32_t *tile_off, int T, int bn,
-                                     cudaStream_t stream) {
-    k_fill_single_range<<<1, 32, 0, stream>>>(row_off, tile_off, T, bn);
+extern "C" int jtk_fill_single_tiles(int4 *tiles, int32_t *ntiles, int T, cudaStream_t stream) {
+    k_fill_single_tiles<<<((T + 63) / 64 + 255) / 256, 256, 0, stream>>>(tiles, ntiles, T);
     return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }

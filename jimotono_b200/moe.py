@@ -55,10 +55,10 @@ def synth_weights(dm: Dims, seed: int) -> dict:
     w = {
         "wg": rng.integers(0, 256, (E, f, d // 4), dtype=np.uint8),
         "wu": rng.integers(0, 256, (E, f, d // 4), dtype=np.uint8),
-        "sg": rng.uniform(0.01, 0.05, (E, f, d // 64)).astype(np.float16),
-        "su": rng.uniform(0.01, 0.05, (E, f, d // 64)).astype(np.float16),
+        "sg": rng.uniform(0.01, 0.05, (E, d // 64, f)).astype(np.float16),
+        "su": rng.uniform(0.01, 0.05, (E, d // 64, f)).astype(np.float16),
         "wd": rng.integers(0, 256, (E, d, f // 2), dtype=np.uint8),
-        "sd": rng.uniform(0.01, 0.05, (E, d, f // 64)).astype(np.float16),
+        "sd": rng.uniform(0.01, 0.05, (E, f // 64, d)).astype(np.float16),
         "wsg": rng.integers(-127, 128, (max(S, 1), fs, d), dtype=np.int8),
         "wsu": rng.integers(-127, 128, (max(S, 1), fs, d), dtype=np.int8),
         "ssg": rng.uniform(4e-4, 8e-4, (max(S, 1), fs)).astype(np.float32),

@@ -358,19 +358,19 @@ static void routed_expert(const jto_moe_dims *dm, const jto_moe_weights *w, int 
     const int d = dm->d, f = dm->f, gd = d / 64, gf = f / 64;
     const uint8_t *wg = w->wg + (size_t)e * f * (d / 4);
     const uint8_t *wu = w->wu + (size_t)e * f * (d / 4);
-    const uint16_t *sg = w->sg + (size_t)e * f * gd;
-    const uint16_t *su = w->su + (size_t)e * f * gd;
+    const uint16_t *sg = w->sg + (size_t)e * gd * f; /* [g][c] */
+    const uint16_t *su = w->su + (size_t)e * gd * f;
     const uint8_t *wd = w->wd + (size_t)e * d * (f / 2);
-    const uint16_t *sd = w->sd + (size_t)e * d * gf;
+    const uint16_t *sd = w->sd + (size_t)e * gf * d; /* [g][o] */
     int32_t P[64];
     for (int c = 0; c < f; c++) {
         jto_lowbit_partials(xq, wg + (size_t)c * (d / 4), 1, d, 2, P);
         float r = 0.0f;
-        for (int g = 0; g < gd; g++) r = fmaf((float)P[g], jto_half_to_float(sg[(size_t)c * gd + g]), r);
+        for (int g = 0; g < gd; g++) r = fmaf((float)P[g], jto_half_to_float(sg[(size_t)g * f + c]), r);
         gbuf[c] = r * xs;
         jto_lowbit_partials(xq, wu + (size_t)c * (d / 4), 1, d, 2, P);
         r = 0.0f;
-        for (int g = 0; g < gd; g++) r = fmaf((float)P[g], jto_half_to_float(su[(size_t)c * gd + g]), r);
+        for (int g = 0; g < gd; g++) r = fmaf((float)P[g], jto_half_to_float(su[(size_t)g * f + c]), r);
         ubuf[c] = r * xs;
         hbuf[c] = jto_swiglu(gbuf[c], ubuf[c]);
     }
@@ -379,7 +379,7 @@ static void routed_expert(const jto_moe_dims *dm, const jto_moe_weights *w, int 
         jto_lowbit_partials(hq, wd + (size_t)o * (f / 2), 1, f, 4, P);
         float r = 0.0f;
         for (int g = 0; g < gf; g++) {
-            const float t = (float)P[g] * jto_half_to_float(sd[(size_t)o * gf + g]);
+            const float t = (float)P[g] * jto_half_to_float(sd[(size_t)g * d + o]);
             r = fmaf(t, hs[g], r);
         }
         yout[o] = r;

@@ -83,9 +83,9 @@ typedef struct jto_moe_dims {
 
 typedef struct jto_moe_weights {
     const uint8_t *wg, *wu;   /* INT2 [E][f][d/4] */
-    const uint16_t *sg, *su;  /* fp16 [E][f][d/64] */
+    const uint16_t *sg, *su;  /* fp16 [E][d/64][f] (group-major) */
     const uint8_t *wd;        /* INT4 [E][d][f/2] */
-    const uint16_t *sd;       /* fp16 [E][d][f/64] */
+    const uint16_t *sd;       /* fp16 [E][f/64][d] (group-major) */
     const int8_t *wsg, *wsu;  /* int8 [S][fs][d] */
     const float *ssg, *ssu;   /* fp32 [S][fs] */
     const int8_t *wsd;        /* int8 [S][d][fs] */
