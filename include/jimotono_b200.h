@@ -100,6 +100,25 @@ int jt_b200_w8a8_gemm(const int8_t *X, int ldx, const float *sx, const int8_t *W
 int jt_b200_w8a8_gemm_i32(const int8_t *X, int ldx, const int8_t *W, int ldw, int32_t *C32,
                           int ldc, int M, int N, int K, void *stream);
 
+/* Per-token quantization of fp32 activations x [M][K] (the per-row form of
+ * jt_w8a8_quant_per_channel) followed by jt_b200_w8a8_gemm, in one call
+ * that allocates no memory: the int8 codes and row scales live in a fixed
+ * device array inside the library.  No counterpart in the reference.
+ *
+ * For callers that must not allocate device memory at all - a runtime
+ * with a fixed memory budget, or one that enqueues work where an
+ * allocation would synchronize the device.  Limits: M <= 4096 and
+ * M * K <= 2 MiB of codes (larger shapes return JT_ERR_INVAL, errno
+ * E2BIG); K and ldw multiples of 16.  The scratch is one per device, so
+ * calls on one device must not overlap: issue them on one stream or order
+ * them.  The first call on a device looks up the scratch address (a
+ * host-side, synchronous step); make it before any stream capture.
+ * Non-finite activations are reported by jt_b200_sync. */
+#define JT_B200_LINEAR_NOALLOC_MAX_ROWS 4096
+#define JT_B200_LINEAR_NOALLOC_MAX_CODES (2 * 1024 * 1024)
+int jt_b200_w8a8_linear_noalloc(const float *x, int M, int K, const int8_t *W, int ldw,
+                                const float *sw, float *C, int ldc, int N, void *stream);
+
 /* ---- quantized MoE layer (prepared weights) ----
  *
  * The layer of jt_moe_fwd_batch (moe_layer.c:980-1614; moe_layer.h:230-246)
