@@ -13,6 +13,10 @@
 extern "C" {
 #endif
 
+/* Token rows per tile of the expert GEMMs (the routed-expert tile table and
+ * the shared-expert tiles are cut to this size). */
+#define JT_TILE_ROWS 128
+
 /* Epilogue modes of the dense int8 tensor-core GEMM. */
 enum jtk_w8a8_epi {
     JTK_EPI_TOKEN_CHANNEL_F32 = 0, /* C = ((float)acc * sx[m]) * sw[n] */
@@ -49,7 +53,8 @@ int jtk_dequant_rows(const int8_t *src, const float *scales, size_t rows, size_t
 /* fp32 -> bf16 (round to nearest even). */
 int jtk_f32_to_bf16(const float *src, uint16_t *dst, size_t n, cudaStream_t stream);
 
-/* Shared-expert tile table: tiles[j] = {0, 64 j, T, 0}, ntiles[0] = ceil(T/64). */
+/* Shared-expert tile table: tiles[j] = {0, JT_TILE_ROWS j, T, 0},
+ * ntiles[0] = ceil(T / JT_TILE_ROWS). */
 int jtk_fill_single_tiles(int4 *tiles, int32_t *ntiles, int T, cudaStream_t stream);
 
 /* MoE routing (jt_route.cu). */
@@ -57,7 +62,7 @@ int jtk_route_topk(const float *logits, const float *bias, int T, int E, int k, 
                    float *w, cudaStream_t stream);
 int jtk_sort_chunks(int T);
 
-/* Capacity sort.  tile_off [E+1]: 64-row token tiles per expert (scan);
+/* Capacity sort.  tile_off [E+1]: JT_TILE_ROWS-row token tiles per expert (scan);
  * tiles: table of {expert, row0, row_end, 0} per token tile; meta[0] kept,
  * meta[1] token tiles (= tile_off[E]), meta[2] max kept per expert. */
 int jtk_moe_sort(const int32_t *ids, const float *w_in, int T, int k, int E, int cap,
@@ -69,7 +74,7 @@ int jtk_quant_dispatch(const float *x, int T, int d, int k, const int32_t *pos,
                        const float *wfin, int8_t *xq, float *xs, int8_t *xd, float4 *row_meta,
                        float4 *sh_meta, cudaStream_t stream);
 
-/* Expert GEMMs (jt_moe_gemm.cu), 64-row token tiles.  tiles / ntiles: tile
+/* Expert GEMMs (jt_moe_gemm.cu), JT_TILE_ROWS-row token tiles.  tiles / ntiles: tile
  * table and its length (device).  row_meta [rows]: float4 records above.
  * Group scales fp16 [E][K/64][n_ch]; h scales hs [rows][hs_ld] with
  * hs_ld = round_up(n_ch/64, 4). */

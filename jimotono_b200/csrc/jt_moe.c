@@ -88,7 +88,7 @@ int jt_b200_moe_plan_create(const jt_b200_moe_dims *dims, jt_b200_moe_plan **out
     const size_t fs = dims->S > 0 ? (size_t)dims->fs : 64;
     const size_t Tk = T * k;
     const size_t nch = (size_t)jtk_sort_chunks(dims->T);
-    const size_t max_tiles = Tk / 64 + E + 1;
+    const size_t max_tiles = Tk / JT_TILE_ROWS + E + 1;
     struct {
         void **dst;
         size_t bytes;
@@ -97,7 +97,7 @@ int jt_b200_moe_plan_create(const jt_b200_moe_dims *dims, jt_b200_moe_plan **out
         {(void **)&p->pos, Tk * 4},          {(void **)&p->hist, nch * E * 4},
         {(void **)&p->off, (E + 1) * 4},     {(void **)&p->tile_off, (E + 1) * 4},
         {(void **)&p->meta, 64},             {(void **)&p->sh_ntiles, 64},
-        {(void **)&p->tiles, max_tiles * 16}, {(void **)&p->sh_tiles, (T / 64 + 1) * 16},
+        {(void **)&p->tiles, max_tiles * 16}, {(void **)&p->sh_tiles, (T / JT_TILE_ROWS + 1) * 16},
         {(void **)&p->row_meta, Tk * 16},    {(void **)&p->sh_meta, T * 16},
         {(void **)&p->w_raw, Tk * 4},        {(void **)&p->w_fin, Tk * 4},
         {(void **)&p->xs, T * 4},            {(void **)&p->hs, Tk * (size_t)hs_ld((int)f) * 4},
@@ -281,11 +281,11 @@ int jt_b200_moe_forward(jt_b200_moe_plan *plan, const jt_b200_moe_weights *w, co
         }
     }
     /* Upper bound of the device-side token-tile count: every non-empty
-     * expert adds at most one partial tile to (kept pairs)/64 full ones. */
+     * expert adds at most one partial tile to (kept pairs)/JT_TILE_ROWS full ones. */
     {
         const long long pairs = (long long)T * k;
         const long long ne = pairs < E ? pairs : E;
-        const long long tl = ne + pairs / 64;
+        const long long tl = ne + pairs / JT_TILE_ROWS;
         gu_hint = tl * (f / 64) > 0x7fffffffLL ? 0 : (int)(tl * (f / 64));
         dn_hint = tl * (d / 128) > 0x7fffffffLL ? 0 : (int)(tl * (d / 128));
     }

@@ -58,17 +58,18 @@
 
 namespace {
 
-constexpr int kBM = 128;  // MMA M: weight rows per tile
-constexpr int kBN = 64;   // MMA N: token rows per tile
-constexpr int kBH = 32;   // token columns per epilogue warp
-constexpr int kBK = 128;  // K per pipeline stage
-constexpr int kThreads = 448;  // 14 warps
-constexpr int kEpiWarp0 = 6;   // warps 6..13: epilogue
+constexpr int kBM = 128;           // MMA M: weight rows per tile
+constexpr int kBN = JT_TILE_ROWS;  // MMA N (max): token rows per tile
+constexpr int kBH = 64;            // token columns per epilogue warp
+constexpr int kBK = 128;           // K per pipeline stage
+constexpr int kThreads = 480;      // 15 warps
+constexpr int kEpiWarp0 = 6;       // warps 6..13: epilogue
+constexpr int kMmaWarp2 = 14;      // second MMA issuer
 constexpr int kEpiThreads = 256;
-constexpr uint32_t kMagicU = 0x4B400000u;
 constexpr float kMagicF = 12582912.0f;
 constexpr int kMaxGroups = 64;  // K <= 4096
 constexpr size_t kSmemLimit = 232448;
+static_assert(kBN == 2 * kBH, "two epilogue warps per TMEM lane quarter");
 
 enum Mode { GU_ROUTED = 0, GU_SHARED = 1, DN_ROUTED = 2, DN_SHARED = 3 };
 
@@ -80,12 +81,11 @@ struct Cfg {
     static constexpr bool kPacked = (MODE == GU_ROUTED || MODE == DN_ROUTED);
     static constexpr bool kDown = !kGateUp;
     static constexpr bool kMagic = (MODE != GU_SHARED);  // 64-K drain units
-    static constexpr int kUB = kMagic ? 2 : 1;           // units per drain pass
     static constexpr int kChTile = kGateUp ? 64 : 128;   // output channels per tile
     static constexpr int kBits = MODE == GU_ROUTED ? 2 : (MODE == DN_ROUTED ? 4 : 8);
     static constexpr uint32_t kPackedRow = kPacked ? (kBK * kBits / 8) : 0;  // bytes/row/stage
     static constexpr uint32_t kAU = kBM * kBK;  // unpacked operand, 16 KB
-    static constexpr uint32_t kX = kBN * kBK;   // token rows, 8 KB
+    static constexpr uint32_t kX = kBN * kBK;   // token rows, 16 KB
     static constexpr uint32_t kAP = kBM * kPackedRow;
     static constexpr uint32_t kStage = kAU + kX + kAP;
     // per-tile slot: info | row meta [kBN] float4 | group scales fp16 [G][128] |
@@ -95,7 +95,11 @@ struct Cfg {
     static constexpr uint32_t kOffBlk = kOffScale + (kPacked ? kMaxGroups * kBM * 2 : 0);
     static constexpr uint32_t kSlot = align_up(kOffBlk + (kDown ? kBN * kMaxGroups * 4 : 0), 1024);
     static constexpr uint32_t kHTile = kGateUp ? 2 * kBN * 64 * 4 : 0;  // g then u [row][64]
-    static constexpr size_t kFixed = 1024 + 2 * (size_t)kSlot + kHTile + 1024;
+    // preset operands of the magic modes: A = bf16 ones [128][16], B = bf16
+    // 786432 [kBN][16]; one kind::f16 MMA of them writes 16 * 786432 =
+    // 12582912.0f (bits 0x4B400000) into every accumulator element
+    static constexpr uint32_t kConst = kMagic ? (kBM + kBN) * 32 : 0;
+    static constexpr size_t kFixed = 1024 + 2 * (size_t)kSlot + kHTile + kConst + 1024;
     static constexpr int kStagesRaw = (int)((kSmemLimit - kFixed) / kStage);
     static constexpr int kStages = kStagesRaw > 6 ? 6 : kStagesRaw;
     static constexpr int kUnitK = kMagic ? 64 : 0;  // 0: one unit per tile
@@ -104,7 +108,7 @@ struct Cfg {
     static constexpr size_t kSmem = kFixed + (size_t)kStages * kStage;
     static_assert(kStages >= 2, "pipeline depth");
     static_assert(kSmem <= kSmemLimit, "shared memory");
-    static_assert(kSlots % 2 == 0, "unit pairs never wrap the slot ring");
+    static_assert(kSlots % 2 == 0, "the two MMA issuers own alternate slots");
 };
 
 struct MoeGemmParams {
@@ -129,7 +133,17 @@ struct MoeGemmParams {
     int *err;
 };
 
-__device__ __forceinline__ void named_bar_epi() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// Barrier of the 8 epilogue warps on an mbarrier (count 8, one arrival per
+// warp), so that a warp which left on an abort cannot strand the others: the
+// wait is bounded like every other wait in the kernel.
+__device__ __forceinline__ bool epi_sync(uint64_t *bar, uint32_t &phase, volatile int *abort_flag,
+                                         int *err) {
+    __syncwarp();
+    if (jt::lane_id() == 0) jt::mbar_arrive(bar);
+    const bool ok = jt::mbar_wait(bar, phase, abort_flag, err);
+    phase ^= 1u;
+    return ok;
+}
 
 // ---------------------------------------------------------------- unpack
 // 16 INT2 codes (one 32-bit packed word, little-endian along K) -> 16 int8
@@ -205,11 +219,17 @@ __device__ __forceinline__ void st_shared_v4(void *p, int4 v) {
                  : "memory");
 }
 
-// Fold one drained 32-column chunk of one 64-K unit into the running sums.
+// Fold one drained 32-column chunk of one 64-K unit into the running sums
+// r2[0..15] (columns 2i, 2i+1).  blk points at the activation group scales
+// of the chunk's first token row (down modes).
 template <int MODE>
-__device__ __forceinline__ void fold_chunk(float2 (&r2)[kBH / 2], const uint32_t (&a)[32], float s,
+__device__ __forceinline__ void fold_chunk(float2 *r2, const uint32_t (&a)[32], float s,
                                            const float *blk, int hs_ld, int g) {
     const float2 s2 = make_float2(s, s);
+    // activation group scales of the chunk's columns (SMEM broadcast), walked
+    // with one running shared-memory address
+    uint32_t hv_addr = jt::smem_u32(blk + g);
+    const uint32_t hv_step = static_cast<uint32_t>(hs_ld) * 4u;
 #pragma unroll
     for (int j = 0; j < 32; j += 2) {
         float2 &rr = r2[j / 2];
@@ -220,13 +240,23 @@ __device__ __forceinline__ void fold_chunk(float2 (&r2)[kBH / 2], const uint32_t
             if (MODE == GU_ROUTED) {
                 rr = __ffma2_rn(pf, s2, rr);
             } else {
-                // activation group scale of columns j, j+1 (SMEM broadcast)
-                const float2 hv = make_float2(blk[j * hs_ld + g], blk[(j + 1) * hs_ld + g]);
+                float2 hv;
+                asm volatile("ld.shared.f32 %0, [%1];" : "=f"(hv.x) : "r"(hv_addr));
+                asm volatile("ld.shared.f32 %0, [%1];" : "=f"(hv.y) : "r"(hv_addr + hv_step));
+                hv_addr += 2u * hv_step;
                 const float2 t = (MODE == DN_ROUTED) ? __fmul2_rn(pf, s2) : pf;
                 rr = __ffma2_rn(t, hv, rr);
             }
         }
     }
+}
+
+// MMA N for a tile of `rows` token rows: rows rounded up to 16 (the kind::i8
+// N granularity at M = 128), at most kBN.
+__device__ __forceinline__ int mma_n(int rows) {
+    int n = (rows + 15) & ~15;
+    n = n < 16 ? 16 : n;
+    return n > kBN ? kBN : n;
 }
 
 template <int MODE>
@@ -239,7 +269,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint8_t *slot_base = smem + S * C::kStage;  // 2 tile slots
     float *h_tile = reinterpret_cast<float *>(slot_base + 2 * C::kSlot);
-    uint8_t *tail = reinterpret_cast<uint8_t *>(h_tile) + C::kHTile;
+    uint8_t *cst = reinterpret_cast<uint8_t *>(h_tile) + C::kHTile;  // preset operands
+    uint8_t *tail = cst + C::kConst;
     uint64_t *full = reinterpret_cast<uint64_t *>(tail);  // TMA landed
     uint64_t *ready = full + S;      // operands unpacked (packed modes)
     uint64_t *empty = ready + S;     // MMAs finished reading the stage
@@ -247,10 +278,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
     uint64_t *tempty = tfull + NS;   // drain slot drained and re-armed
     uint64_t *pfull = tempty + NS;   // tile slot filled (producer)
     uint64_t *pempty = pfull + 2;    // tile slot released (epilogue)
-    uint64_t *drain = pempty + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    uint64_t *drain = pempty + 2;    // [2]: one per MMA issuer
+    uint64_t *epib = drain + 2;      // epilogue-warp barrier
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(epib + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-    static_assert((3 * S + 2 * NS + 5) * 8 + 8 <= 1024, "barrier area");
+    static_assert((3 * S + 2 * NS + 7) * 8 + 8 <= 1024, "barrier area");
 
     const int warp = jt::warp_id(), lane = jt::lane_id();
     const int nch_tiles = p.n_ch / C::kChTile;
@@ -258,14 +290,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
     const int ngroups = p.K / 64;
     const int total = __ldg(p.ntiles) * nch_tiles;
     int *err = p.err;
-    // stage layout: [A unpacked 128 x 128 | X 64 x 128 | A packed 128 x kPackedRow]
+    // stage layout: [A unpacked 128 x 128 | X kBN x 128 | A packed 128 x kPackedRow]
     auto stage_ptr = [&](int s) { return smem + s * C::kStage; };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             jt::mbar_init(&full[s], 1);
             jt::mbar_init(&ready[s], 4);
-            jt::mbar_init(&empty[s], 1);
+            jt::mbar_init(&empty[s], C::kMagic ? 2 : 1);  // one commit per MMA issuer
         }
         for (int b = 0; b < NS; ++b) {
             jt::mbar_init(&tfull[b], 1);
@@ -274,8 +306,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
         for (int b = 0; b < 2; ++b) {
             jt::mbar_init(&pfull[b], 1);
             jt::mbar_init(&pempty[b], 8);
+            jt::mbar_init(&drain[b], 1);
         }
-        jt::mbar_init(drain, 1);
+        jt::mbar_init(epib, 8);
         *abort_flag = 0;
         jt::fence_mbar_init();
     }
@@ -293,6 +326,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
     if (warp == 1) {
         jt::tmem_alloc(tmem_slot, C::kTmemCols);
         jt::tmem_relinquish();
+    }
+    if (C::kMagic) {
+        // Every element of each preset matrix is equal, so their layout inside
+        // the region does not matter.
+        uint32_t *cw = reinterpret_cast<uint32_t *>(cst);
+        for (int i = threadIdx.x; i < (int)(C::kConst / 4); i += kThreads)
+            cw[i] = i < kBM * 8 ? 0x3F803F80u : 0x49404940u;  // bf16 1.0 | bf16 786432
+        jt::fence_proxy_async();
     }
     jt::tc_fence_before();
     __syncthreads();
@@ -386,15 +427,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                 }
             }
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t kIdesc = jt::idesc_i8(kBM, kBN);
-            constexpr int kStepsPerUnit = C::kUnitK == 0 ? 1 : C::kUnitK / 32;
+    } else if (warp == 1 || warp == kMmaWarp2) {
+        // ------------------------------------------------ MMA issuers
+        // Magic modes: each 128-K stage holds two 64-K units; issuer m (0 =
+        // warp 1, 1 = warp 14) issues unit m of every stage into its own
+        // TMEM slots (slot = unit index % NS), so the per-unit barrier work
+        // of the two issuers overlaps.  Whole-K mode: issuer 0 alone.
+        const int m = warp == 1 ? 0 : 1;
+        if (lane == 0 && (C::kMagic || m == 0)) {
             uint32_t stage = 0, phase = 0;
-            uint32_t slot = 0, slot_phase = 0;
+            uint32_t unit = 0;  // units (slot uses) issued by this CTA, both issuers
             bool ok = true;
             for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+                const int4 te = __ldg(&p.tiles[u / nch_tiles]);
+                const int nrun = mma_n(te.z - te.y);
+                const uint32_t idesc = jt::idesc_i8(kBM, nrun);
+                const uint32_t idesc_pre = jt::idesc_bf16(kBM, nrun);
+                const uint64_t d_ones = jt::umma_desc_noswz(jt::smem_u32(cst), 128, 256);
+                const uint64_t d_magic = jt::umma_desc_noswz(jt::smem_u32(cst + kBM * 32), 128, 256);
                 for (int kb = 0; kb < nk && ok; ++kb) {
                     uint64_t *gate = C::kPacked ? &ready[stage] : &full[stage];
                     if (!jt::mbar_wait(gate, phase, abort_flag, err)) {
@@ -405,33 +455,38 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                     const uint32_t base = jt::smem_u32(stage_ptr(stage));
                     const uint64_t dA = jt::umma_desc_sw128(base);
                     const uint64_t dX = jt::umma_desc_sw128(base + C::kAU);
-#pragma unroll
-                    for (int ks = 0; ks < kBK / 32; ++ks) {
-                        const bool unit_start = (C::kUnitK == 0) ? (kb == 0 && ks == 0)
-                                                                 : (ks % kStepsPerUnit == 0);
-                        const bool unit_end = (C::kUnitK == 0)
-                                                  ? (kb == nk - 1 && ks == kBK / 32 - 1)
-                                                  : (ks % kStepsPerUnit == kStepsPerUnit - 1);
-                        if (unit_start) {
-                            // the epilogue arms (and re-arms) every slot
-                            if (!jt::mbar_wait(&tempty[slot], slot_phase, abort_flag, err)) {
+                    if (C::kMagic) {
+                        const uint32_t my = unit + m;
+                        const uint32_t slot = my % NS;
+                        if (!jt::mbar_wait(&tempty[slot], (my / NS) & 1u, abort_flag, err)) {
+                            ok = false;
+                            break;
+                        }
+                        jt::tc_fence_after();
+                        // preset the slot to 0x4B400000, then accumulate the int8 products
+                        jt::mma_bf16(tmem_base + slot * kBN, d_ones, d_magic, idesc_pre, 0u);
+                        jt::mma_i8(tmem_base + slot * kBN, dA + 4u * m, dX + 4u * m, idesc, 1u);
+                        jt::mma_i8(tmem_base + slot * kBN, dA + 4u * m + 2u, dX + 4u * m + 2u, idesc, 1u);
+                        jt::mma_commit(&tfull[slot]);
+                        unit += 2;
+                    } else {
+                        const uint32_t slot = unit % NS;
+                        if (kb == 0) {
+                            if (!jt::mbar_wait(&tempty[slot], (unit / NS) & 1u, abort_flag, err)) {
                                 ok = false;
                                 break;
                             }
                             jt::tc_fence_after();
                         }
-                        // magic-armed slots always accumulate onto 0x4B400000
-                        const uint32_t acc = C::kMagic ? 1u : (unit_start ? 0u : 1u);
-                        jt::mma_i8(tmem_base + slot * kBN, dA + 2u * ks, dX + 2u * ks, kIdesc, acc);
-                        if (unit_end) {
+#pragma unroll
+                        for (int ks = 0; ks < kBK / 32; ++ks)
+                            jt::mma_i8(tmem_base + slot * kBN, dA + 2u * ks, dX + 2u * ks, idesc,
+                                       (kb | ks) != 0 ? 1u : 0u);
+                        if (kb == nk - 1) {
                             jt::mma_commit(&tfull[slot]);
-                            if (++slot == (uint32_t)NS) {
-                                slot = 0;
-                                slot_phase ^= 1u;
-                            }
+                            ++unit;
                         }
                     }
-                    if (!ok) break;
                     jt::mma_commit(&empty[stage]);
                     if (++stage == S) {
                         stage = 0;
@@ -440,9 +495,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                 }
             }
             if (!ok) {  // already-issued MMAs retire before TMEM is released
-                jt::mma_commit(drain);
+                jt::mma_commit(&drain[m]);
                 const long long t0 = clock64();
-                while (!jt::mbar_try_wait(drain, 0) && clock64() - t0 < JT_SPIN_CYCLES / 16) {
+                while (!jt::mbar_try_wait(&drain[m], 0) && clock64() - t0 < JT_SPIN_CYCLES / 16) {
                 }
             }
         }
@@ -473,7 +528,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
     } else {
         // ------------------------------------------------ epilogue warps
         // Two warps per TMEM lane quarter: warp w reads lanes 32*(w%4)..+31
-        // and owns token-column half (w-6)/4 of every accumulator.
+        // and owns token-column half (w-6)/4 (64 columns) of every accumulator.
         const int q = warp & 3;                         // TMEM lane quarter
         const int half = (warp - kEpiWarp0) >> 2;       // column half
         const int lr = q * 32 + lane;                   // operand row = TMEM lane
@@ -483,16 +538,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
         const int lch = C::kGateUp ? (lr & 63) : lr;
         const int j0 = half * kBH;  // first token column owned
         const uint32_t tlane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + j0;
-        // arm every accumulator slot: magic pattern (64-K units) or nothing
-        if (C::kMagic) {
-            for (int b = 0; b < NS; ++b) jt::tmem_st32_fill(tlane + b * kBN, kMagicU);
-            jt::tmem_wait_st();
-        }
-        jt::tc_fence_before();
+        // every accumulator slot starts free (the MMA issuers preset it)
         __syncwarp();
         if (lane == 0)
             for (int b = 0; b < NS; ++b) jt::mbar_arrive(&tempty[b]);
-        uint32_t slot = 0, slot_phase = 0, ts = 0, tphase = 0;
+        uint32_t unit = 0, ts = 0, tphase = 0, ephase = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
             if (!jt::mbar_wait(&pfull[ts], tphase, abort_flag, err)) {
@@ -507,47 +557,33 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
             const float *blk = reinterpret_cast<const float *>(sl + C::kOffBlk) + j0 * p.hs_ld;
             const int sc_stride = C::kGateUp ? 64 : 128;
             const int ch = info.w + lch;  // output channel within the expert
+            // columns of this warp that hold token rows of the tile
+            const bool active = j0 < info.z - info.y;
             float2 r2[kBH / 2];
 #pragma unroll
             for (int j = 0; j < kBH / 2; ++j) r2[j] = make_float2(0.0f, 0.0f);
             const int nunits = C::kUnitK == 0 ? 1 : p.K / C::kUnitK;
-            for (int un = 0; un < nunits; un += C::kUB) {
-                if (!jt::mbar_wait(&tfull[slot], slot_phase, abort_flag, err)) {
-                    ok = false;
-                    break;
-                }
-                if (C::kUB == 2 && !jt::mbar_wait(&tfull[slot + 1], slot_phase, abort_flag, err)) {
+            for (int un = 0; un < nunits; ++un, ++unit) {
+                const uint32_t slot = unit % NS;
+                if (!jt::mbar_wait(&tfull[slot], (unit / NS) & 1u, abort_flag, err)) {
                     ok = false;
                     break;
                 }
                 jt::tc_fence_after();
-                const uint32_t trow = tlane + slot * kBN;
-                uint32_t a0[32], a1[32];
-                jt::tmem_ld32(trow, a0);
-                if (C::kUB == 2) jt::tmem_ld32(trow + kBN, a1);
-                jt::tmem_wait_ld();
-                if (C::kMagic) {
-                    jt::tmem_st32_fill(trow, kMagicU);
-                    if (C::kUB == 2) jt::tmem_st32_fill(trow + kBN, kMagicU);
+                if (active) {
+                    const uint32_t trow = tlane + slot * kBN;
+                    const float s0 = C::kPacked ? __half2float(sc[un * sc_stride]) : 1.0f;
+#pragma unroll
+                    for (int c = 0; c < 2; ++c) {
+                        uint32_t a[32];
+                        jt::tmem_ld32(trow + 32 * c, a);
+                        jt::tmem_wait_ld();
+                        fold_chunk<MODE>(r2 + 16 * c, a, s0, blk + 32 * c * p.hs_ld, p.hs_ld, un);
+                    }
                 }
-                const float s0 = C::kPacked ? __half2float(sc[un * sc_stride]) : 1.0f;
-                fold_chunk<MODE>(r2, a0, s0, blk, p.hs_ld, un);
-                if (C::kUB == 2) {
-                    const float s1 = C::kPacked ? __half2float(sc[(un + 1) * sc_stride]) : 1.0f;
-                    fold_chunk<MODE>(r2, a1, s1, blk, p.hs_ld, un + 1);
-                }
-                if (C::kMagic) jt::tmem_wait_st();
                 jt::tc_fence_before();
                 __syncwarp();
-                if (lane == 0) {
-                    jt::mbar_arrive(&tempty[slot]);
-                    if (C::kUB == 2) jt::mbar_arrive(&tempty[slot + 1]);
-                }
-                slot += C::kUB;
-                if (slot == (uint32_t)NS) {
-                    slot = 0;
-                    slot_phase ^= 1u;
-                }
+                if (lane == 0) jt::mbar_arrive(&tempty[slot]);
             }
             if (!ok) break;
             if constexpr (C::kGateUp) {
@@ -555,44 +591,50 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                 if (MODE == GU_SHARED) cscale = __ldg(is_up ? &p.cs1[ch] : &p.cs0[ch]);
                 // pass 1: stage g and u (activation- and channel-scaled) in SMEM
                 float *dst_tile = h_tile + (is_up ? kBN * 64 : 0);
+                if (active) {
 #pragma unroll
-                for (int j = 0; j < kBH; ++j) {
-                    const float xs = meta[j0 + j].x;
-                    const float rv = (j & 1) ? r2[j / 2].y : r2[j / 2].x;
-                    dst_tile[(j0 + j) * 64 + lch] = (MODE == GU_ROUTED)
-                                                        ? __fmul_rn(rv, xs)
-                                                        : __fmul_rn(__fmul_rn(rv, xs), cscale);
+                    for (int j = 0; j < kBH; ++j) {
+                        const float xs = meta[j0 + j].x;
+                        const float rv = (j & 1) ? r2[j / 2].y : r2[j / 2].x;
+                        dst_tile[(j0 + j) * 64 + lch] = (MODE == GU_ROUTED)
+                                                            ? __fmul_rn(rv, xs)
+                                                            : __fmul_rn(__fmul_rn(rv, xs), cscale);
+                    }
                 }
-                named_bar_epi();
+                if (!epi_sync(epib, ephase, abort_flag, err)) {
+                    ok = false;
+                    break;
+                }
                 // pass 2: h = SwiGLU(g, u) (moe_layer.c:146-148) over all epilogue
-                // threads, written over g
+                // threads, written over g (only the tile's rows)
+                const int nrow = min(info.z - info.y, kBN);
 #pragma unroll 2
-                for (int i = etid; i < kBN * 64; i += kEpiThreads)
+                for (int i = etid; i < nrow * 64; i += kEpiThreads)
                     h_tile[i] = jt::swiglu(h_tile[i], h_tile[kBN * 64 + i]);
-                named_bar_epi();
-                // pass 3: requantize each row's 64 channels (4 threads x 16) -> codes + scale
-                const int j = etid >> 2, part = etid & 3;
-                const float *hr = h_tile + j * 64 + part * 16;
+                if (!epi_sync(epib, ephase, abort_flag, err)) {
+                    ok = false;
+                    break;
+                }
+                // pass 3: requantize each row's 64 channels (2 threads x 32) -> codes + scale
+                const int j = etid >> 1, part = etid & 1;
+                const float *hr = h_tile + j * 64 + part * 32;
                 float m = 0.0f;
                 int nf = 0;
 #pragma unroll
-                for (int i = 0; i < 16; i += 4) {
+                for (int i = 0; i < 32; i += 4) {
                     const float4 v4 = *reinterpret_cast<const float4 *>(hr + i);
                     nf |= !isfinite(v4.x) | !isfinite(v4.y) | !isfinite(v4.z) | !isfinite(v4.w);
                     m = fmaxf(m, fmaxf(fmaxf(fabsf(v4.x), fabsf(v4.y)), fmaxf(fabsf(v4.z), fabsf(v4.w))));
                 }
-#pragma unroll
-                for (int o = 1; o < 4; o <<= 1) {
-                    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-                    nf |= __shfl_xor_sync(0xffffffffu, nf, o);
-                }
+                m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+                nf |= __shfl_xor_sync(0xffffffffu, nf, 1);
                 const int row = info.y + j;
                 if (row < info.z) {
                     if (nf) atomicExch(err, JT_KERR_NONFINITE);
                     const jt::QuantBlock qb = jt::quant_block(m);
-                    uint32_t words[4];
+                    uint32_t words[8];
 #pragma unroll
-                    for (int b4 = 0; b4 < 4; ++b4) {
+                    for (int b4 = 0; b4 < 8; ++b4) {
                         uint32_t word = 0;
 #pragma unroll
                         for (int b2 = 0; b2 < 4; ++b2) {
@@ -601,27 +643,33 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                         }
                         words[b4] = word;
                     }
-                    *reinterpret_cast<uint4 *>(p.hq + (size_t)row * p.n_ch + info.w + part * 16) =
-                        make_uint4(words[0], words[1], words[2], words[3]);
+                    uint4 *dst = reinterpret_cast<uint4 *>(p.hq + (size_t)row * p.n_ch + info.w + part * 32);
+                    dst[0] = make_uint4(words[0], words[1], words[2], words[3]);
+                    dst[1] = make_uint4(words[4], words[5], words[6], words[7]);
                     if (part == 0) p.hs[(size_t)row * p.hs_ld + info.w / 64] = qb.scale_f;
                 }
                 // all slot reads (meta) done before the slot is released
                 __syncwarp();
                 if (lane == 0) jt::mbar_arrive(&pempty[ts]);
-                named_bar_epi();  // h_tile free for the next tile
+                if (!epi_sync(epib, ephase, abort_flag, err)) {  // h_tile free for the next tile
+                    ok = false;
+                    break;
+                }
             } else {
                 float cs = 1.0f;
                 if (MODE == DN_SHARED) cs = __ldg(&p.cs0[ch]);
+                if (active) {
 #pragma unroll
-                for (int j = 0; j < kBH; ++j) {
-                    const int row = info.y + j0 + j;
-                    if (row >= info.z) continue;
-                    const float4 mt = meta[j0 + j];
-                    const float rv = (j & 1) ? r2[j / 2].y : r2[j / 2].x;
-                    const float v = (MODE == DN_ROUTED) ? __fmul_rn(mt.y, rv) : __fmul_rn(rv, cs);
-                    float *dst = p.y + (size_t)__float_as_int(mt.z) * p.n_ch + ch;
-                    if (p.y_accumulate) atomicAdd(dst, v);
-                    else *dst = v;
+                    for (int j = 0; j < kBH; ++j) {
+                        const int row = info.y + j0 + j;
+                        if (row >= info.z) continue;
+                        const float4 mt = meta[j0 + j];
+                        const float rv = (j & 1) ? r2[j / 2].y : r2[j / 2].x;
+                        const float v = (MODE == DN_ROUTED) ? __fmul_rn(mt.y, rv) : __fmul_rn(rv, cs);
+                        float *dst = p.y + (size_t)__float_as_int(mt.z) * p.n_ch + ch;
+                        if (p.y_accumulate) atomicAdd(dst, v);
+                        else *dst = v;
+                    }
                 }
                 __syncwarp();
                 if (lane == 0) jt::mbar_arrive(&pempty[ts]);

@@ -143,6 +143,17 @@ __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t
         : "memory");
 }
 
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, bf16 x bf16 -> fp32 (kind::f16, K = 16).
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Arrive on an mbarrier once all previously issued tcgen05 ops of this thread finish.
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
     asm volatile(
@@ -191,6 +202,14 @@ __device__ __forceinline__ void tmem_st32_fill(uint32_t taddr, uint32_t v) {
         : "memory");
 }
 
+// 32 lanes x 32 bit, 8 consecutive columns per thread, all set to v (the
+// narrow form keeps the number of registers that hold v small).
+__device__ __forceinline__ void tmem_st8_fill(uint32_t taddr, uint32_t v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
+                 "r"(v)
+                 : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_st() {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -210,6 +229,27 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
     d |= static_cast<uint64_t>(1u) << 46;
     d |= static_cast<uint64_t>(2u) << 61;
     return d;
+}
+
+// UMMA shared-memory descriptor, K-major without swizzle: 8-row x 16-byte
+// core matrices, `lbo` bytes apart along K and `sbo` bytes apart along M/N.
+__device__ __forceinline__ uint64_t umma_desc_noswz(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    return d;
+}
+
+// Instruction descriptor, kind::f16 with bf16 A and B and an fp32
+// accumulator, both operands K-major, shape M x N.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+    return (1u << 4)                                   // D format: f32
+           | (1u << 7)                                 // A: bf16
+           | (1u << 10)                                // B: bf16
+           | (static_cast<uint32_t>(N >> 3) << 17)     // N / 8
+           | (static_cast<uint32_t>(M >> 4) << 24);    // M / 16
 }
 
 // Instruction descriptor, kind::i8: signed A and B, int32 accumulator,

@@ -132,7 +132,7 @@ __global__ void k_sort_count(const int32_t *__restrict__ ids, int T, int k, int 
 
 // One CTA.  base[c][e] = pairs of expert e in chunks < c; kept[e] =
 // min(count, cap); off = exclusive scan of kept; tile_off = exclusive scan
-// of ceil(kept/64) (64-row token tiles of the expert GEMMs).
+// of ceil(kept/JT_TILE_ROWS) (token tiles of the expert GEMMs).
 // meta[0] = kept total, meta[1] = total token tiles, meta[2] = max kept.
 __global__ void k_sort_scan(int32_t *__restrict__ hist_base, int nchunks, int E, int cap,
                             int32_t *__restrict__ off, int32_t *__restrict__ tile_off,
@@ -156,7 +156,7 @@ __global__ void k_sort_scan(int32_t *__restrict__ hist_base, int nchunks, int E,
         }
         kept_local[j] = kc;
         ks += kc;
-        ts += (kc + 63) / 64;
+        ts += (kc + JT_TILE_ROWS - 1) / JT_TILE_ROWS;
         mx = kc > mx ? kc : mx;
     }
     sm[tid] = ks;
@@ -182,7 +182,7 @@ __global__ void k_sort_scan(int32_t *__restrict__ hist_base, int nchunks, int E,
             tile_off[e] = run_t;
         }
         run_k += kept_local[j];
-        run_t += (kept_local[j] + 63) / 64;
+        run_t += (kept_local[j] + JT_TILE_ROWS - 1) / JT_TILE_ROWS;
     }
     if (tid == nt - 1) {
         off[E] = sm[tid];
@@ -202,13 +202,14 @@ __global__ void k_sort_scan(int32_t *__restrict__ hist_base, int nchunks, int E,
 }
 
 // Token-tile table of the expert GEMMs: entry v = {expert, first row,
-// expert's end row, 0} for the 64-row tiles of every expert in order, so a
+// expert's end row, 0} for the JT_TILE_ROWS-row tiles of every expert in order, so a
 // GEMM CTA finds its tile with one load instead of a search.
 __global__ void k_build_tiles(const int32_t *__restrict__ off, const int32_t *__restrict__ tile_off,
                               int E, int4 *__restrict__ tiles) {
     for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < E; e += gridDim.x * blockDim.x) {
         const int r0 = off[e], r1 = off[e + 1], t0 = tile_off[e];
-        for (int j = 0; r0 + 64 * j < r1; ++j) tiles[t0 + j] = make_int4(e, r0 + 64 * j, r1, 0);
+        for (int j = 0; r0 + JT_TILE_ROWS * j < r1; ++j)
+            tiles[t0 + j] = make_int4(e, r0 + JT_TILE_ROWS * j, r1, 0);
     }
 }
 
