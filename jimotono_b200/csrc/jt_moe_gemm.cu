@@ -60,16 +60,16 @@ namespace {
 
 constexpr int kBM = 128;           // MMA M: weight rows per tile
 constexpr int kBN = JT_TILE_ROWS;  // MMA N (max): token rows per tile
-constexpr int kBH = 64;            // token columns per epilogue warp
+constexpr int kBH = 32;            // token columns per epilogue warp
 constexpr int kBK = 128;           // K per pipeline stage
-constexpr int kThreads = 480;      // 15 warps
-constexpr int kEpiWarp0 = 6;       // warps 6..13: epilogue
-constexpr int kMmaWarp2 = 14;      // second MMA issuer
-constexpr int kEpiThreads = 256;
+constexpr int kThreads = 736;      // 23 warps
+constexpr int kEpiWarp0 = 6;       // warps 6..21: epilogue
+constexpr int kEpiWarps = 16;
+constexpr int kMmaWarp2 = 22;      // second MMA issuer
 constexpr float kMagicF = 12582912.0f;
 constexpr int kMaxGroups = 64;  // K <= 4096
 constexpr size_t kSmemLimit = 232448;
-static_assert(kBN == 2 * kBH, "two epilogue warps per TMEM lane quarter");
+static_assert(kBN == (kEpiWarps / 4) * kBH, "four epilogue warps per TMEM lane quarter");
 
 enum Mode { GU_ROUTED = 0, GU_SHARED = 1, DN_ROUTED = 2, DN_SHARED = 3 };
 
@@ -133,7 +133,7 @@ struct MoeGemmParams {
     int *err;
 };
 
-// Barrier of the 8 epilogue warps on an mbarrier (count 8, one arrival per
+// Barrier of the epilogue warps on an mbarrier (one arrival per
 // warp), so that a warp which left on an abort cannot strand the others: the
 // wait is bounded like every other wait in the kernel.
 __device__ __forceinline__ bool epi_sync(uint64_t *bar, uint32_t &phase, volatile int *abort_flag,
@@ -301,14 +301,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
         }
         for (int b = 0; b < NS; ++b) {
             jt::mbar_init(&tfull[b], 1);
-            jt::mbar_init(&tempty[b], 8);  // one arrival per epilogue warp
+            jt::mbar_init(&tempty[b], kEpiWarps);  // one arrival per epilogue warp
         }
         for (int b = 0; b < 2; ++b) {
             jt::mbar_init(&pfull[b], 1);
-            jt::mbar_init(&pempty[b], 8);
+            jt::mbar_init(&pempty[b], kEpiWarps);
             jt::mbar_init(&drain[b], 1);
         }
-        jt::mbar_init(epib, 8);
+        jt::mbar_init(epib, kEpiWarps);
         *abort_flag = 0;
         jt::fence_mbar_init();
     }
@@ -527,16 +527,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
         }
     } else {
         // ------------------------------------------------ epilogue warps
-        // Two warps per TMEM lane quarter: warp w reads lanes 32*(w%4)..+31
-        // and owns token-column half (w-6)/4 (64 columns) of every accumulator.
+        // Four warps per TMEM lane quarter: warp w reads lanes 32*(w%4)..+31
+        // and owns token columns 32*((w-6)/4)..+31 of every accumulator.
         const int q = warp & 3;                         // TMEM lane quarter
-        const int half = (warp - kEpiWarp0) >> 2;       // column half
+        const int cq = (warp - kEpiWarp0) >> 2;         // column quarter
         const int lr = q * 32 + lane;                   // operand row = TMEM lane
-        const int etid = threadIdx.x - kEpiWarp0 * 32;  // 0..255
+        const int ew = warp - kEpiWarp0;                // 0..15
         // gate/up: rows 0..63 gate of channel lr, rows 64..127 up of channel lr-64
         const bool is_up = C::kGateUp && lr >= 64;
         const int lch = C::kGateUp ? (lr & 63) : lr;
-        const int j0 = half * kBH;  // first token column owned
+        const int j0 = cq * kBH;  // first token column owned
         const uint32_t tlane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + j0;
         // every accumulator slot starts free (the MMA issuers preset it)
         __syncwarp();
@@ -557,8 +557,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
             const float *blk = reinterpret_cast<const float *>(sl + C::kOffBlk) + j0 * p.hs_ld;
             const int sc_stride = C::kGateUp ? 64 : 128;
             const int ch = info.w + lch;  // output channel within the expert
+            const int nrow = min(info.z - info.y, kBN);
             // columns of this warp that hold token rows of the tile
-            const bool active = j0 < info.z - info.y;
+            const bool active = j0 < nrow;
             float2 r2[kBH / 2];
 #pragma unroll
             for (int j = 0; j < kBH / 2; ++j) r2[j] = make_float2(0.0f, 0.0f);
@@ -571,15 +572,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                 }
                 jt::tc_fence_after();
                 if (active) {
-                    const uint32_t trow = tlane + slot * kBN;
                     const float s0 = C::kPacked ? __half2float(sc[un * sc_stride]) : 1.0f;
-#pragma unroll
-                    for (int c = 0; c < 2; ++c) {
-                        uint32_t a[32];
-                        jt::tmem_ld32(trow + 32 * c, a);
-                        jt::tmem_wait_ld();
-                        fold_chunk<MODE>(r2 + 16 * c, a, s0, blk + 32 * c * p.hs_ld, p.hs_ld, un);
-                    }
+                    uint32_t a[32];
+                    jt::tmem_ld32(tlane + slot * kBN, a);
+                    jt::tmem_wait_ld();
+                    fold_chunk<MODE>(r2, a, s0, blk, p.hs_ld, un);
                 }
                 jt::tc_fence_before();
                 __syncwarp();
@@ -605,50 +602,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                     ok = false;
                     break;
                 }
-                // pass 2: h = SwiGLU(g, u) (moe_layer.c:146-148) over all epilogue
-                // threads, written over g (only the tile's rows)
-                const int nrow = min(info.z - info.y, kBN);
-#pragma unroll 2
-                for (int i = etid; i < nrow * 64; i += kEpiThreads)
-                    h_tile[i] = jt::swiglu(h_tile[i], h_tile[kBN * 64 + i]);
-                if (!epi_sync(epib, ephase, abort_flag, err)) {
-                    ok = false;
-                    break;
-                }
-                // pass 3: requantize each row's 64 channels (2 threads x 32) -> codes + scale
-                const int j = etid >> 1, part = etid & 1;
-                const float *hr = h_tile + j * 64 + part * 32;
-                float m = 0.0f;
-                int nf = 0;
+                // pass 2: one warp per token row (rows ew, ew+16, ...): lane l
+                // forms h = SwiGLU(g, u) (moe_layer.c:146-148) of channels 2l,
+                // 2l+1, the row's 64 channels are requantized together
+                // (w8a8.c:688-747) and stored as 64 contiguous codes.
+                for (int j = ew; j < nrow; j += kEpiWarps) {
+                    const float2 g2 = *reinterpret_cast<const float2 *>(h_tile + j * 64 + 2 * lane);
+                    const float2 u2 = *reinterpret_cast<const float2 *>(h_tile + kBN * 64 + j * 64 + 2 * lane);
+                    const float h0 = jt::swiglu(g2.x, u2.x), h1 = jt::swiglu(g2.y, u2.y);
+                    const bool bad = !isfinite(h0) || !isfinite(h1);
+                    float m = fmaxf(fabsf(h0), fabsf(h1));
 #pragma unroll
-                for (int i = 0; i < 32; i += 4) {
-                    const float4 v4 = *reinterpret_cast<const float4 *>(hr + i);
-                    nf |= !isfinite(v4.x) | !isfinite(v4.y) | !isfinite(v4.z) | !isfinite(v4.w);
-                    m = fmaxf(m, fmaxf(fmaxf(fabsf(v4.x), fabsf(v4.y)), fmaxf(fabsf(v4.z), fabsf(v4.w))));
-                }
-                m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-                nf |= __shfl_xor_sync(0xffffffffu, nf, 1);
-                const int row = info.y + j;
-                if (row < info.z) {
-                    if (nf) atomicExch(err, JT_KERR_NONFINITE);
+                    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicExch(err, JT_KERR_NONFINITE);
                     const jt::QuantBlock qb = jt::quant_block(m);
-                    uint32_t words[8];
-#pragma unroll
-                    for (int b4 = 0; b4 < 8; ++b4) {
-                        uint32_t word = 0;
-#pragma unroll
-                        for (int b2 = 0; b2 < 4; ++b2) {
-                            const int c = jt::quant_code(hr[4 * b4 + b2], qb);
-                            word |= (uint32_t)(uint8_t)(int8_t)c << (8 * b2);
-                        }
-                        words[b4] = word;
-                    }
-                    uint4 *dst = reinterpret_cast<uint4 *>(p.hq + (size_t)row * p.n_ch + info.w + part * 32);
-                    dst[0] = make_uint4(words[0], words[1], words[2], words[3]);
-                    dst[1] = make_uint4(words[4], words[5], words[6], words[7]);
-                    if (part == 0) p.hs[(size_t)row * p.hs_ld + info.w / 64] = qb.scale_f;
+                    const int c0 = jt::quant_code(h0, qb), c1 = jt::quant_code(h1, qb);
+                    const int row = info.y + j;
+                    const uint16_t pair = (uint16_t)(uint8_t)(int8_t)c0 | ((uint16_t)(uint8_t)(int8_t)c1 << 8);
+                    *reinterpret_cast<uint16_t *>(p.hq + (size_t)row * p.n_ch + info.w + 2 * lane) = pair;
+                    if (lane == 0) p.hs[(size_t)row * p.hs_ld + info.w / 64] = qb.scale_f;
                 }
-                // all slot reads (meta) done before the slot is released
+                // all slot reads (meta) and h_tile reads done before release
                 __syncwarp();
                 if (lane == 0) jt::mbar_arrive(&pempty[ts]);
                 if (!epi_sync(epib, ephase, abort_flag, err)) {  // h_tile free for the next tile
