@@ -102,13 +102,15 @@ struct Cfg {
     static constexpr size_t kFixed = 1024 + 2 * (size_t)kSlot + kHTile + kConst + 1024;
     static constexpr int kStagesRaw = (int)((kSmemLimit - kFixed) / kStage);
     static constexpr int kStages = kStagesRaw > 6 ? 6 : kStagesRaw;
-    static constexpr int kUnitK = kMagic ? 64 : 0;  // 0: one unit per tile
     static constexpr int kSlots = 512 / kBN;        // TMEM accumulators
+    // drain groups: the two slots of one 128-K stage (64-K units), or one
+    // slot per tile (whole-K accumulation); one full/empty barrier pair each
+    static constexpr int kGroups = kMagic ? kSlots / 2 : kSlots;
     static constexpr uint32_t kTmemCols = 512;
     static constexpr size_t kSmem = kFixed + (size_t)kStages * kStage;
     static_assert(kStages >= 2, "pipeline depth");
     static_assert(kSmem <= kSmemLimit, "shared memory");
-    static_assert(kSlots % 2 == 0, "the two MMA issuers own alternate slots");
+    static_assert(kSlots == 4, "two drain groups of two slots");
 };
 
 struct MoeGemmParams {
@@ -263,7 +265,7 @@ template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant__ MoeGemmParams p) {
     using C = Cfg<MODE>;
     constexpr int S = C::kStages;
-    constexpr int NS = C::kSlots;
+    constexpr int NG = C::kGroups;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -274,15 +276,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
     uint64_t *full = reinterpret_cast<uint64_t *>(tail);  // TMA landed
     uint64_t *ready = full + S;      // operands unpacked (packed modes)
     uint64_t *empty = ready + S;     // MMAs finished reading the stage
-    uint64_t *tfull = empty + S;     // drain slot filled
-    uint64_t *tempty = tfull + NS;   // drain slot drained and re-armed
-    uint64_t *pfull = tempty + NS;   // tile slot filled (producer)
+    uint64_t *tfull = empty + S;     // drain group filled
+    uint64_t *tempty = tfull + NG;   // drain group drained
+    uint64_t *pfull = tempty + NG;   // tile slot filled (producer)
     uint64_t *pempty = pfull + 2;    // tile slot released (epilogue)
     uint64_t *drain = pempty + 2;    // [2]: one per MMA issuer
     uint64_t *epib = drain + 2;      // epilogue-warp barrier
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(epib + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-    static_assert((3 * S + 2 * NS + 7) * 8 + 8 <= 1024, "barrier area");
+    static_assert((3 * S + 2 * NG + 7) * 8 + 8 <= 1024, "barrier area");
 
     const int warp = jt::warp_id(), lane = jt::lane_id();
     const int nch_tiles = p.n_ch / C::kChTile;
@@ -297,9 +299,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
         for (int s = 0; s < S; ++s) {
             jt::mbar_init(&full[s], 1);
             jt::mbar_init(&ready[s], 4);
-            jt::mbar_init(&empty[s], C::kMagic ? 2 : 1);  // one commit per MMA issuer
+            jt::mbar_init(&empty[s], 1);
         }
-        for (int b = 0; b < NS; ++b) {
+        for (int b = 0; b < NG; ++b) {
             jt::mbar_init(&tfull[b], 1);
             jt::mbar_init(&tempty[b], kEpiWarps);  // one arrival per epilogue warp
         }
@@ -429,70 +431,76 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
         }
     } else if (warp == 1 || warp == kMmaWarp2) {
         // ------------------------------------------------ MMA issuers
-        // Magic modes: each 128-K stage holds two 64-K units; issuer m (0 =
-        // warp 1, 1 = warp 14) issues unit m of every stage into its own
-        // TMEM slots (slot = unit index % NS), so the per-unit barrier work
-        // of the two issuers overlaps.  Whole-K mode: issuer 0 alone.
+        // Magic modes: 128-K stages go to the two issuers alternately (issuer
+        // m = stage count % 2); a stage's two 64-K units land in the slots
+        // of drain group m, so each issuer waits once for its stage operands
+        // and once for its drain group per two units, and the two issuers'
+        // barrier latencies overlap.  Whole-K mode: issuer 0 alone, one slot
+        // (drain group) per tile.
         const int m = warp == 1 ? 0 : 1;
         if (lane == 0 && (C::kMagic || m == 0)) {
             uint32_t stage = 0, phase = 0;
-            uint32_t unit = 0;  // units (slot uses) issued by this CTA, both issuers
+            uint32_t sc = 0;  // stages seen (magic) / tiles seen (whole K)
             bool ok = true;
+            const uint64_t d_ones = jt::umma_desc_noswz(jt::smem_u32(cst), 128, 256);
+            const uint64_t d_magic = jt::umma_desc_noswz(jt::smem_u32(cst + kBM * 32), 128, 256);
             for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
                 const int4 te = __ldg(&p.tiles[u / nch_tiles]);
                 const int nrun = mma_n(te.z - te.y);
                 const uint32_t idesc = jt::idesc_i8(kBM, nrun);
                 const uint32_t idesc_pre = jt::idesc_bf16(kBM, nrun);
-                const uint64_t d_ones = jt::umma_desc_noswz(jt::smem_u32(cst), 128, 256);
-                const uint64_t d_magic = jt::umma_desc_noswz(jt::smem_u32(cst + kBM * 32), 128, 256);
                 for (int kb = 0; kb < nk && ok; ++kb) {
-                    uint64_t *gate = C::kPacked ? &ready[stage] : &full[stage];
-                    if (!jt::mbar_wait(gate, phase, abort_flag, err)) {
-                        ok = false;
-                        break;
-                    }
-                    jt::tc_fence_after();
-                    const uint32_t base = jt::smem_u32(stage_ptr(stage));
-                    const uint64_t dA = jt::umma_desc_sw128(base);
-                    const uint64_t dX = jt::umma_desc_sw128(base + C::kAU);
-                    if (C::kMagic) {
-                        const uint32_t my = unit + m;
-                        const uint32_t slot = my % NS;
-                        if (!jt::mbar_wait(&tempty[slot], (my / NS) & 1u, abort_flag, err)) {
+                    const bool mine = !C::kMagic || (sc & 1u) == (uint32_t)m;
+                    if (mine) {
+                        uint64_t *gate = C::kPacked ? &ready[stage] : &full[stage];
+                        if (!jt::mbar_wait(gate, phase, abort_flag, err)) {
                             ok = false;
                             break;
                         }
                         jt::tc_fence_after();
-                        // preset the slot to 0x4B400000, then accumulate the int8 products
-                        jt::mma_bf16(tmem_base + slot * kBN, d_ones, d_magic, idesc_pre, 0u);
-                        jt::mma_i8(tmem_base + slot * kBN, dA + 4u * m, dX + 4u * m, idesc, 1u);
-                        jt::mma_i8(tmem_base + slot * kBN, dA + 4u * m + 2u, dX + 4u * m + 2u, idesc, 1u);
-                        jt::mma_commit(&tfull[slot]);
-                        unit += 2;
-                    } else {
-                        const uint32_t slot = unit % NS;
-                        if (kb == 0) {
-                            if (!jt::mbar_wait(&tempty[slot], (unit / NS) & 1u, abort_flag, err)) {
+                        const uint32_t base = jt::smem_u32(stage_ptr(stage));
+                        const uint64_t dA = jt::umma_desc_sw128(base);
+                        const uint64_t dX = jt::umma_desc_sw128(base + C::kAU);
+                        if (C::kMagic) {
+                            const uint32_t g = sc & 1u;
+                            if (!jt::mbar_wait(&tempty[g], (sc >> 1) & 1u, abort_flag, err)) {
                                 ok = false;
                                 break;
                             }
                             jt::tc_fence_after();
-                        }
 #pragma unroll
-                        for (int ks = 0; ks < kBK / 32; ++ks)
-                            jt::mma_i8(tmem_base + slot * kBN, dA + 2u * ks, dX + 2u * ks, idesc,
-                                       (kb | ks) != 0 ? 1u : 0u);
-                        if (kb == nk - 1) {
-                            jt::mma_commit(&tfull[slot]);
-                            ++unit;
+                            for (int h = 0; h < 2; ++h) {
+                                const uint32_t acc = tmem_base + (2u * g + h) * kBN;
+                                // preset to 0x4B400000, then accumulate the int8 products
+                                jt::mma_bf16(acc, d_ones, d_magic, idesc_pre, 0u);
+                                jt::mma_i8(acc, dA + 4u * h, dX + 4u * h, idesc, 1u);
+                                jt::mma_i8(acc, dA + 4u * h + 2u, dX + 4u * h + 2u, idesc, 1u);
+                            }
+                            jt::mma_commit(&tfull[g]);
+                        } else {
+                            const uint32_t g = sc % NG;
+                            if (kb == 0) {
+                                if (!jt::mbar_wait(&tempty[g], (sc / NG) & 1u, abort_flag, err)) {
+                                    ok = false;
+                                    break;
+                                }
+                                jt::tc_fence_after();
+                            }
+#pragma unroll
+                            for (int ks = 0; ks < kBK / 32; ++ks)
+                                jt::mma_i8(tmem_base + g * kBN, dA + 2u * ks, dX + 2u * ks, idesc,
+                                           (kb | ks) != 0 ? 1u : 0u);
+                            if (kb == nk - 1) jt::mma_commit(&tfull[g]);
                         }
+                        jt::mma_commit(&empty[stage]);
                     }
-                    jt::mma_commit(&empty[stage]);
                     if (++stage == S) {
                         stage = 0;
                         phase ^= 1u;
                     }
+                    if (C::kMagic) ++sc;
                 }
+                if (!C::kMagic) ++sc;
             }
             if (!ok) {  // already-issued MMAs retire before TMEM is released
                 jt::mma_commit(&drain[m]);
@@ -541,8 +549,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
         // every accumulator slot starts free (the MMA issuers preset it)
         __syncwarp();
         if (lane == 0)
-            for (int b = 0; b < NS; ++b) jt::mbar_arrive(&tempty[b]);
-        uint32_t unit = 0, ts = 0, tphase = 0, ephase = 0;
+            for (int b = 0; b < NG; ++b) jt::mbar_arrive(&tempty[b]);
+        uint32_t sc = 0, ts = 0, tphase = 0, ephase = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
             if (!jt::mbar_wait(&pfull[ts], tphase, abort_flag, err)) {
@@ -552,7 +560,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
             const uint8_t *sl = slot_base + ts * C::kSlot;
             const int4 info = *reinterpret_cast<const int4 *>(sl);  // {e, row0, row_end, c0}
             const float4 *meta = reinterpret_cast<const float4 *>(sl + C::kOffMeta);
-            const __half *sc = reinterpret_cast<const __half *>(sl + C::kOffScale) +
+            const __half *sc_ptr = reinterpret_cast<const __half *>(sl + C::kOffScale) +
                                (C::kGateUp ? ((is_up ? ngroups * 64 : 0) + lch) : lr);
             const float *blk = reinterpret_cast<const float *>(sl + C::kOffBlk) + j0 * p.hs_ld;
             const int sc_stride = C::kGateUp ? 64 : 128;
@@ -563,24 +571,30 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
             float2 r2[kBH / 2];
 #pragma unroll
             for (int j = 0; j < kBH / 2; ++j) r2[j] = make_float2(0.0f, 0.0f);
-            const int nunits = C::kUnitK == 0 ? 1 : p.K / C::kUnitK;
-            for (int un = 0; un < nunits; ++un, ++unit) {
-                const uint32_t slot = unit % NS;
-                if (!jt::mbar_wait(&tfull[slot], (unit / NS) & 1u, abort_flag, err)) {
+            // one drain group per 128-K stage (two 64-K units) or per tile
+            const int npass = C::kMagic ? nk : 1;
+            for (int ps = 0; ps < npass; ++ps, ++sc) {
+                const uint32_t g = C::kMagic ? (sc & 1u) : (sc % NG);
+                const uint32_t gph = C::kMagic ? ((sc >> 1) & 1u) : ((sc / NG) & 1u);
+                if (!jt::mbar_wait(&tfull[g], gph, abort_flag, err)) {
                     ok = false;
                     break;
                 }
                 jt::tc_fence_after();
                 if (active) {
-                    const float s0 = C::kPacked ? __half2float(sc[un * sc_stride]) : 1.0f;
-                    uint32_t a[32];
-                    jt::tmem_ld32(tlane + slot * kBN, a);
-                    jt::tmem_wait_ld();
-                    fold_chunk<MODE>(r2, a, s0, blk, p.hs_ld, un);
+#pragma unroll 1
+                    for (int h = 0; h < (C::kMagic ? 2 : 1); ++h) {
+                        const int un = 2 * ps + h;  // 64-K group index (magic modes)
+                        const float s0 = C::kPacked ? __half2float(sc_ptr[un * sc_stride]) : 1.0f;
+                        uint32_t a[32];
+                        jt::tmem_ld32(tlane + (C::kMagic ? (2u * g + h) : g) * kBN, a);
+                        jt::tmem_wait_ld();
+                        fold_chunk<MODE>(r2, a, s0, blk, p.hs_ld, un);
+                    }
                 }
                 jt::tc_fence_before();
                 __syncwarp();
-                if (lane == 0) jt::mbar_arrive(&tempty[slot]);
+                if (lane == 0) jt::mbar_arrive(&tempty[g]);
             }
             if (!ok) break;
             if constexpr (C::kGateUp) {
@@ -615,8 +629,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
 #pragma unroll
                     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
                     if (__any_sync(0xffffffffu, bad) && lane == 0) atomicExch(err, JT_KERR_NONFINITE);
-                    const jt::QuantBlock qb = jt::quant_block(m);
-                    const int c0 = jt::quant_code(h0, qb), c1 = jt::quant_code(h1, qb);
+                    const jt::QuantBlockF qb = jt::quant_block_f(m);
+                    const int c0 = jt::quant_code_f(h0, qb), c1 = jt::quant_code_f(h1, qb);
                     const int row = info.y + j;
                     const uint16_t pair = (uint16_t)(uint8_t)(int8_t)c0 | ((uint16_t)(uint8_t)(int8_t)c1 << 8);
                     *reinterpret_cast<uint16_t *>(p.hq + (size_t)row * p.n_ch + info.w + 2 * lane) = pair;

@@ -56,4 +56,52 @@ __device__ __forceinline__ int quant_code(float x, const QuantBlock &b) {
     return q;
 }
 
+// Light form for the fused requantization of the expert GEMMs: the same
+// codes and stored scale with single-precision divisions.  For a finite
+// m > 0, (float)((double)m / 127) equals the correctly rounded float
+// quotient m / 127: the two can differ only when the double quotient lands
+// exactly on a float rounding midpoint, and since m has 24 significant bits
+// that happens only when m / 127 is itself that midpoint, where both round
+// to even.  The double scale is formed only on the rare near-tie path.
+struct QuantBlockF {
+    float maxabs;   // 0 for an all-zero block
+    float inv;      // 127 / maxabs, fast-path multiplier
+    float scale_f;  // stored scale (1.0f for a zero block)
+};
+
+__device__ __forceinline__ QuantBlockF quant_block_f(float maxabs) {
+    QuantBlockF b;
+    b.maxabs = maxabs;
+    if (maxabs == 0.0f) {
+        b.inv = 0.0f;
+        b.scale_f = 1.0f;
+    } else {
+        b.inv = __fdiv_rn(127.0f, maxabs);
+        b.scale_f = __fdiv_rn(maxabs, 127.0f);
+    }
+    return b;
+}
+
+static __device__ __noinline__ int quant_code_exact_m(float x, float maxabs) {
+    const double scale_d = __ddiv_rn((double)maxabs, 127.0);
+    return static_cast<int>(round(__ddiv_rn((double)x, scale_d)));
+}
+
+__device__ __forceinline__ int quant_code_f(float x, const QuantBlockF &b) {
+    if (b.maxabs == 0.0f) return 0;
+    const float y = __fmul_rn(x, b.inv);
+    const float ay = fabsf(y);
+    const float fr = __fsub_rn(ay, floorf(ay));
+    int q;
+    if (fabsf(__fsub_rn(fr, 0.5f)) > 1e-3f) {
+        q = static_cast<int>(floorf(__fadd_rn(ay, 0.5f)));
+        if (y < 0.0f) q = -q;
+    } else {
+        q = quant_code_exact_m(x, b.maxabs);
+    }
+    q = q > 127 ? 127 : q;
+    q = q < -127 ? -127 : q;
+    return q;
+}
+
 }  // namespace jt
