@@ -138,3 +138,26 @@ def test_moe_nan_logits_rejected():
     assert lib().jt_b200_sync() != 0  # kernel-reported routing fault surfaces as JT_ERR_CUDA
     assert lib().jt_b200_sync() == 0  # and is cleared
     plan.close()
+
+
+def test_moe_routing_matches_reference_golden():
+    """Routing and capacity sort of the GPU layer against fixtures produced
+    by the reference's jt_routing_topk / jt_moe_batch_sort
+    (tests/golden/make_golden.py); weights after renormalization against
+    the oracle's restatement of moe_layer.c:1171-1201 applied to them."""
+    import os
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "routing_sort.npz"))
+    T, E, k = int(g["T"]), int(g["E"]), int(g["k"])
+    dm = Dims(T, 128, 128, E, k, 0, 0, 1.25)
+    w = synth_weights(dm, seed=3)
+    x, _, _ = synth_inputs(dm, T, seed=4)
+    y_gpu, got = run_gpu(dm, w, x, np.ascontiguousarray(g["logits"]), np.ascontiguousarray(g["bias"]))
+    assert np.array_equal(got["ids"].reshape(T, k), g["ids"])
+    assert got["kept"] == int(g["kept_c125"])
+    assert np.array_equal(got["perm"], g["perm_c125"])
+    assert np.array_equal(got["off"], g["off_c125"])
+    assert np.array_equal(got["drop"], g["drop_c125"])
+    wr = np.ascontiguousarray(g["w"].reshape(-1).copy())
+    drop = np.ascontiguousarray(g["drop_c125"])
+    assert oracle.oracle().jto_renorm(wr.ctypes.data, drop.ctypes.data, T, k) == 0
+    assert np.array_equal(got["w"].view(np.uint32), wr.view(np.uint32))
