@@ -36,7 +36,14 @@ sys.path.insert(0, ROOT)
 CFG5 = dict(T=16384, d=2048, f=1536, E=1024, k=8, S=2, fs=4096, cap=1.5)
 CFG3 = dict(T=4096, d=2048, f=1024, E=256, k=8, S=2, fs=2048, cap=1.5)
 CFG2 = dict(T=1, d=1024, f=256, E=64, k=8, S=2, fs=512, cap=1.5)
+# 1/8 of config 5 (same rows per expert, same shapes per expert): the case the
+# profiler captures run on (`--small`), whose DRAM traffic scales by 8 to a
+# full config-5 launch.
+CFG5_SMALL = dict(T=2048, d=2048, f=1536, E=128, k=8, S=2, fs=4096, cap=1.5)
 METRIC = "MoE-layer tokens/s at 1/2/4/8 B200; W8A8 TOPS; decode HBM GB/s vs peak"
+# DRAM bytes (read + write) of one routed gate/up launch at config 5: the ncu
+# capture of `bench.py --small` (1/8 of config 5) gave 285.3 MB, scaled by 8.
+GU_TRAFFIC_BYTES = 8 * 285_306_880
 
 
 def peaks():
@@ -286,6 +293,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-parts", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--small", action="store_true",
+                    help="time only the MoE layer at 1/8 of config 5 (profiler captures)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -304,6 +313,11 @@ def main():
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     hbm_peak, peak_kind = peaks()
+    if args.small:
+        st = time_layer(torch, CFG5_SMALL, 0, 1, args.steps, args.warmup, seed=5)
+        print(json.dumps({"case": "cfg5/8", "ms_per_step": round(st["ms_per_step"], 4),
+                          "stage_ms": [round(v, 4) for v in st["stage_ms"]], "kept": st["kept"]}))
+        return
 
     with ClockSampler(local) as clk:
         st = time_layer(torch, CFG5, rank, world, args.steps, args.warmup, seed=5)
@@ -364,11 +378,13 @@ def main():
             "stage_ms": {n: round(v, 4) for n, v in zip(
                 ["route", "sort", "dispatch", "shared", "gateup", "down", "output"], stage)},
             "kept_pairs": kept,
-            "roofline": {"bound": "tensor", "kernel": "routed gate/up (k_moe_gemm GU_ROUTED)",
+            "roofline": {"bound": "tensor", "kernel": "routed gate/up (k_moe_gemm mode 0)",
                          "achieved": round(ops_gu / (gu_ms / 1e3) / 1e12, 2), "peak": 4500.0,
                          "unit": "TOPS", "frac": round(ops_gu / (gu_ms / 1e3) / 1e12 / 4500.0, 4),
-                         "peak_kind": "nominal dense int8 (no measured int8 peak in MEASURED_PEAKS)",
-                         "traffic": None},
+                         "peak_kind": "nominal dense int8 (MEASURED_PEAKS has no int8 entry)",
+                         "traffic": GU_TRAFFIC_BYTES,
+                         "traffic_note": "ncu dram read+write of one launch at 1/8 of config 5, x8 "
+                                         "(profiles/k_moe_gemm_routed_cfg5_small.md)"},
             "layer_TOPS": round((ops_gu + ops_dn + ops_sh) / (ms / 1e3) / 1e12, 1),
             "clocks": clocks, "hbm_peak_gbs": hbm_peak, "hbm_peak_kind": peak_kind,
             "parts": parts, "cpu_baseline": cpu,
