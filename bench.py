@@ -285,6 +285,47 @@ def part_w8a8(torch, steps=200):
     return res
 
 
+def part_gemv(torch, hbm_peak, steps=200, rot=4):
+    """Config 4: batch-1 low-bit GEMV over INT2 [49152][2048] + INT4
+    [16384][2048], group-64 fp16 scales; `rot` weight copies (185 MB > L2)
+    cycled so every call streams its weights from HBM."""
+    from jimotono_b200 import lib
+    L = lib()
+    K, n2, n4 = 2048, 49152, 16384
+    g = torch.Generator(device="cuda")
+    g.manual_seed(4)
+    stream = torch.cuda.current_stream().cuda_stream
+    a = torch.randint(-127, 128, (K,), dtype=torch.int8, device="cuda", generator=g)
+    y = torch.empty(n2 + n4, device="cuda")
+    copies = []
+    for _ in range(rot):
+        w2 = torch.randint(0, 256, (n2, K // 4), dtype=torch.uint8, device="cuda", generator=g)
+        w4 = torch.randint(0, 256, (n4, K // 2), dtype=torch.uint8, device="cuda", generator=g)
+        s2 = (torch.rand((n2, K // 64), device="cuda", generator=g) * 0.04 + 0.01).half()
+        s4 = (torch.rand((n4, K // 64), device="cuda", generator=g) * 0.04 + 0.01).half()
+        copies.append((w2, s2, w4, s4))
+
+    def call(i):
+        w2, s2, w4, s4 = copies[i % rot]
+        return L.jt_b200_lowbit_gemv(a.data_ptr(), 0.0123, w2.data_ptr(), s2.data_ptr(), n2,
+                                     w4.data_ptr(), s4.data_ptr(), n4, K, y.data_ptr(), stream)
+    for i in range(10):
+        assert call(i) == 0
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        call(i)
+    e1.record()
+    torch.cuda.synchronize()
+    assert L.jt_b200_sync() == 0
+    us = e0.elapsed_time(e1) / steps * 1e3
+    byts = n2 * (K // 4 + K // 32) + n4 * (K // 2 + K // 32) + K + 4 * (n2 + n4)
+    return {"us": round(us, 3), "bytes": byts, "GBs": round(byts / us / 1e3, 1),
+            "frac_hbm": round(byts / us / 1e3 / hbm_peak, 4),
+            "l2": f"{rot} rotating weight copies ({rot * byts / 1e6:.0f} MB > L2)"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -357,6 +398,7 @@ def main():
             "stage_us": [round(v * 1e3, 2) for v in st2["stage_ms"]], "l2": "8 rotating weight copies (172 MB > L2)"}
         del st2
         parts["cfg1_w8a8"] = part_w8a8(torch)
+        parts["cfg4_gemv"] = part_gemv(torch, hbm_peak)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         from oracle.cpu_baseline import cpu_baseline

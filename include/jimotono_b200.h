@@ -119,6 +119,20 @@ int jt_b200_w8a8_gemm_i32(const int8_t *X, int ldx, const int8_t *W, int ldw, in
 int jt_b200_w8a8_linear_noalloc(const float *x, int M, int K, const int8_t *W, int ldw,
                                 const float *sw, float *C, int ldc, int N, void *stream);
 
+/* Batch-1 low-bit GEMV, the decode replacement of the LUT path
+ * (jt_lowbit_gemm_lut, lowbit.h:52 / lowbit.c:158-267, and
+ * jt_tmac_lookup_accum, tmac.h:69 / tmac.c:387-506), on the packed
+ * group-64 format:
+ *   P[n][g] = sum_{k in group g} a[k] * c[n][k]   (int32, c = 2li - (2^b-1))
+ *   r = 0; for g ascending: r = fmaf((float)P[n][g], s[n][g], r); y[n] = r * sa
+ * y[0..n2) from INT2 rows w2 [n2][K/4], y[n2..n2+n4) from INT4 rows
+ * w4 [n4][K/2] (both little-endian along K), fp16 scales s2 [n2][K/64],
+ * s4 [n4][K/64].  a int8 [K]; K % 64 == 0, K <= 4096; w2, w4 16-byte
+ * aligned.  Device pointers, asynchronous on stream. */
+int jt_b200_lowbit_gemv(const int8_t *a, float sa, const uint8_t *w2, const uint16_t *s2, int n2,
+                        const uint8_t *w4, const uint16_t *s4, int n4, int K, float *y,
+                        void *stream);
+
 /* ---- quantized MoE layer (prepared weights) ----
  *
  * The layer of jt_moe_fwd_batch (moe_layer.c:980-1614; moe_layer.h:230-246)

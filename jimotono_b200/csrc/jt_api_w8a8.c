@@ -375,6 +375,20 @@ int jt_b200_w8a8_gemm_i32(const int8_t *X, int ldx, const int8_t *W, int ldw, in
                                     JTK_EPI_RAW_I32, (cudaStream_t)stream));
 }
 
+int jt_b200_lowbit_gemv(const int8_t *a, float sa, const uint8_t *w2, const uint16_t *s2, int n2,
+                        const uint8_t *w4, const uint16_t *s4, int n4, int K, float *y,
+                        void *stream) {
+    if (a == NULL || y == NULL || n2 < 0 || n4 < 0 || K <= 0 || K % 64 != 0 || K > 4096 ||
+        !isfinite(sa) || (n2 > 0 && (w2 == NULL || s2 == NULL)) ||
+        (n4 > 0 && (w4 == NULL || s4 == NULL)) || ((uintptr_t)w2 & 15u) != 0 ||
+        ((uintptr_t)w4 & 15u) != 0) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    if (n2 + n4 == 0) return JT_OK;
+    return map_launch(jtk_lowbit_gemv(a, sa, w2, s2, n2, w4, s4, n4, K, y, (cudaStream_t)stream));
+}
+
 int jt_b200_sync(void) {
     if (cudaDeviceSynchronize() != cudaSuccess) {
         errno = EIO;

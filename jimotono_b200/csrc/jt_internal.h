@@ -93,6 +93,12 @@ int jtk_moe_down_shared(const int8_t *wsd, const float *ssd, int d, int fs, cons
                         int T, const float *hs, const float4 *sh_meta, const int4 *tiles,
                         const int32_t *ntiles, float *y, int accumulate, cudaStream_t stream);
 
+/* Batch-1 low-bit GEMV (jt_gemv.cu): y[0..n2) from INT2 rows w2 [n2][K/4],
+ * y[n2..n2+n4) from INT4 rows w4 [n4][K/2]; fp16 scales s [rows][K/64]. */
+int jtk_lowbit_gemv(const int8_t *a, float sa, const uint8_t *w2, const uint16_t *s2, int n2,
+                    const uint8_t *w4, const uint16_t *s4, int n4, int K, float *y,
+                    cudaStream_t stream);
+
 /* Device error word shared by all kernels of the library (0 = clean). */
 int jtk_read_and_clear_error(int *out_code);
 int *jtk_error_word(void);
