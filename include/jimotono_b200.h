@@ -127,8 +127,12 @@ int jt_b200_w8a8_linear_noalloc(const float *x, int M, int K, const int8_t *W, i
  *   r = 0; for g ascending: r = fmaf((float)P[n][g], s[n][g], r); y[n] = r * sa
  * y[0..n2) from INT2 rows w2 [n2][K/4], y[n2..n2+n4) from INT4 rows
  * w4 [n4][K/2] (both little-endian along K), fp16 scales s2 [n2][K/64],
- * s4 [n4][K/64].  a int8 [K]; K % 64 == 0, K <= 4096; w2, w4 16-byte
- * aligned.  Device pointers, asynchronous on stream. */
+ * s4 [n4][K/64].  a int8 [K]; K % 64 == 0, K <= 4096; a, w2, w4 16-byte
+ * aligned.  Device pointers, asynchronous on stream.  The kernel starts
+ * streaming w2/w4/s2/s4 before the previous work of the stream has
+ * finished (programmatic dependent launch); a and y are ordered normally.
+ * The weight buffers must not be written by work still pending in the
+ * same stream. */
 int jt_b200_lowbit_gemv(const int8_t *a, float sa, const uint8_t *w2, const uint16_t *s2, int n2,
                         const uint8_t *w4, const uint16_t *s4, int n4, int K, float *y,
                         void *stream);

@@ -381,7 +381,7 @@ int jt_b200_lowbit_gemv(const int8_t *a, float sa, const uint8_t *w2, const uint
     if (a == NULL || y == NULL || n2 < 0 || n4 < 0 || K <= 0 || K % 64 != 0 || K > 4096 ||
         !isfinite(sa) || (n2 > 0 && (w2 == NULL || s2 == NULL)) ||
         (n4 > 0 && (w4 == NULL || s4 == NULL)) || ((uintptr_t)w2 & 15u) != 0 ||
-        ((uintptr_t)w4 & 15u) != 0) {
+        ((uintptr_t)w4 & 15u) != 0 || ((uintptr_t)a & 15u) != 0) {
         errno = EINVAL;
         return JT_ERR_INVAL;
     }
