@@ -221,6 +221,51 @@ enum {
 };
 int jt_b200_moe_debug_copy(jt_b200_moe_plan *plan, int what, void *host_dst, size_t bytes);
 
+/* ---- expert-parallel layer (one process per GPU, NCCL over NVLink) ----
+ *
+ * Rank r of N holds tokens [r*T, (r+1)*T) of the global batch (dims.T = T
+ * tokens per rank, the same on every rank) and routed experts
+ * [r*E/N, (r+1)*E/N) (dims.E = E, the global count; the weights passed to
+ * the forward hold only the rank's E/N experts); shared experts are
+ * replicated.  Routing, capacity and drop follow the reference over the
+ * whole batch: a pair of expert e is kept when fewer than cap pairs of e
+ * precede it in the global q = t*k + p order (moe_layer.c:931-970).
+ * Dispatch and combine are NCCL send/recv; each forward synchronizes its
+ * stream once (to size the exchange from the gathered expert counts).
+ * NCCL is loaded at run time (libnccl.so.2); without it the calls return
+ * JT_ERR_NOSUP. */
+typedef struct jt_b200_ep_comm jt_b200_ep_comm;
+typedef struct jt_b200_moe_ep_plan jt_b200_moe_ep_plan;
+/* 128-byte NCCL unique id, created on one rank and given to all. */
+int jt_b200_ep_unique_id(void *id128);
+/* Communicator of the current CUDA device (collective over the N ranks). */
+int jt_b200_ep_comm_create(const void *id128, int nranks, int rank, jt_b200_ep_comm **out);
+int jt_b200_ep_comm_destroy(jt_b200_ep_comm *comm);
+int jt_b200_moe_ep_plan_create(const jt_b200_moe_dims *dims, jt_b200_ep_comm *comm,
+                               jt_b200_moe_ep_plan **out);
+int jt_b200_moe_ep_plan_destroy(jt_b200_moe_ep_plan *plan);
+/* x [T][d], logits [T][E] of the local tokens; y [T][d] (fp32, or bf16). */
+int jt_b200_moe_ep_forward(jt_b200_moe_ep_plan *plan, const jt_b200_moe_weights *w, const float *x,
+                           const float *logits, const float *bias, void *y, int y_bf16,
+                           void *stream);
+/* Intermediates of the last forward (synchronizes): local JT_B200_DBG_IDS,
+ * _WEIGHTS, _DROP, _XQ, _XS, _PERM (kept local pairs in send order); _HQ
+ * the requantized SwiGLU rows of the owned experts (expert-contiguous);
+ * _META int32 [4] {kept local pairs, owned rows, owned token tiles, cap}. */
+int jt_b200_moe_ep_debug_copy(jt_b200_moe_ep_plan *plan, int what, void *host_dst, size_t bytes);
+/* cap = ceil(cap_factor * T_global * k / E) in double (moe_layer.c:931-943);
+ * -1 when out of range. */
+int jt_b200_ep_capacity(long long T_global, int k, int E, float cap_factor);
+/* Exchange layout of rank `rank` from the per-rank expert counts cnt [N][E]:
+ * gbase [E] pairs of each expert on lower ranks; send_cnt [N] rows to each
+ * owner; recv_cnt [N] rows from each source; own_off [E/N+1] and
+ * own_tile_off [E/N+1] row and token-tile offsets of the owned experts;
+ * gather [N][E/N][4] {first received row, first owned row, rows, 0}.  Host
+ * memory; used by the forward and exposed for tests. */
+int jt_b200_ep_layout(const int32_t *cnt, int N, int E, int rank, int cap, int32_t *gbase,
+                      int32_t *send_cnt, int32_t *recv_cnt, int32_t *own_off,
+                      int32_t *own_tile_off, int32_t *gather);
+
 /* Synchronize the current device and fold any kernel-reported fault into
  * the return code (JT_OK or JT_ERR_CUDA). */
 int jt_b200_sync(void);

@@ -38,6 +38,15 @@ PROTOTYPES = {
     "jt_b200_moe_debug_copy": (I, [P, I, P, SZ]),
     "jt_b200_moe_profile_begin": (I, [P, I]),
     "jt_b200_moe_profile_end": (I, [P, P, I, P]),
+    "jt_b200_ep_unique_id": (I, [P]),
+    "jt_b200_ep_comm_create": (I, [P, I, I, P]),
+    "jt_b200_ep_comm_destroy": (I, [P]),
+    "jt_b200_moe_ep_plan_create": (I, [P, P, P]),
+    "jt_b200_moe_ep_plan_destroy": (I, [P]),
+    "jt_b200_moe_ep_forward": (I, [P, P, P, P, P, P, I, P]),
+    "jt_b200_moe_ep_debug_copy": (I, [P, I, P, SZ]),
+    "jt_b200_ep_capacity": (I, [C.c_longlong, I, I, F]),
+    "jt_b200_ep_layout": (I, [P, I, I, I, I, P, P, P, P, P, P]),
     "jt_b200_sync": (I, []),
     "jt_b200_last_error": (C.c_char_p, []),
     "jt_b200_version": (C.c_char_p, []),

@@ -1,0 +1,434 @@
+/* jt_ep.c - expert-parallel MoE layer over NCCL (one process per GPU).
+ *
+ * Rank r of N holds tokens [r*T, (r+1)*T) of the global batch (T per rank,
+ * the same on every rank) and the routed experts [r*E/N, (r+1)*E/N); the
+ * shared experts are replicated.  One forward:
+ *
+ *   1. top-k routing of the local tokens (routing.c:16-76), local counts
+ *      per expert, NCCL all-gather of the counts;
+ *   2. the global capacity decision (moe_layer.c:931-970) from the gathered
+ *      counts (jt_ep_layout.c), local stable sort with the other ranks'
+ *      pairs as a per-expert base, drop + renormalization at the source
+ *      (moe_layer.c:1171-1201);
+ *   3. per-token int8 quantization; kept rows (codes + {scale, weight})
+ *      sent to the owners of their experts with NCCL send/recv;
+ *   4. on the owner: rows reordered into expert-contiguous order, routed
+ *      gate/up + SwiGLU + requant, down projection writing one weighted
+ *      fp32 row per received row;
+ *   5. rows sent back to their sources, added into the layer output, which
+ *      already holds the shared experts' contribution of the local tokens.
+ *
+ * The host learns the exchange sizes from the gathered counts (one
+ * device-to-host copy and stream synchronization per forward); everything
+ * else is stream-ordered.  No device-side remote loads, no multicast.
+ */
+#include <errno.h>
+#include <math.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <cuda_runtime_api.h>
+
+#include "../../include/jimotono_b200.h"
+#include "jt_internal.h"
+#include "jt_nccl.h"
+
+void jt_set_last_error(const char *what, int code);
+
+struct jt_b200_ep_comm {
+    jt_nccl_comm comm;
+    int nranks, rank, dev;
+};
+
+struct jt_b200_moe_ep_plan {
+    jt_b200_moe_dims dm; /* T = tokens per rank, E = global experts */
+    jt_b200_ep_comm *comm;
+    int El, R_max, cap;
+    void *arena;
+    size_t arena_bytes;
+    /* local routing and dispatch */
+    int32_t *ids, *perm, *pos, *hist, *off, *tile_off, *meta, *sh_ntiles;
+    int4 *tiles, *sh_tiles;
+    float4 *row_meta, *sh_meta;
+    float *w_raw, *w_fin, *xs, *hs_s, *y32;
+    uint8_t *drop;
+    int8_t *xq, *xd, *hq_s;
+    /* exchange */
+    int32_t *cnt, *cnt_all, *gbase, *own_off, *own_tile_off;
+    int4 *gather, *own_tiles;
+    int8_t *rcodes, *own_codes, *own_hq;
+    float4 *rmeta, *own_meta;
+    float *own_hs, *ret, *back;
+    /* host (pinned) */
+    int32_t *h_cnt_all, *h_gbase, *h_send, *h_recv, *h_own_off, *h_own_tile_off, *h_gather;
+};
+
+static size_t align_up(size_t v) { return (v + 255) & ~(size_t)255; }
+static int hs_ld(int n_ch) { return ((n_ch / 64) + 3) & ~3; }
+
+static int nccl_fail(const char *what, int r) {
+    const jt_nccl_api *nc = jt_nccl();
+    char buf[256];
+    snprintf(buf, sizeof buf, "%s: %s", what, nc ? nc->error_string(r) : "nccl unavailable");
+    jt_set_last_error(buf, 0);
+    errno = EIO;
+    return JT_ERR_CUDA;
+}
+
+int jt_b200_ep_unique_id(void *id128) {
+    const jt_nccl_api *nc = jt_nccl();
+    if (id128 == NULL) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    if (nc == NULL) {
+        jt_set_last_error("libnccl.so.2 not found", 0);
+        errno = ENOSYS;
+        return JT_ERR_NOSUP;
+    }
+    jt_nccl_id id;
+    const int r = nc->get_unique_id(&id);
+    if (r != 0) return nccl_fail("ncclGetUniqueId", r);
+    memcpy(id128, &id, sizeof id);
+    return JT_OK;
+}
+
+int jt_b200_ep_comm_create(const void *id128, int nranks, int rank, jt_b200_ep_comm **out) {
+    if (id128 == NULL || out == NULL || nranks <= 0 || rank < 0 || rank >= nranks) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    const jt_nccl_api *nc = jt_nccl();
+    if (nc == NULL) {
+        jt_set_last_error("libnccl.so.2 not found", 0);
+        errno = ENOSYS;
+        return JT_ERR_NOSUP;
+    }
+    jt_b200_ep_comm *c = (jt_b200_ep_comm *)calloc(1, sizeof *c);
+    if (c == NULL) {
+        errno = ENOMEM;
+        return JT_ERR_NOMEM;
+    }
+    jt_nccl_id id;
+    memcpy(&id, id128, sizeof id);
+    if (cudaGetDevice(&c->dev) != cudaSuccess) {
+        free(c);
+        errno = EIO;
+        return JT_ERR_CUDA;
+    }
+    const int r = nc->comm_init_rank(&c->comm, nranks, id, rank);
+    if (r != 0) {
+        free(c);
+        return nccl_fail("ncclCommInitRank", r);
+    }
+    c->nranks = nranks;
+    c->rank = rank;
+    *out = c;
+    return JT_OK;
+}
+
+int jt_b200_ep_comm_destroy(jt_b200_ep_comm *c) {
+    if (c == NULL) return JT_OK;
+    const jt_nccl_api *nc = jt_nccl();
+    if (nc && c->comm) nc->comm_destroy(c->comm);
+    free(c);
+    return JT_OK;
+}
+
+int jt_b200_moe_ep_plan_create(const jt_b200_moe_dims *dims, jt_b200_ep_comm *comm,
+                               jt_b200_moe_ep_plan **out) {
+    if (dims == NULL || comm == NULL || out == NULL) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    const int N = comm->nranks;
+    if (dims->T <= 0 || dims->d <= 0 || dims->d % 128 || dims->f <= 0 || dims->f % 128 ||
+        dims->E <= 0 || dims->E > 4096 || dims->E % N || dims->k <= 0 || dims->k > dims->E ||
+        dims->k > 64 || dims->S < 0 || dims->S > 8 || (dims->S > 0 && (dims->fs <= 0 || dims->fs % 128)) ||
+        !(dims->cap_factor >= 1.0f && dims->cap_factor <= 1.5f)) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    jt_b200_moe_ep_plan *p = (jt_b200_moe_ep_plan *)calloc(1, sizeof *p);
+    if (p == NULL) {
+        errno = ENOMEM;
+        return JT_ERR_NOMEM;
+    }
+    p->dm = *dims;
+    p->comm = comm;
+    p->El = dims->E / N;
+    const long long Tg = (long long)dims->T * N;
+    p->cap = jt_b200_ep_capacity(Tg, dims->k, dims->E, dims->cap_factor);
+    if (p->cap <= 0) {
+        free(p);
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    long long rmax = (long long)p->El * p->cap;
+    if (rmax > Tg * dims->k) rmax = Tg * dims->k;
+    p->R_max = (int)rmax;
+    const size_t T = (size_t)dims->T, k = (size_t)dims->k, E = (size_t)dims->E, El = (size_t)p->El;
+    const size_t d = (size_t)dims->d, f = (size_t)dims->f, R = (size_t)p->R_max;
+    const size_t fs = dims->S > 0 ? (size_t)dims->fs : 64;
+    const size_t Tk = T * k, nch = (size_t)jtk_sort_chunks(dims->T), Nn = (size_t)N;
+    struct {
+        void **dst;
+        size_t bytes;
+    } parts[] = {
+        {(void **)&p->ids, Tk * 4},          {(void **)&p->perm, Tk * 4},
+        {(void **)&p->pos, Tk * 4},          {(void **)&p->hist, nch * E * 4},
+        {(void **)&p->off, (E + 1) * 4},     {(void **)&p->tile_off, (E + 1) * 4},
+        {(void **)&p->meta, 64},             {(void **)&p->sh_ntiles, 64},
+        {(void **)&p->tiles, (Tk / JT_TILE_ROWS + E + 1) * 16},
+        {(void **)&p->sh_tiles, (T / JT_TILE_ROWS + 1) * 16},
+        {(void **)&p->row_meta, Tk * 16},    {(void **)&p->sh_meta, T * 16},
+        {(void **)&p->w_raw, Tk * 4},        {(void **)&p->w_fin, Tk * 4},
+        {(void **)&p->xs, T * 4},            {(void **)&p->hs_s, T * (size_t)hs_ld((int)fs) * 4},
+        {(void **)&p->y32, T * d * 4},       {(void **)&p->drop, Tk},
+        {(void **)&p->xq, T * d},            {(void **)&p->xd, Tk * d},
+        {(void **)&p->hq_s, T * fs},
+        {(void **)&p->cnt, E * 4},           {(void **)&p->cnt_all, Nn * E * 4},
+        {(void **)&p->gbase, E * 4},         {(void **)&p->own_off, (El + 1) * 4},
+        {(void **)&p->own_tile_off, (El + 1) * 4},
+        {(void **)&p->gather, Nn * El * 16}, {(void **)&p->own_tiles, (R / JT_TILE_ROWS + El + 1) * 16},
+        {(void **)&p->rcodes, R * d},        {(void **)&p->own_codes, R * d},
+        {(void **)&p->own_hq, R * f},        {(void **)&p->rmeta, R * 16},
+        {(void **)&p->own_meta, R * 16},     {(void **)&p->own_hs, R * (size_t)hs_ld((int)f) * 4},
+        {(void **)&p->ret, R * d * 4},       {(void **)&p->back, Tk * d * 4},
+    };
+    const size_t nparts = sizeof(parts) / sizeof(parts[0]);
+    size_t total = 0;
+    for (size_t i = 0; i < nparts; i++) total += align_up(parts[i].bytes);
+    if (cudaMalloc(&p->arena, total) != cudaSuccess) {
+        cudaGetLastError();
+        free(p);
+        errno = ENOMEM;
+        return JT_ERR_NOMEM;
+    }
+    /* zero once: rows past the kept counts are read by full token tiles */
+    if (cudaMemset(p->arena, 0, total) != cudaSuccess) {
+        cudaFree(p->arena);
+        free(p);
+        errno = EIO;
+        return JT_ERR_CUDA;
+    }
+    p->arena_bytes = total;
+    size_t offb = 0;
+    for (size_t i = 0; i < nparts; i++) {
+        *parts[i].dst = (char *)p->arena + offb;
+        offb += align_up(parts[i].bytes);
+    }
+    const size_t hbytes = (Nn * E + E + 2 * Nn + 2 * (El + 1) + Nn * El * 4) * sizeof(int32_t);
+    int32_t *h = NULL;
+    if (cudaMallocHost((void **)&h, hbytes) != cudaSuccess) {
+        cudaFree(p->arena);
+        free(p);
+        errno = ENOMEM;
+        return JT_ERR_NOMEM;
+    }
+    p->h_cnt_all = h;
+    p->h_gbase = p->h_cnt_all + Nn * E;
+    p->h_send = p->h_gbase + E;
+    p->h_recv = p->h_send + Nn;
+    p->h_own_off = p->h_recv + Nn;
+    p->h_own_tile_off = p->h_own_off + El + 1;
+    p->h_gather = p->h_own_tile_off + El + 1;
+    *out = p;
+    return JT_OK;
+}
+
+int jt_b200_moe_ep_plan_destroy(jt_b200_moe_ep_plan *p) {
+    if (p == NULL) return JT_OK;
+    cudaFree(p->arena);
+    cudaFreeHost(p->h_cnt_all);
+    free(p);
+    return JT_OK;
+}
+
+#define LAUNCH(expr)                                                          \
+    do {                                                                      \
+        int _r = (expr);                                                      \
+        if (_r != 0) {                                                        \
+            jt_set_last_error(#expr, _r);                                     \
+            errno = _r == -1 ? EINVAL : EIO;                                  \
+            return _r == -1 ? JT_ERR_INVAL : JT_ERR_CUDA;                     \
+        }                                                                     \
+    } while (0)
+
+#define CUDA(expr)                                                            \
+    do {                                                                      \
+        if ((expr) != cudaSuccess) {                                          \
+            jt_set_last_error(#expr, -4);                                     \
+            errno = EIO;                                                      \
+            return JT_ERR_CUDA;                                               \
+        }                                                                     \
+    } while (0)
+
+#define NCCL(expr)                                                            \
+    do {                                                                      \
+        int _r = (expr);                                                      \
+        if (_r != 0) return nccl_fail(#expr, _r);                             \
+    } while (0)
+
+int jt_b200_moe_ep_forward(jt_b200_moe_ep_plan *p, const jt_b200_moe_weights *w, const float *x,
+                           const float *logits, const float *bias, void *y, int y_bf16,
+                           void *stream) {
+    if (p == NULL || w == NULL || x == NULL || logits == NULL || y == NULL) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    const jt_nccl_api *nc = jt_nccl();
+    if (nc == NULL) {
+        errno = ENOSYS;
+        return JT_ERR_NOSUP;
+    }
+    const jt_b200_moe_dims *dm = &p->dm;
+    const int T = dm->T, k = dm->k, E = dm->E, d = dm->d, f = dm->f, S = dm->S, fs = dm->fs;
+    const int N = p->comm->nranks, rank = p->comm->rank, El = p->El;
+    if (!w->wg || !w->wu || !w->sg || !w->su || !w->wd || !w->sd ||
+        (S > 0 && (!w->wsg || !w->wsu || !w->ssg || !w->ssu || !w->wsd || !w->ssd))) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    cudaStream_t st = (cudaStream_t)stream;
+    jt_nccl_comm comm = p->comm->comm;
+    float *yf = y_bf16 ? p->y32 : (float *)y;
+
+    /* 1. routing and the global expert counts */
+    LAUNCH(jtk_route_topk(logits, bias, T, E, k, p->ids, p->w_raw, st));
+    LAUNCH(jtk_ep_count(p->ids, T * k, E, p->cnt, st));
+    NCCL(nc->all_gather(p->cnt, p->cnt_all, (size_t)E, JT_NCCL_INT32, comm, st));
+    CUDA(cudaMemcpyAsync(p->h_cnt_all, p->cnt_all, (size_t)N * E * sizeof(int32_t),
+                         cudaMemcpyDeviceToHost, st));
+    CUDA(cudaStreamSynchronize(st));
+
+    /* 2. global capacity decision, exchange layout */
+    if (jt_b200_ep_layout(p->h_cnt_all, N, E, rank, p->cap, p->h_gbase, p->h_send, p->h_recv,
+                          p->h_own_off, p->h_own_tile_off, p->h_gather) != JT_OK)
+        return JT_ERR_INVAL;
+    CUDA(cudaMemcpyAsync(p->gbase, p->h_gbase, (size_t)E * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    CUDA(cudaMemcpyAsync(p->own_off, p->h_own_off, (size_t)(El + 1) * sizeof(int32_t),
+                         cudaMemcpyHostToDevice, st));
+    CUDA(cudaMemcpyAsync(p->own_tile_off, p->h_own_tile_off, (size_t)(El + 1) * sizeof(int32_t),
+                         cudaMemcpyHostToDevice, st));
+    CUDA(cudaMemcpyAsync(p->gather, p->h_gather, (size_t)N * El * 4 * sizeof(int32_t),
+                         cudaMemcpyHostToDevice, st));
+    LAUNCH(jtk_moe_sort(p->ids, p->w_raw, T, k, E, p->cap, p->gbase, p->hist, p->off, p->tile_off,
+                        p->tiles, p->meta, p->perm, p->pos, p->drop, p->w_fin, st));
+
+    /* 3. quantization (xd/row_meta are the send rows, in expert order) */
+    LAUNCH(jtk_quant_dispatch(x, T, d, k, p->pos, p->w_fin, p->xq, p->xs, p->xd, p->row_meta,
+                              S > 0 ? p->sh_meta : NULL, st));
+    if (S > 0) {
+        LAUNCH(jtk_fill_single_tiles(p->sh_tiles, p->sh_ntiles, T, st));
+        for (int s = 0; s < S; s++) {
+            LAUNCH(jtk_moe_gateup_shared(w->wsg + (size_t)s * fs * d, w->wsu + (size_t)s * fs * d,
+                                         w->ssg + (size_t)s * fs, w->ssu + (size_t)s * fs, fs, d,
+                                         p->xq, T, p->sh_meta, p->sh_tiles, p->sh_ntiles, p->hq_s,
+                                         p->hs_s, st));
+            LAUNCH(jtk_moe_down_shared(w->wsd + (size_t)s * d * fs, w->ssd + (size_t)s * d, d, fs,
+                                       p->hq_s, T, p->hs_s, p->sh_meta, p->sh_tiles, p->sh_ntiles,
+                                       yf, s > 0, st));
+        }
+    } else {
+        CUDA(cudaMemsetAsync(yf, 0, (size_t)T * d * sizeof(float), st));
+    }
+
+    /* dispatch: rows to their experts' owners */
+    long long soff[64 + 1], roff[64 + 1];
+    if (N > 64) return JT_ERR_INVAL;
+    soff[0] = roff[0] = 0;
+    for (int i = 0; i < N; i++) {
+        soff[i + 1] = soff[i] + p->h_send[i];
+        roff[i + 1] = roff[i] + p->h_recv[i];
+    }
+    if (roff[N] > p->R_max) {
+        jt_set_last_error("expert-parallel receive rows exceed the plan capacity", 0);
+        errno = ERANGE;
+        return JT_ERR_INVAL;
+    }
+    NCCL(nc->group_start());
+    for (int o = 0; o < N; o++) {
+        if (p->h_send[o]) {
+            NCCL(nc->send(p->xd + (size_t)soff[o] * d, (size_t)p->h_send[o] * d, JT_NCCL_INT8, o, comm, st));
+            NCCL(nc->send(p->row_meta + soff[o], (size_t)p->h_send[o] * 4, JT_NCCL_FLOAT32, o, comm, st));
+        }
+        if (p->h_recv[o]) {
+            NCCL(nc->recv(p->rcodes + (size_t)roff[o] * d, (size_t)p->h_recv[o] * d, JT_NCCL_INT8, o, comm, st));
+            NCCL(nc->recv(p->rmeta + roff[o], (size_t)p->h_recv[o] * 4, JT_NCCL_FLOAT32, o, comm, st));
+        }
+    }
+    NCCL(nc->group_end());
+
+    /* 4. owned experts */
+    const int own_rows = p->h_own_off[El];
+    const int own_tiles = p->h_own_tile_off[El];
+    if (own_rows > 0) {
+        LAUNCH(jtk_ep_gather(p->gather, N * El, p->rcodes, p->rmeta, d, p->own_codes, p->own_meta, st));
+        LAUNCH(jtk_build_tiles(p->own_off, p->own_tile_off, El, p->own_tiles, st));
+        const int gu_hint = own_tiles * (f / 64), dn_hint = own_tiles * (d / 128);
+        LAUNCH(jtk_moe_gateup_routed(w->wg, w->wu, w->sg, w->su, El, f, d, p->own_codes, p->R_max,
+                                     p->own_meta, p->own_tiles, p->own_tile_off + El, p->own_hq,
+                                     p->own_hs, gu_hint, st));
+        LAUNCH(jtk_moe_down_routed(w->wd, w->sd, El, d, f, p->own_hq, p->R_max, p->own_hs,
+                                   p->own_meta, p->own_tiles, p->own_tile_off + El, p->ret, 0,
+                                   dn_hint, st));
+    }
+
+    /* 5. combine: rows back to their sources, added into y */
+    NCCL(nc->group_start());
+    for (int o = 0; o < N; o++) {
+        if (p->h_recv[o])
+            NCCL(nc->send(p->ret + (size_t)roff[o] * d, (size_t)p->h_recv[o] * d, JT_NCCL_FLOAT32, o, comm, st));
+        if (p->h_send[o])
+            NCCL(nc->recv(p->back + (size_t)soff[o] * d, (size_t)p->h_send[o] * d, JT_NCCL_FLOAT32, o, comm, st));
+    }
+    NCCL(nc->group_end());
+    LAUNCH(jtk_ep_combine(p->perm, (int)soff[N], k, p->back, d, yf, st));
+    if (y_bf16) LAUNCH(jtk_f32_to_bf16(yf, (uint16_t *)y, (size_t)T * d, st));
+    return JT_OK;
+}
+
+int jt_b200_moe_ep_debug_copy(jt_b200_moe_ep_plan *p, int what, void *host_dst, size_t bytes) {
+    if (p == NULL || host_dst == NULL) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    const size_t Tk = (size_t)p->dm.T * p->dm.k;
+    const void *src = NULL;
+    size_t have = 0;
+    switch (what) {
+    case JT_B200_DBG_IDS: src = p->ids; have = Tk * 4; break;
+    case JT_B200_DBG_WEIGHTS: src = p->w_fin; have = Tk * 4; break;
+    case JT_B200_DBG_DROP: src = p->drop; have = Tk; break;
+    case JT_B200_DBG_XQ: src = p->xq; have = (size_t)p->dm.T * p->dm.d; break;
+    case JT_B200_DBG_XS: src = p->xs; have = (size_t)p->dm.T * 4; break;
+    case JT_B200_DBG_PERM: src = p->perm; have = Tk * 4; break;
+    case JT_B200_DBG_HQ: src = p->own_hq; have = (size_t)p->R_max * p->dm.f; break;
+    case JT_B200_DBG_META: {
+        /* kept local pairs, owned rows, owned token tiles, capacity */
+        int32_t m[4] = {0, 0, 0, p->cap};
+        for (int i = 0; i < p->comm->nranks; i++) m[0] += p->h_send[i];
+        m[1] = p->h_own_off[p->El];
+        m[2] = p->h_own_tile_off[p->El];
+        if (bytes > sizeof m) {
+            errno = EINVAL;
+            return JT_ERR_INVAL;
+        }
+        memcpy(host_dst, m, bytes);
+        return JT_OK;
+    }
+    default: errno = EINVAL; return JT_ERR_INVAL;
+    }
+    if (bytes > have) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    if (cudaMemcpy(host_dst, src, bytes, cudaMemcpyDeviceToHost) != cudaSuccess) {
+        errno = EIO;
+        return JT_ERR_CUDA;
+    }
+    return JT_OK;
+}

@@ -65,9 +65,25 @@ int jtk_sort_chunks(int T);
 /* Capacity sort.  tile_off [E+1]: JT_TILE_ROWS-row token tiles per expert (scan);
  * tiles: table of {expert, row0, row_end, 0} per token tile; meta[0] kept,
  * meta[1] token tiles (= tile_off[E]), meta[2] max kept per expert. */
+/* gbase [E] (may be NULL): pairs of each expert that precede this token
+ * range in the global q order (expert-parallel ranks); capacity left for
+ * expert e is cap - gbase[e]. */
 int jtk_moe_sort(const int32_t *ids, const float *w_in, int T, int k, int E, int cap,
+                 const int32_t *gbase,
                  int32_t *hist, int32_t *off, int32_t *tile_off, int4 *tiles, int32_t *meta,
                  int32_t *perm, int32_t *pos, uint8_t *drop, float *w_out, cudaStream_t stream);
+/* Token-tile table from per-expert row offsets off [E+1] and tile offsets
+ * tile_off [E+1] (one CTA list entry {e, row0, row_end, 0} per tile). */
+int jtk_build_tiles(const int32_t *off, const int32_t *tile_off, int E, int4 *tiles,
+                    cudaStream_t stream);
+
+/* Expert-parallel exchange kernels (jt_ep.cu). */
+int jtk_ep_count(const int32_t *ids, int n, int E, int32_t *cnt, cudaStream_t stream);
+int jtk_ep_gather(const int4 *ent, int n_ent, const int8_t *src_codes, const float4 *src_meta,
+                  int d, int8_t *dst_codes, float4 *dst_meta, cudaStream_t stream);
+int jtk_ep_combine(const int32_t *perm, int kept, int k, const float *back, int d, float *y,
+                   cudaStream_t stream);
+
 /* Per-token quantization + dispatch; row_meta[row] = {scale, weight, token bits, 0}
  * for every kept row, sh_meta[t] = {scale, 1, t bits, 0} (may be NULL). */
 int jtk_quant_dispatch(const float *x, int T, int d, int k, const int32_t *pos,
@@ -82,9 +98,12 @@ int jtk_moe_gateup_routed(const uint8_t *wg, const uint8_t *wu, const void *gs, 
                           int E, int f, int d, const int8_t *xd, int rows_cap,
                           const float4 *row_meta, const int4 *tiles, const int32_t *ntiles,
                           int8_t *hq, float *hs, int max_tiles_hint, cudaStream_t stream);
+/* y_accumulate 1: y[token][:] += w * row (combine into the layer output);
+ * 0: y[row_meta.z][:] = w * row (one output row per routed row). */
 int jtk_moe_down_routed(const uint8_t *wd, const void *ds, int E, int d, int f, const int8_t *hq,
                         int rows_cap, const float *hs, const float4 *row_meta, const int4 *tiles,
-                        const int32_t *ntiles, float *y, int max_tiles_hint, cudaStream_t stream);
+                        const int32_t *ntiles, float *y, int y_accumulate, int max_tiles_hint,
+                        cudaStream_t stream);
 int jtk_moe_gateup_shared(const int8_t *wsg, const int8_t *wsu, const float *ssg,
                           const float *ssu, int fs, int d, const int8_t *xq, int T,
                           const float4 *sh_meta, const int4 *tiles, const int32_t *ntiles,

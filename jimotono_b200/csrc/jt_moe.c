@@ -256,7 +256,7 @@ int jt_b200_moe_forward(jt_b200_moe_plan *plan, const jt_b200_moe_weights *w, co
     MARK(JT_B200_STAGE_ROUTE);
     LAUNCH(jtk_route_topk(logits, bias, T, E, k, plan->ids, plan->w_raw, st));
     MARK(JT_B200_STAGE_SORT);
-    LAUNCH(jtk_moe_sort(plan->ids, plan->w_raw, T, k, E, cap, plan->hist, plan->off,
+    LAUNCH(jtk_moe_sort(plan->ids, plan->w_raw, T, k, E, cap, NULL, plan->hist, plan->off,
                         plan->tile_off, plan->tiles, plan->meta, plan->perm, plan->pos, plan->drop,
                         plan->w_fin, st));
     MARK(JT_B200_STAGE_DISPATCH);
@@ -295,7 +295,8 @@ int jt_b200_moe_forward(jt_b200_moe_plan *plan, const jt_b200_moe_weights *w, co
                                  plan->hs, gu_hint, st));
     MARK(JT_B200_STAGE_DOWN);
     LAUNCH(jtk_moe_down_routed(w->wd, w->sd, E, d, f, plan->hq, rows_cap, plan->hs,
-                               plan->row_meta, plan->tiles, plan->tile_off + E, yf, dn_hint, st));
+                               plan->row_meta, plan->tiles, plan->tile_off + E, yf, 1, dn_hint,
+                               st));
     MARK(JT_B200_STAGE_OUTPUT);
     if (y_bf16) LAUNCH(jtk_f32_to_bf16(yf, (uint16_t *)y, (size_t)T * d, st));
     MARK(JT_B200_MOE_NSTAGE);

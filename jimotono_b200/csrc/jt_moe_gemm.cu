@@ -735,8 +735,8 @@ extern "C" int jtk_moe_gateup_routed(const uint8_t *wg, const uint8_t *wu, const
 extern "C" int jtk_moe_down_routed(const uint8_t *wd, const void *ds, int E, int d, int f,
                                    const int8_t *hq, int rows_cap, const float *hs,
                                    const float4 *row_meta, const int4 *tiles,
-                                   const int32_t *ntiles, float *y, int max_tiles_hint,
-                                   cudaStream_t stream) {
+                                   const int32_t *ntiles, float *y, int y_accumulate,
+                                   int max_tiles_hint, cudaStream_t stream) {
     if (d % kBM || f % kBK || f / 64 > kMaxGroups || E <= 0 || rows_cap <= 0) return -1;
     MoeGemmParams p{};
     const uint32_t prow = f / 2, G = f / 64;
@@ -755,7 +755,7 @@ extern "C" int jtk_moe_down_routed(const uint8_t *wd, const void *ds, int E, int
     p.K = f;
     p.hs_ld = hs_ld;
     p.y = y;
-    p.y_accumulate = 1;
+    p.y_accumulate = y_accumulate;
     return launch<DN_ROUTED>(p, max_tiles_hint, stream);
 }
 

@@ -135,6 +135,7 @@ __global__ void k_sort_count(const int32_t *__restrict__ ids, int T, int k, int 
 // of ceil(kept/JT_TILE_ROWS) (token tiles of the expert GEMMs).
 // meta[0] = kept total, meta[1] = total token tiles, meta[2] = max kept.
 __global__ void k_sort_scan(int32_t *__restrict__ hist_base, int nchunks, int E, int cap,
+                            const int32_t *__restrict__ gbase,
                             int32_t *__restrict__ off, int32_t *__restrict__ tile_off,
                             int32_t *__restrict__ meta) {
     extern __shared__ int32_t sm[];  // 2 * blockDim.x
@@ -152,7 +153,10 @@ __global__ void k_sort_scan(int32_t *__restrict__ hist_base, int nchunks, int E,
                 hist_base[(size_t)c * E + e] = run;  // becomes base[c][e]
                 run += h;
             }
-            kc = run < cap ? run : cap;
+            // gbase[e]: pairs of expert e ahead of this token range (other
+            // ranks of an expert-parallel layer); they take capacity first
+            const int cap_e = gbase ? max(cap - gbase[e], 0) : cap;
+            kc = run < cap_e ? run : cap_e;
         }
         kept_local[j] = kc;
         ks += kc;
@@ -218,7 +222,7 @@ __global__ void k_build_tiles(const int32_t *__restrict__ off, const int32_t *__
 // sequential scan of moe_layer.c:955-970.  Then renormalization of the
 // chunk's tokens (moe_layer.c:1171-1201) with the final weights in wout.
 __global__ void k_sort_scatter(const int32_t *__restrict__ ids, const float *__restrict__ win,
-                               int T, int k, int E, int cap,
+                               int T, int k, int E, int cap, const int32_t *__restrict__ gbase,
                                const int32_t *__restrict__ base, const int32_t *__restrict__ off,
                                int32_t *__restrict__ perm, int32_t *__restrict__ pos,
                                uint8_t *__restrict__ drop, float *__restrict__ wout, int *err) {
@@ -249,7 +253,7 @@ __global__ void k_sort_scatter(const int32_t *__restrict__ ids, const float *__r
         __syncwarp();
         if (valid) {
             const int g = base[(size_t)c * E + e] + rank;
-            if (g < cap) {
+            if (g < (gbase ? max(cap - gbase[e], 0) : cap)) {
                 const int p = off[e] + g;
                 perm[p] = q;
                 pos[q] = p;
@@ -372,6 +376,7 @@ extern "C" int jtk_route_topk(const float *logits, const float *bias, int T, int
 extern "C" int jtk_sort_chunks(int T) { return (T + kChunkTok - 1) / kChunkTok; }
 
 extern "C" int jtk_moe_sort(const int32_t *ids, const float *w_in, int T, int k, int E, int cap,
+                            const int32_t *gbase,
                             int32_t *hist, int32_t *off, int32_t *tile_off, int4 *tiles,
                             int32_t *meta, int32_t *perm, int32_t *pos, uint8_t *drop,
                             float *w_out, cudaStream_t stream) {
@@ -381,11 +386,18 @@ extern "C" int jtk_moe_sort(const int32_t *ids, const float *w_in, int T, int k,
     k_sort_count<<<nch, 256, (size_t)E * sizeof(int32_t), stream>>>(ids, T, k, E, hist, err);
     int nt = 1024;
     while (nt / 2 >= E && nt > 32) nt /= 2;
-    k_sort_scan<<<1, nt, 2 * nt * sizeof(int32_t), stream>>>(hist, nch, E, cap, off, tile_off,
+    k_sort_scan<<<1, nt, 2 * nt * sizeof(int32_t), stream>>>(hist, nch, E, cap, gbase, off, tile_off,
                                                              meta);
     k_build_tiles<<<(E + 255) / 256, 256, 0, stream>>>(off, tile_off, E, tiles);
     k_sort_scatter<<<nch, 32, (size_t)E * sizeof(int32_t), stream>>>(
-        ids, w_in, T, k, E, cap, hist, off, perm, pos, drop, w_out, err);
+        ids, w_in, T, k, E, cap, gbase, hist, off, perm, pos, drop, w_out, err);
+    return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
+extern "C" int jtk_build_tiles(const int32_t *off, const int32_t *tile_off, int E, int4 *tiles,
+                               cudaStream_t stream) {
+    if (E <= 0) return -1;
+    k_build_tiles<<<(E + 255) / 256, 256, 0, stream>>>(off, tile_off, E, tiles);
     return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 

@@ -118,3 +118,73 @@ class Plan:
             self.close()
         except Exception:
             pass
+
+
+# ---------------------------------------------------------------- expert parallel
+class EpComm:
+    """NCCL communicator of the current CUDA device over `nranks` processes.
+    `uid` is the 128-byte id from `EpComm.unique_id()` on one rank."""
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = C.create_string_buffer(128)
+        check(lib().jt_b200_ep_unique_id(buf), "jt_b200_ep_unique_id")
+        return buf.raw
+
+    def __init__(self, uid: bytes, nranks: int, rank: int):
+        assert len(uid) == 128
+        self._uid = C.create_string_buffer(uid, 128)
+        self.handle = C.c_void_p()
+        self.nranks, self.rank = nranks, rank
+        check(lib().jt_b200_ep_comm_create(self._uid, nranks, rank, C.byref(self.handle)),
+              "jt_b200_ep_comm_create")
+
+    def close(self) -> None:
+        if self.handle:
+            lib().jt_b200_ep_comm_destroy(self.handle)
+            self.handle = C.c_void_p()
+
+
+class EpPlan:
+    """Expert-parallel layer plan: dm.T tokens per rank, dm.E global experts,
+    weights of the rank's dm.E / nranks experts."""
+
+    def __init__(self, dm: Dims, comm: EpComm):
+        self.dm = dm
+        self.comm = comm
+        self._c = dm.c()
+        self.handle = C.c_void_p()
+        check(lib().jt_b200_moe_ep_plan_create(C.byref(self._c), comm.handle, C.byref(self.handle)),
+              "jt_b200_moe_ep_plan_create")
+
+    def forward(self, wptrs: MoeWeights, x_ptr: int, logits_ptr: int, bias_ptr, y_ptr: int,
+                y_bf16: bool, stream: int) -> None:
+        check(lib().jt_b200_moe_ep_forward(self.handle, C.byref(wptrs), x_ptr, logits_ptr, bias_ptr,
+                                           y_ptr, int(y_bf16), stream), "jt_b200_moe_ep_forward")
+
+    def debug(self, what: int, dtype, count: int) -> np.ndarray:
+        out = np.empty(count, dtype=dtype)
+        if count:
+            check(lib().jt_b200_moe_ep_debug_copy(self.handle, what, out.ctypes.data, out.nbytes),
+                  "jt_b200_moe_ep_debug_copy")
+        return out
+
+    def close(self) -> None:
+        if self.handle:
+            lib().jt_b200_moe_ep_plan_destroy(self.handle)
+            self.handle = C.c_void_p()
+
+
+def ep_layout(cnt: np.ndarray, rank: int, cap: int) -> dict:
+    """Host exchange layout of `rank` from the gathered counts cnt [N][E]."""
+    N, E = cnt.shape
+    El = E // N
+    cnt = np.ascontiguousarray(cnt, np.int32)
+    out = {"gbase": np.zeros(E, np.int32), "send": np.zeros(N, np.int32),
+           "recv": np.zeros(N, np.int32), "own_off": np.zeros(El + 1, np.int32),
+           "own_tile_off": np.zeros(El + 1, np.int32), "gather": np.zeros((N, El, 4), np.int32)}
+    check(lib().jt_b200_ep_layout(cnt.ctypes.data, N, E, rank, cap, out["gbase"].ctypes.data,
+                                  out["send"].ctypes.data, out["recv"].ctypes.data,
+                                  out["own_off"].ctypes.data, out["own_tile_off"].ctypes.data,
+                                  out["gather"].ctypes.data), "jt_b200_ep_layout")
+    return out

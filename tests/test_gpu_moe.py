@@ -133,8 +133,8 @@ def test_moe_nan_logits_rejected():
     wp = MoeWeights(*[dw[n].data_ptr() for n in WEIGHT_FIELDS])
     y = torch.zeros((8, 128), device="cuda")
     plan = Plan(dm)
-    plan.forward(wp, _dev.to_dev(x).data_ptr(), _dev.to_dev(logits).data_ptr(), None, 8,
-                 y.data_ptr(), False, _dev.stream())
+    dx, dl = _dev.to_dev(x), _dev.to_dev(logits)  # alive until the forward has run
+    plan.forward(wp, dx.data_ptr(), dl.data_ptr(), None, 8, y.data_ptr(), False, _dev.stream())
     assert lib().jt_b200_sync() != 0  # kernel-reported routing fault surfaces as JT_ERR_CUDA
     assert lib().jt_b200_sync() == 0  # and is cleared
     plan.close()
