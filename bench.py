@@ -211,6 +211,81 @@ def time_layer(torch, cfg, rank, world, steps, warmup, seed, zipf=None, bf16=Fal
     return out
 
 
+def time_layer_ep(torch, cfg, rank, world, steps, warmup, seed):
+    """Expert-parallel config 5 on `world` ranks: rank r owns tokens
+    [r*T/N, (r+1)*T/N) and routed experts [r*E/N, (r+1)*E/N) (its weight
+    shard generated on its GPU), shared experts replicated; dispatch and
+    combine over NCCL inside every step."""
+    from jimotono_b200 import lib
+    from jimotono_b200.moe import Dims, EpComm, EpPlan
+    T = cfg["T"] // world
+    El = cfg["E"] // world
+    dm_w = Dims(T, cfg["d"], cfg["f"], El, cfg["k"], cfg["S"], cfg["fs"], cfg["cap"])
+    dw, wp = synth_weights_dev(torch, dm_w, seed + 101 * rank)
+    dm = Dims(T, cfg["d"], cfg["f"], cfg["E"], cfg["k"], cfg["S"], cfg["fs"], cfg["cap"])
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed + 1000 * rank)
+    x = torch.randn((T, dm.d), device="cuda", generator=g)
+    logits = torch.randn((T, dm.E), device="cuda", generator=g)
+    y = torch.empty((T, dm.d), device="cuda")
+    uid = [EpComm.unique_id() if rank == 0 else None]
+    torch.distributed.broadcast_object_list(uid, src=0)
+    comm = EpComm(uid[0], world, rank)
+    plan = EpPlan(dm, comm)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def step():
+        plan.forward(wp, x.data_ptr(), logits.data_ptr(), None, y.data_ptr(), False, stream)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if lib().jt_b200_sync() != 0:
+        raise RuntimeError("kernel fault during warm-up")
+    torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    if lib().jt_b200_sync() != 0:
+        raise RuntimeError("kernel fault during the timed region")
+    meta = plan.debug(9, np.int32, 4)
+    # end to end: pinned host x / logits in, y out, every step
+    hx = x.cpu().pin_memory()
+    hl = logits.cpu().pin_memory()
+    hy = torch.empty(y.shape, dtype=y.dtype).pin_memory()
+
+    def step_e2e():
+        x.copy_(hx, non_blocking=True)
+        logits.copy_(hl, non_blocking=True)
+        step()
+        hy.copy_(y, non_blocking=True)
+
+    for _ in range(2):
+        step_e2e()
+    torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    n_e2e = max(2, steps // 2)
+    for _ in range(n_e2e):
+        step_e2e()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / n_e2e
+    h2d = hx.numel() * 4 + hl.numel() * 4
+    d2h = hy.numel() * 4
+    out = dict(T=T, ms_per_step=ms, e2e_ms=e2e_ms, h2d=h2d, d2h=d2h, kept_local=int(meta[0]),
+               owned_rows=int(meta[1]), dims=dm)
+    plan.close()
+    comm.close()
+    del dw
+    return out
+
+
 def e2e_layer(torch, st, steps, warmup):
     """Same layer through the public API with host buffers: H2D of x and the
     router logits from pinned memory, forward, D2H of the output, per step."""
@@ -326,6 +401,44 @@ def part_gemv(torch, hbm_peak, steps=200, rot=4):
             "l2": f"{rot} rotating weight copies ({rot * byts / 1e6:.0f} MB > L2)"}
 
 
+def main_ep(torch, args, rank, world, local, hbm_peak, peak_kind):
+    """N > 1: the expert-parallel layer, max step time over ranks."""
+    with ClockSampler(local) as clk:
+        st = time_layer_ep(torch, CFG5, rank, world, args.steps, args.warmup, seed=5)
+    t = torch.tensor([st["ms_per_step"], st["e2e_ms"]], device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms, e2e_ms = float(t[0].item()), float(t[1].item())
+    kept = torch.tensor([st["kept_local"]], device="cuda")
+    torch.distributed.all_reduce(kept)
+    clocks = clk.summary()
+    dm = st["dims"]
+    T = CFG5["T"]
+    kept_all = int(kept.item())
+    ops = 2.0 * kept_all * (dm.d * 2 * dm.f + dm.f * dm.d) + 2.0 * T * dm.S * (3 * dm.fs * dm.d)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(T / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (seeded; random-init packed weights)",
+            "config": {"workload": "cfg5 EP MoE layer: T=16384 d=2048 E=1024 f=1536 top-8 INT2/INT4 g64 + 2 shared INT8 f=4096, cap 1.5",
+                       "tokens": T, "parallelism": f"ep{world}: {CFG5['E'] // world} experts and {T // world} tokens per GPU, NCCL send/recv dispatch + combine",
+                       "l2": "inputs larger than L2 (weights per GPU > 126 MB)"},
+            "e2e": {"value": round(T / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": st["h2d"] * world, "d2h_bytes_per_step": st["d2h"] * world},
+            "gpu_launches": args.steps * (13 + 2 * dm.S),
+            "kept_pairs": kept_all,
+            "roofline": {"bound": "tensor", "kernel": "whole expert-parallel layer (int8 ops of all GPUs)",
+                         "achieved": round(ops / (ms / 1e3) / 1e12, 2), "peak": 4500.0 * world,
+                         "unit": "TOPS", "frac": round(ops / (ms / 1e3) / 1e12 / (4500.0 * world), 4),
+                         "peak_kind": "nominal dense int8 x GPUs", "traffic": None},
+            "clocks": clocks, "hbm_peak_gbs": hbm_peak, "hbm_peak_kind": peak_kind, "cpu_baseline": None,
+        }
+        print(json.dumps(line), flush=True)
+    torch.distributed.barrier()
+    torch.distributed.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -360,13 +473,12 @@ def main():
                           "stage_ms": [round(v, 4) for v in st["stage_ms"]], "kept": st["kept"]}))
         return
 
+    if world > 1:
+        main_ep(torch, args, rank, world, local, hbm_peak, peak_kind)
+        return
     with ClockSampler(local) as clk:
         st = time_layer(torch, CFG5, rank, world, args.steps, args.warmup, seed=5)
     ms = st["ms_per_step"]
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
     tokens = CFG5["T"] if world > 1 else st["T"]
     value = tokens / (ms / 1e3)
     dm = st["dims"]
