@@ -82,6 +82,36 @@ int jt_w8a8_gemm_per_channel(const int8_t *Aq, const int8_t *Bq, float sA, const
 int jt_w8a8_fakequant_per_tensor(const float *src, size_t n, float *dst);
 int jt_w8a8_fakequant_per_channel(const float *src, size_t rows, size_t cols, float *dst);
 
+/* ---- reference-compatible routing / sort / fp32 GEMM / low-bit helpers ---- */
+
+/* Top-k of one token's logits with ties to the lowest index, NaN -> INVAL,
+ * softmax over the selected logits in double (w = (float)e * (float)(1/sum)),
+ * non-finite softmax -> INVAL.  Replaces routing.h:56-57 (routing.c:16-76). */
+int jt_routing_topk(const float *logits, size_t n, size_t k, size_t *out_ids, float *out_weights);
+/* Stable capacity sort: cap = ceil(cap_factor*T*k/E), the first cap pairs of
+ * each expert in q = t*k + p order kept (perm [kept], off [E+1]), the rest
+ * dropped.  Replaces moe_layer.h:194-198 (moe_layer.c:895-978). */
+int jt_moe_batch_sort(const size_t *ids, int T, int k, int E, float cap_factor, size_t *perm,
+                      size_t *off, unsigned char *drop, size_t *out_kept, size_t *out_dropped);
+/* C[M][N] = A[M][K] B[K][N], fp32, products and sums rounded one by one in
+ * ascending k (no fused multiply-add); M == 0 no-op; non-finite C -> INVAL
+ * (C written).  Replaces moe_gemm.h:59-61 (moe_gemm.c:92-170). */
+int jt_gemm_mat_f32(const float *A, const float *B, float *C, int M, int N, int K);
+/* dst[c][r] = src[r][c].  Replaces moe_gemm.h:65-66 (moe_gemm.c:17-42). */
+int jt_transpose_f32(const float *src, float *dst, int rows, int cols);
+/* Low-bit mode flag 0/1/2 and bit widths (gate/up 2, down 4).  Replace
+ * lowbit.h:30-34 (lowbit.c:16-39). */
+int jt_lowbit_set_mode(int mode);
+int jt_lowbit_get_mode(void);
+int jt_lowbit_bits_for(int is_down, int *out_bits);
+/* Odd-symmetric fake quantization over the whole array (one max-abs):
+ * li = floor(t(n-1)/2 + (n-1)/2 + 0.5), t = w/maxa (double), value
+ * ((2li - (n-1))/(n-1)) * maxa.  Replaces lowbit.h:38-39 (lowbit.c:47-91). */
+int jt_lowbit_fakequant(const float *w, float *fq, size_t n, int bits);
+/* The same codes as bit planes idx[b*(k/4) + g] (bit j = bit b of code
+ * 4g+j), *w_scale = maxa.  Replaces lowbit.h:43-44 (lowbit.c:93-141). */
+int jt_lowbit_col_to_idx(const float *col, size_t k, int bits, uint8_t *idx, float *w_scale);
+
 /* ======================================================================
  * 2. B200 device entry points
  * ====================================================================== */

@@ -27,6 +27,15 @@ PROTOTYPES = {
     "jt_w8a8_fakequant_per_tensor": (I, [P, SZ, P]),
     "jt_w8a8_fakequant_per_channel": (I, [P, SZ, SZ, P]),
     # ---- device entry points ----
+    "jt_routing_topk": (I, [P, SZ, SZ, P, P]),
+    "jt_moe_batch_sort": (I, [P, I, I, I, F, P, P, P, P, P]),
+    "jt_gemm_mat_f32": (I, [P, P, P, I, I, I]),
+    "jt_transpose_f32": (I, [P, P, I, I]),
+    "jt_lowbit_set_mode": (I, [I]),
+    "jt_lowbit_get_mode": (I, []),
+    "jt_lowbit_bits_for": (I, [I, P]),
+    "jt_lowbit_fakequant": (I, [P, P, SZ, I]),
+    "jt_lowbit_col_to_idx": (I, [P, SZ, I, P, P]),
     "jt_b200_w8a8_gemm": (I, [P, I, P, P, I, P, P, I, I, I, I, P]),
     "jt_b200_w8a8_gemm_i32": (I, [P, I, P, I, P, I, I, I, I, P]),
     "jt_b200_w8a8_linear_noalloc": (I, [P, I, I, P, I, P, P, I, I, P]),
