@@ -111,6 +111,35 @@ int jt_lowbit_fakequant(const float *w, float *fq, size_t n, int bits);
 /* The same codes as bit planes idx[b*(k/4) + g] (bit j = bit b of code
  * 4g+j), *w_scale = maxa.  Replaces lowbit.h:43-44 (lowbit.c:93-141). */
 int jt_lowbit_col_to_idx(const float *col, size_t k, int bits, uint8_t *idx, float *w_scale);
+/* Exact fp32 product through the T-MAC tables: activation LUT of X, bit
+ * planes of every column of W [k][h] (row-major), lookups, and the sign
+ * correction Y = (float)((2o - (n-1)*ws*rowsum)/(n-1)); k % 32 != 0 takes
+ * the double-accumulated fallback; me == 0 is a no-op.  Y is unchanged on
+ * failure.  Replaces lowbit.h:52-53 (lowbit.c:158-267). */
+int jt_lowbit_gemm_lut(const float *X, const float *W, float *Y, int me, int h, int k, int bits);
+
+/* ---- reference-compatible T-MAC LUT (tmac.h) ---- */
+#define JT_TMAC_G 4          /* tmac.h:44 */
+#define JT_TMAC_LUT_HALF 8   /* tmac.h:45 */
+#define JT_TMAC_LUT_FULL 16  /* tmac.h:46 */
+#define JT_TMAC_ACT_GROUP 32 /* tmac.h:47 */
+#define JT_TMAC_ALIGN 64     /* tmac.h:48 */
+/* n*(k/4)*8 and n*(k/32)*sizeof(float) bytes (k % 4, k % 32; overflow ->
+ * JT_ERR_NOMEM).  Replace tmac.h:53-54 (tmac.c:168-228). */
+int jt_tmac_qlut_bytes(size_t n, size_t k, size_t *out);
+int jt_tmac_param_bytes(size_t n, size_t k, size_t *out);
+/* Per 32-activation block: 8 groups x patterns p = 8..15 of F(p) = sum_j
+ * +-a_j (double), scale = max|F|/127, bias = sum a, q = clamp(round(F /
+ * scale), -128, 127); all-zero block -> q 0, scale 1.  Non-finite input ->
+ * INVAL (EINVAL), bias overflow -> INVAL (ERANGE); outputs unchanged on
+ * failure.  Replaces tmac.h:59-60 (tmac.c:230-385). */
+int jt_tmac_lut_ctor(const float *act, size_t n, size_t k, int8_t *qlut, float *scales, float *biases);
+/* One dot product: per block and plane the int32 sum of 8 mirrored
+ * lookups, total += ((sc*acc + bi)*0.5)*2^b in double (ascending block,
+ * then plane), *out = (float)(total*w_scale).  Replaces tmac.h:69-72
+ * (tmac.c:387-506). */
+int jt_tmac_lookup_accum(const int8_t *qlut, const uint8_t *idx, const float *scales, const float *biases,
+                         size_t ngroups, size_t nblocks, int bits, float w_scale, float *out);
 
 /* ======================================================================
  * 2. B200 device entry points

@@ -36,6 +36,11 @@ PROTOTYPES = {
     "jt_lowbit_bits_for": (I, [I, P]),
     "jt_lowbit_fakequant": (I, [P, P, SZ, I]),
     "jt_lowbit_col_to_idx": (I, [P, SZ, I, P, P]),
+    "jt_lowbit_gemm_lut": (I, [P, P, P, I, I, I, I]),
+    "jt_tmac_qlut_bytes": (I, [SZ, SZ, P]),
+    "jt_tmac_param_bytes": (I, [SZ, SZ, P]),
+    "jt_tmac_lut_ctor": (I, [P, SZ, SZ, P, P, P]),
+    "jt_tmac_lookup_accum": (I, [P, P, P, P, SZ, SZ, I, F, P]),
     "jt_b200_w8a8_gemm": (I, [P, I, P, P, I, P, P, I, I, I, I, P]),
     "jt_b200_w8a8_gemm_i32": (I, [P, I, P, I, P, I, I, I, I, P]),
     "jt_b200_w8a8_linear_noalloc": (I, [P, I, I, P, I, P, P, I, I, P]),

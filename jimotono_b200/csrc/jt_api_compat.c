@@ -353,3 +353,267 @@ int jt_lowbit_col_to_idx(const float *col, size_t k, int bits, uint8_t *idx, flo
     jt_stage_unlock();
     return rc;
 }
+
+/* ---------------------------------------------------------------- tmac.c / lowbit.c:158-267 */
+int jtk_tmac_ctor(const float *act, size_t n, size_t k, int8_t *qlut, float *scales, float *biases,
+                  unsigned long long *err, cudaStream_t stream);
+int jtk_tmac_lookup_one(const int8_t *qlut, const uint8_t *idx, const float *scales, const float *biases,
+                        size_t ngroups, size_t nblocks, int bits, float w_scale, float *out, int *flag,
+                        cudaStream_t stream);
+int jtk_lut_gemm(const float *X, const float *W, const int8_t *qlut, const float *scales, const float *biases,
+                 double *maxa, void *idxT, double *rowsum, float *Y, int me, int h, int k, int bits,
+                 unsigned long long *err, cudaStream_t stream);
+int jtk_gemm_f64acc(const float *X, const float *W, float *Y, int me, int h, int k, cudaStream_t stream);
+
+#define TMAC_G 4          /* tmac.h:44 */
+#define TMAC_LUT_HALF 8   /* tmac.h:45 */
+#define TMAC_ACT_GROUP 32 /* tmac.h:47 */
+
+static int size_mul_ov(size_t a, size_t b, size_t *out) {
+    if (a == 0 || b == 0) {
+        *out = 0;
+        return 0;
+    }
+    if (a > SIZE_MAX / b) return 1;
+    *out = a * b;
+    return 0;
+}
+
+/* tmac.c:168-197 */
+int jt_tmac_qlut_bytes(size_t n, size_t k, size_t *out) {
+    if (out == NULL) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    *out = 0;
+    if (n == 0 || k == 0 || k % TMAC_G != 0) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    size_t t = 0, bytes = 0;
+    if (size_mul_ov(n, k / TMAC_G, &t) || size_mul_ov(t, TMAC_LUT_HALF, &bytes)) {
+        errno = ENOMEM;
+        return JT_ERR_NOMEM;
+    }
+    *out = bytes;
+    return JT_OK;
+}
+
+/* tmac.c:199-228 */
+int jt_tmac_param_bytes(size_t n, size_t k, size_t *out) {
+    if (out == NULL) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    *out = 0;
+    if (n == 0 || k == 0 || k % TMAC_ACT_GROUP != 0) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    size_t t = 0, bytes = 0;
+    if (size_mul_ov(n, k / TMAC_ACT_GROUP, &t) || size_mul_ov(t, sizeof(float), &bytes)) {
+        errno = ENOMEM;
+        return JT_ERR_NOMEM;
+    }
+    *out = bytes;
+    return JT_OK;
+}
+
+/* Arguments of tmac.c:230-272: 0, or the error to return. */
+static int tmac_ctor_check(const float *act, size_t n, size_t k, const void *qlut, const void *scales,
+                           const void *biases) {
+    if (act == NULL || qlut == NULL || scales == NULL || biases == NULL || n == 0 || k == 0 ||
+        k % TMAC_G != 0 || k % TMAC_ACT_GROUP != 0) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    size_t t = 0, u = 0;
+    if (size_mul_ov(n, k, &t) || size_mul_ov(n, k / TMAC_G, &t) || size_mul_ov(t, TMAC_LUT_HALF, &u) ||
+        size_mul_ov(n, k / TMAC_ACT_GROUP, &t) || size_mul_ov(n * k, sizeof(float), &t)) {
+        errno = ENOMEM;
+        return JT_ERR_NOMEM;
+    }
+    return JT_OK;
+}
+
+/* A ctor error key posted by the kernel: block index << 1 | (1 = ERANGE). */
+static int tmac_err(unsigned long long key) {
+    errno = (key & 1ull) ? ERANGE : EINVAL;
+    return JT_ERR_INVAL;
+}
+
+/* tmac.c:230-385.  On failure the outputs are left unchanged (the
+ * reference has written the blocks before the failing one). */
+int jt_tmac_lut_ctor(const float *act, size_t n, size_t k, int8_t *qlut, float *scales, float *biases) {
+    int rc = tmac_ctor_check(act, n, k, qlut, scales, biases);
+    if (rc != JT_OK) return rc;
+    const size_t nb = k / TMAC_ACT_GROUP, qn = n * (k / TMAC_G) * TMAC_LUT_HALF;
+    jt_stage_lock();
+    float *da = (float *)jt_stage_buf(JT_SLOT_X, n * k * sizeof(float));
+    int8_t *dq = (int8_t *)jt_stage_buf(JT_SLOT_A, qn);
+    float *ds = (float *)jt_stage_buf(JT_SLOT_SCALE, n * nb * sizeof(float));
+    float *dbi = (float *)jt_stage_buf(JT_SLOT_AUX1, n * nb * sizeof(float));
+    unsigned long long *derr = (unsigned long long *)jt_stage_buf(JT_SLOT_FLAGS, 64);
+    unsigned long long key = 0;
+    cudaStream_t st = jt_stage_stream();
+    if (!da || !dq || !ds || !dbi || !derr) {
+        errno = ENOMEM;
+        rc = JT_ERR_NOMEM;
+        goto out;
+    }
+    if (jt_stage_h2d(da, act, n * k * sizeof(float)) ||
+        jtk_tmac_ctor(da, n, k, dq, ds, dbi, derr, st) != 0 || jt_stage_d2h(&key, derr, sizeof key) ||
+        jt_stage_sync()) {
+        rc = cuda_fail();
+        goto out;
+    }
+    if (key != ~0ull) {
+        rc = tmac_err(key);
+        goto out;
+    }
+    if (jt_stage_d2h(qlut, dq, qn) || jt_stage_d2h(scales, ds, n * nb * sizeof(float)) ||
+        jt_stage_d2h(biases, dbi, n * nb * sizeof(float)) || jt_stage_sync()) {
+        rc = cuda_fail();
+        goto out;
+    }
+    rc = JT_OK;
+out:
+    jt_stage_unlock();
+    return rc;
+}
+
+/* tmac.c:387-506 */
+int jt_tmac_lookup_accum(const int8_t *qlut, const uint8_t *idx, const float *scales, const float *biases,
+                         size_t ngroups, size_t nblocks, int bits, float w_scale, float *out) {
+    if (qlut == NULL || idx == NULL || scales == NULL || biases == NULL || out == NULL ||
+        ngroups == 0 || nblocks == 0) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    if (nblocks > SIZE_MAX / 8u) {
+        errno = ENOMEM;
+        return JT_ERR_NOMEM;
+    }
+    if (ngroups != nblocks * 8u || bits < 1 || bits > 4) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    if (ngroups > SIZE_MAX / TMAC_LUT_HALF || ngroups > SIZE_MAX / (size_t)bits) {
+        errno = ENOMEM;
+        return JT_ERR_NOMEM;
+    }
+    if (!isfinite((double)w_scale)) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    int rc = JT_ERR_CUDA;
+    jt_stage_lock();
+    int8_t *dq = (int8_t *)jt_stage_buf(JT_SLOT_A, ngroups * TMAC_LUT_HALF);
+    uint8_t *di = (uint8_t *)jt_stage_buf(JT_SLOT_B, ngroups * (size_t)bits);
+    float *ds = (float *)jt_stage_buf(JT_SLOT_SCALE, nblocks * sizeof(float));
+    float *dbi = (float *)jt_stage_buf(JT_SLOT_AUX1, nblocks * sizeof(float));
+    float *dout = (float *)jt_stage_buf(JT_SLOT_Y, 16);
+    int *dflag = (int *)jt_stage_buf(JT_SLOT_FLAGS, 64);
+    int flag = 0;
+    float o = 0.0f;
+    cudaStream_t st = jt_stage_stream();
+    if (!dq || !di || !ds || !dbi || !dout || !dflag) {
+        errno = ENOMEM;
+        rc = JT_ERR_NOMEM;
+        goto out;
+    }
+    if (cudaMemsetAsync(dflag, 0, 64, st) != cudaSuccess || jt_stage_h2d(dq, qlut, ngroups * TMAC_LUT_HALF) ||
+        jt_stage_h2d(di, idx, ngroups * (size_t)bits) || jt_stage_h2d(ds, scales, nblocks * sizeof(float)) ||
+        jt_stage_h2d(dbi, biases, nblocks * sizeof(float)) ||
+        jtk_tmac_lookup_one(dq, di, ds, dbi, ngroups, nblocks, bits, w_scale, dout, dflag, st) != 0 ||
+        jt_stage_d2h(&flag, dflag, sizeof flag) || jt_stage_d2h(&o, dout, sizeof o) || jt_stage_sync()) {
+        rc = cuda_fail();
+        goto out;
+    }
+    if (flag) {
+        errno = flag == 1 ? EINVAL : ERANGE;
+        rc = JT_ERR_INVAL;
+        goto out;
+    }
+    *out = o;
+    rc = JT_OK;
+out:
+    jt_stage_unlock();
+    return rc;
+}
+
+/* lowbit.c:158-267: Y[me][h] = X[me][k] . W[k][h] through the activation
+ * LUT and per-column bit planes, with the sign correction; k % 32 != 0
+ * takes the double-accumulated fallback.  Y is left unchanged on failure. */
+int jt_lowbit_gemm_lut(const float *X, const float *W, float *Y, int me, int h, int k, int bits) {
+    if (X == NULL || W == NULL || Y == NULL || me < 0 || h <= 0 || k <= 0) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    if (bits != 2 && bits != 4) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    if (me == 0) return JT_OK;
+    const size_t nx = (size_t)me * (size_t)k, nw = (size_t)k * (size_t)h, ny = (size_t)me * (size_t)h;
+    int rc = JT_ERR_CUDA;
+    jt_stage_lock();
+    cudaStream_t st = jt_stage_stream();
+    float *dx = (float *)jt_stage_buf(JT_SLOT_X, nx * sizeof(float));
+    float *dw = (float *)jt_stage_buf(JT_SLOT_W1, nw * sizeof(float));
+    float *dy = (float *)jt_stage_buf(JT_SLOT_Y, ny * sizeof(float));
+    unsigned long long *derr = (unsigned long long *)jt_stage_buf(JT_SLOT_FLAGS, 64);
+    unsigned long long keys[2] = {~0ull, ~0ull};
+    if (!dx || !dw || !dy || !derr) {
+        errno = ENOMEM;
+        rc = JT_ERR_NOMEM;
+        goto out;
+    }
+    if (k % TMAC_ACT_GROUP != 0) {
+        if (jt_stage_h2d(dx, X, nx * sizeof(float)) || jt_stage_h2d(dw, W, nw * sizeof(float)) ||
+            jtk_gemm_f64acc(dx, dw, dy, me, h, k, st) != 0 || jt_stage_d2h(Y, dy, ny * sizeof(float)) ||
+            jt_stage_sync()) {
+            rc = cuda_fail();
+            goto out;
+        }
+        rc = JT_OK;
+        goto out;
+    }
+    {
+        const size_t nb = (size_t)k / TMAC_ACT_GROUP;
+        int8_t *dq = (int8_t *)jt_stage_buf(JT_SLOT_A, (size_t)me * nb * 64);
+        float *ds = (float *)jt_stage_buf(JT_SLOT_SCALE, (size_t)me * nb * sizeof(float));
+        float *dbi = (float *)jt_stage_buf(JT_SLOT_AUX1, (size_t)me * nb * sizeof(float));
+        double *drs = (double *)jt_stage_buf(JT_SLOT_AUX2, (size_t)me * sizeof(double));
+        double *dmx = (double *)jt_stage_buf(JT_SLOT_AUX3, (size_t)h * sizeof(double));
+        void *didx = jt_stage_buf(JT_SLOT_B, (size_t)bits * nb * (size_t)h * 8);
+        if (!dq || !ds || !dbi || !drs || !dmx || !didx) {
+            errno = ENOMEM;
+            rc = JT_ERR_NOMEM;
+            goto out;
+        }
+        if (jt_stage_h2d(dx, X, nx * sizeof(float)) || jt_stage_h2d(dw, W, nw * sizeof(float)) ||
+            jtk_tmac_ctor(dx, (size_t)me, (size_t)k, dq, ds, dbi, derr, st) != 0 ||
+            jtk_lut_gemm(dx, dw, dq, ds, dbi, dmx, didx, drs, dy, me, h, k, bits, derr + 1, st) != 0 ||
+            jt_stage_d2h(keys, derr, sizeof keys) || jt_stage_sync()) {
+            rc = cuda_fail();
+            goto out;
+        }
+        if (keys[0] != ~0ull) { /* the activation table failed first */
+            rc = tmac_err(keys[0]);
+            goto out;
+        }
+        if (keys[1] != ~0ull) { /* column check (EINVAL) or a lookup total (ERANGE) */
+            rc = tmac_err(keys[1]);
+            goto out;
+        }
+        if (jt_stage_d2h(Y, dy, ny * sizeof(float)) || jt_stage_sync()) {
+            rc = cuda_fail();
+            goto out;
+        }
+        rc = JT_OK;
+    }
+out:
+    jt_stage_unlock();
+    return rc;
+}

@@ -1,7 +1,8 @@
 // jt_compat.cu - kernels behind the remaining reference-compatible host
 // entry points (jt_api_compat.c): single-token top-k + softmax of any k,
 // the exact fp32 GEMM / transpose of moe_gemm.c, and the low-bit level rule
-// of lowbit.c (fake-quant values and bit-plane codes).  All arithmetic is
+// of lowbit.c (fake-quant values and bit-plane codes), and the T-MAC
+// activation table, lookup and LUT GEMM of tmac.c / lowbit.c.  All arithmetic is
 // the reference's: sequential k-order fp32 sums without fusion, double
 // precision where the reference uses double.
 #include <cuda_runtime.h>
@@ -187,6 +188,290 @@ __global__ void k_lowbit_idx(const float *__restrict__ col, size_t k, int bits,
     }
 }
 
+// ---------------------------------------------------------------- T-MAC LUT
+// Error keys: the reference stops at its first failure, so every thread that
+// fails posts (position << 1 | kind) with atomicMin and the host reads the
+// smallest one (all ones = no error).  kind 0 = EINVAL, 1 = ERANGE.
+
+// One thread per (row, 32-activation block) of tmac.c:274-376.  Patterns p
+// of a 4-activation group: F(p) = sum_j (bit j of p ? +a_j : -a_j), summed
+// in double in ascending j.  F(15-p) is the exact negation of F(p) (every
+// partial sum flips sign and round-to-nearest is symmetric), so the maximum
+// |F| over the 16 patterns is the maximum over p = 8..15, and the stored
+// half-table holds q(p) for p = 8..15.
+__global__ void k_tmac_ctor(const float *__restrict__ act, size_t nrows, size_t k, int8_t *__restrict__ qlut,
+                            float *__restrict__ scales, float *__restrict__ biases,
+                            unsigned long long *__restrict__ err) {
+    const size_t nb = k / 32;
+    const size_t L = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+    if (L >= nrows * nb) return;
+    const size_t r = L / nb, bb = L % nb;
+    const float4 *src = reinterpret_cast<const float4 *>(act + r * k + bb * 32);
+    float a[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 v = src[i];
+        a[4 * i] = v.x;
+        a[4 * i + 1] = v.y;
+        a[4 * i + 2] = v.z;
+        a[4 * i + 3] = v.w;
+    }
+    bool fin = true;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) fin &= isfinite(a[i]);
+    if (!fin) {
+        atomicMin(err, (unsigned long long)L << 1);
+        return;
+    }
+    double F[8][8];
+    double maxabs = 0.0;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+#pragma unroll
+        for (int ii = 0; ii < 8; ++ii) {
+            const int p = 8 + ii;
+            double s = 0.0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const double av = (double)a[4 * g + j];
+                s = __dadd_rn(s, ((p >> j) & 1) ? av : -av);
+            }
+            F[g][ii] = s;
+            maxabs = fmax(maxabs, fabs(s));
+        }
+    }
+    double asum = 0.0;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) asum = __dadd_rn(asum, (double)a[i]);
+    const float bias_f = (float)asum;
+    if (!isfinite(bias_f)) {
+        atomicMin(err, ((unsigned long long)L << 1) | 1ull);
+        return;
+    }
+    uint32_t w[16];
+    float scale_f = 1.0f;
+    if (maxabs == 0.0) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) w[i] = 0;
+    } else {
+        const double scale_d = __ddiv_rn(maxabs, 127.0);
+        scale_f = (float)scale_d;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                uint32_t word = 0;
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    double qd = round(__ddiv_rn(F[g][4 * h + b], scale_d));
+                    qd = qd > 127.0 ? 127.0 : (qd < -128.0 ? -128.0 : qd);
+                    word |= ((uint32_t)(int)qd & 0xffu) << (8 * b);
+                }
+                w[2 * g + h] = word;
+            }
+        }
+    }
+    uint4 *dst = reinterpret_cast<uint4 *>(qlut + L * 64);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+    scales[L] = scale_f;
+    biases[L] = bias_f;
+}
+
+// plane_acc of tmac.c:80-93 over one block: nibble p of group g selects
+// +q[g][p-8] (p >= 8) or -q[g][7-p] (p < 8); q8 holds the block's 64 bytes
+// as 16 words and idx8 the block's 8 index bytes (low nibble used).
+__device__ __forceinline__ int tmac_plane(const uint32_t (&q8)[16], uint2 idx8) {
+    int acc = 0;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+        const uint32_t byte = ((g < 4 ? idx8.x : idx8.y) >> (8 * (g & 3))) & 0xfu;
+        const uint32_t hi = byte >> 3;                      // 1: p >= 8
+        const uint32_t sel = (byte & 7u) ^ (hi ? 0u : 7u);  // p-8 or 7-p
+        const uint32_t v = __byte_perm(q8[2 * g], q8[2 * g + 1], sel);
+        const int qv = (int)(int8_t)(v & 0xffu);
+        acc += hi ? qv : -qv;
+    }
+    return acc;
+}
+
+// ((sc*acc + bi)*0.5)*2^b, each operation rounded (tmac.c:482-487, no FMA)
+__device__ __forceinline__ double tmac_contrib(double sc, double bi, int acc, int b) {
+    return __dmul_rn(__dmul_rn(__dadd_rn(__dmul_rn(sc, (double)acc), bi), 0.5), (double)(1 << b));
+}
+
+// One dot product of tmac.c:387-506.  flag: 1 = a non-finite scale/bias
+// (EINVAL), 2 = non-finite total or float result (ERANGE).  The reference
+// checks the running total after every add; non-finite values are absorbing
+// under addition, so one check at the end reports the same outcome.
+__global__ void __launch_bounds__(256) k_tmac_lookup_one(const int8_t *__restrict__ qlut,
+                                                          const uint8_t *__restrict__ idx,
+                                                          const float *__restrict__ scales,
+                                                          const float *__restrict__ biases, size_t ngroups,
+                                                          size_t nblocks, int bits, float w_scale,
+                                                          float *__restrict__ out, int *__restrict__ flag) {
+    __shared__ double part[256][4];
+    __shared__ int bad;
+    if (threadIdx.x == 0) bad = 0;
+    __syncthreads();
+    for (size_t bb = threadIdx.x; bb < nblocks; bb += blockDim.x)
+        if (!isfinite(scales[bb]) || !isfinite(biases[bb])) bad = 1;
+    __syncthreads();
+    if (bad) {
+        if (threadIdx.x == 0) flag[0] = 1;
+        return;
+    }
+    double total = 0.0;
+    for (size_t c0 = 0; c0 < nblocks; c0 += blockDim.x) {
+        const size_t bb = c0 + threadIdx.x;
+        if (bb < nblocks) {
+            const uint32_t *qw = reinterpret_cast<const uint32_t *>(qlut + bb * 64);
+            uint32_t q8[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) q8[i] = qw[i];
+            const double sc = (double)scales[bb], bi = (double)biases[bb];
+            for (int b = 0; b < bits; ++b) {
+                const uint8_t *pl = idx + (size_t)b * ngroups + bb * 8;
+                uint2 i8;
+                i8.x = pl[0] | (pl[1] << 8) | (pl[2] << 16) | ((uint32_t)pl[3] << 24);
+                i8.y = pl[4] | (pl[5] << 8) | (pl[6] << 16) | ((uint32_t)pl[7] << 24);
+                part[threadIdx.x][b] = tmac_contrib(sc, bi, tmac_plane(q8, i8), b);
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const size_t n = nblocks - c0 < blockDim.x ? nblocks - c0 : blockDim.x;
+            for (size_t i = 0; i < n; ++i)
+                for (int b = 0; b < bits; ++b) total = __dadd_rn(total, part[i][b]);
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        total = __dmul_rn(total, (double)w_scale);
+        const float f = (float)total;
+        if (!isfinite(total) || !isfinite(f)) {
+            flag[0] = 2;
+            return;
+        }
+        out[0] = f;
+    }
+}
+
+// Column max-abs of W [k][h] (row-major) in double, for lowbit.c:228-237's
+// per-column col_to_idx; a non-finite column posts key j*(me+1) (EINVAL).
+__global__ void __launch_bounds__(256) k_col_absmax(const float *__restrict__ W, int k, int h, int me,
+                                                     double *__restrict__ maxa,
+                                                     unsigned long long *__restrict__ err) {
+    __shared__ double sm[8][32];
+    __shared__ int sbad[8][32];
+    const int j = blockIdx.x * 32 + threadIdx.x;
+    double m = 0.0;
+    int bad = 0;
+    if (j < h)
+        for (int t = threadIdx.y; t < k; t += 8) {
+            const double v = (double)W[(size_t)t * h + j];
+            bad |= !isfinite(v);
+            m = fmax(m, fabs(v));
+        }
+    sm[threadIdx.y][threadIdx.x] = m;
+    sbad[threadIdx.y][threadIdx.x] = bad;
+    __syncthreads();
+    if (threadIdx.y == 0 && j < h) {
+        for (int y = 1; y < 8; ++y) {
+            m = fmax(m, sm[y][threadIdx.x]);
+            bad |= sbad[y][threadIdx.x];
+        }
+        maxa[j] = m;
+        if (bad) atomicMin(err, ((unsigned long long)j * (unsigned long long)(me + 1)) << 1);
+    }
+}
+
+// Bit planes of every column (lowbit.c:117-137) in the layout the LUT GEMM
+// reads: idxT[(b*nb + bb)*h + j] holds the 8 index bytes of groups
+// bb*8 .. bb*8+7 of column j, plane b.  One thread per (bb, j).
+__global__ void k_col_planes(const float *__restrict__ W, int k, int h, int bits, const double *__restrict__ maxa,
+                             uint2 *__restrict__ idxT) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    const int bb = blockIdx.y;
+    if (j >= h) return;
+    const int nb = k / 32, nl = 1 << bits;
+    const double m = maxa[j];
+    uint32_t pl[4][2] = {{0, 0}, {0, 0}, {0, 0}, {0, 0}};
+    for (int t = 0; t < 32; ++t) {
+        const int li = level(W[(size_t)(bb * 32 + t) * h + j], m, nl);
+        const int g = t >> 2, jj = t & 3;
+        for (int b = 0; b < bits; ++b)
+            if ((li >> b) & 1) pl[b][g >> 2] |= 1u << (8 * (g & 3) + jj);
+    }
+    for (int b = 0; b < bits; ++b) idxT[((size_t)b * nb + bb) * h + j] = make_uint2(pl[b][0], pl[b][1]);
+}
+
+// Row sums of X in double, ascending t (lowbit.c:217-224).
+__global__ void k_row_sum_d(const float *__restrict__ X, int me, int k, double *__restrict__ rowsum) {
+    const int m = blockIdx.x * blockDim.x + threadIdx.x;
+    if (m >= me) return;
+    double s = 0.0;
+    for (int t = 0; t < k; ++t) s = __dadd_rn(s, (double)X[(size_t)m * k + t]);
+    rowsum[m] = s;
+}
+
+// The LUT GEMM of lowbit.c:226-257: thread (m, j) runs lookup_accum over
+// row m's table and column j's planes, then the sign correction
+// Y = (float)((2o - ((n-1)*ws)*rowsum) / (n-1)).  A non-finite o posts key
+// j*(me+1) + m + 1 (ERANGE), ordered after column j's own col_to_idx check.
+__global__ void __launch_bounds__(256) k_lut_gemm(const int8_t *__restrict__ qlut, const float *__restrict__ scales,
+                                                   const float *__restrict__ biases, const uint2 *__restrict__ idxT,
+                                                   const double *__restrict__ maxa,
+                                                   const double *__restrict__ rowsum, float *__restrict__ Y, int me,
+                                                   int h, int k, int bits, unsigned long long *__restrict__ err) {
+    const int j = blockIdx.x * 32 + threadIdx.x;
+    const int m = blockIdx.y * 8 + threadIdx.y;
+    if (j >= h || m >= me) return;
+    const int nb = k / 32;
+    const float ws = (float)maxa[j];
+    const uint4 *qrow = reinterpret_cast<const uint4 *>(qlut + (size_t)m * nb * 64);
+    double total = 0.0;
+    for (int bb = 0; bb < nb; ++bb) {
+        uint32_t q8[16];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint4 v = __ldg(qrow + (size_t)bb * 4 + i);
+            q8[4 * i] = v.x;
+            q8[4 * i + 1] = v.y;
+            q8[4 * i + 2] = v.z;
+            q8[4 * i + 3] = v.w;
+        }
+        const double sc = (double)scales[(size_t)m * nb + bb], bi = (double)biases[(size_t)m * nb + bb];
+        for (int b = 0; b < bits; ++b) {
+            const uint2 i8 = idxT[((size_t)b * nb + bb) * h + j];
+            total = __dadd_rn(total, tmac_contrib(sc, bi, tmac_plane(q8, i8), b));
+        }
+    }
+    total = __dmul_rn(total, (double)ws);
+    const float o = (float)total;
+    if (!isfinite(total) || !isfinite(o)) {
+        atomicMin(err, (((unsigned long long)j * (unsigned long long)(me + 1) + (unsigned long long)m + 1ull) << 1) | 1ull);
+        return;
+    }
+    const double n1 = (double)((1 << bits) - 1);
+    const double corr = __dmul_rn(__dmul_rn(n1, (double)ws), rowsum[m]);
+    Y[(size_t)m * h + j] = (float)__ddiv_rn(__dsub_rn(__dmul_rn(2.0, (double)o), corr), n1);
+}
+
+// lowbit.c:143-156: the K % 32 != 0 fallback, Y = (float) sum_t X*W in
+// double, ascending t (products of floats are exact in double).
+__global__ void k_gemm_f64acc(const float *__restrict__ X, const float *__restrict__ W, float *__restrict__ Y,
+                              int me, int h, int k) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= h) return;
+    for (int m = blockIdx.y; m < me; m += gridDim.y) {
+        double acc = 0.0;
+        for (int t = 0; t < k; ++t)
+            acc = __dadd_rn(acc, __dmul_rn((double)X[(size_t)m * k + t], (double)W[(size_t)t * h + j]));
+        Y[(size_t)m * h + j] = (float)acc;
+    }
+}
+
 int grid_for(size_t n, int threads) {
     size_t g = (n + threads - 1) / threads;
     const size_t cap = (size_t)jtk_num_sms() * 8;
@@ -195,6 +480,54 @@ int grid_for(size_t n, int threads) {
 }
 
 }  // namespace
+
+extern "C" int jtk_tmac_ctor(const float *act, size_t n, size_t k, int8_t *qlut, float *scales, float *biases,
+                             unsigned long long *err, cudaStream_t stream) {
+    if (n == 0 || k == 0 || k % 32) return -1;
+    const size_t units = n * (k / 32);
+    const size_t grid = (units + 127) / 128;
+    if (grid > 0x7fffffffull) return -1;
+    if (cudaMemsetAsync(err, 0xff, sizeof(unsigned long long), stream) != cudaSuccess) return -4;
+    k_tmac_ctor<<<(unsigned)grid, 128, 0, stream>>>(act, n, k, qlut, scales, biases, err);
+    return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
+extern "C" int jtk_tmac_lookup_one(const int8_t *qlut, const uint8_t *idx, const float *scales,
+                                   const float *biases, size_t ngroups, size_t nblocks, int bits, float w_scale,
+                                   float *out, int *flag, cudaStream_t stream) {
+    if (nblocks == 0 || ngroups != nblocks * 8 || bits < 1 || bits > 4) return -1;
+    k_tmac_lookup_one<<<1, 256, 0, stream>>>(qlut, idx, scales, biases, ngroups, nblocks, bits, w_scale, out,
+                                             flag);
+    return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
+// LUT GEMM after the table is built: column max-abs, planes, row sums, the
+// lookups.  *err is reset here and receives the first column/lookup error.
+extern "C" int jtk_lut_gemm(const float *X, const float *W, const int8_t *qlut, const float *scales,
+                            const float *biases, double *maxa, void *idx_planes, double *rowsum, float *Y,
+                            int me, int h, int k, int bits, unsigned long long *err, cudaStream_t stream) {
+    uint2 *idxT = static_cast<uint2 *>(idx_planes);
+    if (me <= 0 || h <= 0 || k <= 0 || k % 32 || (bits != 2 && bits != 4) || (me + 7) / 8 > 65535 ||
+        k / 32 > 65535)
+        return -1;
+    if (cudaMemsetAsync(err, 0xff, sizeof(unsigned long long), stream) != cudaSuccess) return -4;
+    const unsigned gx = (unsigned)((h + 31) / 32);
+    k_col_absmax<<<gx, dim3(32, 8), 0, stream>>>(W, k, h, me, maxa, err);
+    k_col_planes<<<dim3((unsigned)((h + 127) / 128), (unsigned)(k / 32)), 128, 0, stream>>>(W, k, h, bits, maxa,
+                                                                                           idxT);
+    k_row_sum_d<<<(me + 127) / 128, 128, 0, stream>>>(X, me, k, rowsum);
+    k_lut_gemm<<<dim3(gx, (unsigned)((me + 7) / 8)), dim3(32, 8), 0, stream>>>(qlut, scales, biases, idxT, maxa,
+                                                                              rowsum, Y, me, h, k, bits, err);
+    return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
+extern "C" int jtk_gemm_f64acc(const float *X, const float *W, float *Y, int me, int h, int k,
+                               cudaStream_t stream) {
+    if (me <= 0 || h <= 0 || k <= 0) return -1;
+    const unsigned gy = (unsigned)(me < 65535 ? me : 65535);
+    k_gemm_f64acc<<<dim3((unsigned)((h + 127) / 128), gy), 128, 0, stream>>>(X, W, Y, me, h, k);
+    return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
 
 extern "C" int jtk_topk_any(const float *logits, int n, int k, uint32_t *taken, int32_t *ids, float *w,
                             int *flag, cudaStream_t stream) {

@@ -100,6 +100,8 @@ def ref() -> C.CDLL:
             "jt_lowbit_set_mode": (I, [I]),
             "jt_lowbit_gemm_lut": (I, [P, P, P, I, I, I, I]),
             "jt_tmac_lut_ctor": (I, [P, SZ, SZ, P, P, P]),
+            "jt_tmac_qlut_bytes": (I, [SZ, SZ, P]),
+            "jt_tmac_param_bytes": (I, [SZ, SZ, P]),
             "jt_tmac_lookup_accum": (I, [P, P, P, P, SZ, SZ, I, F, P]),
             "jt_gemm_mat_f32": (I, [P, P, P, I, I, I]),
             "jt_transpose_f32": (I, [P, P, I, I]),

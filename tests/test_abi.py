@@ -85,3 +85,20 @@ def test_gemm_host_validation_without_device():
     assert L.jt_w8a8_quant_per_tensor(x.ctypes.data, 0, q.ctypes.data, sc.ctypes.data) == 2
     assert L.jt_w8a8_dequant_per_tensor(q.ctypes.data, 0.0, 4, x.ctypes.data) == 2
     assert L.jt_w8a8_dequant_per_tensor(q.ctypes.data, float("nan"), 4, x.ctypes.data) == 2
+
+
+def test_tmac_size_helpers():
+    """tmac.c:168-228 on the host: sizes, k % 4 / k % 32 and overflow."""
+    import ctypes as C
+    from jimotono_b200 import JT_ERR_INVAL, JT_ERR_NOMEM, lib
+    L = lib()
+    out = C.c_size_t(0)
+    assert L.jt_tmac_qlut_bytes(2, 64, C.addressof(out)) == 0 and out.value == 256
+    assert L.jt_tmac_qlut_bytes(3, 4, C.addressof(out)) == 0 and out.value == 24
+    assert L.jt_tmac_param_bytes(2, 64, C.addressof(out)) == 0 and out.value == 16
+    assert L.jt_tmac_param_bytes(3, 4, C.addressof(out)) == JT_ERR_INVAL and out.value == 0
+    assert L.jt_tmac_qlut_bytes(2, 6, C.addressof(out)) == JT_ERR_INVAL
+    assert L.jt_tmac_qlut_bytes(0, 64, C.addressof(out)) == JT_ERR_INVAL
+    assert L.jt_tmac_qlut_bytes(2, 64, None) == JT_ERR_INVAL
+    assert L.jt_tmac_qlut_bytes(1 << 62, 64, C.addressof(out)) == JT_ERR_NOMEM
+    assert L.jt_tmac_param_bytes(1 << 62, 1 << 10, C.addressof(out)) == JT_ERR_NOMEM
