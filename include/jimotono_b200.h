@@ -111,6 +111,41 @@ int jt_lowbit_fakequant(const float *w, float *fq, size_t n, int bits);
 /* The same codes as bit planes idx[b*(k/4) + g] (bit j = bit b of code
  * 4g+j), *w_scale = maxa.  Replaces lowbit.h:43-44 (lowbit.c:93-141). */
 int jt_lowbit_col_to_idx(const float *col, size_t k, int bits, uint8_t *idx, float *w_scale);
+/* The whole MoE layer on the reference's fp32 weights: X [T][n], Wgate
+ * [E][n], Wg/Wu/Wd [E][h][n], shared [S][h][n]; gate logits (4-lane double
+ * dot), top-k + softmax, capacity sort (cap_factor 1.0-1.5) and
+ * renormalization, routed experts in the mode jt_w8a8_set_enabled /
+ * jt_lowbit_set_mode select (fp32, W8A8, low-bit fake-quant, LUT), SwiGLU
+ * in double, double combine in slot order plus the shared experts.
+ * out_ids/out_weights [T][k]; optional caches [T][k*h], [T][k*n],
+ * [T][S*h]; optional perm/off/drop/kept/dropped.  Y is written only on
+ * success.  _unchecked skips the finiteness scan of the inputs.  Replaces
+ * moe_layer.h:230-275 (moe_layer.c:980-1663). */
+int jt_moe_fwd_batch(const float *X, const float *Wgate, const float *Wg, const float *Wu, const float *Wd,
+                     const float *Wg_s, const float *Wu_s, const float *Wd_s, float *Y, int T, int n, int h,
+                     int n_experts, int topk, int n_shared, size_t *out_ids, float *out_weights, float *cache_Gsel,
+                     float *cache_Usel, float *cache_Ysel, float *cache_Gs, float *cache_Us, float cap_factor,
+                     size_t *out_perm, size_t *out_off, unsigned char *out_drop, size_t *out_kept,
+                     size_t *out_dropped);
+int jt_moe_fwd_batch_unchecked(const float *X, const float *Wgate, const float *Wg, const float *Wu,
+                               const float *Wd, const float *Wg_s, const float *Wu_s, const float *Wd_s, float *Y,
+                               int T, int n, int h, int n_experts, int topk, int n_shared, size_t *out_ids,
+                               float *out_weights, float *cache_Gsel, float *cache_Usel, float *cache_Ysel,
+                               float *cache_Gs, float *cache_Us, float cap_factor, size_t *out_perm,
+                               size_t *out_off, unsigned char *out_drop, size_t *out_kept, size_t *out_dropped);
+/* Single-token layer, always fp32: double dots for the logits and the
+ * expert gate/up rows, SwiGLU and down sum in double.  out_logits [E],
+ * caches [k][h], [k][n], [S][h] optional.  Replaces moe_layer.h:73-117
+ * (moe_layer.c:304-545). */
+int jt_moe_fwd(const float *X, const float *Wgate, const float *Wg, const float *Wu, const float *Wd,
+               const float *Wg_s, const float *Wu_s, const float *Wd_s, float *Y, int n, int h, int n_experts,
+               int topk, int n_shared, size_t *out_ids, float *out_weights, float *out_logits, float *cache_Gsel,
+               float *cache_Usel, float *cache_Ysel, float *cache_Gs, float *cache_Us);
+int jt_moe_fwd_unchecked(const float *X, const float *Wgate, const float *Wg, const float *Wu, const float *Wd,
+                         const float *Wg_s, const float *Wu_s, const float *Wd_s, float *Y, int n, int h,
+                         int n_experts, int topk, int n_shared, size_t *out_ids, float *out_weights,
+                         float *out_logits, float *cache_Gsel, float *cache_Usel, float *cache_Ysel,
+                         float *cache_Gs, float *cache_Us);
 /* Exact fp32 product through the T-MAC tables: activation LUT of X, bit
  * planes of every column of W [k][h] (row-major), lookups, and the sign
  * correction Y = (float)((2o - (n-1)*ws*rowsum)/(n-1)); k % 32 != 0 takes

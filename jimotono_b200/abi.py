@@ -37,6 +37,10 @@ PROTOTYPES = {
     "jt_lowbit_fakequant": (I, [P, P, SZ, I]),
     "jt_lowbit_col_to_idx": (I, [P, SZ, I, P, P]),
     "jt_lowbit_gemm_lut": (I, [P, P, P, I, I, I, I]),
+    "jt_moe_fwd_batch": (I, [P] * 9 + [I] * 6 + [P] * 7 + [F] + [P] * 5),
+    "jt_moe_fwd_batch_unchecked": (I, [P] * 9 + [I] * 6 + [P] * 7 + [F] + [P] * 5),
+    "jt_moe_fwd": (I, [P] * 9 + [I] * 5 + [P] * 8),
+    "jt_moe_fwd_unchecked": (I, [P] * 9 + [I] * 5 + [P] * 8),
     "jt_tmac_qlut_bytes": (I, [SZ, SZ, P]),
     "jt_tmac_param_bytes": (I, [SZ, SZ, P]),
     "jt_tmac_lut_ctor": (I, [P, SZ, SZ, P, P, P]),

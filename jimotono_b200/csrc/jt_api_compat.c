@@ -13,8 +13,6 @@
 #include "jt_internal.h"
 #include "jt_stage.h"
 
-int jtk_topk_any(const float *logits, int n, int k, uint32_t *taken, int32_t *ids, float *w, int *flag,
-                 cudaStream_t stream);
 int jtk_gemm_f32_seq(const float *A, const float *B, float *C, int M, int N, int K, cudaStream_t stream);
 int jtk_transpose_f32(const float *src, float *dst, int rows, int cols, cudaStream_t stream);
 int jtk_lowbit_absmax(const float *w, size_t n, unsigned long long *maxbits, int *bad, cudaStream_t stream);
@@ -68,7 +66,7 @@ int jt_routing_topk(const float *logits, size_t n, size_t k, size_t *out_ids, fl
         goto out;
     }
     if (cudaMemsetAsync(dflag, 0, 64, st) != cudaSuccess || jt_stage_h2d(dl, logits, n * sizeof(float)) ||
-        jtk_topk_any(dl, (int)n, (int)k, taken, dids, dw, dflag, st) != 0 ||
+        jtk_topk_any(dl, 1, (int)n, (int)k, taken, dids, dw, dflag, st) != 0 ||
         jt_stage_d2h(&flag, dflag, sizeof(int)) || jt_stage_d2h(hids, dids, k * sizeof(int32_t)) ||
         jt_stage_d2h(hw, dw, k * sizeof(float)) || jt_stage_sync()) {
         rc = cuda_fail();
@@ -355,15 +353,9 @@ int jt_lowbit_col_to_idx(const float *col, size_t k, int bits, uint8_t *idx, flo
 }
 
 /* ---------------------------------------------------------------- tmac.c / lowbit.c:158-267 */
-int jtk_tmac_ctor(const float *act, size_t n, size_t k, int8_t *qlut, float *scales, float *biases,
-                  unsigned long long *err, cudaStream_t stream);
 int jtk_tmac_lookup_one(const int8_t *qlut, const uint8_t *idx, const float *scales, const float *biases,
                         size_t ngroups, size_t nblocks, int bits, float w_scale, float *out, int *flag,
                         cudaStream_t stream);
-int jtk_lut_gemm(const float *X, const float *W, const int8_t *qlut, const float *scales, const float *biases,
-                 double *maxa, void *idxT, double *rowsum, float *Y, int me, int h, int k, int bits,
-                 unsigned long long *err, cudaStream_t stream);
-int jtk_gemm_f64acc(const float *X, const float *W, float *Y, int me, int h, int k, cudaStream_t stream);
 
 #define TMAC_G 4          /* tmac.h:44 */
 #define TMAC_LUT_HALF 8   /* tmac.h:45 */
@@ -571,7 +563,7 @@ int jt_lowbit_gemm_lut(const float *X, const float *W, float *Y, int me, int h, 
     }
     if (k % TMAC_ACT_GROUP != 0) {
         if (jt_stage_h2d(dx, X, nx * sizeof(float)) || jt_stage_h2d(dw, W, nw * sizeof(float)) ||
-            jtk_gemm_f64acc(dx, dw, dy, me, h, k, st) != 0 || jt_stage_d2h(Y, dy, ny * sizeof(float)) ||
+            jtk_gemm_f64acc(dx, dw, 0, h, 1, NULL, dy, me, h, k, st) != 0 || jt_stage_d2h(Y, dy, ny * sizeof(float)) ||
             jt_stage_sync()) {
             rc = cuda_fail();
             goto out;
@@ -594,7 +586,7 @@ int jt_lowbit_gemm_lut(const float *X, const float *W, float *Y, int me, int h, 
         }
         if (jt_stage_h2d(dx, X, nx * sizeof(float)) || jt_stage_h2d(dw, W, nw * sizeof(float)) ||
             jtk_tmac_ctor(dx, (size_t)me, (size_t)k, dq, ds, dbi, derr, st) != 0 ||
-            jtk_lut_gemm(dx, dw, dq, ds, dbi, dmx, didx, drs, dy, me, h, k, bits, derr + 1, st) != 0 ||
+            jtk_lut_gemm(dx, dw, 1, 0, h, 1, NULL, dq, ds, dbi, dmx, didx, drs, dy, me, h, k, bits, derr + 1, st) != 0 ||
             jt_stage_d2h(keys, derr, sizeof keys) || jt_stage_sync()) {
             rc = cuda_fail();
             goto out;

@@ -18,12 +18,17 @@ namespace {
 // then strictly greater values replace it, so ties go to the lowest index
 // and taken entries count as -inf).  Then the softmax of routing.c:54-73 by
 // thread 0: float max, double exp sum, w = (float)e * (float)(1/sum).
-// flag[0] = 1 when the softmax sum is not finite and positive.
+// flag[0] = 1 when the softmax sum is not finite and positive.  One CTA
+// per token (blockIdx.x): logits [T][n], taken [T][ceil(n/32)], ids / w [T][k].
 __global__ void __launch_bounds__(1024) k_topk_any(const float *__restrict__ logits, int n, int k,
                                                    uint32_t *__restrict__ taken, int32_t *__restrict__ ids,
                                                    float *__restrict__ w, int *flag) {
     __shared__ float sv[32];
     __shared__ int si[32];
+    logits += (size_t)blockIdx.x * n;
+    taken += (size_t)blockIdx.x * ((n + 31) / 32);
+    ids += (size_t)blockIdx.x * k;
+    w += (size_t)blockIdx.x * k;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
     for (int i = threadIdx.x; i < (n + 31) / 32; i += blockDim.x) taken[i] = 0;
     __syncthreads();
@@ -357,19 +362,32 @@ __global__ void __launch_bounds__(256) k_tmac_lookup_one(const int8_t *__restric
     }
 }
 
-// Column max-abs of W [k][h] (row-major) in double, for lowbit.c:228-237's
-// per-column col_to_idx; a non-finite column posts key j*(me+1) (EINVAL).
-__global__ void __launch_bounds__(256) k_col_absmax(const float *__restrict__ W, int k, int h, int me,
-                                                     double *__restrict__ maxa,
+// Weight columns of the LUT GEMM.  Column j of expert e has k elements,
+// element t at W + e*ws + t*st + j*sj: st = h, sj = 1 for a row-major
+// [k][h] matrix (lowbit.c:228-231), st = 1, sj = k for a [h][k] matrix
+// whose rows are the columns (the transposed gate/up weights of
+// moe_layer.c:1301-1332).
+struct WCols {
+    const float *W;
+    long long ws, st, sj;
+    __device__ __forceinline__ float at(int e, int t, int j) const {
+        return W[(long long)e * ws + (long long)t * st + (long long)j * sj];
+    }
+};
+
+// Column max-abs in double for lowbit.c:103-115, one (32 columns x 8 row
+// slices) CTA per column block and expert; a non-finite column posts key
+// (e*h + j)*(me+1) (EINVAL).
+__global__ void __launch_bounds__(256) k_col_absmax(WCols w, int k, int h, int me, double *__restrict__ maxa,
                                                      unsigned long long *__restrict__ err) {
     __shared__ double sm[8][32];
     __shared__ int sbad[8][32];
-    const int j = blockIdx.x * 32 + threadIdx.x;
+    const int j = blockIdx.x * 32 + threadIdx.x, e = blockIdx.y;
     double m = 0.0;
     int bad = 0;
     if (j < h)
         for (int t = threadIdx.y; t < k; t += 8) {
-            const double v = (double)W[(size_t)t * h + j];
+            const double v = (double)w.at(e, t, j);
             bad |= !isfinite(v);
             m = fmax(m, fabs(v));
         }
@@ -381,29 +399,30 @@ __global__ void __launch_bounds__(256) k_col_absmax(const float *__restrict__ W,
             m = fmax(m, sm[y][threadIdx.x]);
             bad |= sbad[y][threadIdx.x];
         }
-        maxa[j] = m;
-        if (bad) atomicMin(err, ((unsigned long long)j * (unsigned long long)(me + 1)) << 1);
+        maxa[(size_t)e * h + j] = m;
+        if (bad) atomicMin(err, ((unsigned long long)((long long)e * h + j) * (unsigned long long)(me + 1)) << 1);
     }
 }
 
 // Bit planes of every column (lowbit.c:117-137) in the layout the LUT GEMM
-// reads: idxT[(b*nb + bb)*h + j] holds the 8 index bytes of groups
-// bb*8 .. bb*8+7 of column j, plane b.  One thread per (bb, j).
-__global__ void k_col_planes(const float *__restrict__ W, int k, int h, int bits, const double *__restrict__ maxa,
+// reads: idxT[((e*bits + b)*nb + bb)*h + j] holds the 8 index bytes of
+// groups bb*8 .. bb*8+7 of column j, plane b.  One thread per (bb, j).
+__global__ void k_col_planes(WCols w, int k, int h, int bits, const double *__restrict__ maxa,
                              uint2 *__restrict__ idxT) {
     const int j = blockIdx.x * blockDim.x + threadIdx.x;
-    const int bb = blockIdx.y;
+    const int bb = blockIdx.y, e = blockIdx.z;
     if (j >= h) return;
     const int nb = k / 32, nl = 1 << bits;
-    const double m = maxa[j];
+    const double m = maxa[(size_t)e * h + j];
     uint32_t pl[4][2] = {{0, 0}, {0, 0}, {0, 0}, {0, 0}};
     for (int t = 0; t < 32; ++t) {
-        const int li = level(W[(size_t)(bb * 32 + t) * h + j], m, nl);
+        const int li = level(w.at(e, bb * 32 + t, j), m, nl);
         const int g = t >> 2, jj = t & 3;
         for (int b = 0; b < bits; ++b)
             if ((li >> b) & 1) pl[b][g >> 2] |= 1u << (8 * (g & 3) + jj);
     }
-    for (int b = 0; b < bits; ++b) idxT[((size_t)b * nb + bb) * h + j] = make_uint2(pl[b][0], pl[b][1]);
+    for (int b = 0; b < bits; ++b)
+        idxT[(((size_t)e * bits + b) * nb + bb) * h + j] = make_uint2(pl[b][0], pl[b][1]);
 }
 
 // Row sums of X in double, ascending t (lowbit.c:217-224).
@@ -416,19 +435,23 @@ __global__ void k_row_sum_d(const float *__restrict__ X, int me, int k, double *
 }
 
 // The LUT GEMM of lowbit.c:226-257: thread (m, j) runs lookup_accum over
-// row m's table and column j's planes, then the sign correction
-// Y = (float)((2o - ((n-1)*ws)*rowsum) / (n-1)).  A non-finite o posts key
-// j*(me+1) + m + 1 (ERANGE), ordered after column j's own col_to_idx check.
+// row m's table and column j's planes of row m's expert (rexp[m], or 0),
+// then the sign correction Y = (float)((2o - ((n-1)*ws)*rowsum) / (n-1)).
+// A non-finite o posts key j*(me+1) + m + 1 (ERANGE), ordered after column
+// j's own col_to_idx check.
 __global__ void __launch_bounds__(256) k_lut_gemm(const int8_t *__restrict__ qlut, const float *__restrict__ scales,
                                                    const float *__restrict__ biases, const uint2 *__restrict__ idxT,
                                                    const double *__restrict__ maxa,
-                                                   const double *__restrict__ rowsum, float *__restrict__ Y, int me,
+                                                   const double *__restrict__ rowsum,
+                                                   const int32_t *__restrict__ rexp, float *__restrict__ Y, int me,
                                                    int h, int k, int bits, unsigned long long *__restrict__ err) {
     const int j = blockIdx.x * 32 + threadIdx.x;
     const int m = blockIdx.y * 8 + threadIdx.y;
     if (j >= h || m >= me) return;
     const int nb = k / 32;
-    const float ws = (float)maxa[j];
+    const int e = rexp ? rexp[m] : 0;
+    const float ws = (float)maxa[(size_t)e * h + j];
+    const uint2 *planes = idxT + (size_t)e * bits * nb * h;
     const uint4 *qrow = reinterpret_cast<const uint4 *>(qlut + (size_t)m * nb * 64);
     double total = 0.0;
     for (int bb = 0; bb < nb; ++bb) {
@@ -443,7 +466,7 @@ __global__ void __launch_bounds__(256) k_lut_gemm(const int8_t *__restrict__ qlu
         }
         const double sc = (double)scales[(size_t)m * nb + bb], bi = (double)biases[(size_t)m * nb + bb];
         for (int b = 0; b < bits; ++b) {
-            const uint2 i8 = idxT[((size_t)b * nb + bb) * h + j];
+            const uint2 i8 = planes[((size_t)b * nb + bb) * h + j];
             total = __dadd_rn(total, tmac_contrib(sc, bi, tmac_plane(q8, i8), b));
         }
     }
@@ -458,16 +481,18 @@ __global__ void __launch_bounds__(256) k_lut_gemm(const int8_t *__restrict__ qlu
     Y[(size_t)m * h + j] = (float)__ddiv_rn(__dsub_rn(__dmul_rn(2.0, (double)o), corr), n1);
 }
 
-// lowbit.c:143-156: the K % 32 != 0 fallback, Y = (float) sum_t X*W in
-// double, ascending t (products of floats are exact in double).
-__global__ void k_gemm_f64acc(const float *__restrict__ X, const float *__restrict__ W, float *__restrict__ Y,
-                              int me, int h, int k) {
+// lowbit.c:143-156: the k % 32 != 0 fallback, Y = (float) sum_t X*W in
+// double, ascending t (products of floats are exact in double); W column j
+// of row m's expert as in WCols.
+__global__ void k_gemm_f64acc(const float *__restrict__ X, WCols w, const int32_t *__restrict__ rexp,
+                              float *__restrict__ Y, int me, int h, int k) {
     const int j = blockIdx.x * blockDim.x + threadIdx.x;
     if (j >= h) return;
     for (int m = blockIdx.y; m < me; m += gridDim.y) {
+        const int e = rexp ? rexp[m] : 0;
         double acc = 0.0;
         for (int t = 0; t < k; ++t)
-            acc = __dadd_rn(acc, __dmul_rn((double)X[(size_t)m * k + t], (double)W[(size_t)t * h + j]));
+            acc = __dadd_rn(acc, __dmul_rn((double)X[(size_t)m * k + t], (double)w.at(e, t, j)));
         Y[(size_t)m * h + j] = (float)acc;
     }
 }
@@ -501,38 +526,43 @@ extern "C" int jtk_tmac_lookup_one(const int8_t *qlut, const uint8_t *idx, const
     return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 
-// LUT GEMM after the table is built: column max-abs, planes, row sums, the
-// lookups.  *err is reset here and receives the first column/lookup error.
-extern "C" int jtk_lut_gemm(const float *X, const float *W, const int8_t *qlut, const float *scales,
-                            const float *biases, double *maxa, void *idx_planes, double *rowsum, float *Y,
-                            int me, int h, int k, int bits, unsigned long long *err, cudaStream_t stream) {
-    uint2 *idxT = static_cast<uint2 *>(idx_planes);
-    if (me <= 0 || h <= 0 || k <= 0 || k % 32 || (bits != 2 && bits != 4) || (me + 7) / 8 > 65535 ||
-        k / 32 > 65535)
+// LUT GEMM after the row tables are built (jtk_tmac_ctor): column
+// max-abs and bit planes of every expert's columns, row sums, the lookups.
+// *err is reset here and receives the first column / lookup error.  rexp
+// [me] maps rows to experts (NULL: one expert).
+extern "C" int jtk_lut_gemm(const float *X, const float *W, int E, long long ws, long long st, long long sj,
+                            const int32_t *rexp, const int8_t *qlut, const float *scales, const float *biases,
+                            double *maxa, void *idx_planes, double *rowsum, float *Y, int me, int h, int k,
+                            int bits, unsigned long long *err, cudaStream_t stream) {
+    if (me <= 0 || h <= 0 || k <= 0 || E <= 0 || E > 65535 || k % 32 || (bits != 2 && bits != 4) ||
+        (me + 7) / 8 > 65535 || k / 32 > 65535)
         return -1;
+    uint2 *idxT = static_cast<uint2 *>(idx_planes);
+    const WCols w{W, ws, st, sj};
     if (cudaMemsetAsync(err, 0xff, sizeof(unsigned long long), stream) != cudaSuccess) return -4;
     const unsigned gx = (unsigned)((h + 31) / 32);
-    k_col_absmax<<<gx, dim3(32, 8), 0, stream>>>(W, k, h, me, maxa, err);
-    k_col_planes<<<dim3((unsigned)((h + 127) / 128), (unsigned)(k / 32)), 128, 0, stream>>>(W, k, h, bits, maxa,
-                                                                                           idxT);
+    k_col_absmax<<<dim3(gx, (unsigned)E), dim3(32, 8), 0, stream>>>(w, k, h, me, maxa, err);
+    k_col_planes<<<dim3((unsigned)((h + 127) / 128), (unsigned)(k / 32), (unsigned)E), 128, 0, stream>>>(
+        w, k, h, bits, maxa, idxT);
     k_row_sum_d<<<(me + 127) / 128, 128, 0, stream>>>(X, me, k, rowsum);
     k_lut_gemm<<<dim3(gx, (unsigned)((me + 7) / 8)), dim3(32, 8), 0, stream>>>(qlut, scales, biases, idxT, maxa,
-                                                                              rowsum, Y, me, h, k, bits, err);
+                                                                              rowsum, rexp, Y, me, h, k, bits, err);
     return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 
-extern "C" int jtk_gemm_f64acc(const float *X, const float *W, float *Y, int me, int h, int k,
-                               cudaStream_t stream) {
+extern "C" int jtk_gemm_f64acc(const float *X, const float *W, long long ws, long long st, long long sj,
+                               const int32_t *rexp, float *Y, int me, int h, int k, cudaStream_t stream) {
     if (me <= 0 || h <= 0 || k <= 0) return -1;
     const unsigned gy = (unsigned)(me < 65535 ? me : 65535);
-    k_gemm_f64acc<<<dim3((unsigned)((h + 127) / 128), gy), 128, 0, stream>>>(X, W, Y, me, h, k);
+    k_gemm_f64acc<<<dim3((unsigned)((h + 127) / 128), gy), 128, 0, stream>>>(X, WCols{W, ws, st, sj}, rexp, Y,
+                                                                            me, h, k);
     return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 
-extern "C" int jtk_topk_any(const float *logits, int n, int k, uint32_t *taken, int32_t *ids, float *w,
+extern "C" int jtk_topk_any(const float *logits, int T, int n, int k, uint32_t *taken, int32_t *ids, float *w,
                             int *flag, cudaStream_t stream) {
-    if (n <= 0 || k <= 0 || k > n) return -1;
-    k_topk_any<<<1, 1024, 0, stream>>>(logits, n, k, taken, ids, w, flag);
+    if (T <= 0 || n <= 0 || k <= 0 || k > n) return -1;
+    k_topk_any<<<T, 1024, 0, stream>>>(logits, n, k, taken, ids, w, flag);
     return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 

@@ -118,6 +118,22 @@ int jtk_lowbit_gemv(const int8_t *a, float sa, const uint8_t *w2, const uint16_t
                     const uint8_t *w4, const uint16_t *s4, int n4, int K, float *y,
                     cudaStream_t stream);
 
+/* T-MAC LUT kernels (jt_compat.cu).  Weight column j of expert e has k
+ * elements at W + e*ws + t*st + j*sj.  Error keys (atomicMin, all ones =
+ * none): position << 1 | kind (0 EINVAL, 1 ERANGE). */
+int jtk_tmac_ctor(const float *act, size_t n, size_t k, int8_t *qlut, float *scales, float *biases,
+                  unsigned long long *err, cudaStream_t stream);
+int jtk_lut_gemm(const float *X, const float *W, int E, long long ws, long long st, long long sj,
+                 const int32_t *rexp, const int8_t *qlut, const float *scales, const float *biases,
+                 double *maxa, void *idx_planes, double *rowsum, float *Y, int me, int h, int k, int bits,
+                 unsigned long long *err, cudaStream_t stream);
+int jtk_gemm_f64acc(const float *X, const float *W, long long ws, long long st, long long sj,
+                    const int32_t *rexp, float *Y, int me, int h, int k, cudaStream_t stream);
+/* Top-k + softmax of routing.c:16-76 for T tokens of n logits (one CTA per
+ * token); taken [T][ceil(n/32)] scratch; flag[0] = 1 on a bad softmax. */
+int jtk_topk_any(const float *logits, int T, int n, int k, uint32_t *taken, int32_t *ids, float *w, int *flag,
+                 cudaStream_t stream);
+
 /* Device error word shared by all kernels of the library (0 = clean). */
 int jtk_read_and_clear_error(int *out_code);
 int *jtk_error_word(void);

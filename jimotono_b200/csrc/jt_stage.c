@@ -9,8 +9,6 @@
 #include <pthread.h>
 #include <string.h>
 
-#define JT_STAGE_SLOTS 16
-
 static pthread_mutex_t g_lock = PTHREAD_MUTEX_INITIALIZER;
 static void *g_buf[JT_STAGE_SLOTS];
 static size_t g_cap[JT_STAGE_SLOTS];

@@ -28,8 +28,11 @@ enum {
     JT_SLOT_AUX1,
     JT_SLOT_AUX2,
     JT_SLOT_AUX3,
-    JT_SLOT_AUX4
+    JT_SLOT_AUX4,
+    JT_SLOT_L0 /* first of the slots private to the layer entry points */
 };
+
+#define JT_STAGE_SLOTS 96
 
 void jt_stage_lock(void);
 void jt_stage_unlock(void);

@@ -107,6 +107,7 @@ def ref() -> C.CDLL:
             "jt_transpose_f32": (I, [P, P, I, I]),
             "jt_moe_fwd_batch": (I, [P] * 9 + [I] * 6 + [P] * 7 + [F] + [P] * 5),
             "jt_moe_fwd_batch_unchecked": (I, [P] * 9 + [I] * 6 + [P] * 7 + [F] + [P] * 5),
+            "jt_moe_fwd": (I, [P] * 9 + [I] * 5 + [P] * 8),
         }
         for n, (r, a) in protos.items():
             fn = getattr(h, n)
