@@ -253,6 +253,31 @@ __device__ __forceinline__ void fold_chunk(float2 *r2, const uint32_t (&a)[32], 
     }
 }
 
+// Fold 16 drained columns (columns c0 .. c0+15 of the warp's 32) of one
+// 64-K unit into r2[c0/2 .. c0/2+7]; same arithmetic as fold_chunk.
+template <int MODE>
+__device__ __forceinline__ void fold16(float2 *r2, const uint32_t (&a)[16], float s, const float *blk, int hs_ld,
+                                       int g, int c0) {
+    const float2 s2 = make_float2(s, s);
+    const uint32_t hv_step = static_cast<uint32_t>(hs_ld) * 4u;
+    uint32_t hv_addr = jt::smem_u32(blk + g) + static_cast<uint32_t>(c0) * hv_step;
+#pragma unroll
+    for (int j = 0; j < 16; j += 2) {
+        float2 &rr = r2[(c0 + j) / 2];
+        const float2 pf = __fadd2_rn(as_f2(a[j], a[j + 1]), make_float2(-kMagicF, -kMagicF));
+        if (MODE == GU_ROUTED) {
+            rr = __ffma2_rn(pf, s2, rr);
+        } else {
+            float2 hv;
+            asm volatile("ld.shared.f32 %0, [%1];" : "=f"(hv.x) : "r"(hv_addr));
+            asm volatile("ld.shared.f32 %0, [%1];" : "=f"(hv.y) : "r"(hv_addr + hv_step));
+            hv_addr += 2u * hv_step;
+            const float2 t = (MODE == DN_ROUTED) ? __fmul2_rn(pf, s2) : pf;
+            rr = __ffma2_rn(t, hv, rr);
+        }
+    }
+}
+
 // MMA N for a tile of `rows` token rows: rows rounded up to 16 (the kind::i8
 // N granularity at M = 128), at most kBN.
 __device__ __forceinline__ int mma_n(int rows) {
@@ -582,14 +607,30 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                 }
                 jt::tc_fence_after();
                 if (active) {
-#pragma unroll 1
-                    for (int h = 0; h < (C::kMagic ? 2 : 1); ++h) {
-                        const int un = 2 * ps + h;  // 64-K group index (magic modes)
-                        const float s0 = C::kPacked ? __half2float(sc_ptr[un * sc_stride]) : 1.0f;
+                    if constexpr (C::kMagic) {
+                        // four 16-column chunks (two units x two halves); the
+                        // load of chunk i+1 is in flight while chunk i folds
+                        const uint32_t t0 = tlane + 2u * g * kBN;
+                        const float s0 = C::kPacked ? __half2float(sc_ptr[(2 * ps) * sc_stride]) : 1.0f;
+                        const float s1 = C::kPacked ? __half2float(sc_ptr[(2 * ps + 1) * sc_stride]) : 1.0f;
+                        uint32_t a0[16], a1[16];
+                        jt::tmem_ld16(t0, a0);
+                        jt::tmem_wait_ld16(a0);
+                        jt::tmem_ld16(t0 + 16, a1);
+                        fold16<MODE>(r2, a0, s0, blk, p.hs_ld, 2 * ps, 0);
+                        jt::tmem_wait_ld16(a1);
+                        jt::tmem_ld16(t0 + kBN, a0);
+                        fold16<MODE>(r2, a1, s0, blk, p.hs_ld, 2 * ps, 16);
+                        jt::tmem_wait_ld16(a0);
+                        jt::tmem_ld16(t0 + kBN + 16, a1);
+                        fold16<MODE>(r2, a0, s1, blk, p.hs_ld, 2 * ps + 1, 0);
+                        jt::tmem_wait_ld16(a1);
+                        fold16<MODE>(r2, a1, s1, blk, p.hs_ld, 2 * ps + 1, 16);
+                    } else {
                         uint32_t a[32];
-                        jt::tmem_ld32(tlane + (C::kMagic ? (2u * g + h) : g) * kBN, a);
+                        jt::tmem_ld32(tlane + g * kBN, a);
                         jt::tmem_wait_ld();
-                        fold_chunk<MODE>(r2, a, s0, blk, p.hs_ld, un);
+                        fold_chunk<MODE>(r2, a, 1.0f, blk, p.hs_ld, 0);
                     }
                 }
                 jt::tc_fence_before();
@@ -616,25 +657,47 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                     ok = false;
                     break;
                 }
-                // pass 2: one warp per token row (rows ew, ew+16, ...): lane l
-                // forms h = SwiGLU(g, u) (moe_layer.c:146-148) of channels 2l,
-                // 2l+1, the row's 64 channels are requantized together
-                // (w8a8.c:688-747) and stored as 64 contiguous codes.
-                for (int j = ew; j < nrow; j += kEpiWarps) {
-                    const float2 g2 = *reinterpret_cast<const float2 *>(h_tile + j * 64 + 2 * lane);
-                    const float2 u2 = *reinterpret_cast<const float2 *>(h_tile + kBN * 64 + j * 64 + 2 * lane);
-                    const float h0 = jt::swiglu(g2.x, u2.x), h1 = jt::swiglu(g2.y, u2.y);
-                    const bool bad = !isfinite(h0) || !isfinite(h1);
-                    float m = fmaxf(fabsf(h0), fabsf(h1));
+                // pass 2: one warp per token row (rows ew, ew+16, ...), four
+                // rows at a time so their chains overlap: lane l forms h =
+                // SwiGLU(g, u) (moe_layer.c:146-148) of channels 2l, 2l+1, the
+                // row's 64 channels are requantized together (w8a8.c:688-747)
+                // and stored as 64 contiguous codes.
+                constexpr int kRB = 4;
+                for (int jb = ew; jb < nrow; jb += kRB * kEpiWarps) {
+                    float h0[kRB], h1[kRB], m[kRB];
+                    bool bad = false;
 #pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                    for (int i = 0; i < kRB; ++i) {
+                        const int j = jb + i * kEpiWarps;
+                        h0[i] = 0.0f;
+                        h1[i] = 0.0f;
+                        if (j < nrow) {
+                            const float2 g2 = *reinterpret_cast<const float2 *>(h_tile + j * 64 + 2 * lane);
+                            const float2 u2 =
+                                *reinterpret_cast<const float2 *>(h_tile + kBN * 64 + j * 64 + 2 * lane);
+                            h0[i] = jt::swiglu(g2.x, u2.x);
+                            h1[i] = jt::swiglu(g2.y, u2.y);
+                        }
+                        bad |= !isfinite(h0[i]) || !isfinite(h1[i]);
+                        m[i] = fmaxf(fabsf(h0[i]), fabsf(h1[i]));
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                        for (int i = 0; i < kRB; ++i) m[i] = fmaxf(m[i], __shfl_xor_sync(0xffffffffu, m[i], o));
                     if (__any_sync(0xffffffffu, bad) && lane == 0) atomicExch(err, JT_KERR_NONFINITE);
-                    const jt::QuantBlockF qb = jt::quant_block_f(m);
-                    const int c0 = jt::quant_code_f(h0, qb), c1 = jt::quant_code_f(h1, qb);
-                    const int row = info.y + j;
-                    const uint16_t pair = (uint16_t)(uint8_t)(int8_t)c0 | ((uint16_t)(uint8_t)(int8_t)c1 << 8);
-                    *reinterpret_cast<uint16_t *>(p.hq + (size_t)row * p.n_ch + info.w + 2 * lane) = pair;
-                    if (lane == 0) p.hs[(size_t)row * p.hs_ld + info.w / 64] = qb.scale_f;
+#pragma unroll
+                    for (int i = 0; i < kRB; ++i) {
+                        const int j = jb + i * kEpiWarps;
+                        if (j >= nrow) continue;
+                        const jt::QuantBlockF qb = jt::quant_block_f(m[i]);
+                        const int c0 = jt::quant_code_f(h0[i], qb), c1 = jt::quant_code_f(h1[i], qb);
+                        const int row = info.y + j;
+                        const uint16_t pair =
+                            (uint16_t)(uint8_t)(int8_t)c0 | ((uint16_t)(uint8_t)(int8_t)c1 << 8);
+                        *reinterpret_cast<uint16_t *>(p.hq + (size_t)row * p.n_ch + info.w + 2 * lane) = pair;
+                        if (lane == 0) p.hs[(size_t)row * p.hs_ld + info.w / 64] = qb.scale_f;
+                    }
                 }
                 // all slot reads (meta) and h_tile reads done before release
                 __syncwarp();

@@ -281,7 +281,8 @@ int launch_epi(const int8_t *X, int ldx, const int8_t *W, int ldw, int M, int N,
     if (M <= 16) return launch_bn<16, EPI>(tmW, X, ldx, M, N, K, sx, sw, sA, out, ldo, stream);
     if (M <= 32) return launch_bn<32, EPI>(tmW, X, ldx, M, N, K, sx, sw, sA, out, ldo, stream);
     if (M <= 64) return launch_bn<64, EPI>(tmW, X, ldx, M, N, K, sx, sw, sA, out, ldo, stream);
-    return launch_bn<128, EPI>(tmW, X, ldx, M, N, K, sx, sw, sA, out, ldo, stream);
+    if (M <= 128) return launch_bn<128, EPI>(tmW, X, ldx, M, N, K, sx, sw, sA, out, ldo, stream);
+    return launch_bn<256, EPI>(tmW, X, ldx, M, N, K, sx, sw, sA, out, ldo, stream);
 }
 
 }  // namespace
