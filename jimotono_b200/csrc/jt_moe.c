@@ -50,6 +50,9 @@ struct jt_b200_moe_plan {
     float *w_raw, *w_fin, *xs, *hs, *hs_s, *y32;
     uint8_t *drop;
     int8_t *xq, *xd, *hq, *hq_s;
+    /* batch-1 path: h codes and scales of every shared expert at once */
+    int8_t *hq_d;
+    float *hs_d;
     /* optional per-stage profiling: events[step][JT_B200_MOE_NSTAGE + 1] */
     cudaEvent_t *prof_ev;
     int prof_max, prof_used;
@@ -105,6 +108,8 @@ int jt_b200_moe_plan_create(const jt_b200_moe_dims *dims, jt_b200_moe_plan **out
         {(void **)&p->y32, T * d * 4},       {(void **)&p->drop, Tk},
         {(void **)&p->xq, T * d},            {(void **)&p->xd, Tk * d},
         {(void **)&p->hq, Tk * f},           {(void **)&p->hq_s, T * fs},
+        {(void **)&p->hq_d, (size_t)(dims->S > 0 ? dims->S : 1) * fs},
+        {(void **)&p->hs_d, (size_t)(dims->S > 0 ? dims->S : 1) * (size_t)hs_ld((int)fs) * 4},
     };
     const size_t nparts = sizeof(parts) / sizeof(parts[0]);
     size_t total = 0;
@@ -254,6 +259,32 @@ int jt_b200_moe_forward(jt_b200_moe_plan *plan, const jt_b200_moe_weights *w, co
     } while (0)
 
     MARK(JT_B200_STAGE_ROUTE);
+    if (T == 1) {
+        /* one token: nothing can be dropped (cap >= 1, k distinct experts);
+         * router, gate/up and down as matrix-vector kernels (jt_decode.cu) */
+        MARK(JT_B200_STAGE_SORT);
+        MARK(JT_B200_STAGE_DISPATCH);
+        MARK(JT_B200_STAGE_SHARED);
+        MARK(JT_B200_STAGE_GATEUP);
+        const int r = jtk_moe_decode(x, logits, bias, plan->ids, plan->w_raw, w->wg, w->wu, w->sg, w->su, w->wd, w->sd,
+                                     w->wsg, w->wsu, w->ssg, w->ssu, w->wsd, w->ssd, d, f, E, k, S, fs,
+                                     plan->xq, plan->xs, plan->hq, plan->hs, hs_ld(f), plan->hq_d,
+                                     plan->hs_d, hs_ld(S > 0 ? fs : 64), plan->perm, plan->pos, plan->off,
+                                     plan->tile_off, plan->meta, plan->drop, plan->w_fin,
+                                     y_bf16 ? NULL : (float *)y, y_bf16 ? (uint16_t *)y : NULL, st);
+        if (r == 0) {
+            MARK(JT_B200_STAGE_DOWN);
+            MARK(JT_B200_STAGE_OUTPUT);
+            MARK(JT_B200_MOE_NSTAGE);
+            return JT_OK;
+        }
+        if (r != -1) {
+            jt_set_last_error("jtk_moe_decode", r);
+            errno = EIO;
+            return JT_ERR_CUDA;
+        }
+        /* shape outside the batch-1 kernels: the batched chain below */
+    }
     LAUNCH(jtk_route_topk(logits, bias, T, E, k, plan->ids, plan->w_raw, st));
     MARK(JT_B200_STAGE_SORT);
     LAUNCH(jtk_moe_sort(plan->ids, plan->w_raw, T, k, E, cap, NULL, plan->hist, plan->off,

@@ -17,95 +17,26 @@
 
 #include "jt_internal.h"
 #include "jt_quant.cuh"
+#include "jt_topk.cuh"
 
 namespace {
 
 constexpr int kChunkTok = 64;  // tokens per sort chunk (chunks are token aligned)
 
 // ------------------------------------------------------------------ top-k
-// One warp per token.  Lane l holds logits l, l+32, ...  Each of the k
-// passes takes the maximum of (taken ? -inf : logit) with ties to the lowest
-// index, exactly the strict '>' scan of routing.c:38-52 (including its
-// behaviour when only -inf values remain).
+// One warp per token (jt_topk.cuh).
 __global__ void k_route_topk(const float *__restrict__ logits, const float *__restrict__ bias,
                              int T, int E, int k, int32_t *__restrict__ ids,
                              float *__restrict__ w, int *err) {
     const int warps = blockDim.x >> 5;
     const int t = blockIdx.x * warps + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
     if (t >= T) return;
     extern __shared__ uint32_t taken_all[];  // warps * ceil(E/32) words
-    const int nw = (E + 31) / 32;
-    uint32_t *taken = taken_all + (threadIdx.x >> 5) * nw;
-    for (int i = lane; i < nw; i += 32) taken[i] = 0;
-    __syncwarp();
-    const float *row = logits + (size_t)t * E;
-    int nan_seen = 0;
-    for (int i = lane; i < E; i += 32) {
-        float v = row[i];
-        if (bias) v = __fadd_rn(v, bias[i]);
-        nan_seen |= (v != v);
-    }
-    if (__any_sync(0xffffffffu, nan_seen)) {
-        if (lane == 0) atomicExch(err, 0x81);
-        return;
-    }
+    uint32_t *taken = taken_all + (threadIdx.x >> 5) * ((E + 31) / 32);
     int32_t sel[64];
     float selv[64];
-    for (int p = 0; p < k; ++p) {
-        float best = 0.0f;
-        int bi = E;  // sentinel: "not set", like best == n in routing.c:40
-        for (int i = lane; i < E; i += 32) {
-            float v = row[i];
-            if (bias) v = __fadd_rn(v, bias[i]);
-            if ((taken[i >> 5] >> (i & 31)) & 1u) v = -INFINITY;
-            if (bi == E || v > best) {
-                best = v;
-                bi = i;
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            // candidate with lower index wins unless the other is strictly larger
-            bool take;
-            if (oi == E) take = false;
-            else if (bi == E) take = true;
-            else if (oi < bi) take = !(best > ov);
-            else take = ov > best;
-            if (take) {
-                best = ov;
-                bi = oi;
-            }
-        }
-        sel[p] = bi;
-        if (lane == 0) atomicOr(&taken[bi >> 5], 1u << (bi & 31));
-        __syncwarp();
-        float lv = row[bi];
-        if (bias) lv = __fadd_rn(lv, bias[bi]);
-        selv[p] = lv;
-    }
-    if (lane == 0) {
-        float mx = selv[0];
-        for (int p = 1; p < k; ++p) mx = (selv[p] > mx) ? selv[p] : mx;
-        double sum = 0.0;
-        float ew[64];
-        for (int p = 0; p < k; ++p) {
-            const double e = exp((double)selv[p] - (double)mx);
-            sum += e;
-            ew[p] = (float)e;
-        }
-        if (!(sum > 0.0) || !isfinite(sum)) {
-            atomicExch(err, 0x82);
-            return;
-        }
-        const float inv = (float)(1.0 / sum);
-        for (int p = 0; p < k; ++p) {
-            ids[(size_t)t * k + p] = sel[p];
-            w[(size_t)t * k + p] = __fmul_rn(ew[p], inv);
-        }
-    }
+    jt::warp_topk_softmax(logits + (size_t)t * E, bias, E, k, taken, sel, selv, ids + (size_t)t * k,
+                          w + (size_t)t * k, err);
 }
 
 // ------------------------------------------------------------------ sort

@@ -1,0 +1,97 @@
+// jt_topk.cuh - top-k + softmax of one token's router logits by one warp,
+// shared by the batched router (jt_route.cu) and the batch-1 layer
+// (jt_decode.cu).
+//
+// Lane l holds logits l, l+32, ...  Each of the k passes takes the maximum
+// of (taken ? -inf : logit [+ bias]) with ties to the lowest index, exactly
+// the strict '>' scan of routing.c:38-52 (including its behaviour when only
+// -inf values remain); then the softmax of routing.c:54-73 by lane 0: float
+// max, double exp sum, w = (float)e * (float)(1/sum).  A NaN logit raises
+// err 0x81 (nothing is written), a bad softmax sum 0x82.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace jt {
+
+// taken: ceil(E/32) words of shared memory owned by this warp; sel/selv: k
+// entries of scratch; ids_out/w_out are written by lane 0 (not on a bad
+// softmax sum).  Returns false on a NaN logit.
+__device__ __forceinline__ bool warp_topk_softmax(const float *__restrict__ row, const float *__restrict__ bias,
+                                                  int E, int k, uint32_t *taken, int32_t *sel, float *selv,
+                                                  int32_t *ids_out, float *w_out, int *err) {
+    const int lane = threadIdx.x & 31;
+    const int nw = (E + 31) / 32;
+    for (int i = lane; i < nw; i += 32) taken[i] = 0;
+    __syncwarp();
+    int nan_seen = 0;
+    for (int i = lane; i < E; i += 32) {
+        float v = row[i];
+        if (bias) v = __fadd_rn(v, bias[i]);
+        nan_seen |= (v != v);
+    }
+    if (__any_sync(0xffffffffu, nan_seen)) {
+        if (lane == 0) atomicExch(err, 0x81);
+        return false;
+    }
+    for (int p = 0; p < k; ++p) {
+        float best = 0.0f;
+        int bi = E;  // sentinel: "not set", like best == n in routing.c:40
+        for (int i = lane; i < E; i += 32) {
+            float v = row[i];
+            if (bias) v = __fadd_rn(v, bias[i]);
+            if ((taken[i >> 5] >> (i & 31)) & 1u) v = -INFINITY;
+            if (bi == E || v > best) {
+                best = v;
+                bi = i;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            // candidate with lower index wins unless the other is strictly larger
+            bool take;
+            if (oi == E) take = false;
+            else if (bi == E) take = true;
+            else if (oi < bi) take = !(best > ov);
+            else take = ov > best;
+            if (take) {
+                best = ov;
+                bi = oi;
+            }
+        }
+        sel[p] = bi;
+        if (lane == 0) atomicOr(&taken[bi >> 5], 1u << (bi & 31));
+        __syncwarp();
+        float lv = row[bi];
+        if (bias) lv = __fadd_rn(lv, bias[bi]);
+        selv[p] = lv;
+    }
+    if (lane == 0) {
+        bool ok = true;
+        float mx = selv[0];
+        for (int p = 1; p < k; ++p) mx = (selv[p] > mx) ? selv[p] : mx;
+        double sum = 0.0;
+        float ew[64];
+        for (int p = 0; p < k; ++p) {
+            const double e = exp((double)selv[p] - (double)mx);
+            sum += e;
+            ew[p] = (float)e;
+        }
+        if (!(sum > 0.0) || !isfinite(sum)) {
+            atomicExch(err, 0x82);
+            ok = false;
+        }
+        if (ok) {
+            const float inv = (float)(1.0 / sum);
+            for (int p = 0; p < k; ++p) {
+                ids_out[p] = sel[p];
+                w_out[p] = __fmul_rn(ew[p], inv);
+            }
+        }
+    }
+    return true;
+}
+
+}  // namespace jt
