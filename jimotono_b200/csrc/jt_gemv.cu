@@ -123,8 +123,8 @@ __device__ __forceinline__ int group_partial(const uint8_t *codes, const uint32_
 // Specialization for K = 2048 (32 groups, lane = group) with the chunk's
 // scales in shared memory: all R rows of the stage are processed with fixed
 // trip counts (rows past nrows hold stale bytes and are not stored), the
-// codes are split with shift + mask into four (INT2) or two (INT4)
-// independent signed dp4a chains.
+// codes are masked in place into four (INT2) or two (INT4) independent
+// unsigned x signed dp4a chains whose 4^j / 16 factors are shifted out.
 template <int BITS, int R>
 __device__ __forceinline__ void consume_k2048(const uint8_t *codes, int nrows, const uint32_t *act,
                                              const int *gsum, const uint16_t *sc, float sa, float *y,
@@ -149,24 +149,23 @@ __device__ __forceinline__ void consume_k2048(const uint8_t *codes, int nrows, c
         if (BITS == 2) {
             const uint4 q = *reinterpret_cast<const uint4 *>(base + rr * kRowBytes);
             const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-            int acc[4] = {0, 0, 0, 0};
+            int acc[4] = {0, 0, 0, 0};  // acc[j] = 4^j * sum(li_j * a)
 #pragma unroll
             for (int i = 0; i < 4; ++i)
 #pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    acc[j] = __dp4a(static_cast<int>((w[i] >> (2 * j)) & 0x03030303u), static_cast<int>(ap[4 * i + j]), acc[j]);
-            p = 2 * ((acc[0] + acc[1]) + (acc[2] + acc[3])) - 3 * asum;
+                for (int j = 0; j < 4; ++j) acc[j] = dp4a_us(w[i] & (0x03030303u << (2 * j)), ap[4 * i + j], acc[j]);
+            p = 2 * ((acc[0] + (acc[1] >> 2)) + ((acc[2] >> 4) + (acc[3] >> 6))) - 3 * asum;
         } else {
             const uint4 q0 = *reinterpret_cast<const uint4 *>(base + rr * kRowBytes);
             const uint4 q1 = *reinterpret_cast<const uint4 *>(base + rr * kRowBytes + 16);
             const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
             int lo = 0, hi = 0;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                lo = __dp4a(static_cast<int>(w[i] & 0x0F0F0F0Fu), static_cast<int>(ap[2 * i]), lo);
-                hi = __dp4a(static_cast<int>((w[i] >> 4) & 0x0F0F0F0Fu), static_cast<int>(ap[2 * i + 1]), hi);
+            for (int i = 0; i < 8; ++i) {  // hi = 16 * sum(li_odd * a)
+                lo = dp4a_us(w[i] & 0x0F0F0F0Fu, ap[2 * i], lo);
+                hi = dp4a_us(w[i] & 0xF0F0F0F0u, ap[2 * i + 1], hi);
             }
-            p = 2 * (lo + hi) - 15 * asum;
+            p = 2 * (lo + (hi >> 4)) - 15 * asum;
         }
         Ps[rr * kPld + lane] = p;
     }
