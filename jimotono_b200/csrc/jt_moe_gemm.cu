@@ -657,46 +657,54 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                     ok = false;
                     break;
                 }
-                // pass 2: one warp per token row (rows ew, ew+16, ...), four
-                // rows at a time so their chains overlap: lane l forms h =
-                // SwiGLU(g, u) (moe_layer.c:146-148) of channels 2l, 2l+1, the
-                // row's 64 channels are requantized together (w8a8.c:688-747)
-                // and stored as 64 contiguous codes.
-                constexpr int kRB = 4;
-                for (int jb = ew; jb < nrow; jb += kRB * kEpiWarps) {
-                    float h0[kRB], h1[kRB], m[kRB];
-                    bool bad = false;
+                // pass 2: four token rows per warp step, eight lanes per
+                // row: lane l forms h = SwiGLU(g, u) (moe_layer.c:146-148) of
+                // channels 8(l%8) .. 8(l%8)+7 of its row, the row's 64
+                // channels are requantized together (w8a8.c:688-747) and
+                // stored as 64 contiguous codes.
+                {
+                    const int sl = lane & 7, gq = lane >> 3;
+                    for (int jb = 4 * ew; jb < nrow; jb += 4 * kEpiWarps) {
+                        const int j = jb + gq;
+                        const bool live = j < nrow;
+                        float h[8];
+                        if (live) {
+                            const float4 *gp = reinterpret_cast<const float4 *>(h_tile + j * 64 + 8 * sl);
+                            const float4 *up =
+                                reinterpret_cast<const float4 *>(h_tile + kBN * 64 + j * 64 + 8 * sl);
+                            const float4 g0 = gp[0], g1 = gp[1], u0 = up[0], u1 = up[1];
+                            const float2 ha = jt::swiglu2(make_float2(g0.x, g0.y), make_float2(u0.x, u0.y));
+                            const float2 hb = jt::swiglu2(make_float2(g0.z, g0.w), make_float2(u0.z, u0.w));
+                            const float2 hc = jt::swiglu2(make_float2(g1.x, g1.y), make_float2(u1.x, u1.y));
+                            const float2 hd = jt::swiglu2(make_float2(g1.z, g1.w), make_float2(u1.z, u1.w));
+                            h[0] = ha.x, h[1] = ha.y, h[2] = hb.x, h[3] = hb.y;
+                            h[4] = hc.x, h[5] = hc.y, h[6] = hd.x, h[7] = hd.y;
+                        } else {
 #pragma unroll
-                    for (int i = 0; i < kRB; ++i) {
-                        const int j = jb + i * kEpiWarps;
-                        h0[i] = 0.0f;
-                        h1[i] = 0.0f;
-                        if (j < nrow) {
-                            const float2 g2 = *reinterpret_cast<const float2 *>(h_tile + j * 64 + 2 * lane);
-                            const float2 u2 =
-                                *reinterpret_cast<const float2 *>(h_tile + kBN * 64 + j * 64 + 2 * lane);
-                            h0[i] = jt::swiglu(g2.x, u2.x);
-                            h1[i] = jt::swiglu(g2.y, u2.y);
+                            for (int i = 0; i < 8; ++i) h[i] = 0.0f;
                         }
-                        bad |= !isfinite(h0[i]) || !isfinite(h1[i]);
-                        m[i] = fmaxf(fabsf(h0[i]), fabsf(h1[i]));
-                    }
+                        bool bad = false;
+                        float m = 0.0f;
 #pragma unroll
-                    for (int o = 16; o > 0; o >>= 1)
+                        for (int i = 0; i < 8; ++i) {
+                            bad |= !isfinite(h[i]);
+                            m = fmaxf(m, fabsf(h[i]));
+                        }
+                        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+                        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+                        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+                        if (__any_sync(0xffffffffu, bad) && lane == 0) atomicExch(err, JT_KERR_NONFINITE);
+                        if (live) {
+                            const jt::QuantBlockF qb = jt::quant_block_f(m);
+                            uint32_t wd[2] = {0u, 0u};
 #pragma unroll
-                        for (int i = 0; i < kRB; ++i) m[i] = fmaxf(m[i], __shfl_xor_sync(0xffffffffu, m[i], o));
-                    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicExch(err, JT_KERR_NONFINITE);
-#pragma unroll
-                    for (int i = 0; i < kRB; ++i) {
-                        const int j = jb + i * kEpiWarps;
-                        if (j >= nrow) continue;
-                        const jt::QuantBlockF qb = jt::quant_block_f(m[i]);
-                        const int c0 = jt::quant_code_f(h0[i], qb), c1 = jt::quant_code_f(h1[i], qb);
-                        const int row = info.y + j;
-                        const uint16_t pair =
-                            (uint16_t)(uint8_t)(int8_t)c0 | ((uint16_t)(uint8_t)(int8_t)c1 << 8);
-                        *reinterpret_cast<uint16_t *>(p.hq + (size_t)row * p.n_ch + info.w + 2 * lane) = pair;
-                        if (lane == 0) p.hs[(size_t)row * p.hs_ld + info.w / 64] = qb.scale_f;
+                            for (int i = 0; i < 8; ++i)
+                                wd[i >> 2] |= (uint32_t)(uint8_t)(int8_t)jt::quant_code_f(h[i], qb) << (8 * (i & 3));
+                            const int row = info.y + j;
+                            *reinterpret_cast<uint2 *>(p.hq + (size_t)row * p.n_ch + info.w + 8 * sl) =
+                                make_uint2(wd[0], wd[1]);
+                            if (sl == 0) p.hs[(size_t)row * p.hs_ld + info.w / 64] = qb.scale_f;
+                        }
                     }
                 }
                 // all slot reads (meta) and h_tile reads done before release

@@ -46,4 +46,41 @@ __device__ __forceinline__ float silu(float g) {
 
 __device__ __forceinline__ float swiglu(float g, float u) { return __fmul_rn(silu(g), u); }
 
+// Two lanes of det_expf at once with packed f32x2 arithmetic for the
+// products and the polynomial, bit for bit the scalar results: the same
+// clamps, rounding of k, two-step reduction, polynomial and scaling.  (A NaN
+// input gives a finite value here; the callers' SwiGLU result is NaN either
+// way.)
+__device__ __forceinline__ float2 det_expf2(float2 x) {
+    x.x = fmaxf(fminf(x.x, 89.0f), -104.0f);
+    x.y = fmaxf(fminf(x.y, 89.0f), -104.0f);
+    const float2 kLog2e = make_float2(0x1.715476p+0f, 0x1.715476p+0f);
+    const float2 t = __fmul2_rn(x, kLog2e);
+    const float2 kf = make_float2(rintf(t.x), rintf(t.y));
+    const float2 nkf = make_float2(-kf.x, -kf.y);
+    float2 r = __ffma2_rn(nkf, make_float2(0x1.62e4p-1f, 0x1.62e4p-1f), x);
+    r = __ffma2_rn(nkf, make_float2(0x1.7f7d1cp-20f, 0x1.7f7d1cp-20f), r);
+    float2 p = make_float2(0x1.a01a02p-13f, 0x1.a01a02p-13f);
+    p = __ffma2_rn(p, r, make_float2(0x1.6c16c2p-10f, 0x1.6c16c2p-10f));
+    p = __ffma2_rn(p, r, make_float2(0x1.111112p-7f, 0x1.111112p-7f));
+    p = __ffma2_rn(p, r, make_float2(0x1.555556p-5f, 0x1.555556p-5f));
+    p = __ffma2_rn(p, r, make_float2(0x1.555556p-3f, 0x1.555556p-3f));
+    p = __ffma2_rn(p, r, make_float2(0x1.0p-1f, 0x1.0p-1f));
+    p = __ffma2_rn(p, r, make_float2(1.0f, 1.0f));
+    p = __ffma2_rn(p, r, make_float2(1.0f, 1.0f));
+    const int k0 = static_cast<int>(kf.x), k1 = static_cast<int>(kf.y);
+    const int a0 = k0 >> 1, b0 = k0 - a0, a1 = k1 >> 1, b1 = k1 - a1;
+    const float2 s1 = make_float2(__int_as_float((a0 + 127) << 23), __int_as_float((a1 + 127) << 23));
+    const float2 s2 = make_float2(__int_as_float((b0 + 127) << 23), __int_as_float((b1 + 127) << 23));
+    return __fmul2_rn(__fmul2_rn(p, s1), s2);
+}
+
+// swiglu() of two lanes at once, bit for bit.
+__device__ __forceinline__ float2 swiglu2(float2 g, float2 u) {
+    const float2 e = det_expf2(make_float2(-g.x, -g.y));
+    const float2 den = __fadd2_rn(make_float2(1.0f, 1.0f), e);
+    const float2 sig = make_float2(__frcp_rn(den.x), __frcp_rn(den.y));
+    return __fmul2_rn(__fmul2_rn(g, sig), u);
+}
+
 }  // namespace jt
