@@ -483,6 +483,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--small", action="store_true",
                     help="time only the MoE layer at 1/8 of config 5 (profiler captures)")
+    ap.add_argument("--part", choices=["cfg1", "cfg2", "cfg3", "cfg4"],
+                    help="time only one secondary configuration and print its JSON (profiler captures)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -501,6 +503,20 @@ def main():
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     hbm_peak, peak_kind = peaks()
+    if args.part:
+        if args.part == "cfg1":
+            out = part_w8a8(torch, steps=args.steps)
+        elif args.part == "cfg4":
+            out = part_gemv(torch, hbm_peak, steps=args.steps)
+        elif args.part == "cfg2":
+            st2 = time_layer(torch, CFG2, 0, 1, args.steps, args.warmup, seed=2, nrot=8, profile=False)
+            out = {"us_per_token_stream": round(st2["ms_per_step"] * 1e3, 2),
+                   "us_per_token_graph": round(time_decode_graph(torch, st2, reps=max(1, args.steps // 8)), 2)}
+        else:
+            st3 = time_layer(torch, CFG3, 0, 1, args.steps, args.warmup, seed=3, zipf=1.1, bf16=True)
+            out = {"ms_per_step": round(st3["ms_per_step"], 4), "stage_ms": [round(v, 4) for v in st3["stage_ms"]]}
+        print(json.dumps({"part": args.part, **out}), flush=True)
+        return
     if args.small:
         st = time_layer(torch, CFG5_SMALL, 0, 1, args.steps, args.warmup, seed=5)
         print(json.dumps({"case": "cfg5/8", "ms_per_step": round(st["ms_per_step"], 4),

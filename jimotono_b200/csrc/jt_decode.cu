@@ -80,24 +80,40 @@ struct DecParams {
 
 // Per-token int8 quantization of x (w8a8.c:688-747, as k_quant_dispatch):
 // codes into sx (shared memory), scale returned; a non-finite value raises
-// the error word and gives an all-zero row.
-__device__ float quant_token(const float *__restrict__ x, int d, int8_t *sx, int *err) {
+// the error word and gives an all-zero row.  With `route`, warp 0 runs the
+// router (jt_topk.cuh, results in sids / sw) while the other warps take the
+// max-abs pass, so the two latencies overlap.
+__device__ float quant_token(const float *__restrict__ x, int d, int8_t *sx, int *err, bool route,
+                             const DecParams &p, uint32_t *taken, int32_t *ssel, float *sselv, int32_t *sids,
+                             float *sw) {
     __shared__ float wm[kGuThreads / 32];
     __shared__ int wb[kGuThreads / 32];
+    const int warp = threadIdx.x >> 5;
     float m = 0.0f;
     int bad = 0;
-    for (int i = threadIdx.x; i < d; i += blockDim.x) {
-        const float v = x[i];
-        bad |= !isfinite(v);
-        m = fmaxf(m, fabsf(v));
-    }
-    for (int o = 16; o > 0; o >>= 1) {
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+    if (route && warp == 0) {
+        sids[threadIdx.x] = threadIdx.x;  // fallback: experts 0..31 (k <= 64 below)
+        sids[threadIdx.x + 32] = threadIdx.x + 32;
+        sw[threadIdx.x] = 0.0f;
+        sw[threadIdx.x + 32] = 0.0f;
+        __syncwarp();
+        jt::warp_topk_softmax(p.logits, p.bias, p.E, p.k, taken, ssel, sselv, sids, sw, err);
+    } else {
+        const int t0 = route ? threadIdx.x - 32 : threadIdx.x;
+        const int nt = route ? blockDim.x - 32 : blockDim.x;
+        for (int i = t0; i < d; i += nt) {
+            const float v = x[i];
+            bad |= !isfinite(v);
+            m = fmaxf(m, fabsf(v));
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+        }
     }
     if ((threadIdx.x & 31) == 0) {
-        wm[threadIdx.x >> 5] = m;
-        wb[threadIdx.x >> 5] = bad;
+        wm[warp] = m;
+        wb[warp] = bad;
     }
     __syncthreads();
     m = 0.0f;
@@ -228,29 +244,23 @@ __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (cb * 64 >= n_ch) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // routed CTAs: the router (every routed CTA alike, jt_topk.cuh) overlaps
+    // the max-abs pass; on a NaN logit or a bad softmax (error word raised)
+    // the slots fall back to experts 0..k-1 with zero weight so every index
+    // stays in range
+    const float xs = quant_token(p.x, p.d, sx, p.err, !shared, p, taken, ssel, sselv, sids, sw);
     int e = 0;
     if (!shared) {
-        // the router, computed by every routed CTA alike (jt_topk.cuh); on a
-        // NaN logit or a bad softmax (error word raised) the slots fall back
-        // to experts 0..k-1 with zero weight so every index stays in range
-        if (threadIdx.x < 64) {
-            sids[threadIdx.x] = threadIdx.x;
-            sw[threadIdx.x] = 0.0f;
-        }
-        __syncthreads();
-        if (warp == 0) jt::warp_topk_softmax(p.logits, p.bias, p.E, p.k, taken, ssel, sselv, sids, sw, p.err);
-        __syncthreads();
         e = sids[slot];
         if (slot == 0 && cb == 0 && threadIdx.x < p.k) {
             p.ids[threadIdx.x] = sids[threadIdx.x];
             p.w[threadIdx.x] = sw[threadIdx.x];
         }
     }
-    const float xs = quant_token(p.x, p.d, sx, p.err);
     if (!shared) permute_int2(sx, p.d, xp, gsum);
     // 128 rows: 0..63 gate, 64..127 up of channels cb*64 + (row & 63); each
     // warp takes kRB consecutive rows per step
-    constexpr int kRB = 4;
+    constexpr int kRB = 8;
     for (int r0 = warp * kRB; r0 < 128; r0 += (kGuThreads / 32) * kRB) {
         const bool up = r0 >= 64;
         const int c0 = cb * 64 + (r0 & 63);
@@ -343,15 +353,39 @@ constexpr int kMaxHp = 8192;  // permuted h words of the routed rows (k * f <= 3
 
 // grid d / 8, 256 threads: warp w computes output channel blockIdx.x*8 + w.
 __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constant__ DecParams p) {
+    __shared__ uint32_t taken[kMaxE / 32];
+    __shared__ int32_t sids[64], ssel[64];
+    __shared__ float sw[64], sselv[64];
     {
-        // shared-expert down rows do not depend on the gate/up grid: start
-        // pulling them into L2, then wait for that grid's results
+        // Everything here is independent of the gate/up grid, which may still
+        // be running: the router again (the same function on the same
+        // logits, so the same experts as the gate/up grid), then the down
+        // rows this warp will read are pulled into L2.
+        if (threadIdx.x < 64) {
+            sids[threadIdx.x] = threadIdx.x;
+            sw[threadIdx.x] = 0.0f;
+        }
+        __syncthreads();
+        if ((threadIdx.x >> 5) == 0)
+            jt::warp_topk_softmax(p.logits, p.bias, p.E, p.k, taken, ssel, sselv, sids, sw, p.err);
+        __syncthreads();
         const int o = blockIdx.x * kDnWarps + (threadIdx.x >> 5);
         const int lane = threadIdx.x & 31;
-        if (o < p.d)
+        if (o < p.d) {
+            const int gf = p.f / 64;
+            for (int q = 0; q < p.k; ++q) {
+                int e = sids[q];
+                e = (e < 0 || e >= p.E) ? 0 : e;
+                const uint8_t *row = p.wd + ((size_t)e * p.d + o) * (p.f / 2);
+                for (int b = lane * 128; b < p.f / 2; b += 32 * 128)
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(row + b));
+                if (lane < gf)
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(p.sd + ((size_t)e * gf + lane) * p.d + o));
+            }
             for (int s = 0; s < p.S; ++s)
                 for (int b = lane * 128; b < p.fs; b += 32 * 128)
                     asm volatile("prefetch.global.L2 [%0];" ::"l"(p.wsd + ((size_t)s * p.d + o) * p.fs + b));
+        }
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");
     // routed h rows (sorted rank order) permuted for INT4 words: for packed
@@ -378,9 +412,9 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constan
     const int o = blockIdx.x * kDnWarps + warp;
     if (o >= p.d) return;
     double ya = 0.0;
-    // routed pairs in slot order (moe_layer.c:1443-1463), four rows' loads
+    // routed pairs in slot order (moe_layer.c:1443-1463), eight rows' loads
     // in flight at a time
-    constexpr int kRB = 4;
+    constexpr int kRB = 8;
     for (int q0 = 0; q0 < p.k; q0 += kRB) {
         const uint32_t *row[kRB];
         const __half *sdo[kRB];
@@ -390,7 +424,7 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constan
 #pragma unroll
         for (int i = 0; i < kRB; ++i) {
             const int q = q0 + i < p.k ? q0 + i : p.k - 1;
-            int e = p.ids[q];
+            int e = sids[q];
             e = (e < 0 || e >= p.E) ? 0 : e;
             rr[i] = p.pos[q];
             row[i] = reinterpret_cast<const uint32_t *>(p.wd + ((size_t)e * p.d + o) * (p.f / 2));
@@ -430,7 +464,7 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constan
         }
 #pragma unroll
         for (int i = 0; i < kRB; ++i)
-            if (q0 + i < p.k) ya = __dadd_rn(ya, __dmul_rn((double)p.w[q0 + i], (double)acc[i]));
+            if (q0 + i < p.k) ya = __dadd_rn(ya, __dmul_rn((double)sw[q0 + i], (double)acc[i]));
     }
     // shared experts in s order (moe_layer.c:1549-1559)
     for (int s = 0; s < p.S; ++s) {
