@@ -255,10 +255,27 @@ __device__ __forceinline__ void fold_chunk(float2 *r2, const uint32_t (&a)[32], 
 
 // Fold 16 drained columns (columns c0 .. c0+15 of the warp's 32) of one
 // 64-K unit into r2[c0/2 .. c0/2+7]; same arithmetic as fold_chunk.
-template <int MODE>
+// hvT (down modes, may be NULL): the tile's activation group scales
+// transposed to [group][kBN] and offset to the warp's first column, read
+// four columns per shared-memory load.
+template <int MODE, int TP>
 __device__ __forceinline__ void fold16(float2 *r2, const uint32_t (&a)[16], float s, const float *blk, int hs_ld,
-                                       int g, int c0) {
+                                       int g, int c0, const float *hvT) {
     const float2 s2 = make_float2(s, s);
+    if constexpr (TP != 0) {
+        const float4 *h4p = reinterpret_cast<const float4 *>(hvT + (size_t)g * kBN + c0);
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) {
+            const float4 h4 = h4p[j / 4];
+            const float2 pa = __fadd2_rn(as_f2(a[j], a[j + 1]), make_float2(-kMagicF, -kMagicF));
+            const float2 pb = __fadd2_rn(as_f2(a[j + 2], a[j + 3]), make_float2(-kMagicF, -kMagicF));
+            const float2 ta = (MODE == DN_ROUTED) ? __fmul2_rn(pa, s2) : pa;
+            const float2 tb = (MODE == DN_ROUTED) ? __fmul2_rn(pb, s2) : pb;
+            r2[(c0 + j) / 2] = __ffma2_rn(ta, make_float2(h4.x, h4.y), r2[(c0 + j) / 2]);
+            r2[(c0 + j) / 2 + 1] = __ffma2_rn(tb, make_float2(h4.z, h4.w), r2[(c0 + j) / 2 + 1]);
+        }
+        return;
+    }
     const uint32_t hv_step = static_cast<uint32_t>(hs_ld) * 4u;
     uint32_t hv_addr = jt::smem_u32(blk + g) + static_cast<uint32_t>(c0) * hv_step;
 #pragma unroll
@@ -286,7 +303,9 @@ __device__ __forceinline__ int mma_n(int rows) {
     return n > kBN ? kBN : n;
 }
 
-template <int MODE>
+// TP (down modes): fold with the activation group scales transposed in the
+// tile slot (needs hs_ld + K/64 <= kMaxGroups).
+template <int MODE, int TP = 0>
 __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant__ MoeGemmParams p) {
     using C = Cfg<MODE>;
     constexpr int S = C::kStages;
@@ -307,9 +326,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
     uint64_t *pempty = pfull + 2;    // tile slot released (epilogue)
     uint64_t *drain = pempty + 2;    // [2]: one per MMA issuer
     uint64_t *epib = drain + 2;      // epilogue-warp barrier
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(epib + 1);
+    uint64_t *cqb = epib + 1;        // [4]: the four warps sharing a column quarter
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(cqb + 4);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-    static_assert((3 * S + 2 * NG + 7) * 8 + 8 <= 1024, "barrier area");
+    static_assert((3 * S + 2 * NG + 11) * 8 + 8 <= 1024, "barrier area");
 
     const int warp = jt::warp_id(), lane = jt::lane_id();
     const int nch_tiles = p.n_ch / C::kChTile;
@@ -336,6 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
             jt::mbar_init(&drain[b], 1);
         }
         jt::mbar_init(epib, kEpiWarps);
+        for (int b = 0; b < 4; ++b) jt::mbar_init(&cqb[b], 4);
         *abort_flag = 0;
         jt::fence_mbar_init();
     }
@@ -575,7 +596,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
         __syncwarp();
         if (lane == 0)
             for (int b = 0; b < NG; ++b) jt::mbar_arrive(&tempty[b]);
-        uint32_t sc = 0, ts = 0, tphase = 0, ephase = 0;
+        uint32_t sc = 0, ts = 0, tphase = 0, ephase = 0, cqphase = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
             if (!jt::mbar_wait(&pfull[ts], tphase, abort_flag, err)) {
@@ -588,6 +609,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
             const __half *sc_ptr = reinterpret_cast<const __half *>(sl + C::kOffScale) +
                                (C::kGateUp ? ((is_up ? ngroups * 64 : 0) + lch) : lr);
             const float *blk = reinterpret_cast<const float *>(sl + C::kOffBlk) + j0 * p.hs_ld;
+            // down modes: the four warps of this column quarter transpose the
+            // tile's activation group scales of their 32 columns to
+            // [group][kBN] (behind the row-major copy in the same slot), so
+            // the fold reads four columns per load
+            const float *hvT = nullptr;
+            if constexpr (C::kDown && TP != 0) {
+                float *blkT = reinterpret_cast<float *>(const_cast<uint8_t *>(sl) + C::kOffBlk) + kBN * p.hs_ld;
+                const float *blkR = reinterpret_cast<const float *>(sl + C::kOffBlk);
+                for (int g = q; g < ngroups; g += 4) blkT[g * kBN + j0 + lane] = blkR[(j0 + lane) * p.hs_ld + g];
+                __syncwarp();
+                if (lane == 0) jt::mbar_arrive(&cqb[cq]);
+                if (!jt::mbar_wait(&cqb[cq], cqphase, abort_flag, err)) {
+                    ok = false;
+                    break;
+                }
+                cqphase ^= 1u;
+                hvT = blkT + j0;
+            }
             const int sc_stride = C::kGateUp ? 64 : 128;
             const int ch = info.w + lch;  // output channel within the expert
             const int nrow = min(info.z - info.y, kBN);
@@ -617,15 +656,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                         jt::tmem_ld16(t0, a0);
                         jt::tmem_wait_ld16(a0);
                         jt::tmem_ld16(t0 + 16, a1);
-                        fold16<MODE>(r2, a0, s0, blk, p.hs_ld, 2 * ps, 0);
+                        fold16<MODE, TP>(r2, a0, s0, blk, p.hs_ld, 2 * ps, 0, hvT);
                         jt::tmem_wait_ld16(a1);
                         jt::tmem_ld16(t0 + kBN, a0);
-                        fold16<MODE>(r2, a1, s0, blk, p.hs_ld, 2 * ps, 16);
+                        fold16<MODE, TP>(r2, a1, s0, blk, p.hs_ld, 2 * ps, 16, hvT);
                         jt::tmem_wait_ld16(a0);
                         jt::tmem_ld16(t0 + kBN + 16, a1);
-                        fold16<MODE>(r2, a0, s1, blk, p.hs_ld, 2 * ps + 1, 0);
+                        fold16<MODE, TP>(r2, a0, s1, blk, p.hs_ld, 2 * ps + 1, 0, hvT);
                         jt::tmem_wait_ld16(a1);
-                        fold16<MODE>(r2, a1, s1, blk, p.hs_ld, 2 * ps + 1, 16);
+                        fold16<MODE, TP>(r2, a1, s1, blk, p.hs_ld, 2 * ps + 1, 16, hvT);
                     } else {
                         uint32_t a[32];
                         jt::tmem_ld32(tlane + g * kBN, a);
@@ -730,6 +769,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                         else *dst = v;
                     }
                 }
+                // generic-proxy writes (the transposed scales) precede the
+                // producer's next TMA write of this slot
+                jt::fence_proxy_async();
                 __syncwarp();
                 if (lane == 0) jt::mbar_arrive(&pempty[ts]);
             }
@@ -746,10 +788,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
     }
 }
 
-template <int MODE>
-int launch(MoeGemmParams &p, int max_tiles_hint, cudaStream_t stream) {
+template <int MODE, int TP>
+int launch_tp(MoeGemmParams &p, int max_tiles_hint, cudaStream_t stream) {
     using C = Cfg<MODE>;
-    auto kern = k_moe_gemm<MODE>;
+    auto kern = k_moe_gemm<MODE, TP>;
     static bool attr = false;
     if (!attr) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -762,6 +804,13 @@ int launch(MoeGemmParams &p, int max_tiles_hint, cudaStream_t stream) {
     p.err = jtk_error_word();
     kern<<<grid, kThreads, C::kSmem, stream>>>(p);
     return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
+template <int MODE>
+int launch(MoeGemmParams &p, int max_tiles_hint, cudaStream_t stream) {
+    if constexpr (MODE == DN_ROUTED)
+        if (p.hs_ld + p.K / 64 <= kMaxGroups) return launch_tp<MODE, 1>(p, max_tiles_hint, stream);
+    return launch_tp<MODE, 0>(p, max_tiles_hint, stream);
 }
 
 int hs_stride(int n_ch) { return ((n_ch / 64) + 3) & ~3; }
