@@ -185,7 +185,7 @@ int jt_b200_moe_ep_plan_create(const jt_b200_moe_dims *dims, jt_b200_ep_comm *co
         {(void **)&p->sh_tiles, (T / JT_TILE_ROWS + 1) * 16},
         {(void **)&p->row_meta, Tk * 16},    {(void **)&p->sh_meta, T * 16},
         {(void **)&p->w_raw, Tk * 4},        {(void **)&p->w_fin, Tk * 4},
-        {(void **)&p->xs, T * 4},            {(void **)&p->hs_s, T * (size_t)hs_ld((int)fs) * 4},
+        {(void **)&p->xs, T * 4},            {(void **)&p->hs_s, ((T + 3) & ~(size_t)3) * (size_t)hs_ld((int)fs) * 4},
         {(void **)&p->y32, T * d * 4},       {(void **)&p->drop, Tk},
         {(void **)&p->xq, T * d},            {(void **)&p->xd, Tk * d},
         {(void **)&p->hq_s, T * fs},

@@ -104,7 +104,7 @@ int jt_b200_moe_plan_create(const jt_b200_moe_dims *dims, jt_b200_moe_plan **out
         {(void **)&p->row_meta, Tk * 16},    {(void **)&p->sh_meta, T * 16},
         {(void **)&p->w_raw, Tk * 4},        {(void **)&p->w_fin, Tk * 4},
         {(void **)&p->xs, T * 4},            {(void **)&p->hs, Tk * (size_t)hs_ld((int)f) * 4},
-        {(void **)&p->hs_s, T * (size_t)hs_ld((int)fs) * 4},
+        {(void **)&p->hs_s, ((T + 3) & ~(size_t)3) * (size_t)hs_ld((int)fs) * 4},
         {(void **)&p->y32, T * d * 4},       {(void **)&p->drop, Tk},
         {(void **)&p->xq, T * d},            {(void **)&p->xd, Tk * d},
         {(void **)&p->hq, Tk * f},           {(void **)&p->hq_s, T * fs},

@@ -126,6 +126,7 @@ struct MoeGemmParams {
     int n_ch;   // output channels per expert (f for gate/up, d for down)
     int K;      // reduction length (d for gate/up, f for down)
     int hs_ld;  // row stride of the activation group scales (down) / of hs (gate/up out)
+    int hs_rows;  // shared experts: hs is [K/64 groups][hs_rows] (group-major), hs_rows % 4 == 0
     const float *cs0;  // per-channel scales [n_ch] (shared)
     const float *cs1;
     int8_t *hq;        // gate/up out: codes [rows][n_ch]
@@ -255,15 +256,15 @@ __device__ __forceinline__ void fold_chunk(float2 *r2, const uint32_t (&a)[32], 
 
 // Fold 16 drained columns (columns c0 .. c0+15 of the warp's 32) of one
 // 64-K unit into r2[c0/2 .. c0/2+7]; same arithmetic as fold_chunk.
-// hvT (down modes, may be NULL): the tile's activation group scales
-// transposed to [group][kBN] and offset to the warp's first column, read
-// four columns per shared-memory load.
+// TP != 0 (down modes): hvT points at the tile's activation group scales in
+// group-major order (group stride hs_ld floats), offset to the warp's first
+// column, and is read four columns per shared-memory load.
 template <int MODE, int TP>
 __device__ __forceinline__ void fold16(float2 *r2, const uint32_t (&a)[16], float s, const float *blk, int hs_ld,
                                        int g, int c0, const float *hvT) {
     const float2 s2 = make_float2(s, s);
     if constexpr (TP != 0) {
-        const float4 *h4p = reinterpret_cast<const float4 *>(hvT + (size_t)g * kBN + c0);
+        const float4 *h4p = reinterpret_cast<const float4 *>(hvT + (size_t)g * hs_ld + c0);
 #pragma unroll
         for (int j = 0; j < 16; j += 4) {
             const float4 h4 = h4p[j / 4];
@@ -397,7 +398,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
             constexpr uint32_t kTx = C::kX + (C::kPacked ? C::kAP : C::kAU);
             const uint32_t scale_box = ngroups * (C::kGateUp ? 64 * 2 : 128 * 2);
             const uint32_t slot_tx = kBN * 16 + (C::kPacked ? (C::kGateUp ? 2 : 1) * scale_box : 0) +
-                                     (C::kDown ? kBN * p.hs_ld * 4 : 0);
+                                     (MODE == DN_ROUTED ? kBN * p.hs_ld * 4 : 0) +
+                                     (MODE == DN_SHARED ? 2 * 256 * ngroups : 0);
             for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
                 const int4 te = __ldg(&p.tiles[u / nch_tiles]);  // {e, row0, row_end, 0}
                 const int c0 = (u % nch_tiles) * C::kChTile;
@@ -417,7 +419,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                         jt::tma_load_2d(sl + C::kOffScale + scale_box, &p.tmS1, &pfull[ts], c0 * 2,
                                         te.x * ngroups);
                 }
-                if (C::kDown) jt::tma_load_2d(sl + C::kOffBlk, &p.tmH, &pfull[ts], 0, te.y);
+                if (MODE == DN_ROUTED) jt::tma_load_2d(sl + C::kOffBlk, &p.tmH, &pfull[ts], 0, te.y);
+                if (MODE == DN_SHARED) {  // group-major scales: two [groups][64 rows] boxes
+                    jt::tma_load_2d(sl + C::kOffBlk, &p.tmH, &pfull[ts], te.y * 4, 0);
+                    jt::tma_load_2d(sl + C::kOffBlk + 256 * ngroups, &p.tmH, &pfull[ts], te.y * 4 + 256, 0);
+                }
                 t_issued |= 1u << ts;
                 t_phase = (t_phase & ~(1u << ts)) | (tphase << ts);
                 if (++ts == 2) {
@@ -614,7 +620,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
             // [group][kBN] (behind the row-major copy in the same slot), so
             // the fold reads four columns per load
             const float *hvT = nullptr;
-            if constexpr (C::kDown && TP != 0) {
+            if constexpr (MODE == DN_SHARED && TP != 0)  // the two boxes of 64 rows
+                hvT = reinterpret_cast<const float *>(sl + C::kOffBlk) + (j0 / 64) * ngroups * 64 + (j0 % 64);
+            if constexpr (MODE == DN_ROUTED && TP != 0) {
                 float *blkT = reinterpret_cast<float *>(const_cast<uint8_t *>(sl) + C::kOffBlk) + kBN * p.hs_ld;
                 const float *blkR = reinterpret_cast<const float *>(sl + C::kOffBlk);
                 for (int g = q; g < ngroups; g += 4) blkT[g * kBN + j0 + lane] = blkR[(j0 + lane) * p.hs_ld + g];
@@ -628,6 +636,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                 hvT = blkT + j0;
             }
             const int sc_stride = C::kGateUp ? 64 : 128;
+            // group stride of the activation scales the fold reads
+            const int hv_ld = TP == 0 ? p.hs_ld : (MODE == DN_SHARED ? 64 : kBN);
             const int ch = info.w + lch;  // output channel within the expert
             const int nrow = min(info.z - info.y, kBN);
             // columns of this warp that hold token rows of the tile
@@ -656,15 +666,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                         jt::tmem_ld16(t0, a0);
                         jt::tmem_wait_ld16(a0);
                         jt::tmem_ld16(t0 + 16, a1);
-                        fold16<MODE, TP>(r2, a0, s0, blk, p.hs_ld, 2 * ps, 0, hvT);
+                        fold16<MODE, TP>(r2, a0, s0, blk, hv_ld, 2 * ps, 0, hvT);
                         jt::tmem_wait_ld16(a1);
                         jt::tmem_ld16(t0 + kBN, a0);
-                        fold16<MODE, TP>(r2, a1, s0, blk, p.hs_ld, 2 * ps, 16, hvT);
+                        fold16<MODE, TP>(r2, a1, s0, blk, hv_ld, 2 * ps, 16, hvT);
                         jt::tmem_wait_ld16(a0);
                         jt::tmem_ld16(t0 + kBN + 16, a1);
-                        fold16<MODE, TP>(r2, a0, s1, blk, p.hs_ld, 2 * ps + 1, 0, hvT);
+                        fold16<MODE, TP>(r2, a0, s1, blk, hv_ld, 2 * ps + 1, 0, hvT);
                         jt::tmem_wait_ld16(a1);
-                        fold16<MODE, TP>(r2, a1, s1, blk, p.hs_ld, 2 * ps + 1, 16, hvT);
+                        fold16<MODE, TP>(r2, a1, s1, blk, hv_ld, 2 * ps + 1, 16, hvT);
                     } else {
                         uint32_t a[32];
                         jt::tmem_ld32(tlane + g * kBN, a);
@@ -742,7 +752,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                             const int row = info.y + j;
                             *reinterpret_cast<uint2 *>(p.hq + (size_t)row * p.n_ch + info.w + 8 * sl) =
                                 make_uint2(wd[0], wd[1]);
-                            if (sl == 0) p.hs[(size_t)row * p.hs_ld + info.w / 64] = qb.scale_f;
+                            if (sl == 0) {
+                                if (MODE == GU_SHARED)
+                                    p.hs[(size_t)(info.w / 64) * p.hs_rows + row] = qb.scale_f;
+                                else
+                                    p.hs[(size_t)row * p.hs_ld + info.w / 64] = qb.scale_f;
+                            }
                         }
                     }
                 }
@@ -810,6 +825,7 @@ template <int MODE>
 int launch(MoeGemmParams &p, int max_tiles_hint, cudaStream_t stream) {
     if constexpr (MODE == DN_ROUTED)
         if (p.hs_ld + p.K / 64 <= kMaxGroups) return launch_tp<MODE, 1>(p, max_tiles_hint, stream);
+    if constexpr (MODE == DN_SHARED) return launch_tp<MODE, 1>(p, max_tiles_hint, stream);
     return launch_tp<MODE, 0>(p, max_tiles_hint, stream);
 }
 
@@ -880,7 +896,8 @@ extern "C" int jtk_moe_down_routed(const uint8_t *wd, const void *ds, int E, int
 }
 
 // Shared gate/up (one shared expert): wsg, wsu int8 [fs][d] with per-channel
-// ssg, ssu; x int8 [T][d], sh_meta [T]; writes hq [T][fs] and hs [T][round_up(fs/64, 4)].
+// ssg, ssu; x int8 [T][d], sh_meta [T]; writes hq [T][fs] and hs group-major
+// [fs/64][round_up(T, 4)].
 extern "C" int jtk_moe_gateup_shared(const int8_t *wsg, const int8_t *wsu, const float *ssg,
                                      const float *ssu, int fs, int d, const int8_t *xq, int T,
                                      const float4 *sh_meta, const int4 *tiles,
@@ -900,6 +917,7 @@ extern "C" int jtk_moe_gateup_shared(const int8_t *wsg, const int8_t *wsu, const
     p.n_ch = fs;
     p.K = d;
     p.hs_ld = hs_stride(fs);
+    p.hs_rows = (T + 3) & ~3;
     p.cs0 = ssg;
     p.cs1 = ssu;
     p.hq = hq;
@@ -907,7 +925,7 @@ extern "C" int jtk_moe_gateup_shared(const int8_t *wsg, const int8_t *wsu, const
     return launch<GU_SHARED>(p, ((T + kBN - 1) / kBN) * (fs / 64), stream);
 }
 
-// Shared down: wsd int8 [d][fs] with per-channel ssd; hq [T][fs], hs [T][round_up(fs/64, 4)];
+// Shared down: wsd int8 [d][fs] with per-channel ssd; hq [T][fs], hs group-major [fs/64][round_up(T, 4)];
 // y[t][d] = (accumulate ? y + v : v).
 extern "C" int jtk_moe_down_shared(const int8_t *wsd, const float *ssd, int d, int fs,
                                    const int8_t *hq, int T, const float *hs,
@@ -919,7 +937,8 @@ extern "C" int jtk_moe_down_shared(const int8_t *wsd, const float *ssd, int d, i
     const int hs_ld = hs_stride(fs);
     if (!jt::make_tmap_2d_u8(&p.tmA0, wsd, fs, d, fs, kBK, kBM, true) ||
         !jt::make_tmap_2d_u8(&p.tmX, hq, fs, T, fs, kBK, kBN, true) || !meta_map(&p.tmM, sh_meta, T) ||
-        !jt::make_tmap_2d_u8(&p.tmH, hs, (uint64_t)hs_ld * 4, T, (uint64_t)hs_ld * 4, hs_ld * 4, kBN, false))
+        !jt::make_tmap_2d_u8(&p.tmH, hs, (uint64_t)((T + 3) & ~3) * 4, (uint64_t)(fs / 64),
+                             (uint64_t)((T + 3) & ~3) * 4, 256, fs / 64, false))
         return -2;
     p.tmA1 = p.tmA0;
     p.tmS0 = p.tmA0;
@@ -929,6 +948,7 @@ extern "C" int jtk_moe_down_shared(const int8_t *wsd, const float *ssd, int d, i
     p.n_ch = d;
     p.K = fs;
     p.hs_ld = hs_ld;
+    p.hs_rows = (T + 3) & ~3;
     p.cs0 = ssd;
     p.y = y;
     p.y_accumulate = accumulate;
