@@ -28,6 +28,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <string.h>
 
 #include "jt_internal.h"
 #include "jt_ptx.cuh"
@@ -52,7 +53,7 @@ constexpr size_t kOffAct = (size_t)kStages * kStageBytes;
 constexpr size_t kOffSum = kOffAct + 2 * kMaxG * 16 * 4;
 constexpr size_t kOffA = kOffSum + kMaxG * 4;          // activations, K bytes
 constexpr size_t kOffP = kOffA + 64 * kMaxG;
-constexpr int kPld = 33;  // partial-row stride (words): conflict-free lane-per-row reads
+constexpr int kPld = 36;  // partial-row stride (words): lane-per-row 16-byte reads without bank conflicts
 constexpr size_t kOffBar = kOffP + (size_t)kConsumers * kSub * kPld * 4;
 constexpr size_t kSmem = kOffBar + 2 * kStages * 8 + 16;
 static_assert(kSmem <= 113 * 1024, "two CTAs per SM");
@@ -171,11 +172,37 @@ __device__ __forceinline__ void consume_k2048(const uint8_t *codes, int nrows, c
     }
     __syncwarp();
     if (lane < nrows) {
-        const uint16_t *sr = sc + lane * 32;
+        // the row's 32 partials and 32 fp16 scales with 16-byte loads, then
+        // the fold in ascending group order
+        const uint4 *pp = reinterpret_cast<const uint4 *>(Ps + lane * kPld);
+        const uint4 *sp = reinterpret_cast<const uint4 *>(sc + lane * 32);
+        int32_t P[32];
+        uint32_t hs[16];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint4 v = pp[i];
+            P[4 * i] = (int32_t)v.x;
+            P[4 * i + 1] = (int32_t)v.y;
+            P[4 * i + 2] = (int32_t)v.z;
+            P[4 * i + 3] = (int32_t)v.w;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint4 v = sp[i];
+            hs[4 * i] = v.x;
+            hs[4 * i + 1] = v.y;
+            hs[4 * i + 2] = v.z;
+            hs[4 * i + 3] = v.w;
+        }
         float r = 0.0f;
 #pragma unroll
-        for (int g = 0; g < 32; ++g)
-            r = __fmaf_rn((float)Ps[lane * kPld + g], __half2float(__ushort_as_half(sr[g])), r);
+        for (int i = 0; i < 16; ++i) {  // two scales per conversion (low half = even group)
+            __half2 h2;
+            memcpy(&h2, &hs[i], 4);
+            const float2 s2 = __half22float2(h2);
+            r = __fmaf_rn((float)P[2 * i], s2.x, r);
+            r = __fmaf_rn((float)P[2 * i + 1], s2.y, r);
+        }
         y[lane] = __fmul_rn(r, sa);
     }
     __syncwarp();
