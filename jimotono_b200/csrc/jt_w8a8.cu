@@ -21,6 +21,8 @@
 //   * two TMEM accumulator buffers so the epilogue of tile i overlaps the
 //     MMAs of tile i+1; S-stage SMEM ring between TMA and MMA.
 //   * every mbarrier wait is bounded (jt_ptx.cuh).
+//   * M >= 256: the CTA-pair kernel k_w8a8_pair (cta_group::2, 256 x 256
+//     tiles per 2-CTA cluster), described above its definition.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -54,6 +56,37 @@ __device__ __forceinline__ void tmem_ld_chunk<16>(uint32_t taddr, uint32_t (&v)[
 template <>
 __device__ __forceinline__ void tmem_ld_chunk<32>(uint32_t taddr, uint32_t (&v)[32]) {
     jt::tmem_ld32(taddr, v);
+}
+
+// Stores one TMEM chunk of the epilogue: NCOL consecutive tokens tok0.. of
+// this thread's channel ch.  The chunk's token scales are fetched once,
+// coalesced (lane j holds sx[tok0 + j]), and broadcast by shuffle, so no
+// store waits on a per-element scale load.  Every lane of the warp calls it
+// (the shuffles are warp-wide); stores are predicated on ch_ok and tok < M.
+template <int EPI, int NCOL>
+__device__ __forceinline__ void epi_chunk(const uint32_t (&v)[NCOL], int tok0, int M, int ch,
+                                          bool ch_ok, float swf, double ss,
+                                          const float *__restrict__ sx, void *__restrict__ out,
+                                          int ldo, int lane) {
+    const int nvalid = (M - tok0) < NCOL ? (M - tok0) : NCOL;
+    float sxl = 0.f;
+    if (EPI == JTK_EPI_TOKEN_CHANNEL_F32 && lane < nvalid) sxl = __ldg(&sx[tok0 + lane]);
+    const size_t base = static_cast<size_t>(tok0) * ldo + ch;
+#pragma unroll
+    for (int j = 0; j < NCOL; ++j) {
+        const int32_t acc = static_cast<int32_t>(v[j]);
+        const bool live = ch_ok && j < nvalid;
+        const size_t o = base + static_cast<size_t>(j) * ldo;
+        if (EPI == JTK_EPI_TOKEN_CHANNEL_F32) {
+            const float sj = __shfl_sync(0xffffffffu, sxl, j);
+            const float r = __fmul_rn(__fmul_rn(__int2float_rn(acc), sj), swf);
+            if (live) static_cast<float *>(out)[o] = r;
+        } else if (EPI == JTK_EPI_TENSOR_CHANNEL_F64) {
+            if (live) static_cast<float *>(out)[o] = __double2float_rn(__dmul_rn((double)acc, ss));
+        } else {
+            if (live) static_cast<int32_t *>(out)[o] = acc;
+        }
+    }
 }
 
 template <int BN, int EPI>
@@ -212,26 +245,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (EPI == JTK_EPI_TOKEN_CHANNEL_F32) swf = ch_ok ? sw[ch] : 0.f;
             if (EPI == JTK_EPI_TENSOR_CHANNEL_F64) ss = ch_ok ? sA * (double)sw[ch] : 0.0;
             const uint32_t trow = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+            const int cols = (M - m0) < BN ? (M - m0) : BN;
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += Cfg::kChunk) {
+            for (int c0 = 0; c0 < cols; c0 += Cfg::kChunk) {
                 uint32_t v[Cfg::kChunk];
                 tmem_ld_chunk<Cfg::kChunk>(trow + c0, v);
                 jt::tmem_wait_ld();
-#pragma unroll
-                for (int j = 0; j < Cfg::kChunk; ++j) {
-                    const int tok = m0 + c0 + j;
-                    if (!ch_ok || tok >= M) continue;
-                    const int32_t acc = static_cast<int32_t>(v[j]);
-                    const size_t o = static_cast<size_t>(tok) * ldo + ch;
-                    if (EPI == JTK_EPI_TOKEN_CHANNEL_F32) {
-                        const float a = __int2float_rn(acc);
-                        static_cast<float *>(out)[o] = __fmul_rn(__fmul_rn(a, __ldg(&sx[tok])), swf);
-                    } else if (EPI == JTK_EPI_TENSOR_CHANNEL_F64) {
-                        static_cast<float *>(out)[o] = __double2float_rn(__dmul_rn((double)acc, ss));
-                    } else {
-                        static_cast<int32_t *>(out)[o] = acc;
-                    }
-                }
+                epi_chunk<EPI, Cfg::kChunk>(v, m0 + c0, M, ch, ch_ok, swf, ss, sx, out, ldo, lane);
             }
             jt::tc_fence_before();
             __syncwarp();
@@ -243,6 +263,268 @@ __global__ void __launch_bounds__(kThreads, 1)
         jt::tc_fence_after();
         jt::tmem_dealloc(tmem_base, Cfg::kTmemCols);
     }
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair form for M >= 256: a 2-CTA cluster computes a 256-channel x
+// 256-token tile with tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32).
+// Rank r loads weight channels n0 + 128r .. +127 (its half of A) and tokens
+// m0 + 128r .. +127 (its half of B) into its own shared memory; its TMEM holds
+// D for its 128 channels x all 256 tokens.  Per 128-K stage each SM reads
+// 32 KB from L2 instead of the 48 KB of the single-CTA 128 x 256 tile, and
+// each MMA reads 8 KB of its shared memory instead of 12 KB.
+//
+// Barriers: full[s] on rank 0 counts the bytes of both ranks' boxes of stage
+// s (rank 1's loads report to it through the pair form of the TMA load; rank
+// 0's producer posts the expected 64 KB); empty[s] and tfull[b] in both ranks
+// are signalled by the MMA commit multicast to both; tempty[b] on rank 0
+// counts the four epilogue warps of each rank.
+// The TMA loads carry no multicast: each rank fetches its own halves.
+constexpr int kPairStages = 6;
+constexpr uint32_t kPairBox = 128 * kBK;          // one 128-row x 128-byte box, 16 KB
+constexpr uint32_t kPairStage = 2 * kPairBox;     // weight box + token box
+constexpr uint32_t kPairCols = 512;               // two 256-column accumulators
+// 16 KB between the last stage and the barriers: no operand read of the
+// stage ring can leave the allocation, whatever the descriptors cover.
+constexpr uint32_t kPairSlack = 16384;
+constexpr size_t kPairSmem = 1024 + kPairStages * kPairStage + kPairSlack + 512;
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_w8a8_pair(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                int M, int N, int K, const float *__restrict__ sx, const float *__restrict__ sw,
+                double sA, void *__restrict__ out, int ldo, int *err) {
+    constexpr int S = kPairStages;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + S * kPairStage + kPairSlack);
+    uint64_t *empty = full + S;
+    uint64_t *tfull = empty + S;
+    uint64_t *tempty = tfull + 2;
+    uint64_t *drain = tempty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = jt::warp_id();
+    const int lane = jt::lane_id();
+    const uint32_t rank = jt::cluster_ctarank();
+    const int pair = static_cast<int>(jt::cluster_id_x());
+    const int npairs = static_cast<int>(jt::ncluster_x());
+    const int n_ch_tiles = (N + 255) / 256;
+    const int n_tok_tiles = (M + 255) / 256;
+    const int ntiles = n_ch_tiles * n_tok_tiles;
+    const int nk = (K + kBK - 1) / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            jt::mbar_init(&full[s], 1);
+            jt::mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            jt::mbar_init(&tfull[b], 1);
+            jt::mbar_init(&tempty[b], 8);
+        }
+        jt::mbar_init(drain, 1);
+        *abort_flag = 0;
+        jt::fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        jt::prefetch_tmap(&tmW);
+        jt::prefetch_tmap(&tmX);
+    }
+    if (warp == 1) {
+        jt::tmem_alloc_pair(tmem_slot, kPairCols);
+        jt::tmem_relinquish_pair();
+    }
+    jt::tc_fence_before();
+    __syncthreads();
+    // both ranks' barriers are initialised before any cross-CTA signal
+    jt::cluster_sync();
+    jt::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0;
+            uint32_t issued_mask = 0, issued_phase = 0;
+            bool ok = true;
+            for (int tile = pair; tile < ntiles && ok; tile += npairs) {
+                const int n0 = (tile % n_ch_tiles) * 256 + static_cast<int>(rank) * 128;
+                const int m0 = (tile / n_ch_tiles) * 256 + static_cast<int>(rank) * 128;
+                for (int kb = 0; kb < nk; ++kb) {
+                    if (!jt::mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, err)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *sW = smem + stage * kPairStage;
+                    if (rank == 0) jt::mbar_arrive_expect_tx(&full[stage], 2 * kPairStage);
+                    const uint32_t bar = jt::cluster_addr(&full[stage], 0);
+                    jt::tma_load_2d_pair(sW, &tmW, bar, kb * kBK, n0);
+                    jt::tma_load_2d_pair(sW + kPairBox, &tmX, bar, kb * kBK, m0);
+                    issued_mask |= 1u << stage;
+                    issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // Tail: the MMA commits that release the last stages arrive on
+            // this CTA's barriers asynchronously; wait for every one of them
+            // so none lands after the CTA has exited.
+            for (int i = 0; i < S && ok; ++i) {
+                if (!jt::mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, err)) ok = false;
+                if (++stage == S) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (!ok) {
+                // Every issued box must land before the CTA exits.  Rank 0
+                // waits (bounded) for the last issued phase of each stage;
+                // rank 1 cannot observe its boxes (they report to rank 0)
+                // and waits a fixed, bounded interval instead.
+                if (rank == 0) {
+                    for (int s = 0; s < S; ++s) {
+                        if (!(issued_mask & (1u << s))) continue;
+                        const uint32_t par = (issued_phase >> s) & 1u;
+                        const long long t0 = clock64();
+                        while (!jt::mbar_try_wait(&full[s], par) &&
+                               clock64() - t0 < JT_SPIN_CYCLES / 16) {
+                        }
+                    }
+                } else if (issued_mask) {
+                    const long long t0 = clock64();
+                    while (clock64() - t0 < JT_SPIN_CYCLES / 64) __nanosleep(1000);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // rank 0: the pair's MMA issuer (rank 1's warp 1 only allocates)
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t kIdesc = jt::idesc_i8(256, 256);
+            uint32_t stage = 0, phase = 0;
+            int it = 0;
+            bool ok = true;
+            for (int tile = pair; tile < ntiles && ok; tile += npairs, ++it) {
+                const uint32_t buf = it & 1;
+                const uint32_t use = (it >> 1) & 1;
+                if (!jt::mbar_wait_cluster(&tempty[buf], use ^ 1u, abort_flag, err)) {
+                    ok = false;
+                    break;
+                }
+                jt::tc_fence_after();
+                const uint32_t d_tmem = tmem_base + buf * 256;
+                for (int kb = 0; kb < nk; ++kb) {
+                    if (!jt::mbar_wait_cluster(&full[stage], phase, abort_flag, err)) {
+                        ok = false;
+                        break;
+                    }
+                    jt::tc_fence_after();
+                    const uint32_t aW = jt::smem_u32(smem + stage * kPairStage);
+                    const uint64_t da = jt::umma_desc_sw128(aW);
+                    const uint64_t db = jt::umma_desc_sw128(aW + kPairBox);
+#pragma unroll
+                    for (int j = 0; j < kBK / 32; ++j)
+                        jt::mma_i8_pair(d_tmem, da + 2u * j, db + 2u * j, kIdesc,
+                                        (kb | j) != 0 ? 1u : 0u);
+                    jt::mma_commit_pair(&empty[stage], 0x3);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                jt::mma_commit_pair(&tfull[buf], 0x3);
+            }
+            if (!ok) {
+                jt::mma_commit_pair(drain, 0x1);
+                const long long t0 = clock64();
+                while (!jt::mbar_try_wait(drain, 0) && clock64() - t0 < JT_SPIN_CYCLES / 16) {
+                }
+            }
+        }
+    } else {
+        // Epilogue warps 2..5: TMEM lanes 32*(w%4)..+31 = this rank's channels.
+        const int q = warp & 3;
+        int it = 0;
+        for (int tile = pair; tile < ntiles; tile += npairs, ++it) {
+            const uint32_t buf = it & 1;
+            const uint32_t use = (it >> 1) & 1;
+            if (!jt::mbar_wait_cluster(&tfull[buf], use, abort_flag, err)) break;
+            jt::tc_fence_after();
+            const int ch = (tile % n_ch_tiles) * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
+            const int m0 = (tile / n_ch_tiles) * 256;
+            const bool ch_ok = ch < N;
+            float swf = 0.f;
+            double ss = 0.0;
+            if (EPI == JTK_EPI_TOKEN_CHANNEL_F32) swf = ch_ok ? sw[ch] : 0.f;
+            if (EPI == JTK_EPI_TENSOR_CHANNEL_F64) ss = ch_ok ? sA * (double)sw[ch] : 0.0;
+            const uint32_t trow = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * 256;
+            const int cols = (M - m0) < 256 ? (M - m0) : 256;
+#pragma unroll 1
+            for (int c0 = 0; c0 < cols; c0 += 32) {
+                uint32_t v[32];
+                jt::tmem_ld32(trow + c0, v);
+                jt::tmem_wait_ld();
+                epi_chunk<EPI, 32>(v, m0 + c0, M, ch, ch_ok, swf, ss, sx, out, ldo, lane);
+            }
+            jt::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if (rank == 0)
+                    jt::mbar_arrive(&tempty[buf]);
+                else
+                    jt::mbar_arrive_cluster(&tempty[buf], 0);
+            }
+        }
+    }
+    __syncthreads();
+    // no CTA of the pair releases TMEM or exits while its peer may still
+    // signal its barriers or read its shared memory
+    jt::cluster_sync();
+    if (warp == 1) {
+        jt::tc_fence_after();
+        jt::tmem_dealloc_pair(tmem_base, kPairCols);
+    }
+}
+
+template <int EPI>
+int launch_pair(const CUtensorMap &tmW, const int8_t *X, int ldx, int M, int N, int K,
+                const float *sx, const float *sw, double sA, void *out, int ldo,
+                cudaStream_t stream) {
+    CUtensorMap tmX;
+    if (!jt::make_tmap_2d_u8(&tmX, X, static_cast<uint64_t>(K), static_cast<uint64_t>(M),
+                             static_cast<uint64_t>(ldx), kBK, 128, true))
+        return -2;
+    auto kern = k_w8a8_pair<EPI>;
+    static bool attr_done = false;  // per template instance
+    if (!attr_done) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kPairSmem)) != cudaSuccess)
+            return -3;
+        attr_done = true;
+    }
+    const int ntiles = ((N + 255) / 256) * ((M + 255) / 256);
+    int pairs = jtk_num_sms() / 2;
+    if (pairs > ntiles) pairs = ntiles;
+    int *err = jtk_error_word();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = kPairSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, tmW, tmX, M, N, K, sx, sw, sA, out, ldo, err) != cudaSuccess)
+        return -4;
+    return 0;
 }
 
 template <int BN, int EPI>
@@ -282,7 +564,8 @@ int launch_epi(const int8_t *X, int ldx, const int8_t *W, int ldw, int M, int N,
     if (M <= 32) return launch_bn<32, EPI>(tmW, X, ldx, M, N, K, sx, sw, sA, out, ldo, stream);
     if (M <= 64) return launch_bn<64, EPI>(tmW, X, ldx, M, N, K, sx, sw, sA, out, ldo, stream);
     if (M <= 128) return launch_bn<128, EPI>(tmW, X, ldx, M, N, K, sx, sw, sA, out, ldo, stream);
-    return launch_bn<256, EPI>(tmW, X, ldx, M, N, K, sx, sw, sA, out, ldo, stream);
+    if (M < 256) return launch_bn<256, EPI>(tmW, X, ldx, M, N, K, sx, sw, sA, out, ldo, stream);
+    return launch_pair<EPI>(tmW, X, ldx, M, N, K, sx, sw, sA, out, ldo, stream);
 }
 
 }  // namespace

@@ -21,7 +21,8 @@ pytestmark = pytest.mark.gpu
 
 SHAPES = [  # (M, N, K)
     (1, 128, 128), (16, 256, 256), (17, 200, 144), (64, 4096, 1024), (128, 512, 2048),
-    (200, 384, 1040), (1000, 256, 512), (300, 130, 64),
+    (200, 384, 1040), (1000, 256, 512), (300, 130, 64), (512, 768, 1024), (1024, 1024, 256),
+    (384, 640, 2176),
 ]
 
 
