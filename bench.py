@@ -414,7 +414,35 @@ def part_w8a8(torch, steps=200):
         byts = M * K + N * K + 4 * M * N + 4 * (M + N)
         res[f"{M}x{N}x{K}"] = {"us": round(us, 3), "TOPS": round(2 * M * N * K / us / 1e6, 2),
                                "GBs": round(byts / us / 1e3, 1), "us_graph": round(us_g, 3),
-                               "TOPS_graph": round(2 * M * N * K / us_g / 1e6, 2)}
+                               "TOPS_graph": round(2 * M * N * K / us_g / 1e6, 2),
+                               "frac_of_nominal_int8": round(2 * M * N * K / us / 1e6 / 4500.0, 4)}
+        if M == 4096:
+            # the same GEMM with int32 output, ours and cuBLASLt's (torch._int_mm),
+            # as a measured int8 tensor-core comparator on this GPU
+            Ci = torch.empty((M, N), dtype=torch.int32, device="cuda")
+
+            def t_ev(fn, n):
+                for i in range(5):
+                    fn(i)
+                torch.cuda.synchronize()
+                e0.record()
+                for i in range(n):
+                    fn(i)
+                e1.record()
+                torch.cuda.synchronize()
+                return e0.elapsed_time(e1) / n * 1e3
+
+            us_i32 = t_ev(lambda i: L.jt_b200_w8a8_gemm_i32(
+                bufs[i % rot][0].data_ptr(), K, bufs[i % rot][1].data_ptr(), K, Ci.data_ptr(), N,
+                M, N, K, stream), steps)
+            assert L.jt_b200_sync() == 0
+            res[f"{M}x{N}x{K}"]["i32_us"] = round(us_i32, 3)
+            try:
+                us_lt = t_ev(lambda i: torch._int_mm(bufs[i % rot][0], bufs[i % rot][1].t()), steps)
+                res[f"{M}x{N}x{K}"]["cublaslt_i32_us"] = round(us_lt, 3)
+                res[f"{M}x{N}x{K}"]["cublaslt_TOPS"] = round(2 * M * N * K / us_lt / 1e6, 2)
+            except RuntimeError as e:  # no int8 cuBLASLt kernel for this GPU / build
+                res[f"{M}x{N}x{K}"]["cublaslt_i32_us"] = f"unavailable: {str(e).splitlines()[0][:80]}"
     return res
 
 

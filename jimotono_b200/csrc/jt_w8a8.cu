@@ -278,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // s (rank 1's loads report to it through the pair form of the TMA load; rank
 // 0's producer posts the expected 64 KB); empty[s] and tfull[b] in both ranks
 // are signalled by the MMA commit multicast to both; tempty[b] on rank 0
-// counts the four epilogue warps of each rank.
+// counts the eight epilogue warps of each rank.
 // The TMA loads carry no multicast: each rank fetches its own halves.
 constexpr int kPairStages = 6;
 constexpr uint32_t kPairBox = 128 * kBK;          // one 128-row x 128-byte box, 16 KB
@@ -288,9 +288,31 @@ constexpr uint32_t kPairCols = 512;               // two 256-column accumulators
 // stage ring can leave the allocation, whatever the descriptors cover.
 constexpr uint32_t kPairSlack = 16384;
 constexpr size_t kPairSmem = 1024 + kPairStages * kPairStage + kPairSlack + 512;
+constexpr int kPairThreads = 320;                // 10 warps: TMA, MMA, 8 epilogue
+
+// Runs fn(v, c0) over the 32-column TMEM chunks c0 = cb, cb+32, .. < ce of
+// this warp's lane quarter, the load of the next chunk in flight while fn
+// processes the current one (warp-uniform bounds).
+template <typename Fn>
+__device__ __forceinline__ void tmem_columns(uint32_t trow, int cb, int ce, Fn &&fn) {
+    if (cb >= ce) return;
+    uint32_t va[32], vb[32];
+    jt::tmem_ld32(trow + cb, va);
+#pragma unroll 1
+    for (int c0 = cb; c0 < ce; c0 += 64) {
+        jt::tmem_wait_ld32(va);
+        const bool more = c0 + 32 < ce;
+        if (more) jt::tmem_ld32(trow + c0 + 32, vb);
+        fn(va, c0);
+        if (!more) break;
+        jt::tmem_wait_ld32(vb);
+        if (c0 + 64 < ce) jt::tmem_ld32(trow + c0 + 64, va);
+        fn(vb, c0 + 32);
+    }
+}
 
 template <int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kPairThreads, 1)
     k_w8a8_pair(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                 int M, int N, int K, const float *__restrict__ sx, const float *__restrict__ sw,
                 double sA, void *__restrict__ out, int ldo, int *err) {
@@ -323,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             jt::mbar_init(&tfull[b], 1);
-            jt::mbar_init(&tempty[b], 8);
+            jt::mbar_init(&tempty[b], 16);
         }
         jt::mbar_init(drain, 1);
         *abort_flag = 0;
@@ -446,15 +468,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else {
-        // Epilogue warps 2..5: TMEM lanes 32*(w%4)..+31 = this rank's channels.
+        // Epilogue warps 2..9: warp w reads TMEM lanes 32*(w%4)..+31 (this
+        // rank's channels) and token columns 128*((w-2)/4) .. +127.
         const int q = warp & 3;
+        const int cl = q * 32 + lane;  // channel within this rank's 128
+        const int colh = ((warp - 2) >> 2) * 128;
         int it = 0;
         for (int tile = pair; tile < ntiles; tile += npairs, ++it) {
             const uint32_t buf = it & 1;
             const uint32_t use = (it >> 1) & 1;
             if (!jt::mbar_wait_cluster(&tfull[buf], use, abort_flag, err)) break;
             jt::tc_fence_after();
-            const int ch = (tile % n_ch_tiles) * 256 + static_cast<int>(rank) * 128 + q * 32 + lane;
+            const int ch = (tile % n_ch_tiles) * 256 + static_cast<int>(rank) * 128 + cl;
             const int m0 = (tile / n_ch_tiles) * 256;
             const bool ch_ok = ch < N;
             float swf = 0.f;
@@ -463,13 +488,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (EPI == JTK_EPI_TENSOR_CHANNEL_F64) ss = ch_ok ? sA * (double)sw[ch] : 0.0;
             const uint32_t trow = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * 256;
             const int cols = (M - m0) < 256 ? (M - m0) : 256;
-#pragma unroll 1
-            for (int c0 = 0; c0 < cols; c0 += 32) {
-                uint32_t v[32];
-                jt::tmem_ld32(trow + c0, v);
-                jt::tmem_wait_ld();
+            const int ce = (colh + 128) < cols ? (colh + 128) : cols;
+            tmem_columns(trow, colh, ce, [&](uint32_t(&v)[32], int c0) {
                 epi_chunk<EPI, 32>(v, m0 + c0, M, ch, ch_ok, swf, ss, sx, out, ldo, lane);
-            }
+            });
             jt::tc_fence_before();
             __syncwarp();
             if (lane == 0) {
@@ -512,7 +534,7 @@ int launch_pair(const CUtensorMap &tmW, const int8_t *X, int ldx, int M, int N, 
     int *err = jtk_error_word();
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs, 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3(kPairThreads, 1, 1);
     cfg.dynamicSmemBytes = kPairSmem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];

@@ -23,6 +23,8 @@ SHAPES = [  # (M, N, K)
     (1, 128, 128), (16, 256, 256), (17, 200, 144), (64, 4096, 1024), (128, 512, 2048),
     (200, 384, 1040), (1000, 256, 512), (300, 130, 64), (512, 768, 1024), (1024, 1024, 256),
     (384, 640, 2176),
+    # CTA-pair kernel: fewer tiles than pairs, ragged K, more tiles than pairs
+    (512, 4096, 1024), (256, 2048, 512), (300, 520, 208), (2560, 2048, 384),
 ]
 
 
@@ -73,6 +75,42 @@ def test_token_channel_f32(M, N, K):
     ref64 = acc.astype(np.float64) * (sx.astype(np.float64)[:, None] * sw.astype(np.float64)[None, :])
     err = np.abs(got - ref64).max() / max(np.abs(ref64).max(), 1e-30)
     assert err < 1e-6
+
+
+def test_pair_kernel_repeat_and_graph_replay():
+    """The CTA-pair kernel (cluster launch) stays bit-exact over back-to-back
+    launches and over replays of one captured CUDA graph."""
+    import torch
+    from tests import _dev
+    M, N, K = 512, 4096, 1024
+    rng = np.random.default_rng(77)
+    X = _rand_s8(rng, (M, K))
+    W = _rand_s8(rng, (N, K))
+    want = np.empty((M, N), np.int32)
+    oracle.oracle().jto_gemm_s8(oracle.ptr(X), oracle.ptr(W), oracle.ptr(want), M, N, K)
+    dX, dW = _dev.to_dev(X), _dev.to_dev(W)
+    dC = _dev.zeros((M, N), np.int32)
+
+    def call():
+        return lib().jt_b200_w8a8_gemm_i32(dX.data_ptr(), K, dW.data_ptr(), K, dC.data_ptr(), N,
+                                           M, N, K, torch.cuda.current_stream().cuda_stream)
+    for _ in range(3):
+        dC.zero_()
+        assert call() == 0
+        assert lib().jt_b200_sync() == 0
+        assert np.array_equal(_dev.host(dC), want)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            assert call() == 0
+        for _ in range(3):
+            dC.zero_()
+            g.replay()
+            torch.cuda.synchronize()
+            assert lib().jt_b200_sync() == 0
+            assert np.array_equal(_dev.host(dC), want)
+    del g
 
 
 @pytest.mark.skipif(not oracle.have_ref(), reason="reference library not built")
