@@ -10,17 +10,24 @@
  *      counts (jt_ep_layout.c), local stable sort with the other ranks'
  *      pairs as a per-expert base, drop + renormalization at the source
  *      (moe_layer.c:1171-1201);
- *   3. per-token int8 quantization; kept rows (codes + {scale, weight})
- *      sent to the owners of their experts with NCCL send/recv;
- *   4. on the owner: rows reordered into expert-contiguous order, routed
- *      gate/up + SwiGLU + requant, down projection writing one weighted
- *      fp32 row per received row;
- *   5. rows sent back to their sources, added into the layer output, which
- *      already holds the shared experts' contribution of the local tokens.
+ *   3. per-token int8 quantization; each token's codes sent ONCE to every
+ *      owner holding at least one of its routed slots, plus 16 bytes of
+ *      metadata per kept (token, slot) pair {scale, weight, token row};
+ *   4. on the owner: pairs expanded into expert-contiguous rows (codes
+ *      copied from the received token row), routed gate/up + SwiGLU +
+ *      requant, down projection adding each pair's weighted fp32 row into
+ *      the row of its token: one summed row per received token;
+ *   5. token rows sent back to their sources and added, owner by owner in
+ *      rank order, into the layer output, which already holds the shared
+ *      experts' contribution of the local tokens.
+ *
+ * Sending tokens instead of pairs divides both exchanges by the mean number
+ * of a token's slots that land on one owner (about k/N for k >= N).
  *
  * The host learns the exchange sizes from the gathered counts (one
- * device-to-host copy and stream synchronization per forward); everything
- * else is stream-ordered.  No device-side remote loads, no multicast.
+ * device-to-host copy per forward, waited on through an event while the
+ * token quantization and the shared experts, which need no layout, run on
+ * the device); everything else is stream-ordered.  No device-side remote loads, no multicast.
  */
 #include <errno.h>
 #include <math.h>
@@ -55,14 +62,17 @@ struct jt_b200_moe_ep_plan {
     float *w_raw, *w_fin, *xs, *hs_s, *y32;
     uint8_t *drop;
     int8_t *xq, *xd, *hq_s;
-    /* exchange */
-    int32_t *cnt, *cnt_all, *gbase, *own_off, *own_tile_off;
+    /* exchange: cnt = E expert counts then N token-row counts */
+    int32_t *cnt, *cnt_all, *gbase, *own_off, *own_tile_off, *trow, *tsoff;
     int4 *gather, *own_tiles;
-    int8_t *rcodes, *own_codes, *own_hq;
+    int8_t *send_tok, *rtok, *own_codes, *own_hq;
     float4 *rmeta, *own_meta;
     float *own_hs, *ret, *back;
+    int R_tok; /* received token rows capacity (T * N) */
+    cudaEvent_t ev_counts; /* the gathered counts reached the host buffer */
     /* host (pinned) */
-    int32_t *h_cnt_all, *h_gbase, *h_send, *h_recv, *h_own_off, *h_own_tile_off, *h_gather;
+    int32_t *h_ext, *h_cnt_all, *h_gbase, *h_send, *h_recv, *h_own_off, *h_own_tile_off, *h_gather;
+    int32_t *h_tsend, *h_trecv, *h_tsoff;
 };
 
 static size_t align_up(size_t v) { return (v + 255) & ~(size_t)255; }
@@ -173,6 +183,9 @@ int jt_b200_moe_ep_plan_create(const jt_b200_moe_dims *dims, jt_b200_ep_comm *co
     const size_t d = (size_t)dims->d, f = (size_t)dims->f, R = (size_t)p->R_max;
     const size_t fs = dims->S > 0 ? (size_t)dims->fs : 64;
     const size_t Tk = T * k, nch = (size_t)jtk_sort_chunks(dims->T), Nn = (size_t)N;
+    const size_t Tdst = T * (Nn < k ? Nn : k); /* token rows sent: <= min(N, k) per token */
+    p->R_tok = (int)(T * Nn);
+    const size_t RT = (size_t)p->R_tok;
     struct {
         void **dst;
         size_t bytes;
@@ -187,16 +200,17 @@ int jt_b200_moe_ep_plan_create(const jt_b200_moe_dims *dims, jt_b200_ep_comm *co
         {(void **)&p->w_raw, Tk * 4},        {(void **)&p->w_fin, Tk * 4},
         {(void **)&p->xs, T * 4},            {(void **)&p->hs_s, ((T + 3) & ~(size_t)3) * (size_t)hs_ld((int)fs) * 4},
         {(void **)&p->y32, T * d * 4},       {(void **)&p->drop, Tk},
-        {(void **)&p->xq, T * d},            {(void **)&p->xd, Tk * d},
+        {(void **)&p->xq, T * d},            {(void **)&p->send_tok, Tdst * d},
         {(void **)&p->hq_s, T * fs},
-        {(void **)&p->cnt, E * 4},           {(void **)&p->cnt_all, Nn * E * 4},
+        {(void **)&p->cnt, (E + Nn) * 4},    {(void **)&p->cnt_all, Nn * (E + Nn) * 4},
+        {(void **)&p->trow, T * Nn * 4},     {(void **)&p->tsoff, (Nn + 1) * 4},
         {(void **)&p->gbase, E * 4},         {(void **)&p->own_off, (El + 1) * 4},
         {(void **)&p->own_tile_off, (El + 1) * 4},
         {(void **)&p->gather, Nn * El * 16}, {(void **)&p->own_tiles, (R / JT_TILE_ROWS + El + 1) * 16},
-        {(void **)&p->rcodes, R * d},        {(void **)&p->own_codes, R * d},
+        {(void **)&p->rtok, RT * d},         {(void **)&p->own_codes, R * d},
         {(void **)&p->own_hq, R * f},        {(void **)&p->rmeta, R * 16},
         {(void **)&p->own_meta, R * 16},     {(void **)&p->own_hs, R * (size_t)hs_ld((int)f) * 4},
-        {(void **)&p->ret, R * d * 4},       {(void **)&p->back, Tk * d * 4},
+        {(void **)&p->ret, RT * d * 4},      {(void **)&p->back, Tdst * d * 4},
     };
     const size_t nparts = sizeof(parts) / sizeof(parts[0]);
     size_t total = 0;
@@ -220,7 +234,8 @@ int jt_b200_moe_ep_plan_create(const jt_b200_moe_dims *dims, jt_b200_ep_comm *co
         *parts[i].dst = (char *)p->arena + offb;
         offb += align_up(parts[i].bytes);
     }
-    const size_t hbytes = (Nn * E + E + 2 * Nn + 2 * (El + 1) + Nn * El * 4) * sizeof(int32_t);
+    const size_t hbytes = (Nn * (E + Nn) + Nn * E + E + 2 * Nn + 2 * (El + 1) + Nn * El * 4 +
+                           3 * (Nn + 1)) * sizeof(int32_t);
     int32_t *h = NULL;
     if (cudaMallocHost((void **)&h, hbytes) != cudaSuccess) {
         cudaFree(p->arena);
@@ -228,21 +243,33 @@ int jt_b200_moe_ep_plan_create(const jt_b200_moe_dims *dims, jt_b200_ep_comm *co
         errno = ENOMEM;
         return JT_ERR_NOMEM;
     }
-    p->h_cnt_all = h;
+    p->h_ext = h;
+    p->h_cnt_all = p->h_ext + Nn * (E + Nn);
     p->h_gbase = p->h_cnt_all + Nn * E;
     p->h_send = p->h_gbase + E;
     p->h_recv = p->h_send + Nn;
     p->h_own_off = p->h_recv + Nn;
     p->h_own_tile_off = p->h_own_off + El + 1;
     p->h_gather = p->h_own_tile_off + El + 1;
+    p->h_tsend = p->h_gather + Nn * El * 4;
+    p->h_trecv = p->h_tsend + Nn + 1;
+    p->h_tsoff = p->h_trecv + Nn + 1;
+    if (cudaEventCreateWithFlags(&p->ev_counts, cudaEventDisableTiming) != cudaSuccess) {
+        cudaFreeHost(h);
+        cudaFree(p->arena);
+        free(p);
+        errno = EIO;
+        return JT_ERR_CUDA;
+    }
     *out = p;
     return JT_OK;
 }
 
 int jt_b200_moe_ep_plan_destroy(jt_b200_moe_ep_plan *p) {
     if (p == NULL) return JT_OK;
+    if (p->ev_counts) cudaEventDestroy(p->ev_counts);
     cudaFree(p->arena);
-    cudaFreeHost(p->h_cnt_all);
+    cudaFreeHost(p->h_ext);
     free(p);
     return JT_OK;
 }
@@ -296,30 +323,18 @@ int jt_b200_moe_ep_forward(jt_b200_moe_ep_plan *p, const jt_b200_moe_weights *w,
     jt_nccl_comm comm = p->comm->comm;
     float *yf = y_bf16 ? p->y32 : (float *)y;
 
-    /* 1. routing and the global expert counts */
+    /* 1. routing, the expert counts and the token-row counts of every rank */
     LAUNCH(jtk_route_topk(logits, bias, T, E, k, p->ids, p->w_raw, st));
     LAUNCH(jtk_ep_count(p->ids, T * k, E, p->cnt, st));
-    NCCL(nc->all_gather(p->cnt, p->cnt_all, (size_t)E, JT_NCCL_INT32, comm, st));
-    CUDA(cudaMemcpyAsync(p->h_cnt_all, p->cnt_all, (size_t)N * E * sizeof(int32_t),
+    LAUNCH(jtk_ep_tokens(p->ids, T, k, El, N, p->trow, p->cnt + E, st));
+    NCCL(nc->all_gather(p->cnt, p->cnt_all, (size_t)(E + N), JT_NCCL_INT32, comm, st));
+    CUDA(cudaMemcpyAsync(p->h_ext, p->cnt_all, (size_t)N * (E + N) * sizeof(int32_t),
                          cudaMemcpyDeviceToHost, st));
-    CUDA(cudaStreamSynchronize(st));
+    CUDA(cudaEventRecord(p->ev_counts, st));
 
-    /* 2. global capacity decision, exchange layout */
-    if (jt_b200_ep_layout(p->h_cnt_all, N, E, rank, p->cap, p->h_gbase, p->h_send, p->h_recv,
-                          p->h_own_off, p->h_own_tile_off, p->h_gather) != JT_OK)
-        return JT_ERR_INVAL;
-    CUDA(cudaMemcpyAsync(p->gbase, p->h_gbase, (size_t)E * sizeof(int32_t), cudaMemcpyHostToDevice, st));
-    CUDA(cudaMemcpyAsync(p->own_off, p->h_own_off, (size_t)(El + 1) * sizeof(int32_t),
-                         cudaMemcpyHostToDevice, st));
-    CUDA(cudaMemcpyAsync(p->own_tile_off, p->h_own_tile_off, (size_t)(El + 1) * sizeof(int32_t),
-                         cudaMemcpyHostToDevice, st));
-    CUDA(cudaMemcpyAsync(p->gather, p->h_gather, (size_t)N * El * 4 * sizeof(int32_t),
-                         cudaMemcpyHostToDevice, st));
-    LAUNCH(jtk_moe_sort(p->ids, p->w_raw, T, k, E, p->cap, p->gbase, p->hist, p->off, p->tile_off,
-                        p->tiles, p->meta, p->perm, p->pos, p->drop, p->w_fin, st));
-
-    /* 3. quantization (xd/row_meta are the send rows, in expert order) */
-    LAUNCH(jtk_quant_dispatch(x, T, d, k, p->pos, p->w_fin, p->xq, p->xs, p->xd, p->row_meta,
+    /* the quantization and the shared experts need no exchange layout: they
+     * run while the host waits for the counts and computes the layout */
+    LAUNCH(jtk_quant_dispatch(x, T, d, k, NULL, p->w_raw, p->xq, p->xs, NULL, NULL,
                               S > 0 ? p->sh_meta : NULL, st));
     if (S > 0) {
         LAUNCH(jtk_fill_single_tiles(p->sh_tiles, p->sh_ntiles, T, st));
@@ -335,10 +350,52 @@ int jt_b200_moe_ep_forward(jt_b200_moe_ep_plan *p, const jt_b200_moe_weights *w,
     } else {
         CUDA(cudaMemsetAsync(yf, 0, (size_t)T * d * sizeof(float), st));
     }
+    CUDA(cudaEventSynchronize(p->ev_counts));
+    for (int s = 0; s < N; s++)
+        memcpy(p->h_cnt_all + (size_t)s * E, p->h_ext + (size_t)s * (E + N), (size_t)E * sizeof(int32_t));
 
-    /* dispatch: rows to their experts' owners */
-    long long soff[64 + 1], roff[64 + 1];
+    /* 2. global capacity decision, exchange layout */
+    if (jt_b200_ep_layout(p->h_cnt_all, N, E, rank, p->cap, p->h_gbase, p->h_send, p->h_recv,
+                          p->h_own_off, p->h_own_tile_off, p->h_gather) != JT_OK)
+        return JT_ERR_INVAL;
+    /* token rows: sent to owner o = ext[rank][E + o], received from source
+     * s = ext[s][E + rank]; gather entries carry their source's first
+     * received token row */
+    long long tsoff[64 + 1], rtoff[64 + 1];
     if (N > 64) return JT_ERR_INVAL;
+    tsoff[0] = rtoff[0] = 0;
+    for (int i = 0; i < N; i++) {
+        p->h_tsend[i] = p->h_ext[(size_t)rank * (E + N) + E + i];
+        p->h_trecv[i] = p->h_ext[(size_t)i * (E + N) + E + rank];
+        tsoff[i + 1] = tsoff[i] + p->h_tsend[i];
+        rtoff[i + 1] = rtoff[i] + p->h_trecv[i];
+        p->h_tsoff[i] = (int32_t)tsoff[i];
+    }
+    if (rtoff[N] > p->R_tok) {
+        jt_set_last_error("expert-parallel received token rows exceed the plan capacity", 0);
+        errno = ERANGE;
+        return JT_ERR_INVAL;
+    }
+    for (int s = 0; s < N; s++)
+        for (int el = 0; el < El; el++) p->h_gather[((size_t)s * El + el) * 4 + 3] = (int32_t)rtoff[s];
+    CUDA(cudaMemcpyAsync(p->gbase, p->h_gbase, (size_t)E * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    CUDA(cudaMemcpyAsync(p->own_off, p->h_own_off, (size_t)(El + 1) * sizeof(int32_t),
+                         cudaMemcpyHostToDevice, st));
+    CUDA(cudaMemcpyAsync(p->own_tile_off, p->h_own_tile_off, (size_t)(El + 1) * sizeof(int32_t),
+                         cudaMemcpyHostToDevice, st));
+    CUDA(cudaMemcpyAsync(p->gather, p->h_gather, (size_t)N * El * 4 * sizeof(int32_t),
+                         cudaMemcpyHostToDevice, st));
+    CUDA(cudaMemcpyAsync(p->tsoff, p->h_tsoff, (size_t)N * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    LAUNCH(jtk_moe_sort(p->ids, p->w_raw, T, k, E, p->cap, p->gbase, p->hist, p->off, p->tile_off,
+                        p->tiles, p->meta, p->perm, p->pos, p->drop, p->w_fin, st));
+
+    /* 3. the send buffers: token rows per owner and the kept pairs'
+     * metadata in send (expert) order */
+    LAUNCH(jtk_ep_pack(p->xq, p->xs, T, d, k, El, N, p->ids, p->pos, p->w_fin, p->trow, p->tsoff,
+                       p->send_tok, p->row_meta, st));
+
+    /* dispatch: token rows and pair metadata to the experts' owners */
+    long long soff[64 + 1], roff[64 + 1];
     soff[0] = roff[0] = 0;
     for (int i = 0; i < N; i++) {
         soff[i + 1] = soff[i] + p->h_send[i];
@@ -351,42 +408,45 @@ int jt_b200_moe_ep_forward(jt_b200_moe_ep_plan *p, const jt_b200_moe_weights *w,
     }
     NCCL(nc->group_start());
     for (int o = 0; o < N; o++) {
-        if (p->h_send[o]) {
-            NCCL(nc->send(p->xd + (size_t)soff[o] * d, (size_t)p->h_send[o] * d, JT_NCCL_INT8, o, comm, st));
+        if (p->h_tsend[o])
+            NCCL(nc->send(p->send_tok + (size_t)tsoff[o] * d, (size_t)p->h_tsend[o] * d, JT_NCCL_INT8, o, comm, st));
+        if (p->h_send[o])
             NCCL(nc->send(p->row_meta + soff[o], (size_t)p->h_send[o] * 4, JT_NCCL_FLOAT32, o, comm, st));
-        }
-        if (p->h_recv[o]) {
-            NCCL(nc->recv(p->rcodes + (size_t)roff[o] * d, (size_t)p->h_recv[o] * d, JT_NCCL_INT8, o, comm, st));
+        if (p->h_trecv[o])
+            NCCL(nc->recv(p->rtok + (size_t)rtoff[o] * d, (size_t)p->h_trecv[o] * d, JT_NCCL_INT8, o, comm, st));
+        if (p->h_recv[o])
             NCCL(nc->recv(p->rmeta + roff[o], (size_t)p->h_recv[o] * 4, JT_NCCL_FLOAT32, o, comm, st));
-        }
     }
     NCCL(nc->group_end());
 
-    /* 4. owned experts */
+    /* 4. owned experts; each pair's weighted row is added into its token's
+     * returned row */
     const int own_rows = p->h_own_off[El];
     const int own_tiles = p->h_own_tile_off[El];
+    if (rtoff[N] > 0)
+        CUDA(cudaMemsetAsync(p->ret, 0, (size_t)rtoff[N] * d * sizeof(float), st));
     if (own_rows > 0) {
-        LAUNCH(jtk_ep_gather(p->gather, N * El, p->rcodes, p->rmeta, d, p->own_codes, p->own_meta, st));
+        LAUNCH(jtk_ep_gather(p->gather, N * El, p->rtok, p->rmeta, d, p->own_codes, p->own_meta, st));
         LAUNCH(jtk_build_tiles(p->own_off, p->own_tile_off, El, p->own_tiles, st));
         const int gu_hint = own_tiles * (f / 64), dn_hint = own_tiles * (d / 128);
         LAUNCH(jtk_moe_gateup_routed(w->wg, w->wu, w->sg, w->su, El, f, d, p->own_codes, p->R_max,
                                      p->own_meta, p->own_tiles, p->own_tile_off + El, p->own_hq,
                                      p->own_hs, gu_hint, st));
         LAUNCH(jtk_moe_down_routed(w->wd, w->sd, El, d, f, p->own_hq, p->R_max, p->own_hs,
-                                   p->own_meta, p->own_tiles, p->own_tile_off + El, p->ret, 0,
+                                   p->own_meta, p->own_tiles, p->own_tile_off + El, p->ret, 1,
                                    dn_hint, st));
     }
 
-    /* 5. combine: rows back to their sources, added into y */
+    /* 5. combine: token rows back to their sources, added into y */
     NCCL(nc->group_start());
     for (int o = 0; o < N; o++) {
-        if (p->h_recv[o])
-            NCCL(nc->send(p->ret + (size_t)roff[o] * d, (size_t)p->h_recv[o] * d, JT_NCCL_FLOAT32, o, comm, st));
-        if (p->h_send[o])
-            NCCL(nc->recv(p->back + (size_t)soff[o] * d, (size_t)p->h_send[o] * d, JT_NCCL_FLOAT32, o, comm, st));
+        if (p->h_trecv[o])
+            NCCL(nc->send(p->ret + (size_t)rtoff[o] * d, (size_t)p->h_trecv[o] * d, JT_NCCL_FLOAT32, o, comm, st));
+        if (p->h_tsend[o])
+            NCCL(nc->recv(p->back + (size_t)tsoff[o] * d, (size_t)p->h_tsend[o] * d, JT_NCCL_FLOAT32, o, comm, st));
     }
     NCCL(nc->group_end());
-    LAUNCH(jtk_ep_combine(p->perm, (int)soff[N], k, p->back, d, yf, st));
+    LAUNCH(jtk_ep_combine(p->trow, p->tsoff, T, N, p->back, d, yf, st));
     if (y_bf16) LAUNCH(jtk_f32_to_bf16(yf, (uint16_t *)y, (size_t)T * d, st));
     return JT_OK;
 }

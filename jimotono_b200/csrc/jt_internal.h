@@ -79,10 +79,15 @@ int jtk_build_tiles(const int32_t *off, const int32_t *tile_off, int E, int4 *ti
 
 /* Expert-parallel exchange kernels (jt_ep.cu). */
 int jtk_ep_count(const int32_t *ids, int n, int E, int32_t *cnt, cudaStream_t stream);
-int jtk_ep_gather(const int4 *ent, int n_ent, const int8_t *src_codes, const float4 *src_meta,
-                  int d, int8_t *dst_codes, float4 *dst_meta, cudaStream_t stream);
-int jtk_ep_combine(const int32_t *perm, int kept, int k, const float *back, int d, float *y,
-                   cudaStream_t stream);
+int jtk_ep_tokens(const int32_t *ids, int T, int k, int El, int N, int32_t *trow, int32_t *ntok,
+                  cudaStream_t stream);
+int jtk_ep_pack(const int8_t *xq, const float *xs, int T, int d, int k, int El, int N, const int32_t *ids,
+                const int32_t *pos, const float *wfin, const int32_t *trow, const int32_t *tsoff,
+                int8_t *send_tok, float4 *row_meta, cudaStream_t stream);
+int jtk_ep_gather(const int4 *ent, int n_ent, const int8_t *rtok, const float4 *src_meta, int d,
+                  int8_t *dst_codes, float4 *dst_meta, cudaStream_t stream);
+int jtk_ep_combine(const int32_t *trow, const int32_t *tsoff, int T, int N, const float *back, int d,
+                   float *y, cudaStream_t stream);
 
 /* Per-token quantization + dispatch; row_meta[row] = {scale, weight, token bits, 0}
  * for every kept row, sh_meta[t] = {scale, 1, t bits, 0} (may be NULL). */
