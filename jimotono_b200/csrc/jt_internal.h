@@ -78,6 +78,9 @@ int jtk_build_tiles(const int32_t *off, const int32_t *tile_off, int E, int4 *ti
                     cudaStream_t stream);
 
 /* Expert-parallel exchange kernels (jt_ep.cu). */
+int jtk_shared_gu_pair(const int8_t *wsg, const int8_t *wsu, const float *ssg, const float *ssu, int fs,
+                       int d, const int8_t *xq, const float4 *sh_meta, int T, int8_t *hq, float *hs,
+                       cudaStream_t stream);
 int jtk_ep_count(const int32_t *ids, int n, int E, int32_t *cnt, cudaStream_t stream);
 int jtk_ep_tokens(const int32_t *ids, int T, int k, int El, int N, int32_t *trow, int32_t *ntok,
                   cudaStream_t stream);

@@ -904,6 +904,9 @@ extern "C" int jtk_moe_gateup_shared(const int8_t *wsg, const int8_t *wsu, const
                                      const int32_t *ntiles, int8_t *hq, float *hs,
                                      cudaStream_t stream) {
     if (fs % 64 || d % kBK || T <= 0) return -1;
+    // 256-token CTA-pair tiles when the shape allows (jt_shared_pair.cu)
+    const int rp = jtk_shared_gu_pair(wsg, wsu, ssg, ssu, fs, d, xq, sh_meta, T, hq, hs, stream);
+    if (rp != -1) return rp;
     MoeGemmParams p{};
     if (!jt::make_tmap_2d_u8(&p.tmA0, wsg, d, fs, d, kBK, 64, true) ||
         !jt::make_tmap_2d_u8(&p.tmA1, wsu, d, fs, d, kBK, 64, true) ||

@@ -27,6 +27,7 @@
 #include <cuda_runtime.h>
 
 #include "jt_internal.h"
+#include "jt_pair.cuh"
 #include "jt_ptx.cuh"
 #include "jt_runtime.cuh"
 
@@ -266,250 +267,61 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
-// CTA-pair form for M >= 256: a 2-CTA cluster computes a 256-channel x
-// 256-token tile with tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32).
-// Rank r loads weight channels n0 + 128r .. +127 (its half of A) and tokens
-// m0 + 128r .. +127 (its half of B) into its own shared memory; its TMEM holds
-// D for its 128 channels x all 256 tokens.  Per 128-K stage each SM reads
-// 32 KB from L2 instead of the 48 KB of the single-CTA 128 x 256 tile, and
-// each MMA reads 8 KB of its shared memory instead of 12 KB.
-//
-// Barriers: full[s] on rank 0 counts the bytes of both ranks' boxes of stage
-// s (rank 1's loads report to it through the pair form of the TMA load; rank
-// 0's producer posts the expected 64 KB); empty[s] and tfull[b] in both ranks
-// are signalled by the MMA commit multicast to both; tempty[b] on rank 0
-// counts the eight epilogue warps of each rank.
-// The TMA loads carry no multicast: each rank fetches its own halves.
-constexpr int kPairStages = 6;
-constexpr uint32_t kPairBox = 128 * kBK;          // one 128-row x 128-byte box, 16 KB
-constexpr uint32_t kPairStage = 2 * kPairBox;     // weight box + token box
-constexpr uint32_t kPairCols = 512;               // two 256-column accumulators
-// 16 KB between the last stage and the barriers: no operand read of the
-// stage ring can leave the allocation, whatever the descriptors cover.
-constexpr uint32_t kPairSlack = 16384;
-constexpr size_t kPairSmem = 1024 + kPairStages * kPairStage + kPairSlack + 512;
-constexpr int kPairThreads = 320;                // 10 warps: TMA, MMA, 8 epilogue
-
-// Runs fn(v, c0) over the 32-column TMEM chunks c0 = cb, cb+32, .. < ce of
-// this warp's lane quarter, the load of the next chunk in flight while fn
-// processes the current one (warp-uniform bounds).
-template <typename Fn>
-__device__ __forceinline__ void tmem_columns(uint32_t trow, int cb, int ce, Fn &&fn) {
-    if (cb >= ce) return;
-    uint32_t va[32], vb[32];
-    jt::tmem_ld32(trow + cb, va);
-#pragma unroll 1
-    for (int c0 = cb; c0 < ce; c0 += 64) {
-        jt::tmem_wait_ld32(va);
-        const bool more = c0 + 32 < ce;
-        if (more) jt::tmem_ld32(trow + c0 + 32, vb);
-        fn(va, c0);
-        if (!more) break;
-        jt::tmem_wait_ld32(vb);
-        if (c0 + 64 < ce) jt::tmem_ld32(trow + c0 + 64, va);
-        fn(vb, c0 + 32);
-    }
-}
+// CTA-pair form for M >= 256: 256 weight channels x 256 tokens per 2-CTA
+// cluster on the jt_pair.cuh pipeline (tcgen05 cta_group::2).  Rank r's
+// weight box is channels n0 + 128r .. +127; its epilogue writes those
+// channels for all 256 tokens of the tile.
+constexpr size_t kPairSmem = 1024 + jt::pair::kRing + jt::pair::kBarBytes;
 
 template <int EPI>
-__global__ void __launch_bounds__(kPairThreads, 1)
+__global__ void __launch_bounds__(jt::pair::kThreads, 1)
     k_w8a8_pair(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                 int M, int N, int K, const float *__restrict__ sx, const float *__restrict__ sw,
                 double sA, void *__restrict__ out, int ldo, int *err) {
-    constexpr int S = kPairStages;
+    namespace jp = jt::pair;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + S * kPairStage + kPairSlack);
-    uint64_t *empty = full + S;
-    uint64_t *tfull = empty + S;
-    uint64_t *tempty = tfull + 2;
-    uint64_t *drain = tempty + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-
-    const int warp = jt::warp_id();
-    const int lane = jt::lane_id();
-    const uint32_t rank = jt::cluster_ctarank();
-    const int pair = static_cast<int>(jt::cluster_id_x());
-    const int npairs = static_cast<int>(jt::ncluster_x());
+    jp::Ctx c;
+    const CUtensorMap *maps[2] = {&tmW, &tmX};
+    jp::setup(c, smem, smem + jp::kRing, err, maps, 2);
     const int n_ch_tiles = (N + 255) / 256;
-    const int n_tok_tiles = (M + 255) / 256;
-    const int ntiles = n_ch_tiles * n_tok_tiles;
+    const int ntiles = n_ch_tiles * ((M + 255) / 256);
     const int nk = (K + kBK - 1) / kBK;
 
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) {
-            jt::mbar_init(&full[s], 1);
-            jt::mbar_init(&empty[s], 1);
-        }
-        for (int b = 0; b < 2; ++b) {
-            jt::mbar_init(&tfull[b], 1);
-            jt::mbar_init(&tempty[b], 16);
-        }
-        jt::mbar_init(drain, 1);
-        *abort_flag = 0;
-        jt::fence_mbar_init();
-    }
-    if (warp == 0 && lane == 0) {
-        jt::prefetch_tmap(&tmW);
-        jt::prefetch_tmap(&tmX);
-    }
-    if (warp == 1) {
-        jt::tmem_alloc_pair(tmem_slot, kPairCols);
-        jt::tmem_relinquish_pair();
-    }
-    jt::tc_fence_before();
-    __syncthreads();
-    // both ranks' barriers are initialised before any cross-CTA signal
-    jt::cluster_sync();
-    jt::tc_fence_after();
-    const uint32_t tmem_base = *tmem_slot;
-
-    if (warp == 0) {
-        if (lane == 0) {
-            uint32_t stage = 0, phase = 0;
-            uint32_t issued_mask = 0, issued_phase = 0;
-            bool ok = true;
-            for (int tile = pair; tile < ntiles && ok; tile += npairs) {
-                const int n0 = (tile % n_ch_tiles) * 256 + static_cast<int>(rank) * 128;
-                const int m0 = (tile / n_ch_tiles) * 256 + static_cast<int>(rank) * 128;
-                for (int kb = 0; kb < nk; ++kb) {
-                    if (!jt::mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, err)) {
-                        ok = false;
-                        break;
-                    }
-                    uint8_t *sW = smem + stage * kPairStage;
-                    if (rank == 0) jt::mbar_arrive_expect_tx(&full[stage], 2 * kPairStage);
-                    const uint32_t bar = jt::cluster_addr(&full[stage], 0);
-                    jt::tma_load_2d_pair(sW, &tmW, bar, kb * kBK, n0);
-                    jt::tma_load_2d_pair(sW + kPairBox, &tmX, bar, kb * kBK, m0);
-                    issued_mask |= 1u << stage;
-                    issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
-                    if (++stage == S) {
-                        stage = 0;
-                        phase ^= 1u;
-                    }
-                }
-            }
-            // Tail: the MMA commits that release the last stages arrive on
-            // this CTA's barriers asynchronously; wait for every one of them
-            // so none lands after the CTA has exited.
-            for (int i = 0; i < S && ok; ++i) {
-                if (!jt::mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, err)) ok = false;
-                if (++stage == S) {
-                    stage = 0;
-                    phase ^= 1u;
-                }
-            }
-            if (!ok) {
-                // Every issued box must land before the CTA exits.  Rank 0
-                // waits (bounded) for the last issued phase of each stage;
-                // rank 1 cannot observe its boxes (they report to rank 0)
-                // and waits a fixed, bounded interval instead.
-                if (rank == 0) {
-                    for (int s = 0; s < S; ++s) {
-                        if (!(issued_mask & (1u << s))) continue;
-                        const uint32_t par = (issued_phase >> s) & 1u;
-                        const long long t0 = clock64();
-                        while (!jt::mbar_try_wait(&full[s], par) &&
-                               clock64() - t0 < JT_SPIN_CYCLES / 16) {
-                        }
-                    }
-                } else if (issued_mask) {
-                    const long long t0 = clock64();
-                    while (clock64() - t0 < JT_SPIN_CYCLES / 64) __nanosleep(1000);
-                }
-            }
-        }
-    } else if (warp == 1) {
-        // rank 0: the pair's MMA issuer (rank 1's warp 1 only allocates)
-        if (lane == 0 && rank == 0) {
-            constexpr uint32_t kIdesc = jt::idesc_i8(256, 256);
-            uint32_t stage = 0, phase = 0;
-            int it = 0;
-            bool ok = true;
-            for (int tile = pair; tile < ntiles && ok; tile += npairs, ++it) {
-                const uint32_t buf = it & 1;
-                const uint32_t use = (it >> 1) & 1;
-                if (!jt::mbar_wait_cluster(&tempty[buf], use ^ 1u, abort_flag, err)) {
-                    ok = false;
-                    break;
-                }
-                jt::tc_fence_after();
-                const uint32_t d_tmem = tmem_base + buf * 256;
-                for (int kb = 0; kb < nk; ++kb) {
-                    if (!jt::mbar_wait_cluster(&full[stage], phase, abort_flag, err)) {
-                        ok = false;
-                        break;
-                    }
-                    jt::tc_fence_after();
-                    const uint32_t aW = jt::smem_u32(smem + stage * kPairStage);
-                    const uint64_t da = jt::umma_desc_sw128(aW);
-                    const uint64_t db = jt::umma_desc_sw128(aW + kPairBox);
-#pragma unroll
-                    for (int j = 0; j < kBK / 32; ++j)
-                        jt::mma_i8_pair(d_tmem, da + 2u * j, db + 2u * j, kIdesc,
-                                        (kb | j) != 0 ? 1u : 0u);
-                    jt::mma_commit_pair(&empty[stage], 0x3);
-                    if (++stage == S) {
-                        stage = 0;
-                        phase ^= 1u;
-                    }
-                }
-                if (!ok) break;
-                jt::mma_commit_pair(&tfull[buf], 0x3);
-            }
-            if (!ok) {
-                jt::mma_commit_pair(drain, 0x1);
-                const long long t0 = clock64();
-                while (!jt::mbar_try_wait(drain, 0) && clock64() - t0 < JT_SPIN_CYCLES / 16) {
-                }
-            }
-        }
+    if (c.warp == 0) {
+        if (c.lane == 0)
+            jp::producer(
+                c, &tmX, ntiles, nk,
+                [&](uint8_t *dst, int kb, int tile, uint32_t bar) {
+                    jt::tma_load_2d_pair(dst, &tmW, bar, kb * kBK,
+                                         (tile % n_ch_tiles) * 256 + static_cast<int>(c.rank) * 128);
+                },
+                [&](int tile) { return tile / n_ch_tiles; });
+    } else if (c.warp == 1) {
+        if (c.lane == 0 && c.rank == 0) jp::mma(c, ntiles, nk);
     } else {
-        // Epilogue warps 2..9: warp w reads TMEM lanes 32*(w%4)..+31 (this
-        // rank's channels) and token columns 128*((w-2)/4) .. +127.
-        const int q = warp & 3;
-        const int cl = q * 32 + lane;  // channel within this rank's 128
-        const int colh = ((warp - 2) >> 2) * 128;
+        const int cl = (c.warp & 3) * 32 + c.lane;  // channel within this rank's 128
+        const int colh = ((c.warp - 2) >> 2) * 128;
         int it = 0;
-        for (int tile = pair; tile < ntiles; tile += npairs, ++it) {
-            const uint32_t buf = it & 1;
-            const uint32_t use = (it >> 1) & 1;
-            if (!jt::mbar_wait_cluster(&tfull[buf], use, abort_flag, err)) break;
-            jt::tc_fence_after();
-            const int ch = (tile % n_ch_tiles) * 256 + static_cast<int>(rank) * 128 + cl;
+        for (int tile = c.pair; tile < ntiles; tile += c.npairs, ++it) {
+            if (!jp::epi_acquire(c, it)) break;
+            const int ch = (tile % n_ch_tiles) * 256 + static_cast<int>(c.rank) * 128 + cl;
             const int m0 = (tile / n_ch_tiles) * 256;
             const bool ch_ok = ch < N;
             float swf = 0.f;
             double ss = 0.0;
             if (EPI == JTK_EPI_TOKEN_CHANNEL_F32) swf = ch_ok ? sw[ch] : 0.f;
             if (EPI == JTK_EPI_TENSOR_CHANNEL_F64) ss = ch_ok ? sA * (double)sw[ch] : 0.0;
-            const uint32_t trow = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * 256;
             const int cols = (M - m0) < 256 ? (M - m0) : 256;
             const int ce = (colh + 128) < cols ? (colh + 128) : cols;
-            tmem_columns(trow, colh, ce, [&](uint32_t(&v)[32], int c0) {
-                epi_chunk<EPI, 32>(v, m0 + c0, M, ch, ch_ok, swf, ss, sx, out, ldo, lane);
+            jp::tmem_columns(jp::epi_row(c, it), colh, ce, [&](uint32_t(&v)[32], int c0) {
+                epi_chunk<EPI, 32>(v, m0 + c0, M, ch, ch_ok, swf, ss, sx, out, ldo, c.lane);
             });
-            jt::tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                if (rank == 0)
-                    jt::mbar_arrive(&tempty[buf]);
-                else
-                    jt::mbar_arrive_cluster(&tempty[buf], 0);
-            }
+            jp::epi_release(c, it);
         }
     }
-    __syncthreads();
-    // no CTA of the pair releases TMEM or exits while its peer may still
-    // signal its barriers or read its shared memory
-    jt::cluster_sync();
-    if (warp == 1) {
-        jt::tc_fence_after();
-        jt::tmem_dealloc_pair(tmem_base, kPairCols);
-    }
+    jp::teardown(c);
 }
 
 template <int EPI>
@@ -531,20 +343,10 @@ int launch_pair(const CUtensorMap &tmW, const int8_t *X, int ldx, int M, int N, 
     const int ntiles = ((N + 255) / 256) * ((M + 255) / 256);
     int pairs = jtk_num_sms() / 2;
     if (pairs > ntiles) pairs = ntiles;
-    int *err = jtk_error_word();
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * pairs, 1, 1);
-    cfg.blockDim = dim3(kPairThreads, 1, 1);
-    cfg.dynamicSmemBytes = kPairSmem;
-    cfg.stream = stream;
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, kern, tmW, tmX, M, N, K, sx, sw, sA, out, ldo, err) != cudaSuccess)
+    const cudaLaunchConfig_t cfg = jt::pair::launch_config(pairs, kPairSmem, stream, attr);
+    if (cudaLaunchKernelEx(&cfg, kern, tmW, tmX, M, N, K, sx, sw, sA, out, ldo, jtk_error_word()) !=
+        cudaSuccess)
         return -4;
     return 0;
 }

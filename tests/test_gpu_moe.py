@@ -82,6 +82,8 @@ CASES = [
     (200, 128, 128, 4, 2, 0, 0, 1.0, 1.1),     # drops + renormalization, no shared experts
     (300, 512, 384, 16, 4, 1, 128, 1.25, 1.1),
     (130, 2048, 128, 32, 8, 2, 256, 1.5, 1.1),
+    # shared gate/up on 256-token CTA-pair tiles: 3 channel tiles, ragged last token tile
+    (600, 256, 128, 8, 2, 2, 384, 1.5, None),
 ]
 
 
