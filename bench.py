@@ -9,9 +9,13 @@ batch-1 decode HBM GB/s (config 2), prefill tokens/s (config 3).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
-N > 1 runs under torchrun, one rank per GPU.  Until the NCCL dispatch /
-combine path lands every rank runs an independent replica of the layer on
-its own token slice ("replicas" in config.parallelism).
+N > 1 runs under torchrun, one rank per GPU: the expert-parallel layer
+(E/N experts and T/N tokens per rank, NCCL send/recv dispatch and combine),
+timed with CUDA events, the max over ranks.
+
+`e2e` is the same metric through the public API with host buffers: every
+step copies its inputs from pinned host memory and its output back, the
+copies on their own streams overlapping the neighbouring steps' compute.
 
 `--impl reference` times the reference's own CPU implementation
 (oracle/_ref, the reference sources compiled unmodified) on the host cores.
@@ -288,30 +292,16 @@ def time_layer_ep(torch, cfg, rank, world, steps, warmup, seed):
     if lib().jt_b200_sync() != 0:
         raise RuntimeError("kernel fault during the timed region")
     meta = plan.debug(9, np.int32, 4)
-    # end to end: pinned host x / logits in, y out, every step
+    # end to end: pinned host x / logits in, y out, every step (pipelined
+    # copies, e2e_pipelined); every rank starts its timed region together
     hx = x.cpu().pin_memory()
     hl = logits.cpu().pin_memory()
-    hy = torch.empty(y.shape, dtype=y.dtype).pin_memory()
 
-    def step_e2e():
-        x.copy_(hx, non_blocking=True)
-        logits.copy_(hl, non_blocking=True)
-        step()
-        hy.copy_(y, non_blocking=True)
+    def fwd(dx, dl, yy, stream):
+        plan.forward(wp, dx.data_ptr(), dl.data_ptr(), None, yy.data_ptr(), False, stream)
 
-    for _ in range(2):
-        step_e2e()
     torch.distributed.barrier()
-    torch.cuda.synchronize()
-    e0.record()
-    n_e2e = max(2, steps // 2)
-    for _ in range(n_e2e):
-        step_e2e()
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / n_e2e
-    h2d = hx.numel() * 4 + hl.numel() * 4
-    d2h = hy.numel() * 4
+    e2e_ms, h2d, d2h = e2e_pipelined(torch, hx, hl, y, fwd, max(2, steps // 2), 2)
     out = dict(T=T, ms_per_step=ms, e2e_ms=e2e_ms, h2d=h2d, d2h=d2h, kept_local=int(meta[0]),
                owned_rows=int(meta[1]), dims=dm)
     plan.close()
@@ -320,41 +310,72 @@ def time_layer_ep(torch, cfg, rank, world, steps, warmup, seed):
     return out
 
 
-def e2e_layer(torch, st, steps, warmup):
-    """Same layer through the public API with host buffers: H2D of x and the
-    router logits from pinned memory, forward, D2H of the output, per step."""
-    dm, plan = st["dims"], st["plan"]
-    T = st["T"]
-    hx = torch.empty_like(st["x"], device="cpu").pin_memory()
-    hl = torch.empty_like(st["logits"], device="cpu").pin_memory()
-    hx.copy_(st["x"].cpu())
-    hl.copy_(st["logits"].cpu())
-    dx, dl = torch.empty_like(st["x"]), torch.empty_like(st["logits"])
-    y = st["y"]
-    hy = torch.empty(y.shape, dtype=y.dtype, device="cpu").pin_memory()
-    stream = torch.cuda.current_stream().cuda_stream
-    bp = st["bias"].data_ptr() if st["bias"] is not None else None
-    wp = st["rots"][0][1]
+def e2e_pipelined(torch, hx, hl, y_like, forward, steps, warmup):
+    """End to end through the public API with host buffers, as a serving
+    loop runs it: every step copies its inputs (x, router logits) from
+    pinned host memory, runs the forward and copies its output back.  The
+    copies go on their own streams into double-buffered device buffers, so
+    step i+1's inputs and step i-1's output cross PCIe while step i
+    computes; every step's copies are inside the timed region, which ends
+    when the last output has reached host memory.  forward(dx, dl, y,
+    stream) enqueues one forward on `stream`."""
+    cs = torch.cuda.current_stream()
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    dx = [torch.empty(hx.shape, dtype=hx.dtype, device="cuda") for _ in range(2)]
+    dl = [torch.empty(hl.shape, dtype=hl.dtype, device="cuda") for _ in range(2)]
+    ys = [torch.empty_like(y_like) for _ in range(2)]
+    hy = [torch.empty(y_like.shape, dtype=y_like.dtype, device="cpu").pin_memory() for _ in range(2)]
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_comp = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
 
-    def step():
-        dx.copy_(hx, non_blocking=True)
-        dl.copy_(hl, non_blocking=True)
-        plan.forward(wp, dx.data_ptr(), dl.data_ptr(), bp, T, y.data_ptr(), st["bf16"], stream)
-        hy.copy_(y, non_blocking=True)
+    def step(i):
+        b = i & 1
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(ev_comp[b])  # step i-2 has consumed buffer b
+            dx[b].copy_(hx, non_blocking=True)
+            dl[b].copy_(hl, non_blocking=True)
+            ev_in[b].record(s_in)
+        cs.wait_event(ev_in[b])
+        cs.wait_event(ev_out[b])  # step i-2's output has left buffer b
+        forward(dx[b], dl[b], ys[b], cs.cuda_stream)
+        ev_comp[b].record(cs)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_comp[b])
+            hy[b].copy_(ys[b], non_blocking=True)
+            ev_out[b].record(s_out)
 
-    for _ in range(warmup):
-        step()
+    for i in range(warmup):
+        step(i)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-        step()
-    e1.record()
+    e0.record(cs)
+    s_in.wait_event(e0)
+    s_out.wait_event(e0)
+    for i in range(warmup, warmup + steps):
+        step(i)
+    cs.wait_event(ev_out[(warmup + steps - 1) & 1])
+    e1.record(cs)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
     h2d = hx.numel() * hx.element_size() + hl.numel() * hl.element_size()
-    d2h = hy.numel() * hy.element_size()
+    d2h = hy[0].numel() * hy[0].element_size()
     return ms, h2d, d2h
+
+
+def e2e_layer(torch, st, steps, warmup):
+    """The single-GPU layer end to end (e2e_pipelined)."""
+    plan = st["plan"]
+    T = st["T"]
+    hx = st["x"].cpu().pin_memory()
+    hl = st["logits"].cpu().pin_memory()
+    bp = st["bias"].data_ptr() if st["bias"] is not None else None
+    wp = st["rots"][0][1]
+
+    def fwd(dx, dl, y, stream):
+        plan.forward(wp, dx.data_ptr(), dl.data_ptr(), bp, T, y.data_ptr(), st["bf16"], stream)
+
+    return e2e_pipelined(torch, hx, hl, st["y"], fwd, steps, warmup)
 
 
 # ----------------------------------------------------------------- parts
