@@ -647,7 +647,7 @@ def main():
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+            "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded; random-init packed weights)",
             "config": {"workload": "cfg5 EP MoE layer: T=16384 d=2048 E=1024 f=1536 top-8 INT2/INT4 g64 + 2 shared INT8 f=4096, cap 1.5",
                        "tokens": tokens, "parallelism": f"replicas{world}" if world > 1 else "single GPU",

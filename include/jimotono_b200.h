@@ -231,6 +231,36 @@ int jt_b200_lowbit_gemv(const int8_t *a, float sa, const uint8_t *w2, const uint
                         const uint8_t *w4, const uint16_t *s4, int n4, int K, float *y,
                         void *stream);
 
+/* Weight packer: fp32 masters W [rows][K] (device) -> the packed format
+ * read by jt_b200_lowbit_gemv and the prepared MoE layer.  Replaces the
+ * per-call weight preparation of the reference's low-bit path
+ * (jt_lowbit_col_to_idx, lowbit.h:45 / lowbit.c:93-141, rebuilt for every
+ * column on every call by jt_lowbit_gemm_lut, lowbit.c:228-237) with a
+ * one-time pack.  Its level rule is applied per 64-element K group:
+ * maxa = max |w| of the group, li = floor(w/maxa * (n-1)/2 + (n-1)/2 + 0.5)
+ * clamped to [0, n-1] (double, n = 2^bits), scale = (half)(float)(maxa/(n-1)).
+ * bits 2 or 4; K % 64 == 0; W 8-byte aligned.  packed [rows][K*bits/8];
+ * scales fp16: n_ch == 0 -> [rows][K/64] (GEMV layout); n_ch > 0 -> rows
+ * are blocks of n_ch output channels (one expert each) and the scales are
+ * group-major per block, [rows/n_ch][K/64][n_ch] (jt_b200_moe_weights
+ * layout).  A non-finite weight is reported by jt_b200_sync.  Device
+ * pointers, asynchronous on stream. */
+int jt_b200_lowbit_pack(const float *W, int rows, int K, int bits, int n_ch, uint8_t *packed,
+                        uint16_t *scales, void *stream);
+
+/* Converter from the reference's bit-plane index (jt_lowbit_col_to_idx,
+ * lowbit.h:45 / lowbit.c:117-139) to packed rows: idx holds `cols`
+ * consecutive columns of bits*K/4 bytes each; byte b*K/4 + q of a column
+ * carries, in bit i, bit b of the code of element 4q + i.  packed
+ * [cols][K*bits/8] receives the same codes li.  With w_scale [cols] (the
+ * reference's whole-column max-abs) every group of column j gets the scale
+ * (half)(float)(w_scale[j]/(n-1)), in the layout chosen by n_ch as above;
+ * w_scale and scales are both NULL or both given.  bits 2 or 4, K % 64 == 0.
+ * Device pointers, asynchronous on stream. */
+int jt_b200_lowbit_planes_to_packed(const uint8_t *idx, const float *w_scale, int cols, int K,
+                                    int bits, int n_ch, uint8_t *packed, uint16_t *scales,
+                                    void *stream);
+
 /* ---- quantized MoE layer (prepared weights) ----
  *
  * The layer of jt_moe_fwd_batch (moe_layer.c:980-1614; moe_layer.h:230-246)

@@ -49,6 +49,8 @@ PROTOTYPES = {
     "jt_b200_w8a8_gemm_i32": (I, [P, I, P, I, P, I, I, I, I, P]),
     "jt_b200_w8a8_linear_noalloc": (I, [P, I, I, P, I, P, P, I, I, P]),
     "jt_b200_lowbit_gemv": (I, [P, F, P, P, I, P, P, I, I, P, P]),
+    "jt_b200_lowbit_pack": (I, [P, I, I, I, I, P, P, P]),
+    "jt_b200_lowbit_planes_to_packed": (I, [P, P, I, I, I, I, P, P, P]),
     "jt_b200_moe_plan_create": (I, [P, P]),
     "jt_b200_moe_plan_destroy": (I, [P]),
     "jt_b200_moe_plan_bytes": (SZ, [P]),

@@ -389,6 +389,30 @@ int jt_b200_lowbit_gemv(const int8_t *a, float sa, const uint8_t *w2, const uint
     return map_launch(jtk_lowbit_gemv(a, sa, w2, s2, n2, w4, s4, n4, K, y, (cudaStream_t)stream));
 }
 
+int jt_b200_lowbit_pack(const float *W, int rows, int K, int bits, int n_ch, uint8_t *packed,
+                        uint16_t *scales, void *stream) {
+    if (W == NULL || packed == NULL || scales == NULL || rows <= 0 || K <= 0 || K % 64 != 0 ||
+        (bits != 2 && bits != 4) || n_ch < 0 || (n_ch > 0 && rows % n_ch != 0) ||
+        ((uintptr_t)W & 7u) != 0) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    return map_launch(jtk_pack_lowbit(W, rows, K, bits, n_ch, packed, scales, (cudaStream_t)stream));
+}
+
+int jt_b200_lowbit_planes_to_packed(const uint8_t *idx, const float *w_scale, int cols, int K,
+                                    int bits, int n_ch, uint8_t *packed, uint16_t *scales,
+                                    void *stream) {
+    if (idx == NULL || packed == NULL || cols <= 0 || K <= 0 || K % 64 != 0 ||
+        (bits != 2 && bits != 4) || n_ch < 0 || (n_ch > 0 && cols % n_ch != 0) ||
+        ((w_scale == NULL) != (scales == NULL))) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    return map_launch(jtk_planes_to_packed(idx, w_scale, cols, K, bits, n_ch, packed, scales,
+                                           (cudaStream_t)stream));
+}
+
 int jt_b200_sync(void) {
     if (cudaDeviceSynchronize() != cudaSuccess) {
         errno = EIO;

@@ -126,6 +126,16 @@ int jtk_lowbit_gemv(const int8_t *a, float sa, const uint8_t *w2, const uint16_t
                     const uint8_t *w4, const uint16_t *s4, int n4, int K, float *y,
                     cudaStream_t stream);
 
+/* Weight preparation (jt_pack.cu).  W fp32 [rows][K] -> packed codes
+ * [rows][K*bits/8] + fp16 group-64 scales, row-major [rows][K/64] for
+ * n_ch == 0, group-major per block of n_ch rows otherwise.  The planes
+ * form converts the reference's per-column bit planes (w_scale / scales
+ * both NULL or both given). */
+int jtk_pack_lowbit(const float *W, int rows, int K, int bits, int n_ch, uint8_t *packed,
+                    uint16_t *scales, cudaStream_t stream);
+int jtk_planes_to_packed(const uint8_t *idx, const float *w_scale, int cols, int K, int bits,
+                         int n_ch, uint8_t *packed, uint16_t *scales, cudaStream_t stream);
+
 /* T-MAC LUT kernels (jt_compat.cu).  Weight column j of expert e has k
  * elements at W + e*ws + t*st + j*sj.  Error keys (atomicMin, all ones =
  * none): position << 1 | kind (0 EINVAL, 1 ERANGE). */
