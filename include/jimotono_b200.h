@@ -305,6 +305,19 @@ int jt_b200_moe_plan_create(const jt_b200_moe_dims *dims, jt_b200_moe_plan **out
 int jt_b200_moe_plan_destroy(jt_b200_moe_plan *plan);
 size_t jt_b200_moe_plan_bytes(const jt_b200_moe_plan *plan);
 
+/* Router logits, the gate projection in front of the layer
+ * (moe_layer.c:1114-1137, inside jt_moe_fwd_batch): logits[t][e] =
+ * (float) of the double dot product of x[t] and wgate[e], accumulated in
+ * the order of the reference's AVX2 build (moe_layer.c:67-86: four lanes
+ * over j mod 4, combined as (l0 + l1) + (l2 + l3)), so the logits - and the
+ * experts the top-k picks from them - are bit-identical to the reference's.
+ * x fp32 [T][d], wgate fp32 [E][d] (row-major, 16-byte aligned), logits
+ * fp32 [T][E]; d % 32 == 0, T <= 2097120.  A non-finite dot or logit (an
+ * EINVAL in the reference) is reported by jt_b200_sync.  Device pointers,
+ * asynchronous on stream; feed logits to jt_b200_moe_forward. */
+int jt_b200_moe_router_logits(const float *x, const float *wgate, int T, int d, int E,
+                              float *logits, void *stream);
+
 /* Y[T][d] = sum over kept slots of w * expert(x) + sum of shared experts.
  * x fp32 [T][d], logits fp32 [T][E] (router output), bias fp32 [E] or NULL
  * (added to the logits before selection), y fp32 [T][d] or bf16 when

@@ -54,6 +54,7 @@ PROTOTYPES = {
     "jt_b200_moe_plan_create": (I, [P, P]),
     "jt_b200_moe_plan_destroy": (I, [P]),
     "jt_b200_moe_plan_bytes": (SZ, [P]),
+    "jt_b200_moe_router_logits": (I, [P, P, I, I, I, P, P]),
     "jt_b200_moe_forward": (I, [P, P, P, P, P, I, P, I, P]),
     "jt_b200_moe_debug_copy": (I, [P, I, P, SZ]),
     "jt_b200_moe_profile_begin": (I, [P, I]),

@@ -57,6 +57,11 @@ int jtk_f32_to_bf16(const float *src, uint16_t *dst, size_t n, cudaStream_t stre
  * ntiles[0] = ceil(T / JT_TILE_ROWS). */
 int jtk_fill_single_tiles(int4 *tiles, int32_t *ntiles, int T, cudaStream_t stream);
 
+/* Router logits (jt_router.cu): logits[t][e] = (float) 4-lane double dot of
+ * x[t] and wgate[e]; d % 32 == 0, x and wgate 16-byte aligned. */
+int jtk_router_logits(const float *x, const float *wgate, int T, int d, int E, float *logits,
+                      cudaStream_t stream);
+
 /* MoE routing (jt_route.cu). */
 int jtk_route_topk(const float *logits, const float *bias, int T, int E, int k, int32_t *ids,
                    float *w, cudaStream_t stream);

@@ -210,6 +210,25 @@ size_t jt_b200_moe_plan_bytes(const jt_b200_moe_plan *plan) {
     return plan ? plan->arena_bytes : 0;
 }
 
+int jt_b200_moe_router_logits(const float *x, const float *wgate, int T, int d, int E,
+                              float *logits, void *stream) {
+    if (x == NULL || wgate == NULL || logits == NULL || T <= 0 || T > 2097120 || d <= 0 ||
+        d % 32 != 0 || E <= 0 || (((uintptr_t)x | (uintptr_t)wgate) & 15u) != 0) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    const int r = jtk_router_logits(x, wgate, T, d, E, logits, (cudaStream_t)stream);
+    if (r == -1) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    if (r != 0) {
+        errno = EIO;
+        return JT_ERR_CUDA;
+    }
+    return JT_OK;
+}
+
 static int weights_valid(const jt_b200_moe_weights *w, int S) {
     if (!w->wg || !w->wu || !w->sg || !w->su || !w->wd || !w->sd) return 0;
     if (S > 0 && (!w->wsg || !w->wsu || !w->ssg || !w->ssu || !w->wsd || !w->ssd)) return 0;

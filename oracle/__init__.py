@@ -52,6 +52,7 @@ def oracle() -> C.CDLL:
             "jto_quant_blocks": (I, [P, I, I, I, P, P]),
             "jto_gemm_s8": (None, [P, P, P, I, I, I]),
             "jto_w8a8_token_channel": (None, [P, P, P, P, I, I]),
+            "jto_router_logits": (I, [P, P, I, I, I, P]),
             "jto_route_topk": (I, [P, P, I, I, I, P, P]),
             "jto_batch_sort": (I, [P, I, I, I, F, P, P, P, P]),
             "jto_renorm": (I, [P, P, I, I]),

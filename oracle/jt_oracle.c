@@ -78,6 +78,29 @@ void jto_w8a8_token_channel(const int32_t *acc, const float *sx, const float *sw
 
 /* routing.c:16-76 per token; bias added in float before the call, the way a
  * caller of jt_routing_topk adds a selection bias. */
+/* moe_layer.c:67-86 (jt_moe_avx2_dot) and :1114-1137. */
+int jto_router_logits(const float *x, const float *wgate, int T, int d, int E, float *logits) {
+    if (!x || !wgate || !logits || T <= 0 || d <= 0 || E <= 0) return 2;
+    const int d4 = d & ~3;
+    for (int t = 0; t < T; t++) {
+        const float *xt = x + (size_t)t * d;
+        for (int e = 0; e < E; e++) {
+            const float *we = wgate + (size_t)e * d;
+            double lane[4] = {0.0, 0.0, 0.0, 0.0};
+            int j = 0;
+            for (; j < d4; j += 4)
+                for (int l = 0; l < 4; l++) lane[l] = lane[l] + (double)xt[j + l] * (double)we[j + l];
+            double s = (lane[0] + lane[1]) + (lane[2] + lane[3]);
+            for (; j < d; j++) s += (double)xt[j] * (double)we[j];
+            if (!isfinite(s)) return 2;
+            const float f = (float)s;
+            if (!isfinite(f)) return 2;
+            logits[(size_t)t * E + e] = f;
+        }
+    }
+    return 0;
+}
+
 int jto_route_topk(const float *logits, const float *bias, int T, int E, int k, int32_t *ids,
                    float *w) {
     if (!logits || !ids || !w || T <= 0 || E <= 0 || k <= 0 || k > E) return 2;

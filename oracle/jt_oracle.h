@@ -33,6 +33,14 @@ void jto_gemm_s8(const int8_t *A, const int8_t *W, int32_t *acc, int M, int N, i
 void jto_w8a8_token_channel(const int32_t *acc, const float *sx, const float *sw, float *C,
                             int M, int N);
 
+/* Router logits of moe_layer.c:1114-1137: logits[t][e] = (float) of the
+ * double dot product of x[t] and wgate[e] in the 4-lane order of the
+ * reference's AVX2 build (moe_layer.c:67-86: lane l sums the products of
+ * j = l mod 4 in ascending j, then (l0 + l1) + (l2 + l3), then the tail
+ * j >= d & ~3 in order).  x [T][d], wgate [E][d], logits [T][E].  2 on a
+ * non-finite dot or logit (moe_layer.c:1128-1135). */
+int jto_router_logits(const float *x, const float *wgate, int T, int d, int E, float *logits);
+
 /* Top-k + softmax of routing.c:16-76 on logits[t] (+ bias, added in float
  * before selection) for T tokens.  ids int32 [T][k], w float [T][k]. */
 int jto_route_topk(const float *logits, const float *bias, int T, int E, int k, int32_t *ids,

@@ -248,3 +248,40 @@ def test_live_quant_vs_reference():
     rs = np.zeros(rows, np.float32)
     assert oracle.ref().jt_w8a8_quant_per_channel(P(x), rows, cols, P(rq), P(rs)) == 0
     assert np.array_equal(q, rq) and np.array_equal(s.view(np.uint32), rs.view(np.uint32))
+
+
+@needs_ref
+@pytest.mark.parametrize("T,n,E,k", [(24, 256, 16, 4), (9, 130, 12, 3)])
+def test_live_router_logits_vs_reference_layer(T, n, E, k):
+    """jto_router_logits (4-lane double dot of moe_layer.c:67-86) feeding the
+    pinned top-k gives the reference layer's routing: the same ids, and -
+    for tokens without a capacity drop - the same weights bit for bit (a
+    one-ulp change of a logit moves its softmax weight).  The sums are kept
+    in double and rounded to float once, so another summation order would
+    rarely change a logit; the restatement keeps the reference's order all
+    the same.  n = 130 runs the scalar tail after the four lanes."""
+    rng = np.random.default_rng(T * 7 + n)
+    X = rng.standard_normal((T, n)).astype(np.float32)
+    Wg8 = (rng.standard_normal((E, n)) * 0.3).astype(np.float32)
+    h = 8
+    We = [(rng.standard_normal((E, h, n)) * 0.05).astype(np.float32) for _ in range(3)]
+    ref = oracle.ref()
+    assert ref.jt_w8a8_set_enabled(0) == 0 and ref.jt_lowbit_set_mode(0) == 0
+    Y = np.zeros((T, n), np.float32)
+    ids = np.zeros(T * k, np.uint64)
+    w = np.zeros(T * k, np.float32)
+    drop = np.zeros(T * k, np.uint8)
+    kept, dropped = C.c_size_t(0), C.c_size_t(0)
+    rc = ref.jt_moe_fwd_batch_unchecked(P(X), P(Wg8), P(We[0]), P(We[1]), P(We[2]), None, None, None, P(Y),
+                                        T, n, h, E, k, 0, P(ids), P(w), None, None, None, None, None,
+                                        1.5, None, None, P(drop), C.addressof(kept),
+                                        C.addressof(dropped))
+    assert rc == 0
+    logits = np.zeros((T, E), np.float32)
+    assert oracle.oracle().jto_router_logits(P(X), P(Wg8), T, n, E, P(logits)) == 0
+    rc, oids, ow = topk(logits, k)
+    assert rc == 0
+    assert np.array_equal(oids.reshape(-1).astype(np.uint64), ids)
+    nodrop = ~drop.reshape(T, k).any(axis=1)
+    assert nodrop.any()
+    assert np.array_equal(ow.reshape(T, k)[nodrop].view(np.uint32), w.reshape(T, k)[nodrop].view(np.uint32))
