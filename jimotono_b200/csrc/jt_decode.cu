@@ -97,7 +97,9 @@ __device__ float quant_token(const float *__restrict__ x, int d, int8_t *sx, int
         sw[threadIdx.x] = 0.0f;
         sw[threadIdx.x + 32] = 0.0f;
         __syncwarp();
-        jt::warp_topk_softmax(p.logits, p.bias, p.E, p.k, taken, ssel, sselv, sids, sw, err);
+        // the experts only: the weights are needed by the down kernel, which
+        // computes them itself before it waits for this grid
+        jt::warp_topk_softmax(p.logits, p.bias, p.E, p.k, taken, ssel, sselv, sids, sw, err, false);
     } else {
         const int t0 = route ? threadIdx.x - 32 : threadIdx.x;
         const int nt = route ? blockDim.x - 32 : blockDim.x;
@@ -252,10 +254,7 @@ __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant
     int e = 0;
     if (!shared) {
         e = sids[slot];
-        if (slot == 0 && cb == 0 && threadIdx.x < p.k) {
-            p.ids[threadIdx.x] = sids[threadIdx.x];
-            p.w[threadIdx.x] = sw[threadIdx.x];
-        }
+        if (slot == 0 && cb == 0 && threadIdx.x < p.k) p.ids[threadIdx.x] = sids[threadIdx.x];
     }
     if (!shared) permute_int2(sx, p.d, xp, gsum);
     // 128 rows: 0..63 gate, 64..127 up of channels cb*64 + (row & 63); each
@@ -336,7 +335,6 @@ __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant
             p.perm[row] = q;
             p.pos[q] = row;
             p.drop[q] = 0;
-            p.w_fin[q] = sw[q];
         }
         for (int ex = threadIdx.x; ex <= p.E; ex += blockDim.x) {
             int n = 0;
@@ -369,6 +367,12 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constan
         if ((threadIdx.x >> 5) == 0)
             jt::warp_topk_softmax(p.logits, p.bias, p.E, p.k, taken, ssel, sselv, sids, sw, p.err);
         __syncthreads();
+        // the routing weights (final: nothing is dropped for one token); the
+        // gate/up grid neither reads nor writes them
+        if (blockIdx.x == 0 && threadIdx.x < p.k) {
+            p.w[threadIdx.x] = sw[threadIdx.x];
+            p.w_fin[threadIdx.x] = sw[threadIdx.x];
+        }
         const int o = blockIdx.x * kDnWarps + (threadIdx.x >> 5);
         const int lane = threadIdx.x & 31;
         if (o < p.d) {

@@ -12,7 +12,9 @@
 // FP64 path accumulates in another order): a 256-thread block computes 32
 // tokens x 64 experts, staging 32-element K chunks of both operands in
 // shared memory as doubles (converted once per element and block); each
-// thread holds 2 tokens x 4 experts x 4 lanes of accumulators.
+// thread holds 2 tokens x 4 experts x 4 lanes of accumulators.  Up to 32768
+// logits (decode) a chain kernel with one thread per (logit, lane) is used
+// instead.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -40,22 +42,29 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
 #pragma unroll
             for (int l = 0; l < 4; ++l) acc[u][i][l] = 0.0;
 
+    // each thread stages one 16-byte piece of the activation tile and two of
+    // the weight tile per chunk; the next chunk's pieces are loaded into
+    // registers while the current chunk is multiplied
+    const int sr = threadIdx.x >> 3, sc = 4 * (threadIdx.x & 7);
+    const bool xin = t0 + sr < T, w0in = e0 + sr < E, w1in = e0 + sr + 32 < E;
+    const float *xp = x + (size_t)(t0 + sr) * d + sc;
+    const float *wp0 = wg + (size_t)(e0 + sr) * d + sc;
+    const float *wp1 = wg + (size_t)(e0 + sr + 32) * d + sc;
+    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 px = xin ? __ldg(reinterpret_cast<const float4 *>(xp)) : z4;
+    float4 pw0 = w0in ? __ldg(reinterpret_cast<const float4 *>(wp0)) : z4;
+    float4 pw1 = w1in ? __ldg(reinterpret_cast<const float4 *>(wp1)) : z4;
     for (int k0 = 0; k0 < d; k0 += kKC) {
-        // stage: 32 x 32 activations and 64 x 32 gate weights, four
-        // consecutive K elements per thread and step (16-byte loads)
-        for (int i = threadIdx.x; i < kTT * kKC / 4; i += 256) {
-            const int r = i / (kKC / 4), c = 4 * (i % (kKC / 4));
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (t0 + r < T) v = __ldg(reinterpret_cast<const float4 *>(x + (size_t)(t0 + r) * d + k0 + c));
-            xs[r][c] = v.x, xs[r][c + 1] = v.y, xs[r][c + 2] = v.z, xs[r][c + 3] = v.w;
-        }
-        for (int i = threadIdx.x; i < kTE * kKC / 4; i += 256) {
-            const int r = i / (kKC / 4), c = 4 * (i % (kKC / 4));
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (e0 + r < E) v = __ldg(reinterpret_cast<const float4 *>(wg + (size_t)(e0 + r) * d + k0 + c));
-            ws[r][c] = v.x, ws[r][c + 1] = v.y, ws[r][c + 2] = v.z, ws[r][c + 3] = v.w;
-        }
+        xs[sr][sc] = px.x, xs[sr][sc + 1] = px.y, xs[sr][sc + 2] = px.z, xs[sr][sc + 3] = px.w;
+        ws[sr][sc] = pw0.x, ws[sr][sc + 1] = pw0.y, ws[sr][sc + 2] = pw0.z, ws[sr][sc + 3] = pw0.w;
+        ws[sr + 32][sc] = pw1.x, ws[sr + 32][sc + 1] = pw1.y, ws[sr + 32][sc + 2] = pw1.z, ws[sr + 32][sc + 3] = pw1.w;
         __syncthreads();
+        if (k0 + kKC < d) {
+            const int kn = k0 + kKC;
+            px = xin ? __ldg(reinterpret_cast<const float4 *>(xp + kn)) : z4;
+            pw0 = w0in ? __ldg(reinterpret_cast<const float4 *>(wp0 + kn)) : z4;
+            pw1 = w1in ? __ldg(reinterpret_cast<const float4 *>(wp1 + kn)) : z4;
+        }
 #pragma unroll 2
         for (int j = 0; j < kKC; j += 4) {
 #pragma unroll
@@ -89,6 +98,35 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
     if (bad && err) atomicExch(err, JT_KERR_NONFINITE);
 }
 
+// Few logits (decode): one thread per (token, expert, lane) runs the lane's
+// chain over j = lane mod 4 straight from global memory (L1/L2), and the
+// four lanes of a logit - four neighbouring threads - combine through
+// shuffles in the reference's order: (l0 + l1) + (l2 + l3).  The latency is
+// one chain of d/4 fused multiply-adds instead of the tiled kernel's d/32
+// staging rounds.
+__global__ void __launch_bounds__(256) k_router_chains(const float *__restrict__ x, const float *__restrict__ wg,
+                                                       int T, int d, int E, float *__restrict__ logits, int *err) {
+    const long long gid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int l = static_cast<int>(gid & 3);
+    const long long o = gid >> 2;
+    const bool live = o < static_cast<long long>(T) * E;
+    const int t = live ? static_cast<int>(o / E) : 0, e = live ? static_cast<int>(o % E) : 0;
+    const float *xr = x + (size_t)t * d + l;
+    const float *wr = wg + (size_t)e * d + l;
+    double acc = 0.0;
+#pragma unroll 8
+    for (int j = 0; j < d; j += 4) acc = __fma_rn((double)__ldg(xr + j), (double)__ldg(wr + j), acc);
+    // lanes 0/1 and 2/3 pair up (an exact, symmetric add), then the pairs
+    const double s01 = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
+    const double s23 = __shfl_xor_sync(0xffffffffu, s01, 2);
+    if (live && l == 0) {
+        const double s = __dadd_rn(s01, s23);
+        const float f = __double2float_rn(s);
+        if ((!isfinite(s) || !isfinite(f)) && err) atomicExch(err, JT_KERR_NONFINITE);
+        logits[o] = f;
+    }
+}
+
 }  // namespace
 
 extern "C" int jtk_router_logits(const float *x, const float *wgate, int T, int d, int E, float *logits,
@@ -96,6 +134,12 @@ extern "C" int jtk_router_logits(const float *x, const float *wgate, int T, int 
     if (!x || !wgate || !logits || T <= 0 || d <= 0 || E <= 0 || d % kKC ||
         ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(wgate)) & 15u))
         return -1;
+    const long long n = static_cast<long long>(T) * E;
+    if (n <= 32768) {  // decode-sized: chains (at most 512 CTAs of 256 threads)
+        k_router_chains<<<static_cast<unsigned>((4 * n + 255) / 256), 256, 0, stream>>>(x, wgate, T, d, E, logits,
+                                                                                      jtk_error_word());
+        return cudaGetLastError() == cudaSuccess ? 0 : -4;
+    }
     const dim3 grid((E + kTE - 1) / kTE, (T + kTT - 1) / kTT);
     if (grid.y > 65535u) return -1;
     k_router_logits<<<grid, 256, 0, stream>>>(x, wgate, T, d, E, logits, jtk_error_word());

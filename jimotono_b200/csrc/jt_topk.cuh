@@ -16,10 +16,13 @@ namespace jt {
 
 // taken: ceil(E/32) words of shared memory owned by this warp; sel/selv: k
 // entries of scratch; ids_out/w_out are written by lane 0 (not on a bad
-// softmax sum).  Returns false on a NaN logit.
+// softmax sum).  With softmax == false only the ids are produced (w_out is
+// not touched), for callers that need the experts before the weights.
+// Returns false on a NaN logit.
 __device__ __forceinline__ bool warp_topk_softmax(const float *__restrict__ row, const float *__restrict__ bias,
                                                   int E, int k, uint32_t *taken, int32_t *sel, float *selv,
-                                                  int32_t *ids_out, float *w_out, int *err) {
+                                                  int32_t *ids_out, float *w_out, int *err,
+                                                  bool softmax = true) {
     const int lane = threadIdx.x & 31;
     const int nw = (E + 31) / 32;
     for (int i = lane; i < nw; i += 32) taken[i] = 0;
@@ -67,6 +70,11 @@ __device__ __forceinline__ bool warp_topk_softmax(const float *__restrict__ row,
         float lv = row[bi];
         if (bias) lv = __fadd_rn(lv, bias[bi]);
         selv[p] = lv;
+    }
+    if (!softmax) {
+        if (lane == 0)
+            for (int p = 0; p < k; ++p) ids_out[p] = sel[p];
+        return true;
     }
     if (lane == 0) {
         bool ok = true;

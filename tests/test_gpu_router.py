@@ -20,8 +20,10 @@ def _oracle_logits(x, wg):
     return out
 
 
-@pytest.mark.parametrize("T,d,E", [(1, 1024, 64), (37, 2048, 100), (300, 96, 1024), (64, 4096, 8),
-                                   (33, 2048, 257)])
+# up to 32768 logits the chain kernel runs, above it the tiled kernel (ragged
+# token and expert tiles in the last two cases)
+@pytest.mark.parametrize("T,d,E", [(1, 1024, 64), (37, 2048, 100), (64, 4096, 8), (33, 2048, 257),
+                                   (300, 96, 1024), (200, 2048, 300), (16384, 64, 4)])
 def test_router_logits_match_oracle(T, d, E):
     from tests import _dev
     rng = np.random.default_rng(T + d + E)
@@ -39,14 +41,15 @@ def test_router_logits_match_oracle(T, d, E):
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"mismatches {(got != want).sum()}"
 
 
-def test_router_logits_report_non_finite():
+@pytest.mark.parametrize("T,E", [(4, 8), (64, 1024)])
+def test_router_logits_report_non_finite(T, E):
     from tests import _dev
-    x = np.ones((4, 64), np.float32)
+    x = np.ones((T, 64), np.float32)
     x[1, 3] = np.inf
-    wg = np.ones((8, 64), np.float32)
-    dl = _dev.zeros((4, 8), np.float32)
+    wg = np.ones((E, 64), np.float32)
+    dl = _dev.zeros((T, E), np.float32)
     dx, dw = _dev.to_dev(x), _dev.to_dev(wg)
-    assert lib().jt_b200_moe_router_logits(dx.data_ptr(), dw.data_ptr(), 4, 64, 8, dl.data_ptr(), _dev.stream()) == 0
+    assert lib().jt_b200_moe_router_logits(dx.data_ptr(), dw.data_ptr(), T, 64, E, dl.data_ptr(), _dev.stream()) == 0
     assert lib().jt_b200_sync() != 0
     assert lib().jt_b200_sync() == 0
 
