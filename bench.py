@@ -301,7 +301,7 @@ def time_layer_ep(torch, cfg, rank, world, steps, warmup, seed):
         plan.forward(wp, dx.data_ptr(), dl.data_ptr(), None, yy.data_ptr(), False, stream)
 
     torch.distributed.barrier()
-    e2e_ms, h2d, d2h = e2e_pipelined(torch, hx, hl, y, fwd, max(2, steps // 2), 2)
+    e2e_ms, h2d, d2h = e2e_pipelined(torch, hx, hl, y, fwd, max(8, 2 * steps), 2)
     out = dict(T=T, ms_per_step=ms, e2e_ms=e2e_ms, h2d=h2d, d2h=d2h, kept_local=int(meta[0]),
                owned_rows=int(meta[1]), dims=dm)
     plan.close()
@@ -317,7 +317,10 @@ def e2e_pipelined(torch, hx, hl, y_like, forward, steps, warmup):
     copies go on their own streams into double-buffered device buffers, so
     step i+1's inputs and step i-1's output cross PCIe while step i
     computes; every step's copies are inside the timed region, which ends
-    when the last output has reached host memory.  forward(dx, dl, y,
+    when the last output has reached host memory, so the first step's input
+    copy and the last step's output copy (together about 6 ms at config 5)
+    are paid once per run: the run is long enough (twice the device-timed
+    steps) for them to amortize as in a serving loop.  forward(dx, dl, y,
     stream) enqueues one forward on `stream`."""
     cs = torch.cuda.current_stream()
     s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
@@ -611,7 +614,7 @@ def main():
     ops_gu = 2.0 * kept * dm.d * (2 * dm.f)
     ops_dn = 2.0 * kept * dm.f * dm.d
     ops_sh = 2.0 * st["T"] * dm.S * (2 * dm.fs * dm.d + dm.d * dm.fs)
-    e2e_ms, h2d, d2h = e2e_layer(torch, st, max(2, args.steps // 2), 2)
+    e2e_ms, h2d, d2h = e2e_layer(torch, st, max(8, 2 * args.steps), 2)
     parts = {}
     if rank == 0 and not args.no_parts:
         st3 = time_layer(torch, CFG3, 0, 1, args.steps, args.warmup, seed=3, zipf=1.1, bf16=True)

@@ -259,19 +259,32 @@ __device__ __forceinline__ void fold_chunk(float2 *r2, const uint32_t (&a)[32], 
 // TP != 0 (down modes): hvT points at the tile's activation group scales in
 // group-major order (group stride hs_ld floats), offset to the warp's first
 // column, and is read four columns per shared-memory load.
+//
+// Down projection of the routed experts: the scaled partial (float)P * s is
+// formed in one fused operation from the drained word A = 12582912 + P as
+// fmaf(A, s, -12582912 * s).  The product 12582912 * s is exact (3 * 2^22
+// times an fp16 value: at most 13 significant bits), and A*s - 12582912*s is
+// exactly P*s, so the single rounding gives the same bits as the subtraction
+// followed by the rounded product.
 template <int MODE, int TP>
 __device__ __forceinline__ void fold16(float2 *r2, const uint32_t (&a)[16], float s, const float *blk, int hs_ld,
                                        int g, int c0, const float *hvT) {
     const float2 s2 = make_float2(s, s);
+    const float nms = __fmul_rn(-kMagicF, s);
+    const float2 nms2 = make_float2(nms, nms);
     if constexpr (TP != 0) {
         const float4 *h4p = reinterpret_cast<const float4 *>(hvT + (size_t)g * hs_ld + c0);
 #pragma unroll
         for (int j = 0; j < 16; j += 4) {
             const float4 h4 = h4p[j / 4];
-            const float2 pa = __fadd2_rn(as_f2(a[j], a[j + 1]), make_float2(-kMagicF, -kMagicF));
-            const float2 pb = __fadd2_rn(as_f2(a[j + 2], a[j + 3]), make_float2(-kMagicF, -kMagicF));
-            const float2 ta = (MODE == DN_ROUTED) ? __fmul2_rn(pa, s2) : pa;
-            const float2 tb = (MODE == DN_ROUTED) ? __fmul2_rn(pb, s2) : pb;
+            float2 ta, tb;
+            if (MODE == DN_ROUTED) {
+                ta = __ffma2_rn(as_f2(a[j], a[j + 1]), s2, nms2);
+                tb = __ffma2_rn(as_f2(a[j + 2], a[j + 3]), s2, nms2);
+            } else {
+                ta = __fadd2_rn(as_f2(a[j], a[j + 1]), make_float2(-kMagicF, -kMagicF));
+                tb = __fadd2_rn(as_f2(a[j + 2], a[j + 3]), make_float2(-kMagicF, -kMagicF));
+            }
             r2[(c0 + j) / 2] = __ffma2_rn(ta, make_float2(h4.x, h4.y), r2[(c0 + j) / 2]);
             r2[(c0 + j) / 2 + 1] = __ffma2_rn(tb, make_float2(h4.z, h4.w), r2[(c0 + j) / 2 + 1]);
         }
@@ -282,15 +295,16 @@ __device__ __forceinline__ void fold16(float2 *r2, const uint32_t (&a)[16], floa
 #pragma unroll
     for (int j = 0; j < 16; j += 2) {
         float2 &rr = r2[(c0 + j) / 2];
-        const float2 pf = __fadd2_rn(as_f2(a[j], a[j + 1]), make_float2(-kMagicF, -kMagicF));
         if (MODE == GU_ROUTED) {
+            const float2 pf = __fadd2_rn(as_f2(a[j], a[j + 1]), make_float2(-kMagicF, -kMagicF));
             rr = __ffma2_rn(pf, s2, rr);
         } else {
             float2 hv;
             asm volatile("ld.shared.f32 %0, [%1];" : "=f"(hv.x) : "r"(hv_addr));
             asm volatile("ld.shared.f32 %0, [%1];" : "=f"(hv.y) : "r"(hv_addr + hv_step));
             hv_addr += 2u * hv_step;
-            const float2 t = (MODE == DN_ROUTED) ? __fmul2_rn(pf, s2) : pf;
+            const float2 t = (MODE == DN_ROUTED) ? __ffma2_rn(as_f2(a[j], a[j + 1]), s2, nms2)
+                                                 : __fadd2_rn(as_f2(a[j], a[j + 1]), make_float2(-kMagicF, -kMagicF));
             rr = __ffma2_rn(t, hv, rr);
         }
     }
