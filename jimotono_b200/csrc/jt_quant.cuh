@@ -5,9 +5,11 @@
 //
 // The division is done in fp32 first (x * (float)(127/maxabs)); that
 // estimate is within 2^-23 * 127 < 2e-5 of the exact quotient, so whenever
-// its fractional part is farther than 1e-3 from one half the rounded code is
-// already exact.  Only the rare near-tie case runs the double division the
-// reference uses.
+// it lies farther than 1e-3 from a rounding tie the rounded code is already
+// exact.  Only the rare near-tie case runs the double division the
+// reference uses.  The fast path rounds with the magic-number addition
+// (FMA pipe) rather than floor/convert instructions, which issue at a
+// fraction of the FMA rate.
 #pragma once
 #include <cstdint>
 
@@ -39,18 +41,23 @@ static __device__ __noinline__ int quant_code_exact(float x, double scale_d) {
     return static_cast<int>(round(__ddiv_rn((double)x, scale_d)));
 }
 
+// Nearest integer of an estimate y (|y| < 2^22) on the FMA pipe: y + 1.5*2^23
+// rounds y to an integer (ties to even) and its bit pattern carries that
+// integer; the distance |y - round(y)| is exact.  Away from a tie (distance
+// below 0.499) round-to-even equals the reference's half-away-from-zero
+// rounding.  A non-finite y gives a NaN distance, which takes the exact path.
+__device__ __forceinline__ bool round_fast(float y, int &q) {
+    const float t = __fadd_rn(y, 12582912.0f);
+    const float dist = fabsf(__fsub_rn(y, __fsub_rn(t, 12582912.0f)));
+    q = __float_as_int(t) - 0x4B400000;
+    return dist < 0.499f;
+}
+
 __device__ __forceinline__ int quant_code(float x, const QuantBlock &b) {
     if (b.scale_d == 0.0) return 0;
     const float y = __fmul_rn(x, b.inv);
-    const float ay = fabsf(y);
-    const float fr = __fsub_rn(ay, floorf(ay));
     int q;
-    if (fabsf(__fsub_rn(fr, 0.5f)) > 1e-3f) {
-        q = static_cast<int>(floorf(__fadd_rn(ay, 0.5f)));
-        if (y < 0.0f) q = -q;
-    } else {
-        q = quant_code_exact(x, b.scale_d);
-    }
+    if (!round_fast(y, q)) q = quant_code_exact(x, b.scale_d);
     q = q > 127 ? 127 : q;
     q = q < -127 ? -127 : q;
     return q;
@@ -90,15 +97,8 @@ static __device__ __noinline__ int quant_code_exact_m(float x, float maxabs) {
 __device__ __forceinline__ int quant_code_f(float x, const QuantBlockF &b) {
     if (b.maxabs == 0.0f) return 0;
     const float y = __fmul_rn(x, b.inv);
-    const float ay = fabsf(y);
-    const float fr = __fsub_rn(ay, floorf(ay));
     int q;
-    if (fabsf(__fsub_rn(fr, 0.5f)) > 1e-3f) {
-        q = static_cast<int>(floorf(__fadd_rn(ay, 0.5f)));
-        if (y < 0.0f) q = -q;
-    } else {
-        q = quant_code_exact_m(x, b.maxabs);
-    }
+    if (!round_fast(y, q)) q = quant_code_exact_m(x, b.maxabs);
     q = q > 127 ? 127 : q;
     q = q < -127 ? -127 : q;
     return q;

@@ -17,7 +17,11 @@ __device__ __forceinline__ float det_expf(float x) {
     const float kLog2e = 0x1.715476p+0f;
     const float kLn2Hi = 0x1.62e4p-1f;
     const float kLn2Lo = 0x1.7f7d1cp-20f;
-    const float kf = rintf(__fmul_rn(x, kLog2e));
+    // k = rint(x * log2 e) by the magic-number addition (|x log2 e| < 151):
+    // the same integer as rintf (ties to even) without a conversion
+    // instruction; k itself is read from the sum's bit pattern
+    const float tm = __fadd_rn(__fmul_rn(x, kLog2e), 12582912.0f);
+    const float kf = __fsub_rn(tm, 12582912.0f);
     float r = __fmaf_rn(-kf, kLn2Hi, x);
     r = __fmaf_rn(-kf, kLn2Lo, r);
     float p = 0x1.a01a02p-13f;
@@ -28,7 +32,7 @@ __device__ __forceinline__ float det_expf(float x) {
     p = __fmaf_rn(p, r, 0x1.0p-1f);
     p = __fmaf_rn(p, r, 1.0f);
     p = __fmaf_rn(p, r, 1.0f);
-    const int k = static_cast<int>(kf);
+    const int k = __float_as_int(tm) - 0x4B400000;
     const int k1 = k >> 1, k2 = k - k1;
     const float s1 = __int_as_float((k1 + 127) << 23);
     const float s2 = __int_as_float((k2 + 127) << 23);
@@ -55,8 +59,8 @@ __device__ __forceinline__ float2 det_expf2(float2 x) {
     x.x = fmaxf(fminf(x.x, 89.0f), -104.0f);
     x.y = fmaxf(fminf(x.y, 89.0f), -104.0f);
     const float2 kLog2e = make_float2(0x1.715476p+0f, 0x1.715476p+0f);
-    const float2 t = __fmul2_rn(x, kLog2e);
-    const float2 kf = make_float2(rintf(t.x), rintf(t.y));
+    const float2 tm = __fadd2_rn(__fmul2_rn(x, kLog2e), make_float2(12582912.0f, 12582912.0f));
+    const float2 kf = __fadd2_rn(tm, make_float2(-12582912.0f, -12582912.0f));
     const float2 nkf = make_float2(-kf.x, -kf.y);
     float2 r = __ffma2_rn(nkf, make_float2(0x1.62e4p-1f, 0x1.62e4p-1f), x);
     r = __ffma2_rn(nkf, make_float2(0x1.7f7d1cp-20f, 0x1.7f7d1cp-20f), r);
@@ -68,7 +72,7 @@ __device__ __forceinline__ float2 det_expf2(float2 x) {
     p = __ffma2_rn(p, r, make_float2(0x1.0p-1f, 0x1.0p-1f));
     p = __ffma2_rn(p, r, make_float2(1.0f, 1.0f));
     p = __ffma2_rn(p, r, make_float2(1.0f, 1.0f));
-    const int k0 = static_cast<int>(kf.x), k1 = static_cast<int>(kf.y);
+    const int k0 = __float_as_int(tm.x) - 0x4B400000, k1 = __float_as_int(tm.y) - 0x4B400000;
     const int a0 = k0 >> 1, b0 = k0 - a0, a1 = k1 >> 1, b1 = k1 - a1;
     const float2 s1 = make_float2(__int_as_float((a0 + 127) << 23), __int_as_float((a1 + 127) << 23));
     const float2 s2 = make_float2(__int_as_float((b0 + 127) << 23), __int_as_float((b1 + 127) << 23));
