@@ -59,8 +59,11 @@ __device__ __forceinline__ float2 det_expf2(float2 x) {
     x.x = fmaxf(fminf(x.x, 89.0f), -104.0f);
     x.y = fmaxf(fminf(x.y, 89.0f), -104.0f);
     const float2 kLog2e = make_float2(0x1.715476p+0f, 0x1.715476p+0f);
-    const float2 tm = __fadd2_rn(__fmul2_rn(x, kLog2e), make_float2(12582912.0f, 12582912.0f));
-    const float2 kf = __fadd2_rn(tm, make_float2(-12582912.0f, -12582912.0f));
+    // the rounding to an integer in scalar additions (as det_expf): the
+    // packed f32x2 add did not give these bits for the magic-number form
+    const float2 t = __fmul2_rn(x, kLog2e);
+    const float2 tm = make_float2(__fadd_rn(t.x, 12582912.0f), __fadd_rn(t.y, 12582912.0f));
+    const float2 kf = make_float2(__fsub_rn(tm.x, 12582912.0f), __fsub_rn(tm.y, 12582912.0f));
     const float2 nkf = make_float2(-kf.x, -kf.y);
     float2 r = __ffma2_rn(nkf, make_float2(0x1.62e4p-1f, 0x1.62e4p-1f), x);
     r = __ffma2_rn(nkf, make_float2(0x1.7f7d1cp-20f, 0x1.7f7d1cp-20f), r);
