@@ -46,8 +46,8 @@ CFG2 = dict(T=1, d=1024, f=256, E=64, k=8, S=2, fs=512, cap=1.5)
 CFG5_SMALL = dict(T=2048, d=2048, f=1536, E=128, k=8, S=2, fs=4096, cap=1.5)
 METRIC = "MoE-layer tokens/s at 1/2/4/8 B200; W8A8 TOPS; decode HBM GB/s vs peak"
 # DRAM bytes (read + write) of one routed gate/up launch at config 5: the ncu
-# capture of `bench.py --small` (1/8 of config 5) gave 285.3 MB, scaled by 8.
-GU_TRAFFIC_BYTES = 8 * 285_306_880
+# capture of `bench.py --small` (1/8 of config 5) gave 282.6 MB, scaled by 8.
+GU_TRAFFIC_BYTES = 8 * 282_609_920
 
 
 def peaks():
