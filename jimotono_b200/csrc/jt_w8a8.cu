@@ -114,6 +114,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int n_tok_tiles = (M + BN - 1) / BN;
     const int ntiles = n_ch_tiles * n_tok_tiles;
     const int nk = (K + kBK - 1) / kBK;
+    // programmatic dependent launch: the next kernel of the stream may start
+    // its own set-up on the SMs this grid leaves free
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -140,6 +143,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     jt::tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // the set-up above touches no global memory; everything below may read
+    // what the previous kernel of the stream wrote, so it waits for that
+    // grid to complete
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     if (warp == 0) {
         if (lane == 0) {
@@ -372,7 +379,20 @@ int launch_bn(const CUtensorMap &tmW, const int8_t *X, int ldx, int M, int N, in
     int grid = jtk_num_sms();
     if (grid > ntiles) grid = ntiles;
     int *err = jtk_error_word();
-    kern<<<grid, kThreads, Cfg::kSmem, stream>>>(tmW, tmX, M, N, K, sx, sw, sA, out, ldo, err);
+    // launched with programmatic stream serialization: the kernel's set-up
+    // (barriers, TMEM, descriptor prefetch) overlaps the previous kernel's
+    // tail; it waits for that kernel before its first global access
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, tmW, tmX, M, N, K, sx, sw, sA, out, ldo, err) != cudaSuccess) return -4;
     return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 
