@@ -291,7 +291,11 @@ __global__ void __launch_bounds__(jt::pair::kThreads, 1)
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     jp::Ctx c;
     const CUtensorMap *maps[2] = {&tmW, &tmX};
+    // programmatic dependent launch, as in k_w8a8_gemm: the set-up (no
+    // global memory) overlaps the previous kernel, the rest waits for it
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     jp::setup(c, smem, smem + jp::kRing, err, maps, 2);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int n_ch_tiles = (N + 255) / 256;
     const int ntiles = n_ch_tiles * ((M + 255) / 256);
     const int nk = (K + kBK - 1) / kBK;
@@ -350,8 +354,11 @@ int launch_pair(const CUtensorMap &tmW, const int8_t *X, int ldx, int M, int N, 
     const int ntiles = ((N + 255) / 256) * ((M + 255) / 256);
     int pairs = jtk_num_sms() / 2;
     if (pairs > ntiles) pairs = ntiles;
-    cudaLaunchAttribute attr[1];
-    const cudaLaunchConfig_t cfg = jt::pair::launch_config(pairs, kPairSmem, stream, attr);
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t cfg = jt::pair::launch_config(pairs, kPairSmem, stream, attr);
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 2;
     if (cudaLaunchKernelEx(&cfg, kern, tmW, tmX, M, N, K, sx, sw, sA, out, ldo, jtk_error_word()) !=
         cudaSuccess)
         return -4;
