@@ -109,8 +109,12 @@ def reference_arm(steps: int, warmup: int, metric: str) -> dict:
     value = cores * T / (ms / 1e3)
     return {"impl": "reference", "metric": metric, "value": round(value, 2), "unit": "tokens/s",
             "n_gpus": 0, "steps": steps, "warmup": warmup, "ms_per_step": round(ms, 1),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32+int8",
-            "data": "synthetic", "config": {"workload": "cfg5 expert shape sample (see cpu_baseline)"},
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32+int8",
+            "data": "synthetic",
+            "config": {"workload": "cfg5 EP MoE layer: T=16384 d=2048 E=1024 f=1536 top-8 INT2/INT4 g64 + "
+                                   "2 shared INT8 f=4096, cap 1.5",
+                       "tokens": 16384, "parallelism": "host cores",
+                       "measured_on": "a bounded sample of the workload's expert shapes (see cpu_baseline)"},
             "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": cores,
                              "kind": "reference",
                              "sample": f"{cores} threads x {T}-token calls, E=8 top-8 d=2048 f=1536"},
