@@ -231,12 +231,24 @@ __global__ void __launch_bounds__(256)
     const float *row = x + (size_t)t * d;
     __shared__ float wm[8];
     __shared__ int wb[8];
+    __shared__ int sdst[64];
+    // 16-byte loads when the row allows them (d % 8 == 0, x 16-byte aligned)
+    const bool vec = (d % 8) == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
     float m = 0.0f;
     int bad = 0;
-    for (int i = threadIdx.x; i < d; i += blockDim.x) {
-        const float v = row[i];
-        bad |= !isfinite(v);
-        m = fmaxf(m, fabsf(v));
+    if (vec) {
+        const float4 *row4 = reinterpret_cast<const float4 *>(row);
+        for (int i = threadIdx.x; i < d / 4; i += blockDim.x) {
+            const float4 v = __ldg(row4 + i);
+            bad |= !isfinite(v.x) | !isfinite(v.y) | !isfinite(v.z) | !isfinite(v.w);
+            m = fmaxf(fmaxf(m, fmaxf(fabsf(v.x), fabsf(v.y))), fmaxf(fabsf(v.z), fabsf(v.w)));
+        }
+    } else {
+        for (int i = threadIdx.x; i < d; i += blockDim.x) {
+            const float v = row[i];
+            bad |= !isfinite(v);
+            m = fmaxf(m, fabsf(v));
+        }
     }
     for (int o = 16; o > 0; o >>= 1) {
         m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -256,12 +268,15 @@ __global__ void __launch_bounds__(256)
     const jt::QuantBlock qb = jt::quant_block(bad ? 0.0f : m);
     // Row metadata first: even on a rejected (non-finite) token every kept
     // row must name this token, so later kernels never index a stale token.
-    int dst[64];
     int nd = 0;
     if (pos) {
+        // the kept rows of this token, in slot order, shared by the CTA
         for (int p = 0; p < k; ++p) {
             const int ps = pos[(size_t)t * k + p];
-            if (ps >= 0) dst[nd++] = ps;
+            if (ps >= 0) {
+                if (threadIdx.x == 0) sdst[nd] = ps;
+                ++nd;
+            }
         }
         if (threadIdx.x < k) {
             const int ps = pos[(size_t)t * k + threadIdx.x];
@@ -278,6 +293,24 @@ __global__ void __launch_bounds__(256)
         if (threadIdx.x == 0) atomicExch(err, 0x85);
         return;
     }
+    __syncthreads();  // sdst
+    if (vec) {
+        // 8 codes per thread per step: two 16-byte loads, one 8-byte store
+        // per destination row
+        for (int i = threadIdx.x * 8; i < d; i += blockDim.x * 8) {
+            const float4 a = __ldg(reinterpret_cast<const float4 *>(row + i));
+            const float4 b = __ldg(reinterpret_cast<const float4 *>(row + i + 4));
+            const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+            uint32_t w[2] = {0u, 0u};
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                w[j >> 2] |= (uint32_t)(uint8_t)(int8_t)jt::quant_code(v[j], qb) << (8 * (j & 3));
+            const uint2 word = make_uint2(w[0], w[1]);
+            *reinterpret_cast<uint2 *>(xq + (size_t)t * d + i) = word;
+            for (int j = 0; j < nd; ++j) *reinterpret_cast<uint2 *>(xd + (size_t)sdst[j] * d + i) = word;
+        }
+        return;
+    }
     // 4 codes per thread per step, written as one 32-bit word
     for (int i = threadIdx.x * 4; i < d; i += blockDim.x * 4) {
         uint32_t word = 0;
@@ -288,7 +321,7 @@ __global__ void __launch_bounds__(256)
         }
         *reinterpret_cast<uint32_t *>(xq + (size_t)t * d + i) = word;
         for (int j = 0; j < nd; ++j)
-            *reinterpret_cast<uint32_t *>(xd + (size_t)dst[j] * d + i) = word;
+            *reinterpret_cast<uint32_t *>(xd + (size_t)sdst[j] * d + i) = word;
     }
 }
 
