@@ -78,10 +78,23 @@ __global__ void k_sort_scan(int32_t *__restrict__ hist_base, int nchunks, int E,
         const int e = tid * per + j;
         int kc = 0;
         if (e < E) {
+            // exclusive scan of the column over the chunks; sixteen loads
+            // in flight at a time instead of one dependent round trip each
             int run = 0;
-            for (int c = 0; c < nchunks; ++c) {
+            int c = 0;
+            for (; c + 16 <= nchunks; c += 16) {
+                int h[16];
+#pragma unroll
+                for (int u = 0; u < 16; ++u) h[u] = hist_base[(size_t)(c + u) * E + e];
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    hist_base[(size_t)(c + u) * E + e] = run;  // becomes base[c][e]
+                    run += h[u];
+                }
+            }
+            for (; c < nchunks; ++c) {
                 const int h = hist_base[(size_t)c * E + e];
-                hist_base[(size_t)c * E + e] = run;  // becomes base[c][e]
+                hist_base[(size_t)c * E + e] = run;
                 run += h;
             }
             // gbase[e]: pairs of expert e ahead of this token range (other
