@@ -5,9 +5,10 @@
 // Lane l holds logits l, l+32, ...  Each of the k passes takes the maximum
 // of (taken ? -inf : logit [+ bias]) with ties to the lowest index, exactly
 // the strict '>' scan of routing.c:38-52 (including its behaviour when only
-// -inf values remain); then the softmax of routing.c:54-73 by lane 0: float
-// max, double exp sum, w = (float)e * (float)(1/sum).  A NaN logit raises
-// err 0x81 (nothing is written), a bad softmax sum 0x82.
+// -inf values remain); then the softmax of routing.c:54-73: float max,
+// double exps (one slot per lane) summed in slot order, w = (float)e *
+// (float)(1/sum).  A NaN logit raises err 0x81 (nothing is written), a bad
+// softmax sum 0x82.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -15,8 +16,8 @@
 namespace jt {
 
 // taken: ceil(E/32) words of shared memory owned by this warp; sel/selv: k
-// entries of scratch; ids_out/w_out are written by lane 0 (not on a bad
-// softmax sum).  With softmax == false only the ids are produced (w_out is
+// entries of scratch written identically by every lane; ids_out/w_out
+// entry p is written by lane p mod 32 (nothing on a bad softmax sum).  With softmax == false only the ids are produced (w_out is
 // not touched), for callers that need the experts before the weights.
 // Returns false on a NaN logit.
 __device__ __forceinline__ bool warp_topk_softmax(const float *__restrict__ row, const float *__restrict__ bias,
@@ -76,28 +77,29 @@ __device__ __forceinline__ bool warp_topk_softmax(const float *__restrict__ row,
             for (int p = 0; p < k; ++p) ids_out[p] = sel[p];
         return true;
     }
-    if (lane == 0) {
-        bool ok = true;
-        float mx = selv[0];
-        for (int p = 1; p < k; ++p) mx = (selv[p] > mx) ? selv[p] : mx;
-        double sum = 0.0;
-        float ew[64];
-        for (int p = 0; p < k; ++p) {
-            const double e = exp((double)selv[p] - (double)mx);
-            sum += e;
-            ew[p] = (float)e;
-        }
-        if (!(sum > 0.0) || !isfinite(sum)) {
-            atomicExch(err, 0x82);
-            ok = false;
-        }
-        if (ok) {
-            const float inv = (float)(1.0 / sum);
-            for (int p = 0; p < k; ++p) {
-                ids_out[p] = sel[p];
-                w_out[p] = __fmul_rn(ew[p], inv);
-            }
-        }
+    // softmax (routing.c:54-73): every lane takes the exp of its slots
+    // (lane p: slots p and p + 32); the sum is formed in slot order (on
+    // every lane, from the shuffled terms), as the reference's loop adds
+    float mx = selv[0];
+    for (int p = 1; p < k; ++p) mx = (selv[p] > mx) ? selv[p] : mx;
+    double e0 = 0.0, e1 = 0.0;
+    if (lane < k) e0 = exp((double)selv[lane] - (double)mx);
+    if (lane + 32 < k) e1 = exp((double)selv[lane + 32] - (double)mx);
+    double sum = 0.0;
+    for (int p = 0; p < k; ++p) sum += __shfl_sync(0xffffffffu, p < 32 ? e0 : e1, p & 31);
+    // every lane holds the same sum (the same adds in the same order)
+    if (!(sum > 0.0) || !isfinite(sum)) {
+        if (lane == 0) atomicExch(err, 0x82);
+        return true;
+    }
+    const float inv = (float)(1.0 / sum);
+    if (lane < k) {
+        ids_out[lane] = sel[lane];
+        w_out[lane] = __fmul_rn((float)e0, inv);
+    }
+    if (lane + 32 < k) {
+        ids_out[lane + 32] = sel[lane + 32];
+        w_out[lane + 32] = __fmul_rn((float)e1, inv);
     }
     return true;
 }
