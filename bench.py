@@ -634,7 +634,7 @@ def main():
             "us_per_token": round(dec_us, 2), "bytes_per_token": per_tok,
             "GBs": round(per_tok / (dec_us / 1e6) / 1e9, 1),
             "frac_hbm": round(per_tok / (dec_us / 1e6) / 1e9 / hbm_peak, 4),
-            "timing": "CUDA graph of 8 forward calls (router + 2 decode kernels each), replayed; "
+            "timing": "CUDA graph of 8 forward calls (2 kernels each: gate/up with the router, down), replayed; "
                       "stream-launched with per-stage events: %.2f us" % (st2["ms_per_step"] * 1e3),
             "l2": "8 rotating weight copies (172 MB > L2)"}
         del st2

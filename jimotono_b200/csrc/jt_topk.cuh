@@ -18,9 +18,9 @@ namespace jt {
 // taken: ceil(E/32) words of shared memory owned by this warp; sel/selv: k
 // entries of scratch written identically by every lane; ids_out/w_out
 // entry p is written by lane p mod 32 with the softmax, by lane 0 without
-// it (nothing on a bad softmax sum).  With softmax == false only the ids are produced (w_out is
-// not touched), for callers that need the experts before the weights.
-// Returns false on a NaN logit.
+// it (nothing on a bad softmax sum).  With softmax == false only the ids
+// are produced (w_out is not touched), for callers that need the experts
+// before the weights.  Returns false on a NaN logit.
 __device__ __forceinline__ bool warp_topk_softmax(const float *__restrict__ row, const float *__restrict__ bias,
                                                   int E, int k, uint32_t *taken, int32_t *sel, float *selv,
                                                   int32_t *ids_out, float *w_out, int *err,
