@@ -305,6 +305,29 @@ int jt_b200_moe_plan_create(const jt_b200_moe_dims *dims, jt_b200_moe_plan **out
 int jt_b200_moe_plan_destroy(jt_b200_moe_plan *plan);
 size_t jt_b200_moe_plan_bytes(const jt_b200_moe_plan *plan);
 
+/* On-disk form of the prepared weights (written once, loaded at start-up,
+ * instead of re-deriving the quantized weights from fp32 masters on every
+ * call as the reference layer does, moe_layer.c:185-274, lowbit.c:228-237).
+ * Format: a 4096-byte little-endian header (magic "JTB2MOE1", version 1,
+ * d, f, E, S, fs, and per array its offset, size and FNV-1a 64 checksum),
+ * then the twelve arrays of jt_b200_moe_weights in field order, each at a
+ * 4096-byte aligned offset.  A reader rejects a header that does not match
+ * `dims` (JT_ERR_INVAL) and data that does not match its checksums
+ * (JT_ERR_IO).  _sizes gives each array's byte size for `dims` (T, k and
+ * cap_factor are not part of the weights).  _write_host / _read_host take
+ * host arrays in field order; _save / _load take device buffers (the
+ * pointers in `w`; _load writes into them) and copy through a pinned host
+ * buffer, synchronously. */
+int jt_b200_moe_weights_sizes(const jt_b200_moe_dims *dims, size_t sizes[12]);
+int jt_b200_moe_weights_write_host(const char *path, const jt_b200_moe_dims *dims,
+                                   const void *const arrays[12]);
+int jt_b200_moe_weights_read_host(const char *path, const jt_b200_moe_dims *dims,
+                                  void *const arrays[12]);
+int jt_b200_moe_weights_save(const char *path, const jt_b200_moe_dims *dims,
+                             const jt_b200_moe_weights *w);
+int jt_b200_moe_weights_load(const char *path, const jt_b200_moe_dims *dims,
+                             const jt_b200_moe_weights *w);
+
 /* Router logits, the gate projection in front of the layer
  * (moe_layer.c:1114-1137, inside jt_moe_fwd_batch): logits[t][e] =
  * (float) of the double dot product of x[t] and wgate[e], accumulated in

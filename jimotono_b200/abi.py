@@ -54,6 +54,11 @@ PROTOTYPES = {
     "jt_b200_moe_plan_create": (I, [P, P]),
     "jt_b200_moe_plan_destroy": (I, [P]),
     "jt_b200_moe_plan_bytes": (SZ, [P]),
+    "jt_b200_moe_weights_sizes": (I, [P, P]),
+    "jt_b200_moe_weights_write_host": (I, [C.c_char_p, P, P]),
+    "jt_b200_moe_weights_read_host": (I, [C.c_char_p, P, P]),
+    "jt_b200_moe_weights_save": (I, [C.c_char_p, P, P]),
+    "jt_b200_moe_weights_load": (I, [C.c_char_p, P, P]),
     "jt_b200_moe_router_logits": (I, [P, P, I, I, I, P, P]),
     "jt_b200_moe_forward": (I, [P, P, P, P, P, I, P, I, P]),
     "jt_b200_moe_debug_copy": (I, [P, I, P, SZ]),
