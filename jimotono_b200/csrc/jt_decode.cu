@@ -244,6 +244,10 @@ __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant
     const int n_ch = shared ? p.fs : p.f;
     // the down kernel may launch now; it waits for this grid before reading
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // this grid is itself launched as a dependent of the previous kernel of
+    // the stream (the previous token's down kernel in a decode loop): wait
+    // for it before touching global memory (it reads hq/hs, written below)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if (cb * 64 >= n_ch) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // routed CTAs: the router (every routed CTA alike, jt_topk.cuh) overlaps
@@ -351,6 +355,9 @@ constexpr int kMaxHp = 8192;  // permuted h words of the routed rows (k * f <= 3
 
 // grid d / 8, 256 threads: warp w computes output channel blockIdx.x*8 + w.
 __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constant__ DecParams p) {
+    // the next token's gate/up kernel may launch on the SMs left free; it
+    // waits for this grid before its first global access
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     __shared__ uint32_t taken[kMaxE / 32];
     __shared__ int32_t sids[64], ssel[64];
     __shared__ float sw[64], sselv[64];
@@ -560,7 +567,19 @@ extern "C" int jtk_moe_decode(const float *x, const float *logits, const float *
     p.y_bf16 = y_bf16;
     p.err = jtk_error_word();
     const int nmax = (S > 0 && fs > f) ? fs : f;
-    k_dec_gateup<<<dim3(nmax / 64, k + S), kGuThreads, 0, stream>>>(p);
+    {
+        cudaLaunchConfig_t gcfg{};
+        gcfg.gridDim = dim3(nmax / 64, k + S);
+        gcfg.blockDim = dim3(kGuThreads);
+        gcfg.dynamicSmemBytes = 0;
+        gcfg.stream = stream;
+        cudaLaunchAttribute gattr[1];
+        gattr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        gattr[0].val.programmaticStreamSerializationAllowed = 1;
+        gcfg.attrs = gattr;
+        gcfg.numAttrs = 1;
+        if (cudaLaunchKernelEx(&gcfg, k_dec_gateup, p) != cudaSuccess) return -4;
+    }
     if (cudaGetLastError() != cudaSuccess) return -4;
     // down: programmatic dependent launch, so its launch and prologue overlap
     // the gate/up grid (it waits on griddepcontrol.wait before any read of
