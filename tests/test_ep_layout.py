@@ -4,9 +4,9 @@
   every rank keeps under the layout's rule equal the pairs the reference's
   capacity sort keeps over the whole batch (restated by the oracle's
   jto_batch_sort, which is pinned to moe_layer.c:895-978);
-* two gloo ranks: each rank counts its own pairs, the counts are
+* two and four gloo ranks: each rank counts its own pairs, the counts are
   all-gathered over torch.distributed (gloo, 127.0.0.1), and the send and
-  receive sizes the two ranks compute agree pairwise.
+  receive sizes the ranks compute agree pairwise.
 """
 import ctypes as C
 import os
@@ -95,18 +95,19 @@ def _gloo_worker(rank, world, port, result):
         dist.destroy_process_group()
 
 
-def test_layout_two_gloo_ranks():
+@pytest.mark.parametrize("world", [2, 4])
+def test_layout_gloo_ranks(world):
     import socket
     import torch.multiprocessing as mp
     with socket.socket() as sck:
         sck.bind(("127.0.0.1", 0))
         port = sck.getsockname()[1]
     ctx = mp.get_context("spawn")
-    result = ctx.Array("i", [0, 0])
-    procs = [ctx.Process(target=_gloo_worker, args=(r, 2, port, result)) for r in range(2)]
+    result = ctx.Array("i", [0] * world)
+    procs = [ctx.Process(target=_gloo_worker, args=(r, world, port, result)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(120)
         assert p.exitcode == 0
-    assert list(result) == [1, 1]
+    assert list(result) == [1] * world
