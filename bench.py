@@ -122,32 +122,8 @@ def dev_weights(torch, w: dict):
 
 
 def synth_weights_dev(torch, dm, seed):
-    """Random packed weights generated on the device (same distributions as
-    jimotono_b200.moe.synth_weights; large configurations would take minutes
-    to generate with numpy)."""
-    from jimotono_b200.moe import WEIGHT_FIELDS, MoeWeights
-    g = torch.Generator(device="cuda")
-    g.manual_seed(seed)
-    E, d, f, S, fs = dm.E, dm.d, dm.f, max(dm.S, 1), max(dm.fs, 64)
-
-    def u8(*shape):
-        return torch.randint(0, 256, shape, dtype=torch.uint8, device="cuda", generator=g)
-
-    def s8(*shape):
-        return torch.randint(-127, 128, shape, dtype=torch.int8, device="cuda", generator=g)
-
-    def uni(lo, hi, *shape, dtype=torch.float32):
-        return (torch.rand(shape, device="cuda", generator=g) * (hi - lo) + lo).to(dtype)
-
-    dw = {
-        "wg": u8(E, f, d // 4), "wu": u8(E, f, d // 4),
-        "sg": uni(0.01, 0.05, E, d // 64, f, dtype=torch.float16),
-        "su": uni(0.01, 0.05, E, d // 64, f, dtype=torch.float16),
-        "wd": u8(E, d, f // 2), "sd": uni(0.01, 0.05, E, f // 64, d, dtype=torch.float16),
-        "wsg": s8(S, fs, d), "wsu": s8(S, fs, d), "ssg": uni(4e-4, 8e-4, S, fs),
-        "ssu": uni(4e-4, 8e-4, S, fs), "wsd": s8(S, d, fs), "ssd": uni(4e-4, 8e-4, S, d),
-    }
-    return dw, MoeWeights(*[dw[n].data_ptr() for n in WEIGHT_FIELDS])
+    from jimotono_b200.moe import synth_weights_dev as gen
+    return gen(torch, dm, seed)
 
 
 def weight_bytes(dm) -> int:
@@ -170,11 +146,8 @@ def time_layer(torch, cfg, rank, world, steps, warmup, seed, zipf=None, bf16=Fal
     logits = torch.randn((T, dm.E), device="cuda", generator=g)
     bias = None
     if zipf is not None:
-        rng = np.random.default_rng(seed)
-        ranks = rng.permutation(dm.E) + 1
-        pmf = 1.0 / ranks.astype(np.float64) ** zipf
-        pmf /= pmf.sum()
-        bias = torch.from_numpy(np.log(pmf).astype(np.float32)).cuda()
+        from jimotono_b200.moe import zipf_bias
+        bias = torch.from_numpy(zipf_bias(dm.E, zipf, np.random.default_rng(seed))).cuda()
     y = torch.empty((T, dm.d), dtype=torch.bfloat16 if bf16 else torch.float32, device="cuda")
     plan = Plan(dm)
     stream = torch.cuda.current_stream().cuda_stream
@@ -666,8 +639,7 @@ def main():
                          "unit": "TOPS", "frac": round(ops_gu / (gu_ms / 1e3) / 1e12 / 4500.0, 4),
                          "peak_kind": "nominal dense int8 (MEASURED_PEAKS has no int8 entry)",
                          "traffic": GU_TRAFFIC_BYTES,
-                         "traffic_note": "ncu dram read+write of one launch at 1/8 of config 5, x8 "
-                                         "(profiles/k_moe_gemm_routed_cfg5_small.md)"},
+                         "traffic_note": "ncu dram read+write of one launch at 1/8 of config 5, x8"},
             "layer_TOPS": round((ops_gu + ops_dn + ops_sh) / (ms / 1e3) / 1e12, 1),
             "clocks": clocks, "hbm_peak_gbs": hbm_peak, "hbm_peak_kind": peak_kind,
             "parts": parts, "cpu_baseline": cpu,

@@ -194,20 +194,25 @@ int jt_b200_w8a8_gemm(const int8_t *X, int ldx, const float *sx, const int8_t *W
 int jt_b200_w8a8_gemm_i32(const int8_t *X, int ldx, const int8_t *W, int ldw, int32_t *C32,
                           int ldc, int M, int N, int K, void *stream);
 
-/* Per-token quantization of fp32 activations x [M][K] (the per-row form of
- * jt_w8a8_quant_per_channel) followed by jt_b200_w8a8_gemm, in one call
- * that allocates no memory: the int8 codes and row scales live in a fixed
- * device array inside the library.  No counterpart in the reference.
+/* y = W8A8 linear layer on fp32 activations, in one call that allocates
+ * no memory.  Each row of x [M][K] is quantized to int8 codes with its own
+ * fp32 scale (max|x_row| / 127, round half away from zero), then
+ * C[m][n] = ((float)acc[m][n] * scale[m]) * sw[n] as jt_b200_w8a8_gemm
+ * computes it.  The codes and row scales live in a fixed device array
+ * inside the library.  No counterpart in the reference.
  *
  * For callers that must not allocate device memory at all - a runtime
  * with a fixed memory budget, or one that enqueues work where an
  * allocation would synchronize the device.  Limits: M <= 4096 and
  * M * K <= 2 MiB of codes (larger shapes return JT_ERR_INVAL, errno
- * E2BIG); K and ldw multiples of 16.  The scratch is one per device, so
- * calls on one device must not overlap: issue them on one stream or order
- * them.  The first call on a device looks up the scratch address (a
- * host-side, synchronous step); make it before any stream capture.
- * Non-finite activations are reported by jt_b200_sync. */
+ * E2BIG); K and ldw multiples of 16; W 16-byte aligned (else
+ * JT_ERR_INVAL).  The scratch is one per device and keeps the last call's
+ * contents, so calls on one device must not overlap: issue them on one
+ * stream or order them.  The first call on a device looks up the scratch
+ * address (a host-side, synchronous step); make it before any stream
+ * capture.  A row of x holding a non-finite value comes out as NaN in every
+ * column of C and jt_b200_sync reports JT_ERR_CUDA; the other rows are
+ * valid. */
 #define JT_B200_LINEAR_NOALLOC_MAX_ROWS 4096
 #define JT_B200_LINEAR_NOALLOC_MAX_CODES (2 * 1024 * 1024)
 int jt_b200_w8a8_linear_noalloc(const float *x, int M, int K, const int8_t *W, int ldw,
@@ -313,10 +318,14 @@ size_t jt_b200_moe_plan_bytes(const jt_b200_moe_plan *plan);
  * then the twelve arrays of jt_b200_moe_weights in field order, each at a
  * 4096-byte aligned offset.  A reader rejects a header that does not match
  * `dims` (JT_ERR_INVAL) and data that does not match its checksums
- * (JT_ERR_IO).  _sizes gives each array's byte size for `dims` (T, k and
+ * (JT_ERR_IO); it checks every checksum before it writes any destination,
+ * so a rejected file leaves the arrays untouched (a file modified while it
+ * is being read is reported as JT_ERR_IO too, with the arrays then partly
+ * overwritten).  _sizes gives each array's byte size for `dims` (T, k and
  * cap_factor are not part of the weights).  _write_host / _read_host take
  * host arrays in field order; _save / _load take device buffers (the
- * pointers in `w`; _load writes into them) and copy through a pinned host
+ * pointers in `w`; _load writes into them), wait for all work on the
+ * device to finish (cudaDeviceSynchronize) and copy through a pinned host
  * buffer, synchronously. */
 int jt_b200_moe_weights_sizes(const jt_b200_moe_dims *dims, size_t sizes[12]);
 int jt_b200_moe_weights_write_host(const char *path, const jt_b200_moe_dims *dims,

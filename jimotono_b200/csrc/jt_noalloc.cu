@@ -9,6 +9,8 @@
 // those two calls made in sequence.
 #include <cuda_runtime.h>
 #include <errno.h>
+#include <stdint.h>
+
 #include <mutex>
 
 #include "../../include/jimotono_b200.h"
@@ -54,6 +56,15 @@ int scratch_for_current_device(Scratch *out) {
     return 0;
 }
 
+// Row scales start every call as NaN: the quantizer overwrites the scale of
+// each row it accepts and leaves a row with a non-finite activation (or a
+// scale that underflows) alone, so that row of C comes out NaN in every
+// column instead of carrying an earlier call's codes.
+__global__ void k_nl_begin(float *scales, int M) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < M) scales[i] = __int_as_float(0x7fc00000);
+}
+
 // A non-finite activation or a scale underflow found by the quantizer is
 // moved into the library's error word (reported by jt_b200_sync) and the
 // flag is reset for the next call.
@@ -81,19 +92,32 @@ extern "C" int jt_b200_w8a8_linear_noalloc(const float *x, int M, int K, const i
         errno = E2BIG;
         return JT_ERR_INVAL;
     }
+    // The tensor map of W needs a 16-byte aligned base; the fp32 operands
+    // are read and written as whole floats.
+    if ((reinterpret_cast<uintptr_t>(W) & 15u) != 0 || (reinterpret_cast<uintptr_t>(x) & 3u) != 0 ||
+        (reinterpret_cast<uintptr_t>(sw) & 3u) != 0 || (reinterpret_cast<uintptr_t>(C) & 3u) != 0) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
     Scratch s;
     if (scratch_for_current_device(&s) != 0) {
         errno = EIO;
         return JT_ERR_CUDA;
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    k_nl_begin<<<(M + 255) / 256, 256, 0, st>>>(s.scales, M);
+    if (cudaGetLastError() != cudaSuccess) {
+        errno = EIO;
+        return JT_ERR_CUDA;
+    }
     int r = jtk_quant_blocks(x, M, K, K, 0, s.codes, s.scales, nullptr, s.bad, st);
-    if (r == 0)
+    if (r == 0) {
         r = jtk_w8a8_gemm(s.codes, K, W, ldw, M, N, K, s.scales, sw, 0.0, C, ldc,
                           JTK_EPI_TOKEN_CHANNEL_F32, st);
-    if (r == 0) {
+        // The quantizer ran: whatever happened to the GEMM, its fault flag
+        // is folded into the error word and cleared for the next call.
         k_nl_fold<<<1, 1, 0, st>>>(s.bad, jtk_error_word());
-        if (cudaGetLastError() != cudaSuccess) r = -4;
+        if (cudaGetLastError() != cudaSuccess && r == 0) r = -4;
     }
     if (r == -1) {
         errno = EINVAL;

@@ -167,24 +167,32 @@ static int read_file(const char *path, const jt_b200_moe_dims *dm, wf_put_fn put
         errno = EINVAL;
         return JT_ERR_INVAL;
     }
-    for (int i = 0; i < WF_N; i++) {
-        if (fseek(fp, (long)h.offset[i], SEEK_SET) != 0) return io_fail("seek failed", fp);
-        uint64_t hsum = FNV_INIT;
-        for (size_t o = 0; o < sizes[i]; o += bufsz) {
-            const size_t n = sizes[i] - o < bufsz ? sizes[i] - o : bufsz;
-            if (fread(buf, 1, n, fp) != n) return io_fail("truncated weight file", fp);
-            hsum = fnv1a64(hsum, buf, n);
-            if (put(ctx, i, buf, o, n) != 0) {
-                fclose(fp);
-                errno = EIO;
-                return JT_ERR_CUDA;
+    /* Pass 1 checks every array against its checksum without writing
+     * anything; pass 2 copies into the destinations.  So a corrupt or
+     * truncated file leaves the caller's arrays untouched.  Pass 2 hashes
+     * again and reports a file changed between the passes (the destinations
+     * then hold part of the new contents). */
+    for (int pass = 0; pass < 2; pass++) {
+        for (int i = 0; i < WF_N; i++) {
+            if (fseek(fp, (long)h.offset[i], SEEK_SET) != 0) return io_fail("seek failed", fp);
+            uint64_t hsum = FNV_INIT;
+            for (size_t o = 0; o < sizes[i]; o += bufsz) {
+                const size_t n = sizes[i] - o < bufsz ? sizes[i] - o : bufsz;
+                if (fread(buf, 1, n, fp) != n) return io_fail("truncated weight file", fp);
+                hsum = fnv1a64(hsum, buf, n);
+                if (pass == 1 && put(ctx, i, buf, o, n) != 0) {
+                    fclose(fp);
+                    errno = EIO;
+                    return JT_ERR_CUDA;
+                }
             }
-        }
-        if (hsum != h.fnv[i]) {
-            fclose(fp);
-            jt_set_last_error("weight file checksum mismatch", 0);
-            errno = EIO;
-            return JT_ERR_IO;
+            if (hsum != h.fnv[i]) {
+                fclose(fp);
+                jt_set_last_error(pass == 0 ? "weight file checksum mismatch"
+                                            : "weight file changed while it was read", 0);
+                errno = EIO;
+                return JT_ERR_IO;
+            }
         }
     }
     fclose(fp);
@@ -280,6 +288,13 @@ static int dev_file(const char *path, const jt_b200_moe_dims *dims, const jt_b20
             errno = EINVAL;
             return JT_ERR_INVAL;
         }
+    /* The copies below run on the legacy default stream; work that is still
+     * producing or consuming the weights on other streams (a packer on a
+     * non-blocking stream, a forward) finishes first. */
+    if (cudaDeviceSynchronize() != cudaSuccess) {
+        errno = EIO;
+        return JT_ERR_CUDA;
+    }
     unsigned char *buf = NULL;
     if (cudaMallocHost((void **)&buf, WF_BUF) != cudaSuccess) {
         errno = ENOMEM;

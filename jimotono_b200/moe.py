@@ -69,16 +69,49 @@ def synth_weights(dm: Dims, seed: int) -> dict:
     return w
 
 
+def synth_weights_dev(torch, dm: Dims, seed: int):
+    """The synth_weights distributions generated on the current CUDA device
+    with a seeded torch generator (numpy takes minutes at the largest
+    configurations).  Returns ({name: tensor}, MoeWeights of their device
+    pointers); fp16 scales are torch.float16 tensors."""
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    E, d, f, S, fs = dm.E, dm.d, dm.f, max(dm.S, 1), max(dm.fs, 64)
+
+    def u8(*shape):
+        return torch.randint(0, 256, shape, dtype=torch.uint8, device="cuda", generator=g)
+
+    def s8(*shape):
+        return torch.randint(-127, 128, shape, dtype=torch.int8, device="cuda", generator=g)
+
+    def uni(lo, hi, *shape, dtype=torch.float32):
+        return (torch.rand(shape, device="cuda", generator=g) * (hi - lo) + lo).to(dtype)
+
+    dw = {
+        "wg": u8(E, f, d // 4), "wu": u8(E, f, d // 4),
+        "sg": uni(0.01, 0.05, E, d // 64, f, dtype=torch.float16),
+        "su": uni(0.01, 0.05, E, d // 64, f, dtype=torch.float16),
+        "wd": u8(E, d, f // 2), "sd": uni(0.01, 0.05, E, f // 64, d, dtype=torch.float16),
+        "wsg": s8(S, fs, d), "wsu": s8(S, fs, d), "ssg": uni(4e-4, 8e-4, S, fs),
+        "ssu": uni(4e-4, 8e-4, S, fs), "wsd": s8(S, d, fs), "ssd": uni(4e-4, 8e-4, S, d),
+    }
+    return dw, MoeWeights(*[dw[n].data_ptr() for n in WEIGHT_FIELDS])
+
+
+def zipf_bias(E: int, s: float, rng: np.random.Generator) -> np.ndarray:
+    """Per-expert routing bias log(Zipf(s) pmf) over a seeded permutation of
+    the experts (the skewed-load configuration)."""
+    ranks = rng.permutation(E) + 1
+    pmf = 1.0 / ranks.astype(np.float64) ** s
+    pmf /= pmf.sum()
+    return np.log(pmf).astype(np.float32)
+
+
 def synth_inputs(dm: Dims, T: int, seed: int, zipf_s: float | None = None):
     rng = np.random.default_rng(seed)
     x = rng.standard_normal((T, dm.d), dtype=np.float32)
     logits = rng.standard_normal((T, dm.E), dtype=np.float32)
-    bias = None
-    if zipf_s is not None:
-        ranks = rng.permutation(dm.E) + 1
-        pmf = 1.0 / ranks.astype(np.float64) ** zipf_s
-        pmf /= pmf.sum()
-        bias = np.log(pmf).astype(np.float32)
+    bias = zipf_bias(dm.E, zipf_s, rng) if zipf_s is not None else None
     return x, logits, bias
 
 

@@ -66,6 +66,8 @@ def oracle() -> C.CDLL:
             "jto_lowbit_partials": (None, [P, P, I, I, I, P]),
             "jto_moe_forward": (I, [C.POINTER(MoeDims), C.POINTER(MoeWeights), P, P, P, P,
                                     C.POINTER(MoeTrace)]),
+            "jto_moe_forward_sampled": (I, [C.POINTER(MoeDims), C.POINTER(MoeWeights), P, P, P,
+                                            P, I, P, P, P, I, P, C.POINTER(MoeTrace)]),
         }
         for n, (r, a) in protos.items():
             fn = getattr(h, n)

@@ -551,3 +551,103 @@ out:
     free(yacc);
     return rc;
 }
+
+/* Sampled form of jto_moe_forward for layer shapes whose full restatement
+ * takes too long on one core (the benchmarked configurations).  Routing
+ * (routing.c:16-76), the capacity sort (moe_layer.c:895-978), the
+ * renormalization (moe_layer.c:1171-1201) and the token quantization run in
+ * full and go to `tr` (ids, w, perm, off, drop, xq, xs, kept).  The routed
+ * expert chain runs only for the kept rows rows[i] % kept (perm indices;
+ * the index used is written back to rows[i]) -> hq_rows [n_rows][f],
+ * hs_rows [n_rows][f/64].  The layer output, combined as in
+ * moe_layer.c:1443-1574 (double, slots ascending, then the shared experts
+ * in order), is formed only for the tokens toks[i] -> y_tok [n_tok][d].
+ * Every computed value is the one jto_moe_forward gives for the same row or
+ * token. */
+int jto_moe_forward_sampled(const jto_moe_dims *dm, const jto_moe_weights *w, const float *x,
+                            const float *logits, const float *bias, int32_t *rows, int n_rows,
+                            int8_t *hq_rows, float *hs_rows, const int32_t *toks, int n_tok,
+                            float *y_tok, jto_moe_trace *tr) {
+    const int T = dm->T, d = dm->d, f = dm->f, E = dm->E, k = dm->k, S = dm->S, fs = dm->fs;
+    if (T <= 0 || d <= 0 || f <= 0 || E <= 0 || k <= 0 || k > E || S < 0) return 2;
+    if (d % 128 || f % 128 || (S > 0 && fs % 128)) return 2;
+    if (n_rows < 0 || n_tok < 0) return 2;
+    for (int i = 0; i < n_tok; i++)
+        if (toks[i] < 0 || toks[i] >= T) return 2;
+    const size_t Tk = (size_t)T * k;
+    int rc = 2, kept = 0;
+    int32_t *ids = malloc(Tk * sizeof(int32_t));
+    float *wt = malloc(Tk * sizeof(float));
+    int32_t *perm = malloc(Tk * sizeof(int32_t));
+    int32_t *off = malloc(((size_t)E + 1) * sizeof(int32_t));
+    uint8_t *drop = malloc(Tk);
+    int8_t *xq = malloc((size_t)T * d);
+    float *xs = malloc((size_t)T * sizeof(float));
+    const int fmax_ = f > fs ? f : fs;
+    float *gbuf = malloc((size_t)fmax_ * sizeof(float));
+    float *ubuf = malloc((size_t)fmax_ * sizeof(float));
+    float *hbuf = malloc((size_t)fmax_ * sizeof(float));
+    int8_t *hqtmp = malloc((size_t)fmax_);
+    float *hstmp = malloc((size_t)(fmax_ / 64 + 1) * sizeof(float));
+    float *yrow = malloc((size_t)d * sizeof(float));
+    double *yacc = malloc((size_t)d * sizeof(double));
+    if (!ids || !wt || !perm || !off || !drop || !xq || !xs || !gbuf || !ubuf || !hbuf ||
+        !hqtmp || !hstmp || !yrow || !yacc) {
+        rc = 1;
+        goto out;
+    }
+    if (jto_route_topk(logits, bias, T, E, k, ids, wt)) goto out;
+    if (jto_batch_sort(ids, T, k, E, dm->cap_factor, perm, off, drop, &kept)) goto out;
+    if (jto_renorm(wt, drop, T, k)) goto out;
+    if (jto_quant_blocks(x, T, d, d, xq, xs)) goto out;
+    for (int i = 0; i < n_rows && kept > 0; i++) {
+        const int r = (int)((uint32_t)rows[i] % (uint32_t)kept);
+        rows[i] = r;
+        const int q = perm[r], t = q / k, e = ids[q];
+        routed_expert(dm, w, e, xq + (size_t)t * d, xs[t], hq_rows + (size_t)i * f,
+                      hs_rows + (size_t)i * (f / 64), yrow, gbuf, ubuf, hbuf);
+    }
+    for (int i = 0; i < n_tok; i++) {
+        const int t = toks[i];
+        for (int o = 0; o < d; o++) yacc[o] = 0.0;
+        for (int p = 0; p < k; p++) {
+            const size_t q = (size_t)t * k + p;
+            if (drop[q]) continue;
+            routed_expert(dm, w, ids[q], xq + (size_t)t * d, xs[t], hqtmp, hstmp, yrow, gbuf, ubuf,
+                          hbuf);
+            for (int o = 0; o < d; o++) yacc[o] += (double)wt[q] * (double)yrow[o];
+        }
+        for (int s = 0; s < S; s++) {
+            shared_expert(dm, w, s, xq + (size_t)t * d, xs[t], yrow, hbuf, hqtmp, hstmp);
+            for (int o = 0; o < d; o++) yacc[o] += (double)yrow[o];
+        }
+        for (int o = 0; o < d; o++) y_tok[(size_t)i * d + o] = (float)yacc[o];
+    }
+    if (tr) {
+        if (tr->ids) memcpy(tr->ids, ids, Tk * sizeof(int32_t));
+        if (tr->w) memcpy(tr->w, wt, Tk * sizeof(float));
+        if (tr->perm) memcpy(tr->perm, perm, (size_t)kept * sizeof(int32_t));
+        if (tr->off) memcpy(tr->off, off, ((size_t)E + 1) * sizeof(int32_t));
+        if (tr->drop) memcpy(tr->drop, drop, Tk);
+        if (tr->xq) memcpy(tr->xq, xq, (size_t)T * d);
+        if (tr->xs) memcpy(tr->xs, xs, (size_t)T * sizeof(float));
+        tr->kept = kept;
+    }
+    rc = 0;
+out:
+    free(ids);
+    free(wt);
+    free(perm);
+    free(off);
+    free(drop);
+    free(xq);
+    free(xs);
+    free(gbuf);
+    free(ubuf);
+    free(hbuf);
+    free(hqtmp);
+    free(hstmp);
+    free(yrow);
+    free(yacc);
+    return rc;
+}

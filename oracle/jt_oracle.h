@@ -119,6 +119,16 @@ typedef struct jto_moe_trace {
 int jto_moe_forward(const jto_moe_dims *dm, const jto_moe_weights *w, const float *x,
                     const float *logits, const float *bias, float *y, jto_moe_trace *trace);
 
+/* Sampled form for the benchmarked shapes: routing, sort, renormalization
+ * and token quantization in full (trace ids/w/perm/off/drop/xq/xs/kept);
+ * hq/hs only for the kept rows rows[i] % kept (index written back), the
+ * output only for the tokens toks[i] (y_tok [n_tok][d]).  Same values as
+ * jto_moe_forward for those rows and tokens. */
+int jto_moe_forward_sampled(const jto_moe_dims *dm, const jto_moe_weights *w, const float *x,
+                            const float *logits, const float *bias, int32_t *rows, int n_rows,
+                            int8_t *hq_rows, float *hs_rows, const int32_t *toks, int n_tok,
+                            float *y_tok, jto_moe_trace *trace);
+
 #ifdef __cplusplus
 }
 #endif

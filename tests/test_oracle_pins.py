@@ -285,3 +285,48 @@ def test_live_router_logits_vs_reference_layer(T, n, E, k):
     nodrop = ~drop.reshape(T, k).any(axis=1)
     assert nodrop.any()
     assert np.array_equal(ow.reshape(T, k)[nodrop].view(np.uint32), w.reshape(T, k)[nodrop].view(np.uint32))
+
+
+def test_sampled_layer_equals_full_layer():
+    """jto_moe_forward_sampled (the oracle form the benchmarked-shape GPU
+    tests use) gives, for the rows and tokens it computes, exactly the
+    values of jto_moe_forward."""
+    from jimotono_b200.moe import WEIGHT_FIELDS, Dims, synth_inputs, synth_weights
+    dm = Dims(96, 256, 128, 8, 4, 2, 256, 1.0)
+    w = synth_weights(dm, seed=11)
+    w = {n: np.ascontiguousarray(a.view(np.uint16) if a.dtype == np.float16 else a) for n, a in w.items()}
+    x, logits, bias = synth_inputs(dm, dm.T, seed=12, zipf_s=1.1)
+    od = oracle.MoeDims(dm.T, dm.d, dm.f, dm.E, dm.k, dm.S, dm.fs, dm.cap_factor)
+    ow = oracle.MoeWeights(*[w[n].ctypes.data for n in WEIGHT_FIELDS])
+    Tk = dm.T * dm.k
+    full = {"ids": np.zeros(Tk, np.int32), "w": np.zeros(Tk, np.float32), "perm": np.zeros(Tk, np.int32),
+            "off": np.zeros(dm.E + 1, np.int32), "drop": np.zeros(Tk, np.uint8),
+            "xq": np.zeros(dm.T * dm.d, np.int8), "xs": np.zeros(dm.T, np.float32),
+            "hq": np.zeros(Tk * dm.f, np.int8), "hs": np.zeros(Tk * dm.f // 64, np.float32)}
+    ft = oracle.MoeTrace(*[full[n].ctypes.data for n in ("ids", "w", "perm", "off", "drop", "xq", "xs",
+                                                         "hq", "hs")], None, None, 0)
+    y = np.zeros((dm.T, dm.d), np.float32)
+    o = oracle.oracle()
+    assert o.jto_moe_forward(C.byref(od), C.byref(ow), P(x), P(logits), P(bias), P(y), C.byref(ft)) == 0
+    kept = ft.kept
+    assert full["drop"].sum() > 0
+    samp = {n: np.zeros_like(full[n]) for n in ("ids", "w", "perm", "off", "drop", "xq", "xs")}
+    st = oracle.MoeTrace(*[samp[n].ctypes.data for n in ("ids", "w", "perm", "off", "drop", "xq", "xs")],
+                         None, None, None, None, 0)
+    rows = np.array([0, 5, kept - 1, kept + 3, 2**31 - 2], np.int32)
+    toks = np.array([0, 17, dm.T - 1], np.int32)
+    hq = np.zeros((len(rows), dm.f), np.int8)
+    hs = np.zeros((len(rows), dm.f // 64), np.float32)
+    ys = np.zeros((len(toks), dm.d), np.float32)
+    assert o.jto_moe_forward_sampled(C.byref(od), C.byref(ow), P(x), P(logits), P(bias), P(rows), len(rows),
+                                     P(hq), P(hs), P(toks), len(toks), P(ys), C.byref(st)) == 0
+    assert st.kept == kept
+    for n in ("ids", "w", "off", "drop", "xq", "xs"):
+        assert np.array_equal(samp[n], full[n]), n
+    assert np.array_equal(samp["perm"][:kept], full["perm"][:kept])
+    assert list(rows) == [0, 5, kept - 1, 3, (2**31 - 2) % kept]
+    fhq = full["hq"].reshape(Tk, dm.f)
+    fhs = full["hs"].reshape(Tk, dm.f // 64)
+    assert np.array_equal(hq, fhq[rows])
+    assert np.array_equal(hs.view(np.uint32), fhs[rows].view(np.uint32))
+    assert np.array_equal(ys.view(np.uint32), y[toks].view(np.uint32))

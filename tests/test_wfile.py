@@ -74,10 +74,16 @@ def test_rejects_other_dims_truncation_and_corruption(tmp_path):
     bad[off + 17] ^= 0x40
     bad_path = str(tmp_path / "bad.jtb2")
     bad.tofile(bad_path)
+    sentinel = [np.full_like(a, 0xA5) for a in arrs]
+    back = [a.copy() for a in sentinel]
     assert lib().jt_b200_moe_weights_read_host(bad_path.encode(), C.byref(dm.c()), _ptrs(back)) == JT_ERR_IO
+    # rejected before any destination is written: the arrays in front of the
+    # corrupted one are untouched too
+    assert all(np.array_equal(a, b) for a, b in zip(back, sentinel))
     short_path = str(tmp_path / "short.jtb2")
     raw[:raw.size - 5000].tofile(short_path)
     assert lib().jt_b200_moe_weights_read_host(short_path.encode(), C.byref(dm.c()), _ptrs(back)) == JT_ERR_IO
+    assert all(np.array_equal(a, b) for a, b in zip(back, sentinel))
     assert lib().jt_b200_moe_weights_read_host(str(tmp_path / "missing").encode(), C.byref(dm.c()),
                                                _ptrs(back)) == JT_ERR_IO
     assert lib().jt_b200_moe_weights_write_host(path.encode(), C.byref(dm.c()), None) == JT_ERR_INVAL

@@ -87,3 +87,36 @@ def test_noalloc_rejects_shapes_beyond_its_scratch():
     assert f(p, 4097, 16, p, 16, p, p, 16, 16, None) == JT_ERR_INVAL
     assert f(p, 513, 4096, p, 4096, p, p, 16, 16, None) == JT_ERR_INVAL
     assert f(p, 4, 24, p, 32, p, p, 16, 16, None) == JT_ERR_INVAL  # K not a multiple of 16
+
+
+@pytest.mark.gpu
+def test_noalloc_nonfinite_row_comes_out_nan_and_is_reported():
+    from tests import _dev
+    M, N, K = 64, 128, 256
+    x, W, sw = _case(14, M, N, K)
+    x[5, 17] = np.inf
+    dx, dW, dsw = _dev.to_dev(x), _dev.to_dev(W), _dev.to_dev(sw)
+    dC = _dev.zeros((M, N), np.float32)
+    rc = lib().jt_b200_w8a8_linear_noalloc(dx.data_ptr(), M, K, dW.data_ptr(), K, dsw.data_ptr(),
+                                           dC.data_ptr(), N, N, _dev.stream())
+    assert rc == 0
+    assert lib().jt_b200_sync() != 0  # the non-finite activation is reported ...
+    assert lib().jt_b200_sync() == 0  # ... once
+    got = _dev.host(dC)
+    assert np.isnan(got[5]).all()
+    x[5] = 0.0  # every other row is quantized on its own
+    want = _existing_path(x, W, sw)
+    keep = np.arange(M) != 5
+    scale = float(np.abs(want[keep]).max())
+    assert float(np.abs(got[keep] - want[keep]).max()) / scale <= TOL
+    # the next call starts clean
+    x2, W2, sw2 = _case(15, M, N, K)
+    got2 = _noalloc(x2, W2, sw2)
+    want2 = _existing_path(x2, W2, sw2)
+    assert float(np.abs(got2 - want2).max()) / float(np.abs(want2).max()) <= TOL
+
+
+def test_noalloc_rejects_misaligned_weights():
+    f = lib().jt_b200_w8a8_linear_noalloc
+    p, q = C.c_void_p(16), C.c_void_p(24)
+    assert f(p, 4, 16, q, 16, p, p, 16, 16, None) == JT_ERR_INVAL
