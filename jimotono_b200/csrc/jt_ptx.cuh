@@ -63,6 +63,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+// The same test with a suspend-time hint: a thread whose phase is not yet
+// complete sleeps in the instruction (woken when the phase completes, or
+// after at most JT_SUSPEND_NS) instead of re-issuing the test in a loop, so
+// waiting warps leave the issue slots to the warps doing work.
+#ifndef JT_SUSPEND_NS
+#define JT_SUSPEND_NS 1000000u
+#endif
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(JT_SUSPEND_NS)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait. Returns false (and raises the CTA abort flag + device error
 // word) when the budget runs out or another role already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
@@ -70,7 +89,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_sleep(bar, parity)) return true;
         if (*abort_flag) return false;
         if (clock64() - t0 > JT_SPIN_CYCLES) {
             *abort_flag = 1;
@@ -352,6 +371,18 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t pa
     return ok != 0;
 }
 
+__device__ __forceinline__ bool mbar_try_wait_cluster_sleep(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(JT_SUSPEND_NS)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait (cluster-scope acquire) on a local barrier that CTAs of the
 // cluster arrive on; same abort protocol as mbar_wait.
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity,
@@ -359,7 +390,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity
     if (mbar_try_wait_cluster(bar, parity)) return true;
     const long long t0 = clock64();
     while (true) {
-        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if (mbar_try_wait_cluster_sleep(bar, parity)) return true;
         if (*abort_flag) return false;
         if (clock64() - t0 > JT_SPIN_CYCLES) {
             *abort_flag = 1;

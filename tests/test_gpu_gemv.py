@@ -29,7 +29,8 @@ def _oracle(a, sa, packed, scales, bits):
 @pytest.mark.parametrize("n2,n4,K", [(256, 96, 2048), (70, 33, 1024), (64, 64, 4096), (0, 40, 2048),
                                      (37, 0, 192), (1, 1, 64),
                                      (20000, 7000, 256),    # many chunks per CTA: ring reuse
-                                     (9472, 4736, 2048)])   # 2 + 1 ring turns per SM
+                                     (9472, 4736, 2048),    # 2 + 1 ring turns per SM
+                                     (49152, 16384, 2048)])  # the batch-1 GEMV configuration in full
 def test_lowbit_gemv_matches_oracle(n2, n4, K):
     from tests import _dev
     rng = np.random.default_rng(n2 * 7 + n4 + K)

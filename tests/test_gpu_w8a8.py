@@ -202,3 +202,88 @@ def test_quant_nan_is_rejected_untouched():
     s = np.full(1, 3.0, np.float32)
     assert lib().jt_w8a8_quant_per_tensor(x.ctypes.data, 4, q.ctypes.data, s.ctypes.data) == 2
     assert (q == 9).all() and s[0] == 3.0
+
+
+@pytest.mark.skipif(not oracle.have_ref(), reason="reference library not built")
+@pytest.mark.parametrize("n", [1, 3, 256, 100003, 1 << 20])
+def test_compat_per_tensor_dequant_and_fakequant_match_reference(n):
+    """jt_w8a8_dequant_per_tensor (w8a8.c:749-785) and
+    jt_w8a8_fakequant_per_tensor (w8a8.c:1074-1120) bit for bit against the
+    reference library, including a whole-tensor zero input and the
+    fail-closed cases (-128 code, non-positive / non-finite scale, NaN input:
+    INVAL with the output untouched)."""
+    rng = np.random.default_rng(n)
+    r = oracle.ref()
+    q = _rand_s8(rng, n)
+    scale = np.float32(rng.uniform(0.001, 0.05))
+    dw, dg = np.zeros(n, np.float32), np.zeros(n, np.float32)
+    assert r.jt_w8a8_dequant_per_tensor(oracle.ptr(q), float(scale), n, oracle.ptr(dw)) == 0
+    assert lib().jt_w8a8_dequant_per_tensor(q.ctypes.data, float(scale), n, dg.ctypes.data) == 0
+    assert np.array_equal(dw.view(np.uint32), dg.view(np.uint32))
+    x = (rng.standard_normal(n) * rng.uniform(0.1, 30.0)).astype(np.float32)
+    fw, fg = np.zeros(n, np.float32), np.zeros(n, np.float32)
+    assert r.jt_w8a8_fakequant_per_tensor(oracle.ptr(x), n, oracle.ptr(fw)) == 0
+    assert lib().jt_w8a8_fakequant_per_tensor(x.ctypes.data, n, fg.ctypes.data) == 0
+    assert np.array_equal(fw.view(np.uint32), fg.view(np.uint32))
+    z = np.zeros(n, np.float32)
+    fw[:] = 5.0
+    fg[:] = 5.0
+    assert r.jt_w8a8_fakequant_per_tensor(oracle.ptr(z), n, oracle.ptr(fw)) == 0
+    assert lib().jt_w8a8_fakequant_per_tensor(z.ctypes.data, n, fg.ctypes.data) == 0
+    assert np.array_equal(fw.view(np.uint32), fg.view(np.uint32))
+    # fail-closed: each rejected call leaves its output as it was
+    keep = dg.copy()
+    qbad = q.copy()
+    qbad[n // 2] = -128
+    assert r.jt_w8a8_dequant_per_tensor(oracle.ptr(qbad), float(scale), n, oracle.ptr(dw)) == 2
+    assert lib().jt_w8a8_dequant_per_tensor(qbad.ctypes.data, float(scale), n, dg.ctypes.data) == 2
+    for bad_scale in (0.0, -1.0, float("inf"), float("nan")):
+        assert r.jt_w8a8_dequant_per_tensor(oracle.ptr(q), bad_scale, n, oracle.ptr(dw)) == 2
+        assert lib().jt_w8a8_dequant_per_tensor(q.ctypes.data, bad_scale, n, dg.ctypes.data) == 2
+    assert np.array_equal(dg, keep)
+    xbad = x.copy()
+    xbad[n - 1] = np.nan
+    keep = fg.copy()
+    assert r.jt_w8a8_fakequant_per_tensor(oracle.ptr(xbad), n, oracle.ptr(fw)) == 2
+    assert lib().jt_w8a8_fakequant_per_tensor(xbad.ctypes.data, n, fg.ctypes.data) == 2
+    assert np.array_equal(fg, keep)
+
+
+# Projection shapes of a Gated DeltaNet-2 attention layer (gdn2.h: head dims
+# dk = dv = 128 by default, at most JT_GDN2_MAX_D = 1024) in front of and
+# behind the MoE layer, d_model 1024 / 2048: fused q|k|v|w projection
+# (4 x 16 heads x 128), b (erase) keys, per-head decay gates (16 outputs),
+# and the output projection back to d_model; decode (M = 1) and prefill rows.
+GDN2_SHAPES = [  # (M, N, K)
+    (1, 8192, 2048), (1, 16, 2048), (1, 2048, 2048), (1, 1024, 1024),
+    (7, 2048, 2048), (4096, 8192, 2048), (4096, 16, 2048), (4096, 2048, 2048),
+    (2048, 4096, 1024), (2048, 1024, 1024), (300, 2048, 1024),
+]
+
+
+@pytest.mark.parametrize("M,N,K", GDN2_SHAPES)
+def test_gdn2_projection_shapes(M, N, K):
+    """The W8A8 GEMM at the attention-projection shapes of the GDN-2 path:
+    int32 accumulators and the per-token x per-channel fp32 output bit for
+    bit against the oracle."""
+    from tests import _dev
+    rng = np.random.default_rng(5000 + M + N + K)
+    X = _rand_s8(rng, (M, K))
+    W = _rand_s8(rng, (N, K))
+    sx = rng.uniform(0.005, 0.02, M).astype(np.float32)
+    sw = rng.uniform(0.001, 0.01, N).astype(np.float32)
+    acc = np.empty((M, N), np.int32)
+    want = np.empty((M, N), np.float32)
+    o = oracle.oracle()
+    o.jto_gemm_s8(oracle.ptr(X), oracle.ptr(W), oracle.ptr(acc), M, N, K)
+    o.jto_w8a8_token_channel(oracle.ptr(acc), oracle.ptr(sx), oracle.ptr(sw), oracle.ptr(want), M, N)
+    d = [_dev.to_dev(a) for a in (X, sx, W, sw)]
+    dC = _dev.zeros((M, N), np.float32)
+    dI = _dev.zeros((M, N), np.int32)
+    assert lib().jt_b200_w8a8_gemm(d[0].data_ptr(), K, d[1].data_ptr(), d[2].data_ptr(), K,
+                                   d[3].data_ptr(), dC.data_ptr(), N, M, N, K, _dev.stream()) == 0
+    assert lib().jt_b200_w8a8_gemm_i32(d[0].data_ptr(), K, d[2].data_ptr(), K, dI.data_ptr(), N,
+                                       M, N, K, _dev.stream()) == 0
+    assert lib().jt_b200_sync() == 0
+    assert np.array_equal(_dev.host(dI), acc)
+    assert np.array_equal(_dev.host(dC).view(np.uint32), want.view(np.uint32))
