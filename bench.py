@@ -43,6 +43,8 @@ CFG2 = dict(T=1, d=1024, f=256, E=64, k=8, S=2, fs=512, cap=1.5)
 # 1/8 of config 5 (same rows per expert, same shapes per expert): the case the
 # profiler captures run on (`--small`), whose DRAM traffic scales by 8 to a
 # full config-5 launch.
+# rotating weight copies of the batch-1 timing (each forward touches 5.46 MB)
+DEC_ROT = 48
 CFG5_SMALL = dict(T=2048, d=2048, f=1536, E=128, k=8, S=2, fs=4096, cap=1.5)
 METRIC = "MoE-layer tokens/s at 1/2/4/8 B200; W8A8 TOPS; decode HBM GB/s vs peak"
 # DRAM bytes (read + write) of one routed gate/up launch at config 5: the ncu
@@ -185,27 +187,38 @@ def time_layer(torch, cfg, rank, world, steps, warmup, seed, zipf=None, bf16=Fal
     meta = plan.debug(9, np.int32, 4)
     out = dict(T=T, ms_per_step=ms / steps, stage_ms=stage, kept=int(meta[0]), dims=dm, plan=plan,
                x=x, logits=logits, y=y, rots=rots, bias=bias, bf16=bf16)
+    if nrot > 1:  # a token and router logits of its own for every weight copy
+        out["x_rot"] = [torch.randn((T, dm.d), device="cuda", generator=g) for _ in range(nrot)]
+        out["logits_rot"] = [torch.randn((T, dm.E), device="cuda", generator=g) for _ in range(nrot)]
     return out
 
 
-def time_decode_graph(torch, st, reps=50):
-    """Batch-1 forward captured 8 times (one per rotating weight copy) in a
-    CUDA graph and replayed: per-token device time without host launch
-    overhead.  Returns microseconds per token."""
+def time_decode_graph(torch, st, reps=50, warm=False):
+    """Batch-1 forwards captured in a CUDA graph and replayed: per-token
+    device time without host launch overhead, microseconds per token.
+
+    L2-cold (default): one forward per rotating weight copy, each with its
+    own token and router logits (so each picks its own experts); the copies
+    touch nrot x 5.46 MB, several times the 126 MB L2, so every forward
+    streams its weights from HBM.  warm=True replays the first copy with
+    the first token only (the same 5.46 MB every time, resident in L2)."""
     from jimotono_b200 import lib
-    plan, rots, x, logits, y = st["plan"], st["rots"], st["x"], st["logits"], st["y"]
-    nrot = len(rots)
+    plan, rots, y = st["plan"], st["rots"], st["y"]
+    xs, ls = st["x_rot"], st["logits_rot"]
+    per_graph = len(rots)
     s = torch.cuda.Stream()
     with torch.cuda.stream(s):
-        for i in range(nrot):
-            plan.forward(rots[i][1], x.data_ptr(), logits.data_ptr(), None, 1, y.data_ptr(), st["bf16"],
+        for i in range(per_graph):
+            j = 0 if warm else i
+            plan.forward(rots[j][1], xs[j].data_ptr(), ls[j].data_ptr(), None, 1, y.data_ptr(), st["bf16"],
                          s.cuda_stream)
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=s):
             cs = torch.cuda.current_stream().cuda_stream
-            for i in range(nrot):
-                plan.forward(rots[i][1], x.data_ptr(), logits.data_ptr(), None, 1, y.data_ptr(), st["bf16"], cs)
+            for i in range(per_graph):
+                j = 0 if warm else i
+                plan.forward(rots[j][1], xs[j].data_ptr(), ls[j].data_ptr(), None, 1, y.data_ptr(), st["bf16"], cs)
         for _ in range(5):
             g.replay()
         torch.cuda.synchronize()
@@ -217,7 +230,7 @@ def time_decode_graph(torch, st, reps=50):
         torch.cuda.synchronize()
     if lib().jt_b200_sync() != 0:
         raise RuntimeError("kernel fault in the decode graph")
-    us = e0.elapsed_time(e1) / (reps * nrot) * 1e3
+    us = e0.elapsed_time(e1) / (reps * per_graph) * 1e3
     del g
     return us
 
@@ -558,9 +571,11 @@ def main():
         elif args.part == "cfg4":
             out = part_gemv(torch, hbm_peak, steps=args.steps)
         elif args.part == "cfg2":
-            st2 = time_layer(torch, CFG2, 0, 1, args.steps, args.warmup, seed=2, nrot=8, profile=False)
+            st2 = time_layer(torch, CFG2, 0, 1, args.steps, args.warmup, seed=2, nrot=DEC_ROT, profile=False)
+            reps = max(1, args.steps // DEC_ROT)
             out = {"us_per_token_stream": round(st2["ms_per_step"] * 1e3, 2),
-                   "us_per_token_graph": round(time_decode_graph(torch, st2, reps=max(1, args.steps // 8)), 2)}
+                   "us_per_token_graph": round(time_decode_graph(torch, st2, reps=reps), 2),
+                   "us_per_token_graph_l2_warm": round(time_decode_graph(torch, st2, reps=reps, warm=True), 2)}
         else:
             st3 = time_layer(torch, CFG3, 0, 1, args.steps, args.warmup, seed=3, zipf=1.1, bf16=True)
             out = {"ms_per_step": round(st3["ms_per_step"], 4), "stage_ms": [round(v, 4) for v in st3["stage_ms"]]}
@@ -598,8 +613,9 @@ def main():
             "routed_TOPS": round(2.0 * st3["kept"] * CFG3["d"] * 3 * CFG3["f"] /
                                  ((st3["stage_ms"][4] + st3["stage_ms"][5]) / 1e3) / 1e12, 1)}
         del st3
-        st2 = time_layer(torch, CFG2, 0, 1, 200, 20, seed=2, nrot=8)
-        dec_us = time_decode_graph(torch, st2)
+        st2 = time_layer(torch, CFG2, 0, 1, 200, 20, seed=2, nrot=DEC_ROT)
+        dec_us = time_decode_graph(torch, st2, reps=10)
+        dec_us_warm = time_decode_graph(torch, st2, reps=10, warm=True)
         dm2 = st2["dims"]
         per_tok = (dm2.k * (2 * dm2.f * (dm2.d // 4 + dm2.d // 64 * 2) + dm2.d * (dm2.f // 2 + dm2.f // 64 * 2))
                    + dm2.S * (2 * dm2.fs * (dm2.d + 4) + dm2.d * (dm2.fs + 4)) + dm2.d * 8)
@@ -607,9 +623,11 @@ def main():
             "us_per_token": round(dec_us, 2), "bytes_per_token": per_tok,
             "GBs": round(per_tok / (dec_us / 1e6) / 1e9, 1),
             "frac_hbm": round(per_tok / (dec_us / 1e6) / 1e9 / hbm_peak, 4),
-            "timing": "CUDA graph of 8 forward calls (2 kernels each: gate/up with the router, down), replayed; "
-                      "stream-launched with per-stage events: %.2f us" % (st2["ms_per_step"] * 1e3),
-            "l2": "8 rotating weight copies (172 MB > L2)"}
+            "us_per_token_l2_warm": round(dec_us_warm, 2),
+            "timing": "CUDA graph of %d forward calls (2 kernels each: gate/up with the router, down), replayed; "
+                      "stream-launched with per-stage events: %.2f us" % (DEC_ROT, st2["ms_per_step"] * 1e3),
+            "l2": "%d rotating weight copies, each forward with its own token and logits: %d x 5.46 MB "
+                  "touched per replay, > L2 (l2_warm: one copy, one token)" % (DEC_ROT, DEC_ROT)}
         del st2
         parts["cfg1_w8a8"] = part_w8a8(torch)
         parts["cfg4_gemv"] = part_gemv(torch, hbm_peak)

@@ -3,30 +3,45 @@
 // One token selects k distinct experts and every expert's capacity is at
 // least one pair (cap = ceil(cap_factor * k / E) >= 1), so nothing is
 // dropped, the routing weights are final and the expert GEMMs degenerate to
-// matrix-vector products over the selected experts' rows.  The batched
-// chain (sort, dispatch, persistent tensor-core kernels per projection)
-// spends its time in launches and pipeline fill at this size; this path is
-// two kernels after the router:
+// matrix-vector products over the selected experts' rows.  The whole step
+// is a latency-bound walk through a few MB, spread over many SMs, in two
+// kernels:
 //
-//   k_dec_gateup  one CTA per (expert slot, 64-channel block): quantizes the
-//                 token (w8a8.c:688-747), computes the 64 gate and 64 up rows
-//                 (INT2 group-64 with the same fp32 fold as the grouped
-//                 kernel, or int8 rows of a shared expert), SwiGLU
-//                 (moe_layer.c:146-148) and the per-64-channel requantization
-//                 of h; CTA 0 also writes the sort results (perm, pos, off,
-//                 drop, kept) the batched path would produce for one token.
-//   k_dec_down    one warp per output channel: the down rows of every
-//                 selected expert (INT4 group-64 fold, or int8 rows of a
-//                 shared expert with the activation group scales) and the
-//                 combine in double in slot order, then the shared experts
+//   k_dec_gateup  work units of 128 weight rows: 64 gate rows over the same
+//                 64 up rows of one expert.  Routed unit (slot, 64-channel
+//                 block): INT2 rows, one row per thread, the group partials
+//                 folded in the thread in group order (same fp32 fold as the
+//                 grouped kernel), then SwiGLU (moe_layer.c:146-148) and the
+//                 per-64-channel requantization of h.  Shared-expert unit
+//                 (expert, 64-channel block, K part): the int8 rows of a
+//                 shared expert are d bytes long, so ksplit CTAs each take a
+//                 K part of every row; their exact int32 partial dots meet
+//                 in a device accumulator through integer atomic adds, and
+//                 the CTA that arrives last (ticket counter, no waiting)
+//                 takes the totals - resetting the accumulator for the next
+//                 call - and finishes the unit.  Every CTA quantizes the
+//                 token itself (w8a8.c:688-747); routed CTAs route it first
+//                 (jt_topk.cuh), which only they need, and the token's
+//                 quantization runs while their weight loads are in flight.
+//   k_dec_down    eight output channels per CTA.  Before it waits for the
+//                 gate/up grid (programmatic dependent launch) it routes the
+//                 token again (same function, same experts) with the
+//                 softmax and pulls its down weight rows - those of the
+//                 selected routed experts and of the shared experts, with
+//                 their scales - into shared memory with bulk copies, so
+//                 after the wait only the h rows (a few KB, from L2) are
+//                 read.  Then one thread per dot product (routed: a whole
+//                 INT4 row with its group fold; shared: the int32 partials of
+//                 two groups) and one thread per channel for the combine in
+//                 double in slot order and the shared experts
 //                 (moe_layer.c:1443-1463, :1549-1559), fp32 or bf16 out.
 //
-// Integer dot products use dp4a on codes taken from the packed words in
-// place: for an INT2 word (16 codes, byte b holds k0+4b .. k0+4b+3), the
-// j-th 2-bit field of every byte is the code of k0+4b+j, so it pairs with
-// the activation word {x[k0+j], x[k0+4+j], x[k0+8+j], x[k0+12+j]}; the
-// signed code c = 2 li - (2^bits - 1) enters as 2 dot(li, x) - (2^bits - 1)
-// sum(x) over the 64-element group.
+// Every phase issues all of its loads before it uses any: the chain token
+// -> routing -> selected rows is the critical path.
+//
+// The gate/up CTA (slot 0, block 0) also writes the per-token results the
+// batched chain would produce for one token (perm, pos, off, drop, kept, xq,
+// xs), so the layer's debug views are the same on both paths.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -41,16 +56,20 @@
 
 namespace {
 
-constexpr int kMaxD = 4096;    // token width handled (d <= 4096)
-constexpr int kMaxF = 4096;    // expert ffn handled (f, fs <= 4096)
-constexpr int kMaxE = 4096;    // experts
-constexpr int kGuThreads = 512;
+constexpr int kMaxD = 4096;        // token width handled (d <= 4096)
+constexpr int kMaxF = 4096;        // expert ffn handled (f, fs <= 4096)
+constexpr int kMaxE = 4096;        // experts
+constexpr int kGuThreads = 128;    // one thread per weight row of a unit
+constexpr int kGroupsPerLoad = 8;  // 64-element groups per register batch (INT2: 16 B each)
+constexpr int kSharedPart = 256;   // bytes of one shared-expert row per K part
+constexpr int kDnWarps = 8;        // output channels per down CTA
+constexpr size_t kDnSmemMax = 200 * 1024;
 
 struct DecParams {
     const float *x;          // [d] token row
     const float *logits;     // [E] router logits
     const float *bias;       // [E] or NULL
-    int32_t *ids;            // [k] selected experts (slot order), written by CTA (0, 0)
+    int32_t *ids;            // [k] selected experts (slot order)
     float *w;                // [k] routing weights (final: nothing is dropped)
     const uint8_t *wg, *wu;  // [E][f][d/4] INT2
     const __half *sg, *su;   // [E][d/64][f]
@@ -62,6 +81,10 @@ struct DecParams {
     const float *ssd;        // [S][d]
     int d, f, E, k, S, fs;
     int hs_ld, hs_ld_s;      // row strides of the h scales (routed, shared)
+    int n_routed_units;      // k * (f / 64)
+    int ksplit;              // K parts of a shared-expert row
+    int32_t *acc_s;          // [S][2][fs] shared partial dots (zero between calls)
+    int32_t *cnt_s;          // [S][fs/64] arrival tickets (zero between calls)
     // outputs of the gate/up kernel (and debug copies of the batched path)
     int8_t *xq;
     float *xs;
@@ -78,147 +101,13 @@ struct DecParams {
     int *err;
 };
 
-// Per-token int8 quantization of x (w8a8.c:688-747, as k_quant_dispatch):
-// codes into sx (shared memory), scale returned; a non-finite value raises
-// the error word and gives an all-zero row.  With `route`, warp 0 runs the
-// router (jt_topk.cuh, results in sids / sw) while the other warps take the
-// max-abs pass, so the two latencies overlap.
-__device__ float quant_token(const float *__restrict__ x, int d, int8_t *sx, int *err, bool route,
-                             const DecParams &p, uint32_t *taken, int32_t *ssel, float *sselv, int32_t *sids,
-                             float *sw) {
-    __shared__ float wm[kGuThreads / 32];
-    __shared__ int wb[kGuThreads / 32];
-    const int warp = threadIdx.x >> 5;
-    float m = 0.0f;
-    int bad = 0;
-    if (route && warp == 0) {
-        sids[threadIdx.x] = threadIdx.x;  // fallback: experts 0..31 (k <= 64 below)
-        sids[threadIdx.x + 32] = threadIdx.x + 32;
-        sw[threadIdx.x] = 0.0f;
-        sw[threadIdx.x + 32] = 0.0f;
-        __syncwarp();
-        // the experts only: the weights are needed by the down kernel, which
-        // computes them itself before it waits for this grid
-        jt::warp_topk_softmax(p.logits, p.bias, p.E, p.k, taken, ssel, sselv, sids, sw, err, false);
-    } else {
-        const int t0 = route ? threadIdx.x - 32 : threadIdx.x;
-        const int nt = route ? blockDim.x - 32 : blockDim.x;
-        for (int i = t0; i < d; i += nt) {
-            const float v = x[i];
-            bad |= !isfinite(v);
-            m = fmaxf(m, fabsf(v));
-        }
-        for (int o = 16; o > 0; o >>= 1) {
-            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            bad |= __shfl_xor_sync(0xffffffffu, bad, o);
-        }
-    }
-    if ((threadIdx.x & 31) == 0) {
-        wm[warp] = m;
-        wb[warp] = bad;
-    }
-    __syncthreads();
-    m = 0.0f;
-    bad = 0;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) {
-        m = fmaxf(m, wm[i]);
-        bad |= wb[i];
-    }
-    const jt::QuantBlock qb = jt::quant_block(bad ? 0.0f : m);
-    if (bad && threadIdx.x == 0) atomicExch(err, 0x85);
-    for (int i = threadIdx.x; i < d; i += blockDim.x) sx[i] = bad ? 0 : (int8_t)jt::quant_code(x[i], qb);
-    __syncthreads();
-    return qb.scale_f;
+// dp4a of unsigned bytes a against signed bytes b (the masked INT2 fields
+// reach 192, beyond a signed byte).
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
 }
-
-// Activation words permuted for INT2 words: xp[4w + j] = bytes
-// {x[16w+j], x[16w+4+j], x[16w+8+j], x[16w+12+j]}; gsum[g] = sum of the 64
-// codes of group g.
-__device__ void permute_int2(const int8_t *sx, int d, uint32_t *xp, int *gsum) {
-    for (int i = threadIdx.x; i < d / 4; i += blockDim.x) {
-        const int w = i >> 2, j = i & 3;
-        const uint8_t *b = reinterpret_cast<const uint8_t *>(sx) + 16 * w + j;
-        xp[i] = (uint32_t)b[0] | ((uint32_t)b[4] << 8) | ((uint32_t)b[8] << 16) | ((uint32_t)b[12] << 24);
-    }
-    for (int g = threadIdx.x; g < d / 64; g += blockDim.x) {
-        int s = 0;
-        for (int i = 0; i < 64; ++i) s += sx[64 * g + i];
-        gsum[g] = s;
-    }
-    __syncthreads();
-}
-
-// RB INT2 rows (d/4 packed bytes each, fp16 scales srow[i][g * sstride])
-// against the permuted activation, all rows' loads in flight together.  Per
-// row the fold r = fmaf((float)P_g, s_g, r) runs over the groups in
-// ascending order, identically in every lane.  Lane l takes 8-byte chunks
-// l, l+32, ... (chunk c covers half of group c/2) and, per pass of 32
-// chunks, the scale of group g0 + l for l < 16.
-template <int RB>
-__device__ __forceinline__ void rows_int2(const uint8_t *const (&row)[RB], const __half *const (&srow)[RB],
-                                          int sstride, int d, const uint32_t *xp, const int *gsum, int lane,
-                                          float (&r)[RB]) {
-    const int nchunk = d / 32;
-    const int ng = d / 64;
-#pragma unroll
-    for (int i = 0; i < RB; ++i) r[i] = 0.0f;
-    for (int c0 = 0; c0 < nchunk; c0 += 32) {
-        const int c = c0 + lane, g0 = c0 / 2;
-        uint2 wv[RB];
-        float sv[RB];
-#pragma unroll
-        for (int i = 0; i < RB; ++i) {
-            wv[i] = c < nchunk ? __ldg(reinterpret_cast<const uint2 *>(row[i]) + c) : make_uint2(0u, 0u);
-            sv[i] = (lane < 16 && g0 + lane < ng) ? __half2float(srow[i][(size_t)(g0 + lane) * sstride]) : 0.0f;
-        }
-        int part[RB];
-#pragma unroll
-        for (int i = 0; i < RB; ++i) {
-            part[i] = 0;
-            const uint32_t *xw = xp + 8 * (c < nchunk ? c : 0);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                part[i] = __dp4a((int)((wv[i].x >> (2 * j)) & 0x03030303u), (int)xw[j], part[i]);
-                part[i] = __dp4a((int)((wv[i].y >> (2 * j)) & 0x03030303u), (int)xw[4 + j], part[i]);
-            }
-            part[i] += __shfl_xor_sync(0xffffffffu, part[i], 1);  // the two halves of a group
-        }
-        for (int gi = 0; gi < 16 && g0 + gi < ng; ++gi) {
-            const int gs = 3 * gsum[g0 + gi];
-#pragma unroll
-            for (int i = 0; i < RB; ++i) {
-                const int P = 2 * __shfl_sync(0xffffffffu, part[i], 2 * gi) - gs;
-                r[i] = fmaf((float)P, __shfl_sync(0xffffffffu, sv[i], gi), r[i]);
-            }
-        }
-    }
-}
-
-// RB int8 rows of K = d bytes: exact int32 dots, reduced over the warp.
-template <int RB>
-__device__ __forceinline__ void rows_int8(const int8_t *const (&row)[RB], int d, const int8_t *sx, int lane,
-                                          int (&acc)[RB]) {
-#pragma unroll
-    for (int i = 0; i < RB; ++i) acc[i] = 0;
-    for (int k0 = lane * 16; k0 < d; k0 += 32 * 16) {
-        int4 wv[RB];
-#pragma unroll
-        for (int i = 0; i < RB; ++i) wv[i] = __ldg(reinterpret_cast<const int4 *>(row[i] + k0));
-        const int4 xv = *reinterpret_cast<const int4 *>(sx + k0);
-#pragma unroll
-        for (int i = 0; i < RB; ++i) {
-            acc[i] = __dp4a(wv[i].x, xv.x, acc[i]);
-            acc[i] = __dp4a(wv[i].y, xv.y, acc[i]);
-            acc[i] = __dp4a(wv[i].z, xv.z, acc[i]);
-            acc[i] = __dp4a(wv[i].w, xv.w, acc[i]);
-        }
-    }
-#pragma unroll
-    for (int i = 0; i < RB; ++i)
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
-}
-
 
 // Sorted row of slot p: experts ascending, as the capacity sort orders the
 // kept pairs of one token.
@@ -229,8 +118,52 @@ __device__ __forceinline__ int slot_rank(const int32_t *ids, int k, int p) {
     return r;
 }
 
-// grid (max(f, fs)/64, k + S), 256 threads.  blockIdx.y < k: routed slot,
-// else shared expert blockIdx.y - k.
+// SwiGLU of the 64 channels staged in gu (scaled gate, scaled up), the
+// requantization of h over the 64 channels (w8a8.c:688-747), codes to
+// hq[0..63] and the scale to *hs.  Warp 0 only.
+__device__ __forceinline__ void swiglu_requant64(const float (&gu)[2][64], int8_t *hq, float *hs, int *err) {
+    const int lane = threadIdx.x & 31;
+    const float h0 = jt::swiglu(gu[0][2 * lane], gu[1][2 * lane]);
+    const float h1 = jt::swiglu(gu[0][2 * lane + 1], gu[1][2 * lane + 1]);
+    const bool bad = !isfinite(h0) || !isfinite(h1);
+    float m = fmaxf(fabsf(h0), fabsf(h1));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicExch(err, JT_KERR_NONFINITE);
+    const jt::QuantBlockF qb = jt::quant_block_f(m);
+    const int q0 = jt::quant_code_f(h0, qb), q1 = jt::quant_code_f(h1, qb);
+    *reinterpret_cast<uint16_t *>(hq + 2 * lane) =
+        (uint16_t)(uint8_t)(int8_t)q0 | ((uint16_t)(uint8_t)(int8_t)q1 << 8);
+    if (lane == 0) *hs = qb.scale_f;
+}
+
+// Group partial P of one INT2 group (16 packed bytes, codes li little-endian
+// along K) against the token: byte b of word i holds the codes of
+// k = 16i + 4b + j in bits 2j, so field j of every byte pairs with the
+// activation word xp[4i + j] = {x[16i+j], x[16i+4+j], x[16i+8+j],
+// x[16i+12+j]}.  The field is used in place (times 4^j) and the four sums
+// are scaled back exactly; P = 2 sum(li x) - 3 sum(x).
+__device__ __forceinline__ int int2_group(const uint4 w, const uint32_t *xp, int gs) {
+    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+    int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint4 xv = *reinterpret_cast<const uint4 *>(xp + 4 * i);
+        a0 = dp4a_us(ww[i] & 0x03030303u, xv.x, a0);
+        a1 = dp4a_us(ww[i] & 0x0C0C0C0Cu, xv.y, a1);
+        a2 = dp4a_us(ww[i] & 0x30303030u, xv.z, a2);
+        a3 = dp4a_us(ww[i] & 0xC0C0C0C0u, xv.w, a3);
+    }
+    const int s = a0 + (a1 >> 2) + (a2 >> 4) + (a3 >> 6);
+    return 2 * s - 3 * gs;
+}
+
+// grid n_routed_units + S * (fs/64) * ksplit, kGuThreads threads.
+//
+// The token row is read once, as float4 per thread, and kept in registers;
+// raw fp16 scales are kept until the fold; the weight rows of a shared
+// expert (which depend neither on the token nor on the routing) are loaded
+// before the wait for the previous kernel of the stream.
 __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant__ DecParams p) {
     __shared__ __align__(16) int8_t sx[kMaxD];
     __shared__ __align__(16) uint32_t xp[kMaxD / 4];
@@ -239,274 +172,477 @@ __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant
     __shared__ uint32_t taken[kMaxE / 32];
     __shared__ int32_t sids[64], ssel[64];
     __shared__ float sw[64], sselv[64];
-    const int slot = blockIdx.y, cb = blockIdx.x;
-    const bool shared = slot >= p.k;
-    const int n_ch = shared ? p.fs : p.f;
+    __shared__ float wm[kGuThreads / 32];
+    __shared__ int wb[kGuThreads / 32];
+    __shared__ int ticket;
     // the down kernel may launch now; it waits for this grid before reading
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int d = p.d, ng = d / 64;
+    const bool routed = (int)blockIdx.x < p.n_routed_units;
+    const int r = threadIdx.x;  // 0..63 gate rows, 64..127 up rows
+    const bool up = r >= 64;
+    int slot = 0, cb = 0, s = 0, kq = 0;
+    if (routed) {
+        const int nb = p.f / 64;
+        slot = blockIdx.x / nb;
+        cb = blockIdx.x % nb;
+    } else {
+        const int u = blockIdx.x - p.n_routed_units;
+        const int nb = p.fs / 64;
+        s = u / (nb * p.ksplit);
+        cb = (u / p.ksplit) % nb;
+        kq = u % p.ksplit;
+    }
+    const int part_bytes = d / p.ksplit;  // shared units: bytes of the row's K part
+    uint4 wv[2][kGroupsPerLoad];
+    __half sv[2][kGroupsPerLoad];
+    if (!routed) {
+        const int c = cb * 64 + (r & 63);
+        const uint4 *wrow = reinterpret_cast<const uint4 *>(
+            reinterpret_cast<const uint8_t *>((up ? p.wsu : p.wsg) + ((size_t)s * p.fs + c) * d) + kq * part_bytes);
+#pragma unroll
+        for (int b = 0; b < 2; ++b)
+#pragma unroll
+            for (int i = 0; i < kGroupsPerLoad; ++i) {
+                const int j = b * kGroupsPerLoad + i;
+                if (16 * j < part_bytes) wv[b][i] = __ldg(wrow + j);
+            }
+    }
     // this grid is itself launched as a dependent of the previous kernel of
     // the stream (the previous token's down kernel in a decode loop): wait
-    // for it before touching global memory (it reads hq/hs, written below)
+    // for it before reading the token or writing hq/hs
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (cb * 64 >= n_ch) return;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // routed CTAs: the router (every routed CTA alike, jt_topk.cuh) overlaps
-    // the max-abs pass; on a NaN logit or a bad softmax (error word raised)
-    // the slots fall back to experts 0..k-1 with zero weight so every index
-    // stays in range
-    const float xs = quant_token(p.x, p.d, sx, p.err, !shared, p, taken, ssel, sselv, sids, sw);
-    int e = 0;
-    if (!shared) {
-        e = sids[slot];
-        if (slot == 0 && cb == 0 && threadIdx.x < p.k) p.ids[threadIdx.x] = sids[threadIdx.x];
+    // ---- the token row, once, into registers (indices clamped so every
+    // load is issued unconditionally)
+    constexpr int kXv = kMaxD / 4 / kGuThreads;
+    const int nx4 = d / 4;
+    float4 xv[kXv];
+#pragma unroll
+    for (int i = 0; i < kXv; ++i) {
+        const int j = threadIdx.x + i * kGuThreads;
+        xv[i] = reinterpret_cast<const float4 *>(p.x)[j < nx4 ? j : nx4 - 1];
     }
-    if (!shared) permute_int2(sx, p.d, xp, gsum);
-    // 128 rows: 0..63 gate, 64..127 up of channels cb*64 + (row & 63); each
-    // warp takes kRB consecutive rows per step
-    constexpr int kRB = 8;
-    for (int r0 = warp * kRB; r0 < 128; r0 += (kGuThreads / 32) * kRB) {
-        const bool up = r0 >= 64;
-        const int c0 = cb * 64 + (r0 & 63);
-        float v[kRB];
-        if (!shared) {
-            const uint8_t *wrow[kRB];
-            const __half *srow[kRB];
+    if (routed && warp == 0) {
+        sids[lane] = lane;  // fallback on a routing fault: experts 0..k-1 stay in range
+        sids[lane + 32] = lane + 32;
+        __syncwarp();
+        jt::warp_topk_softmax(p.logits, p.bias, p.E, p.k, taken, ssel, sselv, sids, sw, p.err, false);
+    }
+    float m = 0.0f;
+    int bad = 0;
 #pragma unroll
-            for (int i = 0; i < kRB; ++i) {
-                wrow[i] = (up ? p.wu : p.wg) + ((size_t)e * p.f + c0 + i) * (p.d / 4);
-                srow[i] = (up ? p.su : p.sg) + (size_t)e * (p.d / 64) * p.f + c0 + i;
-            }
-            float r[kRB];
-            rows_int2<kRB>(wrow, srow, p.f, p.d, xp, gsum, lane, r);
-#pragma unroll
-            for (int i = 0; i < kRB; ++i) v[i] = __fmul_rn(r[i], xs);
-        } else {
-            const int s = slot - p.k;
-            const int8_t *wrow[kRB];
-#pragma unroll
-            for (int i = 0; i < kRB; ++i) wrow[i] = (up ? p.wsu : p.wsg) + ((size_t)s * p.fs + c0 + i) * p.d;
-            int acc[kRB];
-            rows_int8<kRB>(wrow, p.d, sx, lane, acc);
-#pragma unroll
-            for (int i = 0; i < kRB; ++i) {
-                const float cs = (up ? p.ssu : p.ssg)[(size_t)s * p.fs + c0 + i];
-                v[i] = __fmul_rn(__fmul_rn(__int2float_rn(acc[i]), xs), cs);
-            }
+    for (int i = 0; i < kXv; ++i) {
+        if (threadIdx.x + i * kGuThreads < nx4) {
+            const float4 v = xv[i];
+            bad |= !isfinite(v.x) | !isfinite(v.y) | !isfinite(v.z) | !isfinite(v.w);
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
         }
-        if (lane == 0)
-#pragma unroll
-            for (int i = 0; i < kRB; ++i) gu[up][(r0 & 63) + i] = v[i];
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+    }
+    if (lane == 0) {
+        wm[warp] = m;
+        wb[warp] = bad;
     }
     __syncthreads();
-    if (warp == 0) {
-        // h = SwiGLU(g, u) of channels 2l, 2l+1, requantized per 64 channels
-        const float h0 = jt::swiglu(gu[0][2 * lane], gu[1][2 * lane]);
-        const float h1 = jt::swiglu(gu[0][2 * lane + 1], gu[1][2 * lane + 1]);
-        const bool bad = !isfinite(h0) || !isfinite(h1);
-        float m = fmaxf(fabsf(h0), fabsf(h1));
+    // ---- routed units: the selected expert's rows (and raw scales)
+    const uint4 *wrow = nullptr;
+    const __half *srow = nullptr;
+    if (routed) {
+        int e = sids[slot];
+        e = (e < 0 || e >= p.E) ? 0 : e;
+        const int c = cb * 64 + (r & 63);
+        wrow = reinterpret_cast<const uint4 *>((up ? p.wu : p.wg) + ((size_t)e * p.f + c) * (d / 4));
+        srow = (up ? p.su : p.sg) + (size_t)e * ng * p.f + c;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (__any_sync(0xffffffffu, bad) && lane == 0) atomicExch(p.err, JT_KERR_NONFINITE);
-        const jt::QuantBlockF qb = jt::quant_block_f(m);
-        const int q0 = jt::quant_code_f(h0, qb), q1 = jt::quant_code_f(h1, qb);
-        const uint16_t pair = (uint16_t)(uint8_t)(int8_t)q0 | ((uint16_t)(uint8_t)(int8_t)q1 << 8);
-        int8_t *hq;
-        float *hs;
-        if (!shared) {
+        for (int b = 0; b < 2; ++b)
+#pragma unroll
+            for (int i = 0; i < kGroupsPerLoad; ++i) {
+                const int g = b * kGroupsPerLoad + i;
+                if (g < ng) {
+                    wv[b][i] = __ldg(wrow + g);
+                    sv[b][i] = srow[(size_t)g * p.f];
+                }
+            }
+    }
+    // ---- quantize the token (w8a8.c:688-747) from the registers, in the
+    // single-precision form of the quantizer: the same codes and stored scale
+    // as the double formula (jt_quant.cuh), without double divisions
+    m = 0.0f;
+    bad = 0;
+    for (int i = 0; i < kGuThreads / 32; ++i) {
+        m = fmaxf(m, wm[i]);
+        bad |= wb[i];
+    }
+    const jt::QuantBlockF qb = jt::quant_block_f(bad ? 0.0f : m);
+    if (bad && threadIdx.x == 0) atomicExch(p.err, 0x85);
+#pragma unroll
+    for (int i = 0; i < kXv; ++i) {
+        const int j = threadIdx.x + i * kGuThreads;
+        if (j < nx4) {
+            const float4 v = xv[i];
+            uint32_t w4 = 0u;
+            if (!bad)
+                w4 = (uint32_t)(uint8_t)(int8_t)jt::quant_code_f(v.x, qb) |
+                     ((uint32_t)(uint8_t)(int8_t)jt::quant_code_f(v.y, qb) << 8) |
+                     ((uint32_t)(uint8_t)(int8_t)jt::quant_code_f(v.z, qb) << 16) |
+                     ((uint32_t)(uint8_t)(int8_t)jt::quant_code_f(v.w, qb) << 24);
+            reinterpret_cast<uint32_t *>(sx)[j] = w4;
+        }
+    }
+    const float xs = qb.scale_f;
+    __syncthreads();
+    if (routed) {
+        // activation words permuted for the INT2 fields: 16-byte block w gives
+        // xp[4w + j] = bytes {j, 4+j, 8+j, 12+j}; group sums by dp4a
+        for (int w = threadIdx.x; w < d / 16; w += kGuThreads) {
+            const uint4 v = reinterpret_cast<const uint4 *>(sx)[w];
+            const uint32_t lo01 = __byte_perm(v.x, v.y, 0x5140), lo23 = __byte_perm(v.z, v.w, 0x5140);
+            const uint32_t hi01 = __byte_perm(v.x, v.y, 0x7362), hi23 = __byte_perm(v.z, v.w, 0x7362);
+            uint4 o;
+            o.x = __byte_perm(lo01, lo23, 0x5410);
+            o.y = __byte_perm(lo01, lo23, 0x7632);
+            o.z = __byte_perm(hi01, hi23, 0x5410);
+            o.w = __byte_perm(hi01, hi23, 0x7632);
+            reinterpret_cast<uint4 *>(xp)[w] = o;
+        }
+        for (int g = threadIdx.x; g < ng; g += kGuThreads) {
+            const int4 *q4 = reinterpret_cast<const int4 *>(sx + 64 * g);
+            int sm = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int4 v = q4[j];
+                sm = __dp4a(v.x, 0x01010101, sm);
+                sm = __dp4a(v.y, 0x01010101, sm);
+                sm = __dp4a(v.z, 0x01010101, sm);
+                sm = __dp4a(v.w, 0x01010101, sm);
+            }
+            gsum[g] = sm;
+        }
+        __syncthreads();
+        // fold r = fmaf((float)P_g, s_g, r) over the groups in order; the
+        // next batch of groups is loaded while the current one is folded
+        float acc = 0.0f;
+        for (int g0 = 0; g0 < ng; g0 += 2 * kGroupsPerLoad) {
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+#pragma unroll
+                for (int i = 0; i < kGroupsPerLoad; ++i) {
+                    const int g = g0 + b * kGroupsPerLoad + i;
+                    if (g < ng) {
+                        const int P = int2_group(wv[b][i], xp + 16 * g, gsum[g]);
+                        acc = fmaf((float)P, __half2float(sv[b][i]), acc);
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < kGroupsPerLoad; ++i) {
+                    const int g = g0 + (b + 2) * kGroupsPerLoad + i;
+                    if (g < ng) {
+                        wv[b][i] = __ldg(wrow + g);
+                        sv[b][i] = srow[(size_t)g * p.f];
+                    }
+                }
+            }
+        }
+        gu[up][r & 63] = __fmul_rn(acc, xs);
+        __syncthreads();
+        if (warp == 0) {
             const int row = slot_rank(sids, p.k, slot);
-            hq = p.hq + (size_t)row * p.f;
-            hs = p.hs + (size_t)row * p.hs_ld;
-        } else {
-            const int s = slot - p.k;
-            hq = p.hq_s + (size_t)s * p.fs;
-            hs = p.hs_s + (size_t)s * p.hs_ld_s;
+            swiglu_requant64(gu, p.hq + (size_t)row * p.f + cb * 64, p.hs + (size_t)row * p.hs_ld + cb, p.err);
         }
-        *reinterpret_cast<uint16_t *>(hq + cb * 64 + 2 * lane) = pair;
-        if (lane == 0) hs[cb] = qb.scale_f;
+        if (blockIdx.x == 0) {
+            // the batched path's per-token results for one token
+            for (int i = threadIdx.x; i < d / 16; i += kGuThreads)
+                reinterpret_cast<int4 *>(p.xq)[i] = reinterpret_cast<const int4 *>(sx)[i];
+            if (threadIdx.x == 0) {
+                p.xs[0] = xs;
+                p.meta[0] = p.k;
+                p.meta[1] = p.k;
+                p.meta[2] = 1;
+            }
+            if (threadIdx.x < p.k) {
+                const int q = threadIdx.x;
+                const int row = slot_rank(sids, p.k, q);
+                p.ids[q] = sids[q];
+                p.perm[row] = q;
+                p.pos[q] = row;
+                p.drop[q] = 0;
+            }
+            for (int ex = threadIdx.x; ex <= p.E; ex += kGuThreads) {
+                int n = 0;
+                for (int q = 0; q < p.k; ++q) n += sids[q] < ex;
+                p.off[ex] = n;
+                p.tile_off[ex] = n;
+            }
+        }
+        return;
     }
-    if (slot == 0 && cb == 0) {
-        // the batched path's per-token results for one token
-        for (int i = threadIdx.x; i < p.d; i += blockDim.x) p.xq[i] = sx[i];
-        if (threadIdx.x == 0) {
-            p.xs[0] = xs;
-            p.meta[0] = p.k;
-            p.meta[1] = p.k;
-            p.meta[2] = 1;
-        }
-        if (threadIdx.x < p.k) {
-            const int q = threadIdx.x;
-            const int row = slot_rank(sids, p.k, q);
-            p.perm[row] = q;
-            p.pos[q] = row;
-            p.drop[q] = 0;
-        }
-        for (int ex = threadIdx.x; ex <= p.E; ex += blockDim.x) {
-            int n = 0;
-            for (int q = 0; q < p.k; ++q) n += sids[q] < ex;
-            p.off[ex] = n;
-            p.tile_off[ex] = n;
-        }
+    // ---- shared-expert unit: exact int32 partial dot over this K part
+    int dot = 0;
+    {
+        const int8_t *xk = sx + kq * part_bytes;
+#pragma unroll
+        for (int b = 0; b < 2; ++b)
+#pragma unroll
+            for (int i = 0; i < kGroupsPerLoad; ++i) {
+                const int j = b * kGroupsPerLoad + i;
+                if (16 * j < part_bytes) {
+                    const int4 xk4 = *reinterpret_cast<const int4 *>(xk + 16 * j);
+                    dot = __dp4a((int)wv[b][i].x, xk4.x, dot);
+                    dot = __dp4a((int)wv[b][i].y, xk4.y, dot);
+                    dot = __dp4a((int)wv[b][i].z, xk4.z, dot);
+                    dot = __dp4a((int)wv[b][i].w, xk4.w, dot);
+                }
+            }
     }
+    int32_t *acc = p.acc_s + ((size_t)s * 2 + up) * p.fs + cb * 64 + (r & 63);
+    int total = dot;
+    if (p.ksplit > 1) {
+        atomicAdd(acc, dot);
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) ticket = atomicAdd(&p.cnt_s[s * (p.fs / 64) + cb], 1);
+        __syncthreads();
+        if (ticket != p.ksplit - 1) return;  // another CTA of the unit finishes it
+        __threadfence();
+        total = atomicExch(acc, 0);  // the sum of every part; cleared for the next call
+        if (threadIdx.x == 0) p.cnt_s[s * (p.fs / 64) + cb] = 0;
+    }
+    const int c = cb * 64 + (r & 63);
+    const float cs = (up ? p.ssu : p.ssg)[(size_t)s * p.fs + c];
+    gu[up][r & 63] = __fmul_rn(__fmul_rn(__int2float_rn(total), xs), cs);
+    __syncthreads();
+    if (warp == 0)
+        swiglu_requant64(gu, p.hq_s + (size_t)s * p.fs + cb * 64, p.hs_s + (size_t)s * p.hs_ld_s + cb, p.err);
 }
 
+// Layout of the down kernel's dynamic shared memory (byte offsets).  Rows
+// are padded by 16 bytes so that rows read by neighbouring threads start in
+// different banks.
+struct DnLayout {
+    uint32_t wr, wsc, ws, ssc, hp, hsum, hsr, hqs, hss, racc, sp, bar, total;
+};
 
-constexpr int kDnWarps = 8;
-constexpr int kMaxHp = 8192;  // permuted h words of the routed rows (k * f <= 32768)
+__host__ __device__ inline uint32_t dn_take(uint32_t &o, uint32_t bytes) {
+    const uint32_t at = o;
+    o = (o + bytes + 15u) & ~15u;
+    return at;
+}
 
-// grid d / 8, 256 threads: warp w computes output channel blockIdx.x*8 + w.
+__host__ __device__ inline DnLayout dn_layout(int k, int f, int S, int fs) {
+    DnLayout L;
+    uint32_t o = 0;
+    L.wr = dn_take(o, (uint32_t)k * kDnWarps * (f / 2 + 16));      // routed down rows [k][8], padded
+    L.wsc = dn_take(o, (uint32_t)k * (f / 64) * kDnWarps * 2);     // their fp16 scales [k][f/64][8]
+    L.ws = dn_take(o, (uint32_t)S * kDnWarps * (fs + 16));         // shared down rows [S][8], padded
+    L.ssc = dn_take(o, (uint32_t)S * kDnWarps * 4);                // their channel scales [S][8]
+    L.hp = dn_take(o, (uint32_t)k * (f / 4 + 4) * 4);              // routed h, permuted words [k], padded
+    L.hsum = dn_take(o, (uint32_t)k * (f / 64) * 4);               // per (row, group) code sums
+    L.hsr = dn_take(o, (uint32_t)k * (f / 64) * 4);                // routed h scales [k][f/64]
+    L.hqs = dn_take(o, (uint32_t)S * fs);                          // shared h codes [S][fs]
+    L.hss = dn_take(o, (uint32_t)S * (fs / 64) * 4);               // shared h scales [S][fs/64]
+    L.racc = dn_take(o, (uint32_t)kDnWarps * k * 4);               // folded routed rows [8][k]
+    L.sp = dn_take(o, (uint32_t)kDnWarps * S * (fs / 64) * 4);     // shared group partials [8][S][fs/64]
+    L.bar = dn_take(o, 8);
+    L.total = o;
+    return L;
+}
+
+// grid d / 8, 256 threads: output channels blockIdx.x*8 .. +7.
 __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constant__ DecParams p) {
     // the next token's gate/up kernel may launch on the SMs left free; it
     // waits for this grid before its first global access
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    extern __shared__ __align__(16) uint8_t dsm[];
     __shared__ uint32_t taken[kMaxE / 32];
-    __shared__ int32_t sids[64], ssel[64];
+    __shared__ int32_t sids[64], ssel[64], srank[64];
     __shared__ float sw[64], sselv[64];
-    {
-        // Everything here is independent of the gate/up grid, which may still
-        // be running: the router again (the same function on the same
-        // logits, so the same experts as the gate/up grid), then the down
-        // rows this warp will read are pulled into L2.
-        if (threadIdx.x < 64) {
-            sids[threadIdx.x] = threadIdx.x;
-            sw[threadIdx.x] = 0.0f;
+    __shared__ int abort_flag;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int d = p.d, f = p.f, fs = p.fs, k = p.k, S = p.S, gf = f / 64;
+    const int o0 = blockIdx.x * kDnWarps;
+    const DnLayout L = dn_layout(k, f, S, fs);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(dsm + L.bar);
+    if (threadIdx.x < 64) {
+        sids[threadIdx.x] = threadIdx.x;
+        sw[threadIdx.x] = 0.0f;
+    }
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        jt::mbar_init(bar, 1);
+        jt::fence_mbar_init();
+    }
+    __syncthreads();
+    // ---- independent of the gate/up grid: routing with the softmax (the same
+    // function on the same logits as the gate/up grid), then this CTA's down
+    // weights into shared memory
+    if (warp == 0) jt::warp_topk_softmax(p.logits, p.bias, p.E, k, taken, ssel, sselv, sids, sw, p.err);
+    __syncthreads();
+    if (threadIdx.x < k) {
+        const int q = threadIdx.x;
+        const int e = sids[q];
+        sids[q] = (e < 0 || e >= p.E) ? 0 : e;
+        if (blockIdx.x == 0) {
+            p.w[q] = sw[q];
+            p.w_fin[q] = sw[q];
         }
-        __syncthreads();
-        if ((threadIdx.x >> 5) == 0)
-            jt::warp_topk_softmax(p.logits, p.bias, p.E, p.k, taken, ssel, sselv, sids, sw, p.err);
-        __syncthreads();
-        // the routing weights (final: nothing is dropped for one token); the
-        // gate/up grid neither reads nor writes them
-        if (blockIdx.x == 0 && threadIdx.x < p.k) {
-            p.w[threadIdx.x] = sw[threadIdx.x];
-            p.w_fin[threadIdx.x] = sw[threadIdx.x];
-        }
-        const int o = blockIdx.x * kDnWarps + (threadIdx.x >> 5);
-        const int lane = threadIdx.x & 31;
-        if (o < p.d) {
-            const int gf = p.f / 64;
-            for (int q = 0; q < p.k; ++q) {
-                int e = sids[q];
-                e = (e < 0 || e >= p.E) ? 0 : e;
-                const uint8_t *row = p.wd + ((size_t)e * p.d + o) * (p.f / 2);
-                for (int b = lane * 128; b < p.f / 2; b += 32 * 128)
-                    asm volatile("prefetch.global.L2 [%0];" ::"l"(row + b));
-                if (lane < gf)
-                    asm volatile("prefetch.global.L2 [%0];" ::"l"(p.sd + ((size_t)e * gf + lane) * p.d + o));
+    }
+    __syncthreads();
+    if (threadIdx.x < k) srank[threadIdx.x] = slot_rank(sids, k, threadIdx.x);
+    if (warp == 0) {
+        const uint32_t rbytes = (uint32_t)(f / 2), rstride = rbytes + 16u;
+        const uint32_t sstride = (uint32_t)fs + 16u;
+        const uint32_t tx = (uint32_t)k * kDnWarps * rbytes + (uint32_t)k * gf * 16u +
+                            (uint32_t)S * kDnWarps * (fs + 4);
+        if (lane == 0) jt::mbar_arrive_expect_tx(bar, tx);
+        __syncwarp();
+        // lane l issues the copies l, l + 32, ... of: k * 8 routed rows,
+        // k * gf scale pieces, S * 8 shared rows, S shared scale pieces
+        const int n_rows = k * kDnWarps, n_sc = k * gf, n_srows = S * kDnWarps;
+        for (int i = lane; i < n_rows + n_sc + n_srows + S; i += 32) {
+            if (i < n_rows) {
+                const int q = i / kDnWarps, j = i % kDnWarps;
+                jt::bulk_load(dsm + L.wr + (size_t)i * rstride, p.wd + ((size_t)sids[q] * d + o0 + j) * (f / 2),
+                              rbytes, bar);
+            } else if (i < n_rows + n_sc) {
+                const int u = i - n_rows, q = u / gf, g = u % gf;
+                jt::bulk_load(dsm + L.wsc + (size_t)u * 16, p.sd + ((size_t)sids[q] * gf + g) * d + o0, 16, bar);
+            } else if (i < n_rows + n_sc + n_srows) {
+                const int u = i - n_rows - n_sc, sh = u / kDnWarps, j = u % kDnWarps;
+                jt::bulk_load(dsm + L.ws + (size_t)u * sstride, p.wsd + ((size_t)sh * d + o0 + j) * fs, fs, bar);
+            } else {
+                const int sh = i - n_rows - n_sc - n_srows;
+                jt::bulk_load(dsm + L.ssc + (size_t)sh * kDnWarps * 4, p.ssd + (size_t)sh * d + o0, kDnWarps * 4, bar);
             }
-            for (int s = 0; s < p.S; ++s)
-                for (int b = lane * 128; b < p.fs; b += 32 * 128)
-                    asm volatile("prefetch.global.L2 [%0];" ::"l"(p.wsd + ((size_t)s * p.d + o) * p.fs + b));
         }
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    // routed h rows (sorted rank order) permuted for INT4 words: for packed
-    // word w (codes 8w .. 8w+7, even k in the low nibbles) hp[2w] holds the
-    // even codes {h[8w], h[8w+2], h[8w+4], h[8w+6]} and hp[2w+1] the odd ones
-    __shared__ uint32_t hp[kMaxHp];
-    __shared__ int hsum[kMaxHp / 16];  // per (row, 64-group) sum of codes
-    const int nw = p.f / 8;            // packed INT4 words per row
-    const int gf = p.f / 64;
-    for (int i = threadIdx.x; i < p.k * nw; i += blockDim.x) {
-        const int r = i / nw, w = i % nw;
-        const uint8_t *b = reinterpret_cast<const uint8_t *>(p.hq) + (size_t)r * p.f + 8 * w;
-        hp[2 * i] = (uint32_t)b[0] | ((uint32_t)b[2] << 8) | ((uint32_t)b[4] << 16) | ((uint32_t)b[6] << 24);
-        hp[2 * i + 1] = (uint32_t)b[1] | ((uint32_t)b[3] << 8) | ((uint32_t)b[5] << 16) | ((uint32_t)b[7] << 24);
+    // ---- h of the routed rows (rank order) permuted for INT4 words: for
+    // packed word w (codes 8w .. 8w+7, even k in the low nibbles) the even
+    // codes {h[8w], h[8w+2], h[8w+4], h[8w+6]} at hp[2w], the odd ones at
+    // hp[2w+1]; per (row, group) code sums; the shared h as stored.  One
+    // pass over 16-byte chunks, every load issued before it is used.
+    uint32_t *hp = reinterpret_cast<uint32_t *>(dsm + L.hp);
+    int *hsum = reinterpret_cast<int *>(dsm + L.hsum);
+    float *hsr = reinterpret_cast<float *>(dsm + L.hsr);
+    int8_t *hqs = reinterpret_cast<int8_t *>(dsm + L.hqs);
+    float *hss = reinterpret_cast<float *>(dsm + L.hss);
+    const int nw = f / 8;    // packed INT4 words per routed row
+    const int nck = f / 16;  // 16-byte chunks of h per routed row (4 per group)
+    for (int base = warp * 32; base < k * nck; base += kDnWarps * 32) {
+        const int i = base + lane;
+        const bool ok = i < k * nck;
+        const int ii = ok ? i : 0;
+        const int rr = ii / nck, c = ii % nck;
+        const uint4 v = *reinterpret_cast<const uint4 *>(p.hq + (size_t)rr * f + 16 * c);
+        int sm = __dp4a((int)v.x, 0x01010101, 0);
+        sm = __dp4a((int)v.y, 0x01010101, sm);
+        sm = __dp4a((int)v.z, 0x01010101, sm);
+        sm = __dp4a((int)v.w, 0x01010101, sm);
+        sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+        sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+        if (ok) {
+            uint4 o;
+            o.x = __byte_perm(v.x, v.y, 0x6420);
+            o.y = __byte_perm(v.x, v.y, 0x7531);
+            o.z = __byte_perm(v.z, v.w, 0x6420);
+            o.w = __byte_perm(v.z, v.w, 0x7531);
+            reinterpret_cast<uint4 *>(hp + (size_t)rr * (2 * nw + 4))[c] = o;
+            if ((c & 3) == 0) hsum[rr * gf + c / 4] = sm;
+        }
     }
-    for (int i = threadIdx.x; i < p.k * gf; i += blockDim.x) {
-        const int8_t *h = p.hq + (size_t)(i / gf) * p.f + 64 * (i % gf);
-        int sm = 0;
-        for (int j = 0; j < 64; ++j) sm += h[j];
-        hsum[i] = sm;
+    for (int i = threadIdx.x; i < k * gf; i += blockDim.x) hsr[i] = p.hs[(size_t)(i / gf) * p.hs_ld + i % gf];
+    for (int i = threadIdx.x; i < S * fs / 16; i += blockDim.x) {
+        const int sh = i / (fs / 16), j = i % (fs / 16);
+        reinterpret_cast<int4 *>(hqs)[i] = reinterpret_cast<const int4 *>(p.hq_s + (size_t)sh * fs)[j];
+    }
+    for (int i = threadIdx.x; i < S * (fs / 64); i += blockDim.x)
+        hss[i] = p.hs_s[(size_t)(i / (fs / 64)) * p.hs_ld_s + i % (fs / 64)];
+    __syncthreads();
+    if (!jt::mbar_wait(bar, 0, &abort_flag, p.err)) return;
+    // ---- one thread per dot product.  Routed item (slot q, channel j): the
+    // whole INT4 row against its h row, folded over the groups in order
+    // (t = (float)P * s_g; r = fmaf(t, hs_g, r)).  Shared item (128-byte
+    // part, expert sh, channel j): the int32 partials of its two groups.
+    // Neighbouring threads take neighbouring (padded) rows.
+    const uint32_t *wr = reinterpret_cast<const uint32_t *>(dsm + L.wr);
+    const __half *wsc = reinterpret_cast<const __half *>(dsm + L.wsc);
+    const int8_t *ws = reinterpret_cast<const int8_t *>(dsm + L.ws);
+    const float *ssc = reinterpret_cast<const float *>(dsm + L.ssc);
+    float *racc = reinterpret_cast<float *>(dsm + L.racc);
+    int *sp = reinterpret_cast<int *>(dsm + L.sp);
+    const int gs = fs / 64;
+    const int n_r = kDnWarps * k, n_s = kDnWarps * S * (fs / 128);
+    for (int it = threadIdx.x; it < n_r + n_s; it += blockDim.x) {
+        if (it < n_r) {
+            const int q = it / kDnWarps, j = it % kDnWarps;
+            const int rr = srank[q];
+            const uint4 *row = reinterpret_cast<const uint4 *>(wr + ((size_t)q * kDnWarps + j) * (nw + 4));
+            const uint4 *hrow = reinterpret_cast<const uint4 *>(hp + (size_t)rr * (2 * nw + 4));
+            float acc = 0.0f;
+            for (int g = 0; g < gf; ++g) {
+                int part = 0;
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {  // 8 words = 64 codes = one group
+                    const uint4 v = row[2 * g + c];
+                    const uint4 h0 = hrow[4 * g + 2 * c], h1 = hrow[4 * g + 2 * c + 1];
+                    part = __dp4a((int)(v.x & 0x0F0F0F0Fu), (int)h0.x, part);
+                    part = __dp4a((int)((v.x >> 4) & 0x0F0F0F0Fu), (int)h0.y, part);
+                    part = __dp4a((int)(v.y & 0x0F0F0F0Fu), (int)h0.z, part);
+                    part = __dp4a((int)((v.y >> 4) & 0x0F0F0F0Fu), (int)h0.w, part);
+                    part = __dp4a((int)(v.z & 0x0F0F0F0Fu), (int)h1.x, part);
+                    part = __dp4a((int)((v.z >> 4) & 0x0F0F0F0Fu), (int)h1.y, part);
+                    part = __dp4a((int)(v.w & 0x0F0F0F0Fu), (int)h1.z, part);
+                    part = __dp4a((int)((v.w >> 4) & 0x0F0F0F0Fu), (int)h1.w, part);
+                }
+                const int P = 2 * part - 15 * hsum[rr * gf + g];
+                const float t = __fmul_rn((float)P, __half2float(wsc[((size_t)q * gf + g) * kDnWarps + j]));
+                acc = fmaf(t, hsr[rr * gf + g], acc);
+            }
+            racc[j * k + q] = acc;
+        } else {
+            const int u = it - n_r;
+            const int pt = u / (S * kDnWarps), sh = (u / kDnWarps) % S, j = u % kDnWarps;
+            const int4 *row = reinterpret_cast<const int4 *>(ws + ((size_t)sh * kDnWarps + j) * (fs + 16) + 128 * pt);
+            const int4 *h = reinterpret_cast<const int4 *>(hqs + (size_t)sh * fs + 128 * pt);
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {
+                int part = 0;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const int4 wv = row[4 * g + c], hv = h[4 * g + c];
+                    part = __dp4a(wv.x, hv.x, part);
+                    part = __dp4a(wv.y, hv.y, part);
+                    part = __dp4a(wv.z, hv.z, part);
+                    part = __dp4a(wv.w, hv.w, part);
+                }
+                sp[(j * S + sh) * gs + 2 * pt + g] = part;
+            }
+        }
     }
     __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int o = blockIdx.x * kDnWarps + warp;
-    if (o >= p.d) return;
+    // ---- one thread per output channel: the combine in double, routed rows
+    // in slot order (moe_layer.c:1443-1463), then the shared experts in s
+    // order, each folded over its groups (moe_layer.c:1549-1559)
+    if (threadIdx.x >= kDnWarps) return;
+    const int j = threadIdx.x, o = o0 + j;
+    if (o >= d) return;
     double ya = 0.0;
-    // routed pairs in slot order (moe_layer.c:1443-1463), eight rows' loads
-    // in flight at a time
-    constexpr int kRB = 8;
-    for (int q0 = 0; q0 < p.k; q0 += kRB) {
-        const uint32_t *row[kRB];
-        const __half *sdo[kRB];
-        const float *hsr[kRB];
-        int rr[kRB];
-        float acc[kRB];
-#pragma unroll
-        for (int i = 0; i < kRB; ++i) {
-            const int q = q0 + i < p.k ? q0 + i : p.k - 1;
-            int e = sids[q];
-            e = (e < 0 || e >= p.E) ? 0 : e;
-            rr[i] = p.pos[q];
-            row[i] = reinterpret_cast<const uint32_t *>(p.wd + ((size_t)e * p.d + o) * (p.f / 2));
-            sdo[i] = p.sd + (size_t)e * gf * p.d + o;
-            hsr[i] = p.hs + (size_t)rr[i] * p.hs_ld;
-            acc[i] = 0.0f;
-        }
-        for (int c0 = 0; c0 < nw; c0 += 32) {  // 4-byte chunks, 8 per group
-            const int c = c0 + lane, g0 = c0 / 8;
-            uint32_t wv[kRB];
-            float sv[kRB], hv[kRB];
-#pragma unroll
-            for (int i = 0; i < kRB; ++i) {
-                wv[i] = c < nw ? __ldg(row[i] + c) : 0u;
-                const bool gl = lane < 4 && g0 + lane < gf;
-                sv[i] = gl ? __half2float(sdo[i][(size_t)(g0 + lane) * p.d]) : 0.0f;
-                hv[i] = gl ? hsr[i][g0 + lane] : 0.0f;
-            }
-            int part[kRB];
-#pragma unroll
-            for (int i = 0; i < kRB; ++i) {
-                const uint32_t *hw = hp + 2 * ((size_t)rr[i] * nw + (c < nw ? c : 0));
-                part[i] = __dp4a((int)(wv[i] & 0x0F0F0F0Fu), (int)hw[0], 0);
-                part[i] = __dp4a((int)((wv[i] >> 4) & 0x0F0F0F0Fu), (int)hw[1], part[i]);
-                part[i] += __shfl_xor_sync(0xffffffffu, part[i], 1);
-                part[i] += __shfl_xor_sync(0xffffffffu, part[i], 2);
-                part[i] += __shfl_xor_sync(0xffffffffu, part[i], 4);
-            }
-            for (int gi = 0; gi < 4 && g0 + gi < gf; ++gi) {
-#pragma unroll
-                for (int i = 0; i < kRB; ++i) {
-                    const int P = 2 * __shfl_sync(0xffffffffu, part[i], 8 * gi) - 15 * hsum[rr[i] * gf + g0 + gi];
-                    const float t = __fmul_rn((float)P, __shfl_sync(0xffffffffu, sv[i], gi));
-                    acc[i] = fmaf(t, __shfl_sync(0xffffffffu, hv[i], gi), acc[i]);
-                }
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < kRB; ++i)
-            if (q0 + i < p.k) ya = __dadd_rn(ya, __dmul_rn((double)sw[q0 + i], (double)acc[i]));
-    }
-    // shared experts in s order (moe_layer.c:1549-1559)
-    for (int s = 0; s < p.S; ++s) {
-        const int8_t *row = p.wsd + ((size_t)s * p.d + o) * p.fs;
-        const int8_t *h = p.hq_s + (size_t)s * p.fs;
-        const float *hss = p.hs_s + (size_t)s * p.hs_ld_s;
-        const int nb = p.fs / 64;
+    for (int q = 0; q < k; ++q) ya = __dadd_rn(ya, __dmul_rn((double)sw[q], (double)racc[j * k + q]));
+    for (int sh = 0; sh < S; ++sh) {
         float acc = 0.0f;
-        for (int c0 = 0; c0 < p.fs / 4; c0 += 32) {  // 4-byte chunks, 16 per block
-            const int c = c0 + lane;
-            int part = 0;
-            if (c < p.fs / 4)
-                part = __dp4a(__ldg(reinterpret_cast<const int *>(row) + c), __ldg(reinterpret_cast<const int *>(h) + c), 0);
-#pragma unroll
-            for (int m = 1; m < 16; m <<= 1) part += __shfl_xor_sync(0xffffffffu, part, m);
-            const int b0 = c0 / 16;
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                if (b0 + i >= nb) break;
-                const int P = __shfl_sync(0xffffffffu, part, 16 * i);
-                acc = fmaf((float)P, hss[b0 + i], acc);
-            }
-        }
-        ya = __dadd_rn(ya, (double)__fmul_rn(acc, p.ssd[(size_t)s * p.d + o]));
+        for (int g = 0; g < gs; ++g) acc = fmaf((float)sp[(j * S + sh) * gs + g], hss[sh * gs + g], acc);
+        ya = __dadd_rn(ya, (double)__fmul_rn(acc, ssc[sh * kDnWarps + j]));
     }
-    if (lane == 0) {
-        const float yv = (float)ya;
-        if (p.y) p.y[o] = yv;
-        if (p.y_bf16) p.y_bf16[o] = __bfloat16_as_ushort(__float2bfloat16_rn(yv));
-    }
+    const float yv = (float)ya;
+    if (p.y) p.y[o] = yv;
+    if (p.y_bf16) p.y_bf16[o] = __bfloat16_as_ushort(__float2bfloat16_rn(yv));
 }
+
+bool aligned16(const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; }
 
 }  // namespace
 
@@ -517,13 +653,21 @@ extern "C" int jtk_moe_decode(const float *x, const float *logits, const float *
                               const uint8_t *wd, const void *sd, const int8_t *wsg, const int8_t *wsu,
                               const float *ssg, const float *ssu, const int8_t *wsd, const float *ssd, int d,
                               int f, int E, int k, int S, int fs, int8_t *xq, float *xs, int8_t *hq, float *hs,
-                              int hs_ld, int8_t *hq_s, float *hs_s, int hs_ld_s, int32_t *perm, int32_t *pos,
-                              int32_t *off, int32_t *tile_off, int32_t *meta, uint8_t *drop, float *w_fin,
-                              float *y, uint16_t *y_bf16, cudaStream_t stream) {
+                              int hs_ld, int8_t *hq_s, float *hs_s, int hs_ld_s, int32_t *acc_s,
+                              int32_t *cnt_s, int32_t *perm, int32_t *pos, int32_t *off, int32_t *tile_off,
+                              int32_t *meta, uint8_t *drop, float *w_fin, float *y, uint16_t *y_bf16,
+                              cudaStream_t stream) {
+    const int fs_eff = S > 0 ? fs : 128;
     if (d <= 0 || d > kMaxD || d % 128 || f <= 0 || f > kMaxF || f % 64 || E <= 0 || E > kMaxE || k <= 0 ||
-        k > 64 || k > E || (long long)k * (f / 8) * 2 > kMaxHp || (long long)k * (f / 64) > kMaxHp / 16 ||
-        S < 0 || (S > 0 && (fs <= 0 || fs > kMaxF || fs % 64)))
+        k > 64 || k > E || S < 0 || (S > 0 && (fs <= 0 || fs > kMaxF || fs % 128)))
         return -1;
+    // bulk copies and 16-byte loads need 16-byte aligned bases
+    if (!aligned16(x) || !aligned16(wg) || !aligned16(wu) || !aligned16(wd) || !aligned16(sd) ||
+        !aligned16(hq) ||
+        (S > 0 && (!aligned16(wsg) || !aligned16(wsu) || !aligned16(wsd) || !aligned16(ssd) || !aligned16(hq_s))))
+        return -1;
+    const DnLayout L = dn_layout(k, f, S, fs_eff);
+    if (L.total > kDnSmemMax) return -1;
     DecParams p{};
     p.x = x;
     p.logits = logits;
@@ -547,9 +691,14 @@ extern "C" int jtk_moe_decode(const float *x, const float *logits, const float *
     p.E = E;
     p.k = k;
     p.S = S;
-    p.fs = S > 0 ? fs : 64;
+    p.fs = fs_eff;
     p.hs_ld = hs_ld;
     p.hs_ld_s = hs_ld_s;
+    p.n_routed_units = k * (f / 64);
+    // K parts of kSharedPart bytes (half that when d is an odd multiple of 128)
+    p.ksplit = d % kSharedPart == 0 ? d / kSharedPart : d / (kSharedPart / 2);
+    p.acc_s = acc_s;
+    p.cnt_s = cnt_s;
     p.xq = xq;
     p.xs = xs;
     p.hq = hq;
@@ -566,10 +715,10 @@ extern "C" int jtk_moe_decode(const float *x, const float *logits, const float *
     p.y = y;
     p.y_bf16 = y_bf16;
     p.err = jtk_error_word();
-    const int nmax = (S > 0 && fs > f) ? fs : f;
+    const int n_shared_units = S * (fs_eff / 64) * p.ksplit;
     {
         cudaLaunchConfig_t gcfg{};
-        gcfg.gridDim = dim3(nmax / 64, k + S);
+        gcfg.gridDim = dim3(p.n_routed_units + n_shared_units);
         gcfg.blockDim = dim3(kGuThreads);
         gcfg.dynamicSmemBytes = 0;
         gcfg.stream = stream;
@@ -580,14 +729,20 @@ extern "C" int jtk_moe_decode(const float *x, const float *logits, const float *
         gcfg.numAttrs = 1;
         if (cudaLaunchKernelEx(&gcfg, k_dec_gateup, p) != cudaSuccess) return -4;
     }
-    if (cudaGetLastError() != cudaSuccess) return -4;
-    // down: programmatic dependent launch, so its launch and prologue overlap
-    // the gate/up grid (it waits on griddepcontrol.wait before any read of
-    // that grid's results)
+    static bool attr_set = false;
+    if (!attr_set) {
+        if (cudaFuncSetAttribute(k_dec_down, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDnSmemMax) !=
+            cudaSuccess)
+            return -3;
+        attr_set = true;
+    }
+    // down: programmatic dependent launch, so its launch, routing and weight
+    // copies overlap the gate/up grid (it waits on griddepcontrol.wait before
+    // any read of that grid's results)
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((d + kDnWarps - 1) / kDnWarps);
     cfg.blockDim = dim3(kDnWarps * 32);
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = L.total;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -160,15 +160,17 @@ int jtk_topk_any(const float *logits, int T, int n, int k, uint32_t *taken, int3
 /* Batch-1 layer (jt_decode.cu): router, gate/up + SwiGLU + requant, and
  * down + combine as two matrix-vector kernels; also writes the router
  * output (ids, w) and the per-token results of the sort (perm, pos, off, tile_off, meta, drop,
- * w_fin, xq, xs, hq, hs).  -1: shape not handled (use the batched chain). */
+ * w_fin, xq, xs, hq, hs).  acc_s [S][2][fs] and cnt_s [S][fs/64] are int32
+ * scratch that must be zero before the first call (each call leaves them
+ * zero).  -1: shape not handled (use the batched chain). */
 int jtk_moe_decode(const float *x, const float *logits, const float *bias, int32_t *ids, float *w,
                    const uint8_t *wg, const uint8_t *wu,
                    const void *sg, const void *su, const uint8_t *wd, const void *sd, const int8_t *wsg,
                    const int8_t *wsu, const float *ssg, const float *ssu, const int8_t *wsd, const float *ssd,
                    int d, int f, int E, int k, int S, int fs, int8_t *xq, float *xs, int8_t *hq, float *hs,
-                   int hs_ld, int8_t *hq_s, float *hs_s, int hs_ld_s, int32_t *perm, int32_t *pos,
-                   int32_t *off, int32_t *tile_off, int32_t *meta, uint8_t *drop, float *w_fin, float *y,
-                   uint16_t *y_bf16, cudaStream_t stream);
+                   int hs_ld, int8_t *hq_s, float *hs_s, int hs_ld_s, int32_t *acc_s, int32_t *cnt_s,
+                   int32_t *perm, int32_t *pos, int32_t *off, int32_t *tile_off, int32_t *meta,
+                   uint8_t *drop, float *w_fin, float *y, uint16_t *y_bf16, cudaStream_t stream);
 
 /* Device error word shared by all kernels of the library (0 = clean). */
 int jtk_read_and_clear_error(int *out_code);

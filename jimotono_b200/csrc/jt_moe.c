@@ -53,6 +53,7 @@ struct jt_b200_moe_plan {
     /* batch-1 path: h codes and scales of every shared expert at once */
     int8_t *hq_d;
     float *hs_d;
+    int32_t *dec_acc, *dec_cnt; /* K-split partial dots of the shared experts (zero between calls) */
     /* optional per-stage profiling: events[step][JT_B200_MOE_NSTAGE + 1] */
     cudaEvent_t *prof_ev;
     int prof_max, prof_used;
@@ -110,6 +111,8 @@ int jt_b200_moe_plan_create(const jt_b200_moe_dims *dims, jt_b200_moe_plan **out
         {(void **)&p->hq, Tk * f},           {(void **)&p->hq_s, T * fs},
         {(void **)&p->hq_d, (size_t)(dims->S > 0 ? dims->S : 1) * fs},
         {(void **)&p->hs_d, (size_t)(dims->S > 0 ? dims->S : 1) * (size_t)hs_ld((int)fs) * 4},
+        {(void **)&p->dec_acc, (size_t)(dims->S > 0 ? dims->S : 1) * 2 * fs * 4},
+        {(void **)&p->dec_cnt, (size_t)(dims->S > 0 ? dims->S : 1) * (fs / 64) * 4},
     };
     const size_t nparts = sizeof(parts) / sizeof(parts[0]);
     size_t total = 0;
@@ -288,7 +291,8 @@ int jt_b200_moe_forward(jt_b200_moe_plan *plan, const jt_b200_moe_weights *w, co
         const int r = jtk_moe_decode(x, logits, bias, plan->ids, plan->w_raw, w->wg, w->wu, w->sg, w->su, w->wd, w->sd,
                                      w->wsg, w->wsu, w->ssg, w->ssu, w->wsd, w->ssd, d, f, E, k, S, fs,
                                      plan->xq, plan->xs, plan->hq, plan->hs, hs_ld(f), plan->hq_d,
-                                     plan->hs_d, hs_ld(S > 0 ? fs : 64), plan->perm, plan->pos, plan->off,
+                                     plan->hs_d, hs_ld(S > 0 ? fs : 64), plan->dec_acc, plan->dec_cnt,
+                                     plan->perm, plan->pos, plan->off,
                                      plan->tile_off, plan->meta, plan->drop, plan->w_fin,
                                      y_bf16 ? NULL : (float *)y, y_bf16 ? (uint16_t *)y : NULL, st);
         if (r == 0) {

@@ -15,6 +15,51 @@
 
 namespace jt {
 
+// Selection for E <= 64 logits without the k dependent passes: lane l holds
+// logits l and l + 32 (+ bias) and counts the logits that a pass would take
+// before each of them - the larger ones, and the equal ones of lower index -
+// which is its pass number (routing.c:38-52 takes, at every pass, the
+// largest remaining logit with ties to the lowest index).  All counts are
+// formed at once.  The ranking equals the passes' order whenever no logit is
+// -inf (a pass that finds only -inf left may take an index again, which a
+// ranking cannot express); in that case, or for a NaN, it returns false and
+// the caller runs the passes.  Every lane writes sel/selv entries 0..k-1
+// (the same values), as the passes do.
+__device__ __forceinline__ bool small_select(float v0, float v1, bool ok0, bool ok1, int E, int k,
+                                             int32_t *sel, float *selv) {
+    const int lane = threadIdx.x & 31;
+    const bool odd = (ok0 && (v0 != v0 || v0 == -INFINITY)) || (ok1 && (v1 != v1 || v1 == -INFINITY));
+    if (__any_sync(0xffffffffu, odd)) return false;
+    int r0 = 0, r1 = 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const float vj = __shfl_sync(0xffffffffu, v0, j);
+        if (j < E) {
+            r0 += (vj > v0) || (vj == v0 && j < lane);
+            r1 += (vj >= v1);  // j < 32 <= lane + 32: ties count
+        }
+    }
+#pragma unroll
+    for (int j = 32; j < 64; ++j) {
+        const float vj = __shfl_sync(0xffffffffu, v1, j - 32);
+        if (j < E) {
+            r0 += (vj > v0);  // j >= 32 > lane: ties do not count
+            r1 += (vj > v1) || (vj == v1 && j < lane + 32);
+        }
+    }
+    // entry p comes from the lane whose logit has count p
+    for (int q = 0; q < k; ++q) {
+        const uint32_t m0 = __ballot_sync(0xffffffffu, ok0 && r0 == q);
+        const uint32_t m1 = __ballot_sync(0xffffffffu, ok1 && r1 == q);
+        const int src = m0 ? __ffs(m0) - 1 : __ffs(m1) - 1;
+        const float a = __shfl_sync(0xffffffffu, v0, src), b = __shfl_sync(0xffffffffu, v1, src);
+        sel[q] = m0 ? src : src + 32;
+        selv[q] = m0 ? a : b;
+    }
+    __syncwarp();
+    return true;
+}
+
 // taken: ceil(E/32) words of shared memory owned by this warp; sel/selv: k
 // entries of scratch written identically by every lane; ids_out/w_out
 // entry p is written by lane p mod 32 with the softmax, by lane 0 without
@@ -29,49 +74,65 @@ __device__ __forceinline__ bool warp_topk_softmax(const float *__restrict__ row,
     const int nw = (E + 31) / 32;
     for (int i = lane; i < nw; i += 32) taken[i] = 0;
     __syncwarp();
-    int nan_seen = 0;
-    for (int i = lane; i < E; i += 32) {
-        float v = row[i];
-        if (bias) v = __fadd_rn(v, bias[i]);
-        nan_seen |= (v != v);
-    }
-    if (__any_sync(0xffffffffu, nan_seen)) {
-        if (lane == 0) atomicExch(err, 0x81);
-        return false;
-    }
-    for (int p = 0; p < k; ++p) {
-        float best = 0.0f;
-        int bi = E;  // sentinel: "not set", like best == n in routing.c:40
+    bool selected = false;
+    if (E <= 64) {
+        // lane l holds logits l and l + 32 (+ bias), read once
+        const bool ok0 = lane < E, ok1 = lane + 32 < E;
+        float v0 = 0.0f, v1 = 0.0f;
+        if (ok0) v0 = bias ? __fadd_rn(row[lane], bias[lane]) : row[lane];
+        if (ok1) v1 = bias ? __fadd_rn(row[lane + 32], bias[lane + 32]) : row[lane + 32];
+        if (__any_sync(0xffffffffu, (ok0 && v0 != v0) || (ok1 && v1 != v1))) {
+            if (lane == 0) atomicExch(err, 0x81);
+            return false;
+        }
+        selected = small_select(v0, v1, ok0, ok1, E, k, sel, selv);
+    } else {
+        int nan_seen = 0;
         for (int i = lane; i < E; i += 32) {
             float v = row[i];
             if (bias) v = __fadd_rn(v, bias[i]);
-            if ((taken[i >> 5] >> (i & 31)) & 1u) v = -INFINITY;
-            if (bi == E || v > best) {
-                best = v;
-                bi = i;
-            }
+            nan_seen |= (v != v);
         }
+        if (__any_sync(0xffffffffu, nan_seen)) {
+            if (lane == 0) atomicExch(err, 0x81);
+            return false;
+        }
+    }
+    if (!selected) {
+        for (int p = 0; p < k; ++p) {
+            float best = 0.0f;
+            int bi = E;  // sentinel: "not set", like best == n in routing.c:40
+            for (int i = lane; i < E; i += 32) {
+                float v = row[i];
+                if (bias) v = __fadd_rn(v, bias[i]);
+                if ((taken[i >> 5] >> (i & 31)) & 1u) v = -INFINITY;
+                if (bi == E || v > best) {
+                    best = v;
+                    bi = i;
+                }
+            }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            // candidate with lower index wins unless the other is strictly larger
-            bool take;
-            if (oi == E) take = false;
-            else if (bi == E) take = true;
-            else if (oi < bi) take = !(best > ov);
-            else take = ov > best;
-            if (take) {
-                best = ov;
-                bi = oi;
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                // candidate with lower index wins unless the other is strictly larger
+                bool take;
+                if (oi == E) take = false;
+                else if (bi == E) take = true;
+                else if (oi < bi) take = !(best > ov);
+                else take = ov > best;
+                if (take) {
+                    best = ov;
+                    bi = oi;
+                }
             }
+            sel[p] = bi;
+            if (lane == 0) atomicOr(&taken[bi >> 5], 1u << (bi & 31));
+            __syncwarp();
+            float lv = row[bi];
+            if (bias) lv = __fadd_rn(lv, bias[bi]);
+            selv[p] = lv;
         }
-        sel[p] = bi;
-        if (lane == 0) atomicOr(&taken[bi >> 5], 1u << (bi & 31));
-        __syncwarp();
-        float lv = row[bi];
-        if (bias) lv = __fadd_rn(lv, bias[bi]);
-        selv[p] = lv;
     }
     if (!softmax) {
         if (lane == 0)

@@ -84,6 +84,13 @@ CASES = [
     (130, 2048, 128, 32, 8, 2, 256, 1.5, 1.1),
     # shared gate/up on 256-token CTA-pair tiles: 3 channel tiles, ragged last token tile
     (600, 256, 128, 8, 2, 2, 384, 1.5, None),
+    # batch-1 kernels: configuration 5's expert shapes, an odd multiple of 128
+    # for d (K parts of 128 bytes), no shared experts with more than 64
+    # experts (the pass-based top-k), a routing bias
+    (1, 2048, 1536, 128, 8, 2, 4096, 1.5, None),
+    (1, 384, 128, 16, 4, 1, 256, 1.0, None),
+    (1, 256, 128, 200, 6, 0, 0, 1.5, None),
+    (1, 1024, 256, 64, 8, 2, 512, 1.5, 1.1),
 ]
 
 
@@ -163,3 +170,28 @@ def test_moe_routing_matches_reference_golden():
     drop = np.ascontiguousarray(g["drop_c125"])
     assert oracle.oracle().jto_renorm(wr.ctypes.data, drop.ctypes.data, T, k) == 0
     assert np.array_equal(got["w"].view(np.uint32), wr.view(np.uint32))
+
+
+@pytest.mark.parametrize("T", [1, 37])
+def test_moe_routing_with_negative_infinite_logits(T):
+    """Logits of -inf (the router's masking value): the top-k follows the
+    reference's passes (routing.c:38-52), including a pass that finds only
+    -inf left; the rank-based selection for E <= 64 hands such rows to the
+    passes."""
+    dm = Dims(T, 128, 128, 16, 4, 1, 128, 1.5)
+    w = synth_weights(dm, seed=T + 40)
+    x, logits, _ = synth_inputs(dm, T, seed=T + 41)
+    rng = np.random.default_rng(T)
+    logits[rng.random(logits.shape) < 0.6] = -np.inf
+    logits[:, 3] = rng.standard_normal(T).astype(np.float32)  # one finite logit per token at least
+    if T > 1:
+        logits[0, :] = -np.inf
+        logits[0, 5] = 0.25  # a single finite logit: three passes see only -inf
+    y_ref, tr = run_oracle(dm, w, x, logits, None)
+    y_gpu, got = run_gpu(dm, w, x, logits, None)
+    assert np.array_equal(got["ids"], tr["ids"])
+    assert np.array_equal(got["w"].view(np.uint32), tr["w"].view(np.uint32))
+    assert got["kept"] == tr["kept"]
+    assert np.array_equal(got["perm"], tr["perm"][:tr["kept"]])
+    scale = max(float(np.abs(y_ref).max()), 1e-30)
+    assert float(np.abs(y_gpu - y_ref).max()) / scale < 1e-5
