@@ -42,6 +42,7 @@
 // The gate/up CTA (slot 0, block 0) also writes the per-token results the
 // batched chain would produce for one token (perm, pos, off, drop, kept, xq,
 // xs), so the layer's debug views are the same on both paths.
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -66,6 +67,8 @@ constexpr int kDnWarps = 8;        // output channels per down CTA
 constexpr size_t kDnSmemMax = 200 * 1024;
 
 struct DecParams {
+    CUtensorMap tmG, tmU;    // routed gate / up rows [E*f][d/4], 64-row x 128-byte boxes, 128B swizzle
+    int tma;                 // 1: routed rows by tensor map (d % 512 == 0), 0: register loads
     const float *x;          // [d] token row
     const float *logits;     // [E] router logits
     const float *bias;       // [E] or NULL
@@ -169,12 +172,18 @@ __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant
     __shared__ __align__(16) uint32_t xp[kMaxD / 4];
     __shared__ int gsum[kMaxD / 64];
     __shared__ float gu[2][64];
-    __shared__ uint32_t taken[kMaxE / 32];
+    __shared__ __align__(16) uint32_t taken[kMaxE / 32];
     __shared__ int32_t sids[64], ssel[64];
     __shared__ float sw[64], sselv[64];
     __shared__ float wm[kGuThreads / 32];
     __shared__ int wb[kGuThreads / 32];
     __shared__ int ticket;
+    __shared__ uint64_t wbar;
+    __shared__ int abort_flag;
+    // routed units: the unit's 64 gate then 64 up rows as 64-row x 128-byte
+    // boxes (1024-byte aligned for the swizzle)
+    extern __shared__ __align__(1024) uint8_t wsm_raw[];
+    uint8_t *wsm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(wsm_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     // the down kernel may launch now; it waits for this grid before reading
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -195,8 +204,12 @@ __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant
         kq = u % p.ksplit;
     }
     const int part_bytes = d / p.ksplit;  // shared units: bytes of the row's K part
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        jt::mbar_init(&wbar, 1);
+        jt::fence_mbar_init();
+    }
     uint4 wv[2][kGroupsPerLoad];
-    __half sv[2][kGroupsPerLoad];
     if (!routed) {
         const int c = cb * 64 + (r & 63);
         const uint4 *wrow = reinterpret_cast<const uint4 *>(
@@ -228,6 +241,19 @@ __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant
         sids[lane + 32] = lane + 32;
         __syncwarp();
         jt::warp_topk_softmax(p.logits, p.bias, p.E, p.k, taken, ssel, sselv, sids, sw, p.err, false);
+        __syncwarp();
+        // the selected expert's 64 gate and 64 up rows: 64-row x 128-byte
+        // boxes of the tensor maps, 128-byte swizzled in shared memory
+        if (p.tma && lane == 0) {
+            int e = sids[slot];
+            e = (e < 0 || e >= p.E) ? 0 : e;
+            const int nbox = d / 512;
+            jt::mbar_arrive_expect_tx(&wbar, 2u * 64u * (uint32_t)(d / 4));
+            for (int j = 0; j < nbox; ++j) {
+                jt::tma_load_2d(wsm + (size_t)j * 8192, &p.tmG, &wbar, 128 * j, e * p.f + cb * 64);
+                jt::tma_load_2d(wsm + (size_t)(nbox + j) * 8192, &p.tmU, &wbar, 128 * j, e * p.f + cb * 64);
+            }
+        }
     }
     float m = 0.0f;
     int bad = 0;
@@ -248,25 +274,30 @@ __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant
         wb[warp] = bad;
     }
     __syncthreads();
-    // ---- routed units: the selected expert's rows (and raw scales)
-    const uint4 *wrow = nullptr;
+    // ---- routed units: this thread's raw fp16 scales (coalesced over the
+    // block's 64 channels; groups past 16 are read in the fold), and its row
+    // when the rows do not come by tensor map
+    __half sv[16];
+    const uint4 *grow = nullptr;
     const __half *srow = nullptr;
     if (routed) {
         int e = sids[slot];
         e = (e < 0 || e >= p.E) ? 0 : e;
         const int c = cb * 64 + (r & 63);
-        wrow = reinterpret_cast<const uint4 *>((up ? p.wu : p.wg) + ((size_t)e * p.f + c) * (d / 4));
         srow = (up ? p.su : p.sg) + (size_t)e * ng * p.f + c;
+        grow = reinterpret_cast<const uint4 *>((up ? p.wu : p.wg) + ((size_t)e * p.f + c) * (d / 4));
 #pragma unroll
-        for (int b = 0; b < 2; ++b)
+        for (int g = 0; g < 16; ++g)
+            if (g < ng) sv[g] = srow[(size_t)g * p.f];
+        if (!p.tma) {
 #pragma unroll
-            for (int i = 0; i < kGroupsPerLoad; ++i) {
-                const int g = b * kGroupsPerLoad + i;
-                if (g < ng) {
-                    wv[b][i] = __ldg(wrow + g);
-                    sv[b][i] = srow[(size_t)g * p.f];
+            for (int b = 0; b < 2; ++b)
+#pragma unroll
+                for (int i = 0; i < kGroupsPerLoad; ++i) {
+                    const int g = b * kGroupsPerLoad + i;
+                    if (g < ng) wv[b][i] = __ldg(grow + g);
                 }
-            }
+        }
     }
     // ---- quantize the token (w8a8.c:688-747) from the registers, in the
     // single-precision form of the quantizer: the same codes and stored scale
@@ -323,26 +354,45 @@ __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant
             gsum[g] = sm;
         }
         __syncthreads();
-        // fold r = fmaf((float)P_g, s_g, r) over the groups in order; the
-        // next batch of groups is loaded while the current one is folded
         float acc = 0.0f;
-        for (int g0 = 0; g0 < ng; g0 += 2 * kGroupsPerLoad) {
+        if (p.tma) {
+            if (!jt::mbar_wait(&wbar, 0, &abort_flag, p.err)) return;
+            // fold r = fmaf((float)P_g, s_g, r) over the groups in order; row
+            // rr of a box holds its 16-byte chunk c at chunk c ^ (rr % 8)
+            const int rr = r & 63, nbox = d / 512;
+            const uint8_t *rowb = wsm + (size_t)(up ? nbox : 0) * 8192 + (size_t)rr * 128;
+            for (int g0 = 0; g0 < ng; g0 += 16) {
 #pragma unroll
-            for (int b = 0; b < 2; ++b) {
-#pragma unroll
-                for (int i = 0; i < kGroupsPerLoad; ++i) {
-                    const int g = g0 + b * kGroupsPerLoad + i;
+                for (int i = 0; i < 16; ++i) {
+                    const int g = g0 + i;
                     if (g < ng) {
-                        const int P = int2_group(wv[b][i], xp + 16 * g, gsum[g]);
-                        acc = fmaf((float)P, __half2float(sv[b][i]), acc);
+                        const uint4 w = *reinterpret_cast<const uint4 *>(rowb + (size_t)(g >> 3) * 8192 +
+                                                                          (((g & 7) ^ (rr & 7)) << 4));
+                        const __half sg = g0 == 0 ? sv[i] : srow[(size_t)g * p.f];
+                        const int P = int2_group(w, xp + 16 * g, gsum[g]);
+                        acc = fmaf((float)P, __half2float(sg), acc);
                     }
                 }
+            }
+        } else {
+            // register path: groups in batches, the next batch loaded while
+            // the current one is folded
+            for (int g0 = 0; g0 < ng; g0 += 2 * kGroupsPerLoad) {
 #pragma unroll
-                for (int i = 0; i < kGroupsPerLoad; ++i) {
-                    const int g = g0 + (b + 2) * kGroupsPerLoad + i;
-                    if (g < ng) {
-                        wv[b][i] = __ldg(wrow + g);
-                        sv[b][i] = srow[(size_t)g * p.f];
+                for (int b = 0; b < 2; ++b) {
+#pragma unroll
+                    for (int i = 0; i < kGroupsPerLoad; ++i) {
+                        const int g = g0 + b * kGroupsPerLoad + i;
+                        if (g < ng) {
+                            const __half sg = g0 == 0 ? sv[b * kGroupsPerLoad + i] : srow[(size_t)g * p.f];
+                            const int P = int2_group(wv[b][i], xp + 16 * g, gsum[g]);
+                            acc = fmaf((float)P, __half2float(sg), acc);
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < kGroupsPerLoad; ++i) {
+                        const int g = g0 + (b + 2) * kGroupsPerLoad + i;
+                        if (g < ng) wv[b][i] = __ldg(grow + g);
                     }
                 }
             }
@@ -532,19 +582,44 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constan
     float *hss = reinterpret_cast<float *>(dsm + L.hss);
     const int nw = f / 8;    // packed INT4 words per routed row
     const int nck = f / 16;  // 16-byte chunks of h per routed row (4 per group)
-    for (int base = warp * 32; base < k * nck; base += kDnWarps * 32) {
-        const int i = base + lane;
-        const bool ok = i < k * nck;
-        const int ii = ok ? i : 0;
-        const int rr = ii / nck, c = ii % nck;
-        const uint4 v = *reinterpret_cast<const uint4 *>(p.hq + (size_t)rr * f + 16 * c);
+    // every global load of this phase first, then the shared-memory writes
+    // (one round trip to L2)
+    constexpr int kHq = 4;   // routed h chunks per thread (k * f / 16 <= 1024 below)
+    uint4 hv[kHq];
+    float hsv[2];
+    int4 hqv[2];
+    float hssv[2];
+    const int n_hq = k * nck, n_hs = k * gf, n_hqs = S * fs / 16, n_hss = S * (fs / 64);
+#pragma unroll
+    for (int t = 0; t < kHq; ++t) {
+        const int i = threadIdx.x + t * (int)blockDim.x;
+        const int ii = i < n_hq ? i : 0;
+        hv[t] = *reinterpret_cast<const uint4 *>(p.hq + (size_t)(ii / nck) * f + 16 * (ii % nck));
+    }
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+        const int i = threadIdx.x + t * (int)blockDim.x;
+        if (i < n_hs) hsv[t] = p.hs[(size_t)(i / gf) * p.hs_ld + i % gf];
+        if (i < n_hqs) hqv[t] = reinterpret_cast<const int4 *>(p.hq_s + (size_t)(i / (fs / 16)) * fs)[i % (fs / 16)];
+        if (i < n_hss) hssv[t] = p.hs_s[(size_t)(i / (fs / 64)) * p.hs_ld_s + i % (fs / 64)];
+    }
+    // routed h permuted for INT4 words: for packed word w (codes 8w .. 8w+7,
+    // even k in the low nibbles) the even codes {h[8w], h[8w+2], h[8w+4],
+    // h[8w+6]} at hp[2w], the odd ones at hp[2w+1]; per (row, group) code
+    // sums from the four chunks of a group (four neighbouring lanes)
+#pragma unroll
+    for (int t = 0; t < kHq; ++t) {
+        const int i = threadIdx.x + t * (int)blockDim.x;
+        if (t * (int)blockDim.x >= n_hq) break;  // uniform over the block
+        const uint4 v = hv[t];
         int sm = __dp4a((int)v.x, 0x01010101, 0);
         sm = __dp4a((int)v.y, 0x01010101, sm);
         sm = __dp4a((int)v.z, 0x01010101, sm);
         sm = __dp4a((int)v.w, 0x01010101, sm);
         sm += __shfl_xor_sync(0xffffffffu, sm, 1);
         sm += __shfl_xor_sync(0xffffffffu, sm, 2);
-        if (ok) {
+        if (i < n_hq) {
+            const int rr = i / nck, c = i % nck;
             uint4 o;
             o.x = __byte_perm(v.x, v.y, 0x6420);
             o.y = __byte_perm(v.x, v.y, 0x7531);
@@ -554,13 +629,13 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constan
             if ((c & 3) == 0) hsum[rr * gf + c / 4] = sm;
         }
     }
-    for (int i = threadIdx.x; i < k * gf; i += blockDim.x) hsr[i] = p.hs[(size_t)(i / gf) * p.hs_ld + i % gf];
-    for (int i = threadIdx.x; i < S * fs / 16; i += blockDim.x) {
-        const int sh = i / (fs / 16), j = i % (fs / 16);
-        reinterpret_cast<int4 *>(hqs)[i] = reinterpret_cast<const int4 *>(p.hq_s + (size_t)sh * fs)[j];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+        const int i = threadIdx.x + t * (int)blockDim.x;
+        if (i < n_hs) hsr[i] = hsv[t];
+        if (i < n_hqs) reinterpret_cast<int4 *>(hqs)[i] = hqv[t];
+        if (i < n_hss) hss[i] = hssv[t];
     }
-    for (int i = threadIdx.x; i < S * (fs / 64); i += blockDim.x)
-        hss[i] = p.hs_s[(size_t)(i / (fs / 64)) * p.hs_ld_s + i % (fs / 64)];
     __syncthreads();
     if (!jt::mbar_wait(bar, 0, &abort_flag, p.err)) return;
     // ---- one thread per dot product.  Routed item (slot q, channel j): the
@@ -662,13 +737,24 @@ extern "C" int jtk_moe_decode(const float *x, const float *logits, const float *
         k > 64 || k > E || S < 0 || (S > 0 && (fs <= 0 || fs > kMaxF || fs % 128)))
         return -1;
     // bulk copies and 16-byte loads need 16-byte aligned bases
-    if (!aligned16(x) || !aligned16(wg) || !aligned16(wu) || !aligned16(wd) || !aligned16(sd) ||
+    if (!aligned16(x) || !aligned16(wg) || !aligned16(wu) || !aligned16(sg) || !aligned16(su) ||
+        !aligned16(wd) || !aligned16(sd) ||
         !aligned16(hq) ||
         (S > 0 && (!aligned16(wsg) || !aligned16(wsu) || !aligned16(wsd) || !aligned16(ssd) || !aligned16(hq_s))))
         return -1;
     const DnLayout L = dn_layout(k, f, S, fs_eff);
     if (L.total > kDnSmemMax) return -1;
+    // the down kernel stages h in one pass of its 256 threads: at most 4
+    // routed chunks and 2 of each shared piece per thread
+    if (k * (f / 16) > 4 * kDnWarps * 32 || k * (f / 64) > 2 * kDnWarps * 32 ||
+        S * fs_eff / 16 > 2 * kDnWarps * 32)
+        return -1;
     DecParams p{};
+    p.tma = d % 512 == 0;
+    if (p.tma && (!jt::make_tmap_2d_u8(&p.tmG, wg, (uint64_t)(d / 4), (uint64_t)E * f, (uint64_t)(d / 4), 128, 64, true) ||
+                  !jt::make_tmap_2d_u8(&p.tmU, wu, (uint64_t)(d / 4), (uint64_t)E * f, (uint64_t)(d / 4), 128, 64, true)))
+        return -2;
+    const size_t gu_smem = p.tma ? 128 * (size_t)(d / 4) + 1024 : 0;
     p.x = x;
     p.logits = logits;
     p.bias = bias;
@@ -716,11 +802,20 @@ extern "C" int jtk_moe_decode(const float *x, const float *logits, const float *
     p.y_bf16 = y_bf16;
     p.err = jtk_error_word();
     const int n_shared_units = S * (fs_eff / 64) * p.ksplit;
+    static bool attr_set = false;
+    if (!attr_set) {
+        if (cudaFuncSetAttribute(k_dec_down, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDnSmemMax) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(k_dec_gateup, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)(128 * (kMaxD / 4) + 1024)) != cudaSuccess)
+            return -3;
+        attr_set = true;
+    }
     {
         cudaLaunchConfig_t gcfg{};
         gcfg.gridDim = dim3(p.n_routed_units + n_shared_units);
         gcfg.blockDim = dim3(kGuThreads);
-        gcfg.dynamicSmemBytes = 0;
+        gcfg.dynamicSmemBytes = gu_smem;
         gcfg.stream = stream;
         cudaLaunchAttribute gattr[1];
         gattr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -728,13 +823,6 @@ extern "C" int jtk_moe_decode(const float *x, const float *logits, const float *
         gcfg.attrs = gattr;
         gcfg.numAttrs = 1;
         if (cudaLaunchKernelEx(&gcfg, k_dec_gateup, p) != cudaSuccess) return -4;
-    }
-    static bool attr_set = false;
-    if (!attr_set) {
-        if (cudaFuncSetAttribute(k_dec_down, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDnSmemMax) !=
-            cudaSuccess)
-            return -3;
-        attr_set = true;
     }
     // down: programmatic dependent launch, so its launch, routing and weight
     // copies overlap the gate/up grid (it waits on griddepcontrol.wait before

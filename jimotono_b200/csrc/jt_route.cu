@@ -31,8 +31,8 @@ __global__ void k_route_topk(const float *__restrict__ logits, const float *__re
     const int warps = blockDim.x >> 5;
     const int t = blockIdx.x * warps + (threadIdx.x >> 5);
     if (t >= T) return;
-    extern __shared__ uint32_t taken_all[];  // warps * ceil(E/32) words
-    uint32_t *taken = taken_all + (threadIdx.x >> 5) * ((E + 31) / 32);
+    extern __shared__ __align__(16) uint32_t taken_all[];  // warps * topk_scratch_words(E)
+    uint32_t *taken = taken_all + (threadIdx.x >> 5) * jt::topk_scratch_words(E);
     int32_t sel[64];
     float selv[64];
     jt::warp_topk_softmax(logits + (size_t)t * E, bias, E, k, taken, sel, selv, ids + (size_t)t * k,
@@ -344,7 +344,7 @@ extern "C" int jtk_route_topk(const float *logits, const float *bias, int T, int
                               int32_t *ids, float *w, cudaStream_t stream) {
     if (T <= 0 || E <= 0 || k <= 0 || k > E || k > 64) return -1;
     const int warps = 4;
-    const size_t sm = (size_t)warps * ((E + 31) / 32) * sizeof(uint32_t);
+    const size_t sm = (size_t)warps * jt::topk_scratch_words(E) * sizeof(uint32_t);
     k_route_topk<<<(T + warps - 1) / warps, warps * 32, sm, stream>>>(logits, bias, T, E, k, ids,
                                                                       w, jtk_error_word());
     return cudaGetLastError() == cudaSuccess ? 0 : -4;

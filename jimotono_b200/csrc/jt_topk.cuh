@@ -15,52 +15,66 @@
 
 namespace jt {
 
+// Shared-memory words a warp passes as `taken` to warp_topk_softmax.
+__host__ __device__ inline int topk_scratch_words(int E) { return E <= 64 ? 128 : (E + 31) / 32; }
+
 // Selection for E <= 64 logits without the k dependent passes: lane l holds
 // logits l and l + 32 (+ bias) and counts the logits that a pass would take
 // before each of them - the larger ones, and the equal ones of lower index -
 // which is its pass number (routing.c:38-52 takes, at every pass, the
 // largest remaining logit with ties to the lowest index).  All counts are
-// formed at once.  The ranking equals the passes' order whenever no logit is
-// -inf (a pass that finds only -inf left may take an index again, which a
-// ranking cannot express); in that case, or for a NaN, it returns false and
-// the caller runs the passes.  Every lane writes sel/selv entries 0..k-1
-// (the same values), as the passes do.
-__device__ __forceinline__ bool small_select(float v0, float v1, bool ok0, bool ok1, int E, int k,
+// formed at once, from the 64 logits staged in shared memory (scratch, 128
+// words owned by the warp) and read back as broadcasts.  The ranking equals
+// the passes' order whenever no logit is -inf (a pass that finds only -inf
+// left may take an index again, which a ranking cannot express); in that
+// case, or for a NaN, it returns false before touching scratch and the
+// caller runs the passes.  Every lane writes sel/selv entries 0..k-1 (the
+// same values), as the passes do.
+__device__ __forceinline__ bool small_select(float v0, float v1, bool ok0, bool ok1, int k, uint32_t *scratch,
                                              int32_t *sel, float *selv) {
     const int lane = threadIdx.x & 31;
     const bool odd = (ok0 && (v0 != v0 || v0 == -INFINITY)) || (ok1 && (v1 != v1 || v1 == -INFINITY));
     if (__any_sync(0xffffffffu, odd)) return false;
-    int r0 = 0, r1 = 0;
+    // missing logits (E < 64) read as -inf, which beats no present logit
+    // (none is -inf here), so the counts need no bound
+    float *val = reinterpret_cast<float *>(scratch);
+    int32_t *slot = reinterpret_cast<int32_t *>(scratch) + 64;
+    const float w0 = ok0 ? v0 : -INFINITY, w1 = ok1 ? v1 : -INFINITY;
+    val[lane] = w0;
+    val[lane + 32] = w1;
+    __syncwarp();
+    int c0[4] = {0, 0, 0, 0}, c1[4] = {0, 0, 0, 0};
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        const float vj = __shfl_sync(0xffffffffu, v0, j);
-        if (j < E) {
-            r0 += (vj > v0) || (vj == v0 && j < lane);
-            r1 += (vj >= v1);  // j < 32 <= lane + 32: ties count
+    for (int j4 = 0; j4 < 8; ++j4) {
+        const float4 a = reinterpret_cast<const float4 *>(val)[j4];      // logits 4 j4 ..
+        const float4 b = reinterpret_cast<const float4 *>(val + 32)[j4]; // logits 32 + 4 j4 ..
+        const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const int j = 4 * j4 + t;
+            c0[t] += (av[t] > w0) || (av[t] == w0 && j < lane);  // logit j against lane
+            c1[t] += (av[t] >= w1);                              // j < lane + 32: ties count
+            c0[t] += (bv[t] > w0);                               // 32 + j > lane: ties do not count
+            c1[t] += (bv[t] > w1) || (bv[t] == w1 && j < lane);  // 32 + j against lane + 32
         }
     }
-#pragma unroll
-    for (int j = 32; j < 64; ++j) {
-        const float vj = __shfl_sync(0xffffffffu, v1, j - 32);
-        if (j < E) {
-            r0 += (vj > v0);  // j >= 32 > lane: ties do not count
-            r1 += (vj > v1) || (vj == v1 && j < lane + 32);
-        }
-    }
-    // entry p comes from the lane whose logit has count p
+    const int r0 = (c0[0] + c0[1]) + (c0[2] + c0[3]);
+    const int r1 = (c1[0] + c1[1]) + (c1[2] + c1[3]);
+    // the logit of count q goes to slot q
+    if (ok0 && r0 < k) slot[r0] = lane;
+    if (ok1 && r1 < k) slot[r1] = lane + 32;
+    __syncwarp();
     for (int q = 0; q < k; ++q) {
-        const uint32_t m0 = __ballot_sync(0xffffffffu, ok0 && r0 == q);
-        const uint32_t m1 = __ballot_sync(0xffffffffu, ok1 && r1 == q);
-        const int src = m0 ? __ffs(m0) - 1 : __ffs(m1) - 1;
-        const float a = __shfl_sync(0xffffffffu, v0, src), b = __shfl_sync(0xffffffffu, v1, src);
-        sel[q] = m0 ? src : src + 32;
-        selv[q] = m0 ? a : b;
+        const int id = slot[q];
+        sel[q] = id;
+        selv[q] = val[id];
     }
     __syncwarp();
     return true;
 }
 
-// taken: ceil(E/32) words of shared memory owned by this warp; sel/selv: k
+// taken: max(ceil(E/32), 128 if E <= 64) words of shared memory owned by
+// this warp (the selection for E <= 64 uses 128 words of it as scratch); sel/selv: k
 // entries of scratch written identically by every lane; ids_out/w_out
 // entry p is written by lane p mod 32 with the softmax, by lane 0 without
 // it (nothing on a bad softmax sum).  With softmax == false only the ids
@@ -85,7 +99,7 @@ __device__ __forceinline__ bool warp_topk_softmax(const float *__restrict__ row,
             if (lane == 0) atomicExch(err, 0x81);
             return false;
         }
-        selected = small_select(v0, v1, ok0, ok1, E, k, sel, selv);
+        selected = small_select(v0, v1, ok0, ok1, k, taken, sel, selv);
     } else {
         int nan_seen = 0;
         for (int i = lane; i < E; i += 32) {
