@@ -5,6 +5,7 @@
 #include <stdint.h>
 
 #include "jt_internal.h"
+#include "jt_quant.cuh"
 
 namespace {
 
@@ -102,7 +103,11 @@ __global__ void k_ep_gather(const int4 *__restrict__ ent, const int8_t *__restri
         const int tr = g.w + __float_as_int(src_meta[g.x + r].z);
         const uint4 *s = reinterpret_cast<const uint4 *>(rtok + (size_t)tr * d);
         uint4 *t = reinterpret_cast<uint4 *>(dst_codes + (size_t)(g.y + r) * d);
-        for (int i = threadIdx.x; i < nv; i += blockDim.x) t[i] = s[i];
+        // the owner's expert rows in the K order of the routed gate/up GEMM
+        for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+            const uint4 v = s[i];
+            t[i] = jt::int2_order16(v.x, v.y, v.z, v.w);
+        }
     }
     for (int r = threadIdx.x; r < g.z; r += blockDim.x) {
         float4 m = src_meta[g.x + r];

@@ -149,25 +149,21 @@ __device__ __forceinline__ bool epi_sync(uint64_t *bar, uint32_t &phase, volatil
 }
 
 // ---------------------------------------------------------------- unpack
-// 16 INT2 codes (one 32-bit packed word, little-endian along K) -> 16 int8
-// values c = 2*li - 3.  Per byte: ((li << 1) + 125) ^ 0x80 = 2*li - 3 with
-// no carry between bytes (2*li + 125 <= 131).
+// 16 INT2 codes (one 32-bit packed word, little-endian along K: code q at
+// bits 2q) -> 16 int8 values c = 2*li - 3, by byte permutes against the
+// table {-3, -1, 1, 3}: the codes are spread into 4-bit selectors, codes
+// {0, 1, 4, 5, 8, 9, 12, 13} from w and {2, 3, 6, 7, 10, 11, 14, 15} from
+// w >> 4 (with the odd codes moved up a nibble).  The 16 values come out in
+// the K order jt::kInt2Order16 (xd rows are stored in the same order).
 __device__ __forceinline__ uint4 unpack_int2_x16(uint32_t w) {
-    uint32_t v[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const uint32_t c = (w >> (2 * j)) & 0x03030303u;
-        v[j] = ((c << 1) + 0x7D7D7D7Du) ^ 0x80808080u;
-    }
-    const uint32_t t01l = __byte_perm(v[0], v[1], 0x5140);
-    const uint32_t t23l = __byte_perm(v[2], v[3], 0x5140);
-    const uint32_t t01h = __byte_perm(v[0], v[1], 0x7362);
-    const uint32_t t23h = __byte_perm(v[2], v[3], 0x7362);
+    constexpr uint32_t kLut = 0x0301FFFDu;  // bytes -3, -1, 1, 3
+    const uint32_t s01 = (w & 0x03030303u) | ((w << 2) & 0x30303030u);
+    const uint32_t s23 = ((w >> 4) & 0x03030303u) | ((w >> 2) & 0x30303030u);
     uint4 o;
-    o.x = __byte_perm(t01l, t23l, 0x5410);
-    o.y = __byte_perm(t01l, t23l, 0x7632);
-    o.z = __byte_perm(t01h, t23h, 0x5410);
-    o.w = __byte_perm(t01h, t23h, 0x7632);
+    o.x = __byte_perm(kLut, kLut, s01);
+    o.y = __byte_perm(kLut, kLut, s01 >> 16);
+    o.z = __byte_perm(kLut, kLut, s23);
+    o.w = __byte_perm(kLut, kLut, s23 >> 16);
     return o;
 }
 
@@ -190,7 +186,7 @@ template <int BITS>
 __device__ __forceinline__ void unpack_row(const uint8_t *src, uint8_t *dst_tile, int r) {
     uint8_t *row = dst_tile + r * 128;
     if (BITS == 2) {
-#pragma unroll 1
+#pragma unroll
         for (int h = 0; h < 2; ++h) {  // 16 packed bytes -> 64 codes per pass
             const uint4 a = *reinterpret_cast<const uint4 *>(src + 16 * h);
             const uint32_t w[4] = {a.x, a.y, a.z, a.w};

@@ -15,6 +15,23 @@
 
 namespace jt {
 
+// K order inside every 16-byte block of the expert-ordered token rows (xd)
+// that feed the routed gate/up GEMM: position p of the block holds element
+// kInt2Order16[p] of the block, the order in which the INT2 unpack of that
+// GEMM produces the weight codes.  int2_order16 applies it to one block held
+// as four 32-bit words (natural order in, stored order out).
+constexpr int kInt2Order16[16] = {0, 1, 4, 5, 8, 9, 12, 13, 2, 3, 6, 7, 10, 11, 14, 15};
+
+__host__ __device__ __forceinline__ uint4 int2_order16(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3) {
+#ifdef __CUDA_ARCH__
+    return make_uint4(__byte_perm(w0, w1, 0x5410), __byte_perm(w2, w3, 0x5410), __byte_perm(w0, w1, 0x7632),
+                      __byte_perm(w2, w3, 0x7632));
+#else
+    return make_uint4((w0 & 0xFFFFu) | (w1 << 16), (w2 & 0xFFFFu) | (w3 << 16), (w0 >> 16) | (w1 & 0xFFFF0000u),
+                      (w2 >> 16) | (w3 & 0xFFFF0000u));
+#endif
+}
+
 struct QuantBlock {
     double scale_d;   // maxabs / 127 (0 when maxabs == 0)
     float inv;        // (float)(127 / maxabs), fast-path multiplier

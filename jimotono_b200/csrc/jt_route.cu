@@ -307,34 +307,32 @@ __global__ void __launch_bounds__(256)
         return;
     }
     __syncthreads();  // sdst
-    if (vec) {
-        // 8 codes per thread per step: two 16-byte loads, one 8-byte store
-        // per destination row
-        for (int i = threadIdx.x * 8; i < d; i += blockDim.x * 8) {
-            const float4 a = __ldg(reinterpret_cast<const float4 *>(row + i));
-            const float4 b = __ldg(reinterpret_cast<const float4 *>(row + i + 4));
-            const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-            uint32_t w[2] = {0u, 0u};
+    // 16 codes per thread per step: xq in natural order, the kept rows xd in
+    // the K order of the routed gate/up GEMM's INT2 unpack (jt::int2_order16)
+    for (int i = threadIdx.x * 16; i < d; i += blockDim.x * 16) {
+        float v[16];
+        if (vec) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-                w[j >> 2] |= (uint32_t)(uint8_t)(int8_t)jt::quant_code(v[j], qb) << (8 * (j & 3));
-            const uint2 word = make_uint2(w[0], w[1]);
-            *reinterpret_cast<uint2 *>(xq + (size_t)t * d + i) = word;
-            for (int j = 0; j < nd; ++j) *reinterpret_cast<uint2 *>(xd + (size_t)sdst[j] * d + i) = word;
-        }
-        return;
-    }
-    // 4 codes per thread per step, written as one 32-bit word
-    for (int i = threadIdx.x * 4; i < d; i += blockDim.x * 4) {
-        uint32_t word = 0;
+            for (int j = 0; j < 4; ++j) {
+                const float4 a = __ldg(reinterpret_cast<const float4 *>(row + i + 4 * j));
+                v[4 * j] = a.x;
+                v[4 * j + 1] = a.y;
+                v[4 * j + 2] = a.z;
+                v[4 * j + 3] = a.w;
+            }
+        } else {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int c = jt::quant_code(row[i + j], qb);
-            word |= (uint32_t)(uint8_t)(int8_t)c << (8 * j);
+            for (int j = 0; j < 16; ++j) v[j] = row[i + j];
         }
-        *reinterpret_cast<uint32_t *>(xq + (size_t)t * d + i) = word;
-        for (int j = 0; j < nd; ++j)
-            *reinterpret_cast<uint32_t *>(xd + (size_t)sdst[j] * d + i) = word;
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            w[j >> 2] |= (uint32_t)(uint8_t)(int8_t)jt::quant_code(v[j], qb) << (8 * (j & 3));
+        *reinterpret_cast<uint4 *>(xq + (size_t)t * d + i) = make_uint4(w[0], w[1], w[2], w[3]);
+        if (nd > 0) {
+            const uint4 pw = jt::int2_order16(w[0], w[1], w[2], w[3]);
+            for (int j = 0; j < nd; ++j) *reinterpret_cast<uint4 *>(xd + (size_t)sdst[j] * d + i) = pw;
+        }
     }
 }
 
@@ -381,7 +379,7 @@ extern "C" int jtk_build_tiles(const int32_t *off, const int32_t *tile_off, int 
 extern "C" int jtk_quant_dispatch(const float *x, int T, int d, int k, const int32_t *pos,
                                   const float *wfin, int8_t *xq, float *xs, int8_t *xd,
                                   float4 *row_meta, float4 *sh_meta, cudaStream_t stream) {
-    if (T <= 0 || d <= 0 || (d % 4) != 0 || k > 64) return -1;
+    if (T <= 0 || d <= 0 || (d % 16) != 0 || k > 64) return -1;
     k_quant_dispatch<<<T, 256, 0, stream>>>(x, T, d, k, pos, wfin, xq, xs, xd, row_meta, sh_meta,
                                             jtk_error_word());
     return cudaGetLastError() == cudaSuccess ? 0 : -4;
