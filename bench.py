@@ -634,7 +634,7 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         from oracle.cpu_baseline import cpu_baseline
-        cpu = cpu_baseline(seconds=20.0)
+        cpu = cpu_baseline(seconds=60.0)
     clocks = clk.summary()
     if rank == 0:
         gu_ms = stage[4]

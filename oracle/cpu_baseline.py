@@ -13,7 +13,10 @@ a CPU, so the sample keeps the configuration's per-expert shapes (model dim
 2048, expert ffn 1536, top-8) with 8 experts and 128 tokens per call: every
 expert then sees 128 tokens per call, the configuration's average, so the
 per-call weight preparation the reference does (moe_layer.c:1301-1397,
-lowbit.c:228-237) is amortized as it would be at full size.  The
+lowbit.c:228-237) is amortized as it would be at full size (the reference
+arm).  The single-core baseline uses 64-token calls, so that several timed
+trials fit in its time budget; that amortizes the weight preparation over
+half as many tokens, which is to the reference's disadvantage.  The
 reference's API forces the shared experts' ffn to equal the routed one
 (1536 instead of 4096), which favours the reference.
 """
@@ -65,17 +68,71 @@ class _Sample:
         return dt
 
 
-def cpu_baseline(seconds: float = 20.0) -> dict | None:
-    """One core: a 128-token call of the sample (see module docstring)."""
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as fh:
+            for ln in fh:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def _median_mad(xs):
+    xs = sorted(xs)
+    med = xs[len(xs) // 2] if len(xs) % 2 else 0.5 * (xs[len(xs) // 2 - 1] + xs[len(xs) // 2])
+    dev = sorted(abs(x - med) for x in xs)
+    mad = dev[len(dev) // 2] if len(dev) % 2 else 0.5 * (dev[len(dev) // 2 - 1] + dev[len(dev) // 2])
+    return med, mad
+
+
+def trials(T: int, seconds: float, max_trials: int = 11, min_trials: int = 3) -> list:
+    """Seconds per call of the sample at T tokens: at least min_trials calls,
+    then more until `seconds` have passed or max_trials are done."""
+    smp = _Sample()
+    smp.call(1, 0)  # pages the weights in, loads libm
+    out = []
+    t_end = time.perf_counter() + seconds
+    while len(out) < max_trials and (len(out) < min_trials or time.perf_counter() < t_end):
+        out.append(smp.call(T, 1 + len(out)))
+    return out
+
+
+def cpu_baseline(seconds: float = 60.0, T: int = 64) -> dict | None:
+    """One pinned core: the reference layer on the sample (module docstring),
+    repeated while `seconds` last (3 to 11 trials), median and MAD of the
+    per-call time.  Runs in a child process under taskset so the pinning does
+    not touch the caller."""
     if not have_ref():
         return None
-    smp = _Sample()
-    T = 128
-    dt = smp.call(T, 1)
-    return {"value": round(T / dt, 3), "unit": "tokens/s", "cores": 1, "kind": "reference",
+    import json
+    import subprocess
+    import sys
+    cores = sorted(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else [0]
+    core = cores[-1]
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = ("import json, sys; sys.path.insert(0, %r); from oracle.cpu_baseline import trials; "
+            "print(json.dumps(trials(%d, %f)))" % (root, T, seconds))
+    cmd = [sys.executable, "-c", code]
+    pinned = False
+    try:
+        res = subprocess.run(["taskset", "-c", str(core)] + cmd, capture_output=True, text=True,
+                             timeout=seconds * 4 + 300)
+        pinned = res.returncode == 0
+    except (OSError, subprocess.TimeoutExpired):
+        res = None
+    if not pinned:  # no taskset: unpinned child
+        res = subprocess.run(cmd, capture_output=True, text=True, timeout=seconds * 4 + 300)
+    times = json.loads(res.stdout.strip().splitlines()[-1])
+    med, mad = _median_mad(times)
+    return {"value": round(T / med, 3), "unit": "tokens/s", "cores": 1, "kind": "reference",
+            "trials": len(times), "median_s_per_call": round(med, 3), "mad_s_per_call": round(mad, 3),
+            "pinned": f"taskset -c {core}" if pinned else "unpinned", "cpu_model": cpu_model(),
+            "host_cores": os.cpu_count(),
             "sample": f"reference jt_moe_fwd_batch_unchecked (LUT routed + W8A8 shared) at "
-                      f"d=2048 f=1536 top-8, E=8, S=2 (ffn 1536), {T} tokens/call "
-                      f"(128 tokens per expert as in the full config), 1 thread, {dt:.1f} s"}
+                      f"d=2048 f=1536 top-8, E=8, S=2 (ffn 1536), {T} tokens/call, 1 thread; "
+                      f"{len(times)} trials, value = tokens / median seconds per call"}
 
 
 def reference_arm(steps: int, warmup: int, metric: str) -> dict:
@@ -84,7 +141,8 @@ def reference_arm(steps: int, warmup: int, metric: str) -> dict:
     if not have_ref():
         return {"impl": "reference", "unavailable": "oracle/_ref/libjtref.so not built"}
     smp = _Sample()
-    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    cpus = sorted(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else list(range(os.cpu_count()))
+    cores = len(cpus)
     T = 128
     smp.call(1, 0)  # warm-up (page in weights, libm)
     times = []
@@ -93,6 +151,8 @@ def reference_arm(steps: int, warmup: int, metric: str) -> dict:
 
         def work(i):
             try:
+                if hasattr(os, "sched_setaffinity"):  # this thread on its own core
+                    os.sched_setaffinity(0, {cpus[i % len(cpus)]})
                 smp.call(T, 100 * s + i)
             except Exception as e:  # pragma: no cover
                 errs.append(e)
@@ -105,7 +165,8 @@ def reference_arm(steps: int, warmup: int, metric: str) -> dict:
         times.append(time.perf_counter() - t0)
         if errs:
             raise errs[0]
-    ms = 1e3 * sum(times) / len(times)
+    med, mad = _median_mad(times)
+    ms = 1e3 * med
     value = cores * T / (ms / 1e3)
     return {"impl": "reference", "metric": metric, "value": round(value, 2), "unit": "tokens/s",
             "n_gpus": 0, "steps": steps, "warmup": warmup, "ms_per_step": round(ms, 1),
@@ -116,7 +177,9 @@ def reference_arm(steps: int, warmup: int, metric: str) -> dict:
                        "tokens": 16384, "parallelism": "host cores",
                        "measured_on": "a bounded sample of the workload's expert shapes (see cpu_baseline)"},
             "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": cores,
-                             "kind": "reference",
-                             "sample": f"{cores} threads x {T}-token calls, E=8 top-8 d=2048 f=1536"},
+                             "kind": "reference", "cpu_model": cpu_model(),
+                             "median_ms_per_step": round(ms, 1), "mad_ms_per_step": round(1e3 * mad, 1),
+                             "sample": f"{cores} threads (one per core, pinned) x {T}-token calls, "
+                                       f"E=8 top-8 d=2048 f=1536; median over {len(times)} steps"},
             "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
