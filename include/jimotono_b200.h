@@ -439,6 +439,25 @@ int jt_b200_ep_layout(const int32_t *cnt, int N, int E, int rank, int cap, int32
  * the return code (JT_OK or JT_ERR_CUDA). */
 int jt_b200_sync(void);
 
+/* jt_b200_sync, with the code a kernel reported (0 when none) written to
+ * *kernel_code: JT_B200_KERR_TIMEOUT (a bounded wait of a kernel ran out;
+ * the kernel drained and returned), JT_B200_KERR_SHAPE, JT_B200_KERR_NONFINITE,
+ * JT_B200_KERR_RANGE, or 0x81-0x85 (routing: NaN logit, bad softmax sum,
+ * expert id out of range, -, non-finite activation). */
+#define JT_B200_KERR_TIMEOUT 0x71
+#define JT_B200_KERR_SHAPE 0x72
+#define JT_B200_KERR_NONFINITE 0x73
+#define JT_B200_KERR_RANGE 0x74
+int jt_b200_sync_code(int *kernel_code);
+
+/* Diagnostic of the failure-detection path: one kernel waits, with the same
+ * bounded wait every kernel of the library uses, on a barrier that nothing
+ * completes, for budget_cycles SM clock cycles (1 .. 4e9), then raises
+ * JT_B200_KERR_TIMEOUT and returns.  jt_b200_sync_code then reports it and
+ * the context stays usable.  No counterpart in the reference (which has no
+ * device). */
+int jt_b200_selftest_bounded_wait(long long budget_cycles, void *stream);
+
 /* Human-readable description of the last failed launch on this thread. */
 const char *jt_b200_last_error(void);
 

@@ -74,6 +74,8 @@ PROTOTYPES = {
     "jt_b200_ep_capacity": (I, [C.c_longlong, I, I, F]),
     "jt_b200_ep_layout": (I, [P, I, I, I, I, P, P, P, P, P, P]),
     "jt_b200_sync": (I, []),
+    "jt_b200_sync_code": (I, [P]),
+    "jt_b200_selftest_bounded_wait": (I, [C.c_longlong, P]),
     "jt_b200_last_error": (C.c_char_p, []),
     "jt_b200_version": (C.c_char_p, []),
 }

@@ -82,21 +82,28 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t pari
     return ok != 0;
 }
 
-// Bounded wait. Returns false (and raises the CTA abort flag + device error
-// word) when the budget runs out or another role already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
-                                          int *err) {
+// Bounded wait with a budget in clock cycles.  Returns false (and raises
+// the CTA abort flag + device error word) when the budget runs out or
+// another role already aborted.
+__device__ __forceinline__ bool mbar_wait_budget(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                                 int *err, long long budget) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (true) {
         if (mbar_try_wait_sleep(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (clock64() - t0 > JT_SPIN_CYCLES) {
+        if (clock64() - t0 > budget) {
             *abort_flag = 1;
             if (err) atomicExch(err, JT_KERR_TIMEOUT);
             return false;
         }
     }
+}
+
+// The bounded wait of every kernel of the library (budget ~2 s).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                          int *err) {
+    return mbar_wait_budget(bar, parity, abort_flag, err, JT_SPIN_CYCLES);
 }
 
 // ---------------------------------------------------------------- TMA
