@@ -9,10 +9,11 @@
 // same experts.
 //
 // Tiled GEMM on the FP64 pipe (one DFMA per product; the tensor cores'
-// FP64 path accumulates in another order): a 256-thread block computes 32
+// FP64 path accumulates in another order): a 256-thread block computes 64
 // tokens x 64 experts, staging 32-element K chunks of both operands in
 // shared memory as doubles (converted once per element and block); each
-// thread holds 2 tokens x 4 experts x 4 lanes of accumulators.  Up to 32768
+// thread holds 4 tokens x 4 experts x 4 lanes of accumulators and reads its
+// operands as 16-byte pairs, one shared-memory load per four DFMA.  Up to 32768
 // logits (decode) a chain kernel with one thread per (logit, lane) is used
 // instead.
 #include <cuda_runtime.h>
@@ -23,66 +24,88 @@
 
 namespace {
 
-constexpr int kTT = 32;  // tokens per block
+constexpr int kTT = 64;  // tokens per block
 constexpr int kTE = 64;  // experts per block
 constexpr int kKC = 32;  // K elements per chunk (a multiple of 4: lanes stay j mod 4)
-constexpr int kLd = kKC + 1;
+constexpr int kLd = kKC + 2;  // row stride in doubles: 16-byte loads of neighbouring rows hit other banks
 
 __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__ x, const float *__restrict__ wg,
                                                        int T, int d, int E, float *__restrict__ logits, int *err) {
-    __shared__ double xs[kTT][kLd];
-    __shared__ double ws[kTE][kLd];
-    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // experts tx + 16i, tokens ty + 16u
+    __shared__ __align__(16) double xs[kTT][kLd];
+    __shared__ __align__(16) double ws[kTE][kLd];
+    // experts tx + 16i, tokens ty + 16u; a warp covers 8 expert rows x 4
+    // token rows, so each of its 16-byte operand loads is one wavefront
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tx = (warp & 1) * 8 + (lane & 7), ty = (warp >> 1) * 4 + (lane >> 3);
     const int t0 = blockIdx.y * kTT, e0 = blockIdx.x * kTE;
-    double acc[2][4][4];
+    double acc[4][4][4];  // [token u][expert i][lane l]
 #pragma unroll
-    for (int u = 0; u < 2; ++u)
+    for (int u = 0; u < 4; ++u)
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
             for (int l = 0; l < 4; ++l) acc[u][i][l] = 0.0;
 
-    // each thread stages one 16-byte piece of the activation tile and two of
-    // the weight tile per chunk; the next chunk's pieces are loaded into
-    // registers while the current chunk is multiplied
+    // staging: each thread moves two 16-byte pieces of the activation tile
+    // and two of the weight tile per chunk (rows sr and sr + 32, elements
+    // sc .. sc+3); the next chunk is loaded into registers while the current
+    // one is multiplied
     const int sr = threadIdx.x >> 3, sc = 4 * (threadIdx.x & 7);
-    const bool xin = t0 + sr < T, w0in = e0 + sr < E, w1in = e0 + sr + 32 < E;
-    const float *xp = x + (size_t)(t0 + sr) * d + sc;
-    const float *wp0 = wg + (size_t)(e0 + sr) * d + sc;
-    const float *wp1 = wg + (size_t)(e0 + sr + 32) * d + sc;
+    const bool x0in = t0 + sr < T, x1in = t0 + sr + 32 < T, w0in = e0 + sr < E, w1in = e0 + sr + 32 < E;
+    const float *xp0 = x + (size_t)(x0in ? t0 + sr : 0) * d + sc;
+    const float *xp1 = x + (size_t)(x1in ? t0 + sr + 32 : 0) * d + sc;
+    const float *wp0 = wg + (size_t)(w0in ? e0 + sr : 0) * d + sc;
+    const float *wp1 = wg + (size_t)(w1in ? e0 + sr + 32 : 0) * d + sc;
     const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
-    float4 px = xin ? __ldg(reinterpret_cast<const float4 *>(xp)) : z4;
+    float4 px0 = x0in ? __ldg(reinterpret_cast<const float4 *>(xp0)) : z4;
+    float4 px1 = x1in ? __ldg(reinterpret_cast<const float4 *>(xp1)) : z4;
     float4 pw0 = w0in ? __ldg(reinterpret_cast<const float4 *>(wp0)) : z4;
     float4 pw1 = w1in ? __ldg(reinterpret_cast<const float4 *>(wp1)) : z4;
     for (int k0 = 0; k0 < d; k0 += kKC) {
-        xs[sr][sc] = px.x, xs[sr][sc + 1] = px.y, xs[sr][sc + 2] = px.z, xs[sr][sc + 3] = px.w;
-        ws[sr][sc] = pw0.x, ws[sr][sc + 1] = pw0.y, ws[sr][sc + 2] = pw0.z, ws[sr][sc + 3] = pw0.w;
-        ws[sr + 32][sc] = pw1.x, ws[sr + 32][sc + 1] = pw1.y, ws[sr + 32][sc + 2] = pw1.z, ws[sr + 32][sc + 3] = pw1.w;
+        *reinterpret_cast<double2 *>(&xs[sr][sc]) = make_double2(px0.x, px0.y);
+        *reinterpret_cast<double2 *>(&xs[sr][sc + 2]) = make_double2(px0.z, px0.w);
+        *reinterpret_cast<double2 *>(&xs[sr + 32][sc]) = make_double2(px1.x, px1.y);
+        *reinterpret_cast<double2 *>(&xs[sr + 32][sc + 2]) = make_double2(px1.z, px1.w);
+        *reinterpret_cast<double2 *>(&ws[sr][sc]) = make_double2(pw0.x, pw0.y);
+        *reinterpret_cast<double2 *>(&ws[sr][sc + 2]) = make_double2(pw0.z, pw0.w);
+        *reinterpret_cast<double2 *>(&ws[sr + 32][sc]) = make_double2(pw1.x, pw1.y);
+        *reinterpret_cast<double2 *>(&ws[sr + 32][sc + 2]) = make_double2(pw1.z, pw1.w);
         __syncthreads();
         if (k0 + kKC < d) {
             const int kn = k0 + kKC;
-            px = xin ? __ldg(reinterpret_cast<const float4 *>(xp + kn)) : z4;
+            px0 = x0in ? __ldg(reinterpret_cast<const float4 *>(xp0 + kn)) : z4;
+            px1 = x1in ? __ldg(reinterpret_cast<const float4 *>(xp1 + kn)) : z4;
             pw0 = w0in ? __ldg(reinterpret_cast<const float4 *>(wp0 + kn)) : z4;
             pw1 = w1in ? __ldg(reinterpret_cast<const float4 *>(wp1 + kn)) : z4;
         }
-#pragma unroll 2
+        // four K elements (one per lane) per step, ascending j in every lane
+#pragma unroll 1
         for (int j = 0; j < kKC; j += 4) {
+            double a[4][4], b[4][4];
 #pragma unroll
-            for (int l = 0; l < 4; ++l) {
-                const double a0 = xs[ty][j + l], a1 = xs[ty + 16][j + l];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const double b = ws[tx + 16 * i][j + l];
-                    acc[0][i][l] = __fma_rn(a0, b, acc[0][i][l]);
-                    acc[1][i][l] = __fma_rn(a1, b, acc[1][i][l]);
-                }
+            for (int u = 0; u < 4; ++u) {
+                const double2 lo = *reinterpret_cast<const double2 *>(&xs[ty + 16 * u][j]);
+                const double2 hi = *reinterpret_cast<const double2 *>(&xs[ty + 16 * u][j + 2]);
+                a[u][0] = lo.x, a[u][1] = lo.y, a[u][2] = hi.x, a[u][3] = hi.y;
             }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const double2 lo = *reinterpret_cast<const double2 *>(&ws[tx + 16 * i][j]);
+                const double2 hi = *reinterpret_cast<const double2 *>(&ws[tx + 16 * i][j + 2]);
+                b[i][0] = lo.x, b[i][1] = lo.y, b[i][2] = hi.x, b[i][3] = hi.y;
+            }
+#pragma unroll
+            for (int l = 0; l < 4; ++l)
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) acc[u][i][l] = __fma_rn(a[u][l], b[i][l], acc[u][i][l]);
         }
         __syncthreads();
     }
     bool bad = false;
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
+    for (int u = 0; u < 4; ++u) {
         const int t = t0 + ty + 16 * u;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
