@@ -9,10 +9,12 @@
 //
 //   k_dec_gateup  work units of 128 weight rows: 64 gate rows over the same
 //                 64 up rows of one expert.  Routed unit (slot, 64-channel
-//                 block): INT2 rows, one row per thread, the group partials
-//                 folded in the thread in group order (same fp32 fold as the
-//                 grouped kernel), then SwiGLU (moe_layer.c:146-148) and the
-//                 per-64-channel requantization of h.  Shared-expert unit
+//                 block): INT2 rows, one row per thread; each group's exact
+//                 integer partials give its dot with the fp16 weights
+//                 fp16_rn(code * scale) of the batched kernel (jt_moe_gu16.cu),
+//                 folded in fp32 in group order; then SwiGLU
+//                 (moe_layer.c:146-148) and the per-64-channel requantization
+//                 of h.  Shared-expert unit
 //                 (expert, 64-channel block, K part): the int8 rows of a
 //                 shared expert are d bytes long, so ksplit CTAs each take a
 //                 K part of every row; their exact int32 partial dots meet
@@ -140,25 +142,44 @@ __device__ __forceinline__ void swiglu_requant64(const float (&gu)[2][64], int8_
     if (lane == 0) *hs = qb.scale_f;
 }
 
-// Group partial P of one INT2 group (16 packed bytes, codes li little-endian
+// Group partials of one INT2 group (16 packed bytes, codes li little-endian
 // along K) against the token: byte b of word i holds the codes of
 // k = 16i + 4b + j in bits 2j, so field j of every byte pairs with the
 // activation word xp[4i + j] = {x[16i+j], x[16i+4+j], x[16i+8+j],
-// x[16i+12+j]}.  The field is used in place (times 4^j) and the four sums
-// are scaled back exactly; P = 2 sum(li x) - 3 sum(x).
-__device__ __forceinline__ int int2_group(const uint4 w, const uint32_t *xp, int gs) {
+// x[16i+12+j]}.  Each bit of a field is used in place (times 2^(2j) or
+// 2^(2j+1)) and the sums are scaled back exactly: with li = b0 + 2 b1,
+//   P  = sum x c            = 2 B0 + 4 B1 - 3 X   (c = 2 li - 3)
+//   A3 = sum x [|c| = 3] sgn(c) = B0 + B1 - X       ([li=3] - [li=0] = b0 + b1 - 1)
+// with B0 = sum x b0, B1 = sum x b1, X = sum x.  The routed gate/up weight
+// of code c is fp16_rn(c s) = c s + [|c| = 3] sgn(c) (t - 3 s) with
+// t = fp16_rn(3 s), so the group's dot with the weights is s P + (t - 3s) A3.
+__device__ __forceinline__ int2 int2_group(const uint4 w, const uint32_t *xp, int gs) {
     const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-    int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+    int l0 = 0, l1 = 0, l2 = 0, l3 = 0, h0 = 0, h1 = 0, h2 = 0, h3 = 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const uint4 xv = *reinterpret_cast<const uint4 *>(xp + 4 * i);
-        a0 = dp4a_us(ww[i] & 0x03030303u, xv.x, a0);
-        a1 = dp4a_us(ww[i] & 0x0C0C0C0Cu, xv.y, a1);
-        a2 = dp4a_us(ww[i] & 0x30303030u, xv.z, a2);
-        a3 = dp4a_us(ww[i] & 0xC0C0C0C0u, xv.w, a3);
+        l0 = dp4a_us(ww[i] & 0x01010101u, xv.x, l0);
+        h0 = dp4a_us(ww[i] & 0x02020202u, xv.x, h0);
+        l1 = dp4a_us(ww[i] & 0x04040404u, xv.y, l1);
+        h1 = dp4a_us(ww[i] & 0x08080808u, xv.y, h1);
+        l2 = dp4a_us(ww[i] & 0x10101010u, xv.z, l2);
+        h2 = dp4a_us(ww[i] & 0x20202020u, xv.z, h2);
+        l3 = dp4a_us(ww[i] & 0x40404040u, xv.w, l3);
+        h3 = dp4a_us(ww[i] & 0x80808080u, xv.w, h3);
     }
-    const int s = a0 + (a1 >> 2) + (a2 >> 4) + (a3 >> 6);
-    return 2 * s - 3 * gs;
+    const int b0 = l0 + (l1 >> 2) + (l2 >> 4) + (l3 >> 6);
+    const int b1 = (h0 >> 1) + (h1 >> 3) + (h2 >> 5) + (h3 >> 7);
+    return make_int2(2 * b0 + 4 * b1 - 3 * gs, b0 + b1 - gs);
+}
+
+// fp32 dot of one group with its fp16 weights: s P + (t - 3s) A3 (see
+// int2_group; t - 3s is exact in fp32).
+__device__ __forceinline__ float int2_fold(float acc, int2 pa, __half sg) {
+    const float s = __half2float(sg);
+    const float s3 = 3.0f * s;
+    const float dt = __half2float(__float2half_rn(s3)) - s3;
+    return fmaf((float)pa.y, dt, fmaf((float)pa.x, s, acc));
 }
 
 // grid n_routed_units + S * (fs/64) * ksplit, kGuThreads threads.
@@ -357,7 +378,7 @@ __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant
         float acc = 0.0f;
         if (p.tma) {
             if (!jt::mbar_wait(&wbar, 0, &abort_flag, p.err)) return;
-            // fold r = fmaf((float)P_g, s_g, r) over the groups in order; row
+            // fold the groups' dots with the fp16 weights in order; row
             // rr of a box holds its 16-byte chunk c at chunk c ^ (rr % 8)
             const int rr = r & 63, nbox = d / 512;
             const uint8_t *rowb = wsm + (size_t)(up ? nbox : 0) * 8192 + (size_t)rr * 128;
@@ -369,8 +390,7 @@ __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant
                         const uint4 w = *reinterpret_cast<const uint4 *>(rowb + (size_t)(g >> 3) * 8192 +
                                                                           (((g & 7) ^ (rr & 7)) << 4));
                         const __half sg = g0 == 0 ? sv[i] : srow[(size_t)g * p.f];
-                        const int P = int2_group(w, xp + 16 * g, gsum[g]);
-                        acc = fmaf((float)P, __half2float(sg), acc);
+                        acc = int2_fold(acc, int2_group(w, xp + 16 * g, gsum[g]), sg);
                     }
                 }
             }
@@ -385,8 +405,7 @@ __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant
                         const int g = g0 + b * kGroupsPerLoad + i;
                         if (g < ng) {
                             const __half sg = g0 == 0 ? sv[b * kGroupsPerLoad + i] : srow[(size_t)g * p.f];
-                            const int P = int2_group(wv[b][i], xp + 16 * g, gsum[g]);
-                            acc = fmaf((float)P, __half2float(sg), acc);
+                            acc = int2_fold(acc, int2_group(wv[b][i], xp + 16 * g, gsum[g]), sg);
                         }
                     }
 #pragma unroll

@@ -61,11 +61,12 @@ struct jt_b200_moe_ep_plan {
     float4 *row_meta, *sh_meta;
     float *w_raw, *w_fin, *xs, *hs_s, *y32;
     uint8_t *drop;
-    int8_t *xq, *xd, *hq_s;
+    int8_t *xq, *hq_s;
     /* exchange: cnt = E expert counts then N token-row counts */
     int32_t *cnt, *cnt_all, *gbase, *own_off, *own_tile_off, *trow, *tsoff;
     int4 *gather, *own_tiles;
-    int8_t *send_tok, *rtok, *own_codes, *own_hq;
+    int8_t *send_tok, *rtok, *own_hq;
+    uint16_t *own_x; /* owned pairs' token rows, fp16, expert order (jtk_ep_gather) */
     float4 *rmeta, *own_meta;
     float *own_hs, *ret, *back;
     int R_tok; /* received token rows capacity (T * N) */
@@ -207,7 +208,7 @@ int jt_b200_moe_ep_plan_create(const jt_b200_moe_dims *dims, jt_b200_ep_comm *co
         {(void **)&p->gbase, E * 4},         {(void **)&p->own_off, (El + 1) * 4},
         {(void **)&p->own_tile_off, (El + 1) * 4},
         {(void **)&p->gather, Nn * El * 16}, {(void **)&p->own_tiles, (R / JT_TILE_ROWS + El + 1) * 16},
-        {(void **)&p->rtok, RT * d},         {(void **)&p->own_codes, R * d},
+        {(void **)&p->rtok, RT * d},         {(void **)&p->own_x, R * d * 2},
         {(void **)&p->own_hq, R * f},        {(void **)&p->rmeta, R * 16},
         {(void **)&p->own_meta, R * 16},     {(void **)&p->own_hs, R * (size_t)hs_ld((int)f) * 4},
         {(void **)&p->ret, RT * d * 4},      {(void **)&p->back, Tdst * d * 4},
@@ -426,10 +427,10 @@ int jt_b200_moe_ep_forward(jt_b200_moe_ep_plan *p, const jt_b200_moe_weights *w,
     if (rtoff[N] > 0)
         CUDA(cudaMemsetAsync(p->ret, 0, (size_t)rtoff[N] * d * sizeof(float), st));
     if (own_rows > 0) {
-        LAUNCH(jtk_ep_gather(p->gather, N * El, p->rtok, p->rmeta, d, p->own_codes, p->own_meta, st));
+        LAUNCH(jtk_ep_gather(p->gather, N * El, p->rtok, p->rmeta, d, p->own_x, p->own_meta, st));
         LAUNCH(jtk_build_tiles(p->own_off, p->own_tile_off, El, p->own_tiles, st));
-        const int gu_hint = own_tiles * (f / 64), dn_hint = own_tiles * (d / 128);
-        LAUNCH(jtk_moe_gateup_routed(w->wg, w->wu, w->sg, w->su, El, f, d, p->own_codes, p->R_max,
+        const int gu_hint = own_tiles * (f / 128), dn_hint = own_tiles * (d / 128);
+        LAUNCH(jtk_moe_gateup_routed(w->wg, w->wu, w->sg, w->su, El, f, d, p->own_x, p->R_max,
                                      p->own_meta, p->own_tiles, p->own_tile_off + El, p->own_hq,
                                      p->own_hs, gu_hint, st));
         LAUNCH(jtk_moe_down_routed(w->wd, w->sd, El, d, f, p->own_hq, p->R_max, p->own_hs,

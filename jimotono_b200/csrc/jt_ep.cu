@@ -94,7 +94,7 @@ __global__ void k_ep_pack(const int8_t *__restrict__ xq, const float *__restrict
 // row; the metadata's third field becomes the received token row, which is
 // where the down projection adds that pair's weighted output.
 __global__ void k_ep_gather(const int4 *__restrict__ ent, const int8_t *__restrict__ rtok,
-                            const float4 *__restrict__ src_meta, int d, int8_t *__restrict__ dst_codes,
+                            const float4 *__restrict__ src_meta, int d, uint16_t *__restrict__ dst_x,
                             float4 *__restrict__ dst_meta) {
     // {first received pair, first owned row, pairs, first received token row of the source}
     const int4 g = ent[blockIdx.x];
@@ -102,11 +102,11 @@ __global__ void k_ep_gather(const int4 *__restrict__ ent, const int8_t *__restri
     for (int r = 0; r < g.z; ++r) {
         const int tr = g.w + __float_as_int(src_meta[g.x + r].z);
         const uint4 *s = reinterpret_cast<const uint4 *>(rtok + (size_t)tr * d);
-        uint4 *t = reinterpret_cast<uint4 *>(dst_codes + (size_t)(g.y + r) * d);
-        // the owner's expert rows in the K order of the routed gate/up GEMM
+        uint4 *t = reinterpret_cast<uint4 *>(dst_x + (size_t)(g.y + r) * d);
+        // the owner's expert rows as fp16 in the K order of the routed gate/up GEMM
         for (int i = threadIdx.x; i < nv; i += blockDim.x) {
             const uint4 v = s[i];
-            t[i] = jt::int2_order16(v.x, v.y, v.z, v.w);
+            jt::x16_block(v.x, v.y, v.z, v.w, t[2 * i], t[2 * i + 1]);
         }
     }
     for (int r = threadIdx.x; r < g.z; r += blockDim.x) {
@@ -169,10 +169,10 @@ extern "C" int jtk_ep_pack(const int8_t *xq, const float *xs, int T, int d, int 
 }
 
 extern "C" int jtk_ep_gather(const int4 *ent, int n_ent, const int8_t *rtok, const float4 *src_meta,
-                             int d, int8_t *dst_codes, float4 *dst_meta, cudaStream_t stream) {
+                             int d, uint16_t *dst_x, float4 *dst_meta, cudaStream_t stream) {
     if (n_ent < 0 || d <= 0 || d % 16) return -1;
     if (n_ent == 0) return 0;
-    k_ep_gather<<<n_ent, 256, 0, stream>>>(ent, rtok, src_meta, d, dst_codes, dst_meta);
+    k_ep_gather<<<n_ent, 256, 0, stream>>>(ent, rtok, src_meta, d, dst_x, dst_meta);
     return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 

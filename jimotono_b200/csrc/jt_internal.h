@@ -92,15 +92,20 @@ int jtk_ep_tokens(const int32_t *ids, int T, int k, int El, int N, int32_t *trow
 int jtk_ep_pack(const int8_t *xq, const float *xs, int T, int d, int k, int El, int N, const int32_t *ids,
                 const int32_t *pos, const float *wfin, const int32_t *trow, const int32_t *tsoff,
                 int8_t *send_tok, float4 *row_meta, cudaStream_t stream);
+/* dst_x: the owner's expert-ordered token rows as fp16 in the routed gate/up
+ * GEMM's K order (as jtk_quant_dispatch's xd). */
 int jtk_ep_gather(const int4 *ent, int n_ent, const int8_t *rtok, const float4 *src_meta, int d,
-                  int8_t *dst_codes, float4 *dst_meta, cudaStream_t stream);
+                  uint16_t *dst_x, float4 *dst_meta, cudaStream_t stream);
 int jtk_ep_combine(const int32_t *trow, const int32_t *tsoff, int T, int N, const float *back, int d,
                    float *y, cudaStream_t stream);
 
 /* Per-token quantization + dispatch; row_meta[row] = {scale, weight, token bits, 0}
- * for every kept row, sh_meta[t] = {scale, 1, t bits, 0} (may be NULL). */
+ * for every kept row, sh_meta[t] = {scale, 1, t bits, 0} (may be NULL).
+ * xq [T][d] int8; xd [kept rows][d] the same codes as exact fp16 values, in
+ * expert order and in the K order of the routed gate/up GEMM (jt::kX16Order
+ * inside every 16-element block). */
 int jtk_quant_dispatch(const float *x, int T, int d, int k, const int32_t *pos,
-                       const float *wfin, int8_t *xq, float *xs, int8_t *xd, float4 *row_meta,
+                       const float *wfin, int8_t *xq, float *xs, uint16_t *xd, float4 *row_meta,
                        float4 *sh_meta, cudaStream_t stream);
 
 /* Expert GEMMs (jt_moe_gemm.cu), JT_TILE_ROWS-row token tiles.  tiles / ntiles: tile
@@ -108,7 +113,7 @@ int jtk_quant_dispatch(const float *x, int T, int d, int k, const int32_t *pos,
  * Group scales fp16 [E][K/64][n_ch]; h scales hs [rows][hs_ld] with
  * hs_ld = round_up(n_ch/64, 4). */
 int jtk_moe_gateup_routed(const uint8_t *wg, const uint8_t *wu, const void *gs, const void *us,
-                          int E, int f, int d, const int8_t *xd, int rows_cap,
+                          int E, int f, int d, const uint16_t *xd, int rows_cap,
                           const float4 *row_meta, const int4 *tiles, const int32_t *ntiles,
                           int8_t *hq, float *hs, int max_tiles_hint, cudaStream_t stream);
 /* y_accumulate 1: y[token][:] += w * row (combine into the layer output);

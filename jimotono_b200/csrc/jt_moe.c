@@ -49,7 +49,8 @@ struct jt_b200_moe_plan {
     float4 *row_meta, *sh_meta;
     float *w_raw, *w_fin, *xs, *hs, *hs_s, *y32;
     uint8_t *drop;
-    int8_t *xq, *xd, *hq, *hq_s;
+    int8_t *xq, *hq, *hq_s;
+    uint16_t *xd; /* kept token rows, fp16, expert order (jtk_quant_dispatch) */
     /* batch-1 path: h codes and scales of every shared expert at once */
     int8_t *hq_d;
     float *hs_d;
@@ -107,7 +108,7 @@ int jt_b200_moe_plan_create(const jt_b200_moe_dims *dims, jt_b200_moe_plan **out
         {(void **)&p->xs, T * 4},            {(void **)&p->hs, Tk * (size_t)hs_ld((int)f) * 4},
         {(void **)&p->hs_s, ((T + 3) & ~(size_t)3) * (size_t)hs_ld((int)fs) * 4},
         {(void **)&p->y32, T * d * 4},       {(void **)&p->drop, Tk},
-        {(void **)&p->xq, T * d},            {(void **)&p->xd, Tk * d},
+        {(void **)&p->xq, T * d},            {(void **)&p->xd, Tk * d * 2},
         {(void **)&p->hq, Tk * f},           {(void **)&p->hq_s, T * fs},
         {(void **)&p->hq_d, (size_t)(dims->S > 0 ? dims->S : 1) * fs},
         {(void **)&p->hs_d, (size_t)(dims->S > 0 ? dims->S : 1) * (size_t)hs_ld((int)fs) * 4},
@@ -340,7 +341,7 @@ int jt_b200_moe_forward(jt_b200_moe_plan *plan, const jt_b200_moe_weights *w, co
         const long long pairs = (long long)T * k;
         const long long ne = pairs < E ? pairs : E;
         const long long tl = ne + pairs / JT_TILE_ROWS;
-        gu_hint = tl * (f / 64) > 0x7fffffffLL ? 0 : (int)(tl * (f / 64));
+        gu_hint = tl * (f / 128) > 0x7fffffffLL ? 0 : (int)(tl * (f / 128));
         dn_hint = tl * (d / 128) > 0x7fffffffLL ? 0 : (int)(tl * (d / 128));
     }
     MARK(JT_B200_STAGE_GATEUP);

@@ -1,11 +1,8 @@
 // jt_moe_gemm.cu - expert GEMMs of the quantized MoE layer on the sm_100a
 // tensor cores (tcgen05.mma kind::i8, TMEM accumulators, TMA operand feed).
 //
-// One kernel template, four modes:
-//   GU_ROUTED  gate/up of the routed experts: INT2 weights with one fp16
-//              scale per 64 K (group-64 format), int8 token rows in expert
-//              order.  Epilogue: fold of the group partials, SwiGLU, and
-//              requantization of h per (row, 64-channel group).
+// One kernel template, three modes (the routed gate/up runs on fp16
+// operands in jt_moe_gu16.cu):
 //   GU_SHARED  gate/up of a shared expert: int8 weights with per-channel
 //              fp32 scales (w8a8.c:1021-1072 with per-token A scales).
 //   DN_ROUTED  down projection of the routed experts: INT4 weights with
@@ -24,13 +21,15 @@
 // tile_off[e]..tile_off[e+1] over rows row_off[e]..row_off[e+1]), so one
 // persistent launch covers every expert whatever the routing produced.
 //
-// Warp roles (14 warps): w0 TMA producer (operands every 128 K, the tile's
-// fp16 group scales once per tile), w1 TMEM allocator + MMA issuer, w2-5
-// unpack (packed INT2/INT4 bytes -> int8 codes in the 128-byte-swizzled
-// K-major layout), w6-13 epilogue (two warps per TMEM lane quarter, one per
-// half of the token columns).
+// Warp roles (23 warps): w0 TMA producer (operands every 128 K, the tile's
+// fp16 group scales once per tile), w1 TMEM allocator + MMA issuer and w22
+// second MMA issuer, w2-5 unpack (packed INT4 bytes -> int8 codes in the
+// 128-byte-swizzled K-major layout), w6-21 epilogue (four warps per TMEM
+// lane quarter, one per quarter of the token columns).
 //
-// Group scales force a drain of the int32 accumulator every 64 K.  The drain
+// Group scales of the down projections (the INT4 weights' and the
+// activations' per-64-K scales) force a drain of the int32 accumulator
+// every 64 K.  The drain
 // is kept cheap and off the tensor core's critical path:
 //   * a ring of 512/BN TMEM accumulators lets the MMAs run several groups
 //     ahead of the epilogue;
@@ -71,18 +70,18 @@ constexpr int kMaxGroups = 64;  // K <= 4096
 constexpr size_t kSmemLimit = 232448;
 static_assert(kBN == (kEpiWarps / 4) * kBH, "four epilogue warps per TMEM lane quarter");
 
-enum Mode { GU_ROUTED = 0, GU_SHARED = 1, DN_ROUTED = 2, DN_SHARED = 3 };
+enum Mode { GU_SHARED = 1, DN_ROUTED = 2, DN_SHARED = 3 };
 
 __host__ __device__ constexpr uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
 template <int MODE>
 struct Cfg {
-    static constexpr bool kGateUp = (MODE == GU_ROUTED || MODE == GU_SHARED);
-    static constexpr bool kPacked = (MODE == GU_ROUTED || MODE == DN_ROUTED);
+    static constexpr bool kGateUp = (MODE == GU_SHARED);
+    static constexpr bool kPacked = (MODE == DN_ROUTED);
     static constexpr bool kDown = !kGateUp;
     static constexpr bool kMagic = (MODE != GU_SHARED);  // 64-K drain units
     static constexpr int kChTile = kGateUp ? 64 : 128;   // output channels per tile
-    static constexpr int kBits = MODE == GU_ROUTED ? 2 : (MODE == DN_ROUTED ? 4 : 8);
+    static constexpr int kBits = MODE == DN_ROUTED ? 4 : 8;
     static constexpr uint32_t kPackedRow = kPacked ? (kBK * kBits / 8) : 0;  // bytes/row/stage
     static constexpr uint32_t kAU = kBM * kBK;  // unpacked operand, 16 KB
     static constexpr uint32_t kX = kBN * kBK;   // token rows, 16 KB
@@ -149,24 +148,6 @@ __device__ __forceinline__ bool epi_sync(uint64_t *bar, uint32_t &phase, volatil
 }
 
 // ---------------------------------------------------------------- unpack
-// 16 INT2 codes (one 32-bit packed word, little-endian along K: code q at
-// bits 2q) -> 16 int8 values c = 2*li - 3, by byte permutes against the
-// table {-3, -1, 1, 3}: the codes are spread into 4-bit selectors, codes
-// {0, 1, 4, 5, 8, 9, 12, 13} from w and {2, 3, 6, 7, 10, 11, 14, 15} from
-// w >> 4 (with the odd codes moved up a nibble).  The 16 values come out in
-// the K order jt::kInt2Order16 (xd rows are stored in the same order).
-__device__ __forceinline__ uint4 unpack_int2_x16(uint32_t w) {
-    constexpr uint32_t kLut = 0x0301FFFDu;  // bytes -3, -1, 1, 3
-    const uint32_t s01 = (w & 0x03030303u) | ((w << 2) & 0x30303030u);
-    const uint32_t s23 = ((w >> 4) & 0x03030303u) | ((w >> 2) & 0x30303030u);
-    uint4 o;
-    o.x = __byte_perm(kLut, kLut, s01);
-    o.y = __byte_perm(kLut, kLut, s01 >> 16);
-    o.z = __byte_perm(kLut, kLut, s23);
-    o.w = __byte_perm(kLut, kLut, s23 >> 16);
-    return o;
-}
-
 // 8 INT4 codes (one 32-bit word; even k in the low nibble) -> 8 int8 values
 // c = 2*li - 15 via ((li << 1) + 113) ^ 0x80 per byte (<= 143, no carry).
 __device__ __forceinline__ uint2 unpack_int4_x8(uint32_t w) {
@@ -182,29 +163,15 @@ __device__ __forceinline__ uint2 unpack_int4_x8(uint32_t w) {
 // One operand row: packed bytes of a 128-K stage -> 128 int8 codes written
 // into the 128-byte-swizzled K-major tile (16-byte chunk i of row r lands in
 // chunk i ^ (r % 8), the layout TMA's 128B swizzle produces).
-template <int BITS>
-__device__ __forceinline__ void unpack_row(const uint8_t *src, uint8_t *dst_tile, int r) {
+__device__ __forceinline__ void unpack_row_int4(const uint8_t *src, uint8_t *dst_tile, int r) {
     uint8_t *row = dst_tile + r * 128;
-    if (BITS == 2) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {  // 16 packed bytes -> 64 codes per pass
-            const uint4 a = *reinterpret_cast<const uint4 *>(src + 16 * h);
-            const uint32_t w[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int chunk = 4 * h + i;
-                *reinterpret_cast<uint4 *>(row + ((chunk ^ (r & 7)) << 4)) = unpack_int2_x16(w[i]);
-            }
-        }
-    } else {
 #pragma unroll 1
-        for (int h = 0; h < 4; ++h) {  // 16 packed bytes -> 32 codes per pass
-            const uint4 a = *reinterpret_cast<const uint4 *>(src + 16 * h);
-            const uint2 l0 = unpack_int4_x8(a.x), h0 = unpack_int4_x8(a.y);
-            const uint2 l1 = unpack_int4_x8(a.z), h1 = unpack_int4_x8(a.w);
-            *reinterpret_cast<uint4 *>(row + (((2 * h) ^ (r & 7)) << 4)) = make_uint4(l0.x, l0.y, h0.x, h0.y);
-            *reinterpret_cast<uint4 *>(row + (((2 * h + 1) ^ (r & 7)) << 4)) = make_uint4(l1.x, l1.y, h1.x, h1.y);
-        }
+    for (int h = 0; h < 4; ++h) {  // 16 packed bytes -> 32 codes per pass
+        const uint4 a = *reinterpret_cast<const uint4 *>(src + 16 * h);
+        const uint2 l0 = unpack_int4_x8(a.x), h0 = unpack_int4_x8(a.y);
+        const uint2 l1 = unpack_int4_x8(a.z), h1 = unpack_int4_x8(a.w);
+        *reinterpret_cast<uint4 *>(row + (((2 * h) ^ (r & 7)) << 4)) = make_uint4(l0.x, l0.y, h0.x, h0.y);
+        *reinterpret_cast<uint4 *>(row + (((2 * h + 1) ^ (r & 7)) << 4)) = make_uint4(l1.x, l1.y, h1.x, h1.y);
     }
 }
 
@@ -236,16 +203,12 @@ __device__ __forceinline__ void fold_chunk(float2 *r2, const uint32_t (&a)[32], 
             rr = make_float2(__int2float_rn((int32_t)a[j]), __int2float_rn((int32_t)a[j + 1]));
         } else {
             const float2 pf = __fadd2_rn(as_f2(a[j], a[j + 1]), make_float2(-kMagicF, -kMagicF));
-            if (MODE == GU_ROUTED) {
-                rr = __ffma2_rn(pf, s2, rr);
-            } else {
-                float2 hv;
-                asm volatile("ld.shared.f32 %0, [%1];" : "=f"(hv.x) : "r"(hv_addr));
-                asm volatile("ld.shared.f32 %0, [%1];" : "=f"(hv.y) : "r"(hv_addr + hv_step));
-                hv_addr += 2u * hv_step;
-                const float2 t = (MODE == DN_ROUTED) ? __fmul2_rn(pf, s2) : pf;
-                rr = __ffma2_rn(t, hv, rr);
-            }
+            float2 hv;
+            asm volatile("ld.shared.f32 %0, [%1];" : "=f"(hv.x) : "r"(hv_addr));
+            asm volatile("ld.shared.f32 %0, [%1];" : "=f"(hv.y) : "r"(hv_addr + hv_step));
+            hv_addr += 2u * hv_step;
+            const float2 t = (MODE == DN_ROUTED) ? __fmul2_rn(pf, s2) : pf;
+            rr = __ffma2_rn(t, hv, rr);
         }
     }
 }
@@ -291,18 +254,13 @@ __device__ __forceinline__ void fold16(float2 *r2, const uint32_t (&a)[16], floa
 #pragma unroll
     for (int j = 0; j < 16; j += 2) {
         float2 &rr = r2[(c0 + j) / 2];
-        if (MODE == GU_ROUTED) {
-            const float2 pf = __fadd2_rn(as_f2(a[j], a[j + 1]), make_float2(-kMagicF, -kMagicF));
-            rr = __ffma2_rn(pf, s2, rr);
-        } else {
-            float2 hv;
-            asm volatile("ld.shared.f32 %0, [%1];" : "=f"(hv.x) : "r"(hv_addr));
-            asm volatile("ld.shared.f32 %0, [%1];" : "=f"(hv.y) : "r"(hv_addr + hv_step));
-            hv_addr += 2u * hv_step;
-            const float2 t = (MODE == DN_ROUTED) ? __ffma2_rn(as_f2(a[j], a[j + 1]), s2, nms2)
-                                                 : __fadd2_rn(as_f2(a[j], a[j + 1]), make_float2(-kMagicF, -kMagicF));
-            rr = __ffma2_rn(t, hv, rr);
-        }
+        float2 hv;
+        asm volatile("ld.shared.f32 %0, [%1];" : "=f"(hv.x) : "r"(hv_addr));
+        asm volatile("ld.shared.f32 %0, [%1];" : "=f"(hv.y) : "r"(hv_addr + hv_step));
+        hv_addr += 2u * hv_step;
+        const float2 t = (MODE == DN_ROUTED) ? __ffma2_rn(as_f2(a[j], a[j + 1]), s2, nms2)
+                                             : __fadd2_rn(as_f2(a[j], a[j + 1]), make_float2(-kMagicF, -kMagicF));
+        rr = __ffma2_rn(t, hv, rr);
     }
 }
 
@@ -376,10 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
         if (C::kGateUp) jt::prefetch_tmap(&p.tmA1);
         jt::prefetch_tmap(&p.tmX);
         jt::prefetch_tmap(&p.tmM);
-        if (C::kPacked) {
-            jt::prefetch_tmap(&p.tmS0);
-            if (C::kGateUp) jt::prefetch_tmap(&p.tmS1);
-        }
+        if (C::kPacked) jt::prefetch_tmap(&p.tmS0);
         if (C::kDown) jt::prefetch_tmap(&p.tmH);
     }
     if (warp == 1) {
@@ -406,8 +361,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
             uint32_t ts = 0, tphase = 0, t_issued = 0, t_phase = 0;
             bool ok = true;
             constexpr uint32_t kTx = C::kX + (C::kPacked ? C::kAP : C::kAU);
-            const uint32_t scale_box = ngroups * (C::kGateUp ? 64 * 2 : 128 * 2);
-            const uint32_t slot_tx = kBN * 16 + (C::kPacked ? (C::kGateUp ? 2 : 1) * scale_box : 0) +
+            const uint32_t scale_box = ngroups * 128 * 2;
+            const uint32_t slot_tx = kBN * 16 + (C::kPacked ? scale_box : 0) +
                                      (MODE == DN_ROUTED ? kBN * p.hs_ld * 4 : 0) +
                                      (MODE == DN_SHARED ? 2 * 256 * ngroups : 0);
             for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
@@ -423,12 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                 st_shared_v4(sl, make_int4(te.x, te.y, te.z, c0));
                 jt::mbar_arrive_expect_tx(&pfull[ts], slot_tx);
                 jt::tma_load_2d(sl + C::kOffMeta, &p.tmM, &pfull[ts], 0, te.y);
-                if (C::kPacked) {
-                    jt::tma_load_2d(sl + C::kOffScale, &p.tmS0, &pfull[ts], c0 * 2, te.x * ngroups);
-                    if (C::kGateUp)
-                        jt::tma_load_2d(sl + C::kOffScale + scale_box, &p.tmS1, &pfull[ts], c0 * 2,
-                                        te.x * ngroups);
-                }
+                if (C::kPacked) jt::tma_load_2d(sl + C::kOffScale, &p.tmS0, &pfull[ts], c0 * 2, te.x * ngroups);
                 if (MODE == DN_ROUTED) jt::tma_load_2d(sl + C::kOffBlk, &p.tmH, &pfull[ts], 0, te.y);
                 if (MODE == DN_SHARED) {  // group-major scales: two [groups][64 rows] boxes
                     jt::tma_load_2d(sl + C::kOffBlk, &p.tmH, &pfull[ts], te.y * 4, 0);
@@ -450,13 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                     uint8_t *xs = st + C::kAU, *ap = xs + C::kX;
                     jt::mbar_arrive_expect_tx(&full[stage], kTx);
                     if (C::kPacked) {
-                        if (C::kGateUp) {
-                            jt::tma_load_2d(ap, &p.tmA0, &full[stage], kb * C::kPackedRow, wrow);
-                            jt::tma_load_2d(ap + 64 * C::kPackedRow, &p.tmA1, &full[stage],
-                                            kb * C::kPackedRow, wrow);
-                        } else {
-                            jt::tma_load_2d(ap, &p.tmA0, &full[stage], kb * C::kPackedRow, wrow);
-                        }
+                        jt::tma_load_2d(ap, &p.tmA0, &full[stage], kb * C::kPackedRow, wrow);
                     } else {
                         if (C::kGateUp) {
                             jt::tma_load_2d(st, &p.tmA0, &full[stage], kb * kBK, wrow);
@@ -584,7 +528,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                         break;
                     }
                     uint8_t *st = stage_ptr(stage);
-                    unpack_row<C::kBits>(st + C::kAU + C::kX + r * C::kPackedRow, st, r);
+                    unpack_row_int4(st + C::kAU + C::kX + r * C::kPackedRow, st, r);
                     jt::fence_proxy_async();
                     __syncwarp();
                     if (lane == 0) jt::mbar_arrive(&ready[stage]);
@@ -622,8 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
             const uint8_t *sl = slot_base + ts * C::kSlot;
             const int4 info = *reinterpret_cast<const int4 *>(sl);  // {e, row0, row_end, c0}
             const float4 *meta = reinterpret_cast<const float4 *>(sl + C::kOffMeta);
-            const __half *sc_ptr = reinterpret_cast<const __half *>(sl + C::kOffScale) +
-                               (C::kGateUp ? ((is_up ? ngroups * 64 : 0) + lch) : lr);
+            const __half *sc_ptr = reinterpret_cast<const __half *>(sl + C::kOffScale) + lr;
             const float *blk = reinterpret_cast<const float *>(sl + C::kOffBlk) + j0 * p.hs_ld;
             // down modes: the four warps of this column quarter transpose the
             // tile's activation group scales of their 32 columns to
@@ -698,8 +641,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
             }
             if (!ok) break;
             if constexpr (C::kGateUp) {
-                float cscale = 1.0f;
-                if (MODE == GU_SHARED) cscale = __ldg(is_up ? &p.cs1[ch] : &p.cs0[ch]);
+                const float cscale = __ldg(is_up ? &p.cs1[ch] : &p.cs0[ch]);
                 // pass 1: stage g and u (activation- and channel-scaled) in SMEM
                 float *dst_tile = h_tile + (is_up ? kBN * 64 : 0);
                 if (active) {
@@ -707,9 +649,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                     for (int j = 0; j < kBH; ++j) {
                         const float xs = meta[j0 + j].x;
                         const float rv = (j & 1) ? r2[j / 2].y : r2[j / 2].x;
-                        dst_tile[(j0 + j) * 64 + lch] = (MODE == GU_ROUTED)
-                                                            ? __fmul_rn(rv, xs)
-                                                            : __fmul_rn(__fmul_rn(rv, xs), cscale);
+                        dst_tile[(j0 + j) * 64 + lch] = __fmul_rn(__fmul_rn(rv, xs), cscale);
                     }
                 }
                 if (!epi_sync(epib, ephase, abort_flag, err)) {
@@ -762,12 +702,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gemm(const __grid_constant_
                             const int row = info.y + j;
                             *reinterpret_cast<uint2 *>(p.hq + (size_t)row * p.n_ch + info.w + 8 * sl) =
                                 make_uint2(wd[0], wd[1]);
-                            if (sl == 0) {
-                                if (MODE == GU_SHARED)
-                                    p.hs[(size_t)(info.w / 64) * p.hs_rows + row] = qb.scale_f;
-                                else
-                                    p.hs[(size_t)row * p.hs_ld + info.w / 64] = qb.scale_f;
-                            }
+                            if (sl == 0) p.hs[(size_t)(info.w / 64) * p.hs_rows + row] = qb.scale_f;
                         }
                     }
                 }
@@ -846,35 +781,6 @@ bool meta_map(CUtensorMap *m, const float4 *row_meta, int rows) {
 }
 
 }  // namespace
-
-// Routed gate/up: wg, wu packed INT2 [E][f][d/4]; gs, us fp16 [E][d/64][f];
-// xd int8 [rows][d] in expert order; writes hq [rows][f] and hs
-// [rows][round_up(f/64, 4)].
-extern "C" int jtk_moe_gateup_routed(const uint8_t *wg, const uint8_t *wu, const void *gs,
-                                     const void *us, int E, int f, int d, const int8_t *xd,
-                                     int rows_cap, const float4 *row_meta, const int4 *tiles,
-                                     const int32_t *ntiles, int8_t *hq, float *hs,
-                                     int max_tiles_hint, cudaStream_t stream) {
-    if (f % 64 || d % kBK || d / 64 > kMaxGroups || E <= 0 || rows_cap <= 0) return -1;
-    MoeGemmParams p{};
-    const uint32_t prow = d / 4, G = d / 64;
-    if (!jt::make_tmap_2d_u8(&p.tmA0, wg, prow, (uint64_t)E * f, prow, 32, 64, false) ||
-        !jt::make_tmap_2d_u8(&p.tmA1, wu, prow, (uint64_t)E * f, prow, 32, 64, false) ||
-        !jt::make_tmap_2d_u8(&p.tmX, xd, d, rows_cap, d, kBK, kBN, true) ||
-        !jt::make_tmap_2d_u8(&p.tmS0, gs, (uint64_t)f * 2, (uint64_t)E * G, (uint64_t)f * 2, 128, G, false) ||
-        !jt::make_tmap_2d_u8(&p.tmS1, us, (uint64_t)f * 2, (uint64_t)E * G, (uint64_t)f * 2, 128, G, false) ||
-        !meta_map(&p.tmM, row_meta, rows_cap))
-        return -2;
-    p.tmH = p.tmM;
-    p.tiles = tiles;
-    p.ntiles = ntiles;
-    p.n_ch = f;
-    p.K = d;
-    p.hs_ld = hs_stride(f);
-    p.hq = hq;
-    p.hs = hs;
-    return launch<GU_ROUTED>(p, max_tiles_hint, stream);
-}
 
 // Routed down: wd packed INT4 [E][d][f/2], ds fp16 [E][f/64][d]; hq [rows][f]
 // with hs [rows][round_up(f/64, 4)]; y[tok][d] += w_row * y_pair (atomic).

@@ -11,25 +11,35 @@
 // (FMA pipe) rather than floor/convert instructions, which issue at a
 // fraction of the FMA rate.
 #pragma once
+#include <cuda_fp16.h>
+
 #include <cstdint>
 
 namespace jt {
 
-// K order inside every 16-byte block of the expert-ordered token rows (xd)
-// that feed the routed gate/up GEMM: position p of the block holds element
-// kInt2Order16[p] of the block, the order in which the INT2 unpack of that
-// GEMM produces the weight codes.  int2_order16 applies it to one block held
-// as four 32-bit words (natural order in, stored order out).
-constexpr int kInt2Order16[16] = {0, 1, 4, 5, 8, 9, 12, 13, 2, 3, 6, 7, 10, 11, 14, 15};
+// K order inside every 16-element block of the expert-ordered token rows
+// (xd, fp16) that feed the routed gate/up GEMM: position p of the block holds
+// element kX16Order[p] = 4 (p % 4) + p / 4 of the block (a 4 x 4 transpose),
+// the order in which that GEMM's INT2 unpack produces the weight values.
+constexpr int kX16Order[16] = {0, 4, 8, 12, 1, 5, 9, 13, 2, 6, 10, 14, 3, 7, 11, 15};
 
-__host__ __device__ __forceinline__ uint4 int2_order16(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3) {
-#ifdef __CUDA_ARCH__
-    return make_uint4(__byte_perm(w0, w1, 0x5410), __byte_perm(w2, w3, 0x5410), __byte_perm(w0, w1, 0x7632),
-                      __byte_perm(w2, w3, 0x7632));
-#else
-    return make_uint4((w0 & 0xFFFFu) | (w1 << 16), (w2 & 0xFFFFu) | (w3 << 16), (w0 >> 16) | (w1 & 0xFFFF0000u),
-                      (w2 >> 16) | (w3 & 0xFFFF0000u));
-#endif
+// Byte i of word a and byte i of word b as the fp16 pair (a_i, b_i) (exact):
+// the byte q is biased to the fp16 bit pattern of 1152 + q, then 1152 is
+// subtracted.
+__device__ __forceinline__ uint32_t x16_pair(uint32_t a, uint32_t b, uint32_t i) {
+    const uint32_t t = __byte_perm(a, b, i | (i << 4) | ((4u + i) << 8) | ((4u + i) << 12));
+    uint32_t r = (t & 0x00FF00FFu) ^ 0x64806480u;
+    const __half2 h = __hsub2(*reinterpret_cast<const __half2 *>(&r), __half2half2(__ushort_as_half(0x6480u)));
+    r = *reinterpret_cast<const uint32_t *>(&h);
+    return r;
+}
+
+// 16 int8 codes in natural order (four little-endian words) -> 16 exact fp16
+// values in kX16Order, positions 0-7 in lo and 8-15 in hi.
+__device__ __forceinline__ void x16_block(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, uint4 &lo,
+                                          uint4 &hi) {
+    lo = make_uint4(x16_pair(w0, w1, 0), x16_pair(w2, w3, 0), x16_pair(w0, w1, 1), x16_pair(w2, w3, 1));
+    hi = make_uint4(x16_pair(w0, w1, 2), x16_pair(w2, w3, 2), x16_pair(w0, w1, 3), x16_pair(w2, w3, 3));
 }
 
 struct QuantBlock {

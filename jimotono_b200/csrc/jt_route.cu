@@ -237,7 +237,7 @@ __global__ void k_sort_scatter(const int32_t *__restrict__ ids, const float *__r
 __global__ void __launch_bounds__(256)
     k_quant_dispatch(const float *__restrict__ x, int T, int d, int k,
                      const int32_t *__restrict__ pos, const float *__restrict__ wfin,
-                     int8_t *__restrict__ xq, float *__restrict__ xs, int8_t *__restrict__ xd,
+                     int8_t *__restrict__ xq, float *__restrict__ xs, uint16_t *__restrict__ xd,
                      float4 *__restrict__ row_meta, float4 *__restrict__ sh_meta, int *err) {
     const int t = blockIdx.x;
     if (t >= T) return;
@@ -307,8 +307,9 @@ __global__ void __launch_bounds__(256)
         return;
     }
     __syncthreads();  // sdst
-    // 16 codes per thread per step: xq in natural order, the kept rows xd in
-    // the K order of the routed gate/up GEMM's INT2 unpack (jt::int2_order16)
+    // 16 codes per thread per step: xq in natural order, the kept rows xd as
+    // exact fp16 values in the K order of the routed gate/up GEMM's INT2
+    // unpack (jt::kX16Order)
     for (int i = threadIdx.x * 16; i < d; i += blockDim.x * 16) {
         float v[16];
         if (vec) {
@@ -330,8 +331,13 @@ __global__ void __launch_bounds__(256)
             w[j >> 2] |= (uint32_t)(uint8_t)(int8_t)jt::quant_code(v[j], qb) << (8 * (j & 3));
         *reinterpret_cast<uint4 *>(xq + (size_t)t * d + i) = make_uint4(w[0], w[1], w[2], w[3]);
         if (nd > 0) {
-            const uint4 pw = jt::int2_order16(w[0], w[1], w[2], w[3]);
-            for (int j = 0; j < nd; ++j) *reinterpret_cast<uint4 *>(xd + (size_t)sdst[j] * d + i) = pw;
+            uint4 lo, hi;
+            jt::x16_block(w[0], w[1], w[2], w[3], lo, hi);
+            for (int j = 0; j < nd; ++j) {
+                uint4 *dst = reinterpret_cast<uint4 *>(xd + (size_t)sdst[j] * d + i);
+                dst[0] = lo;
+                dst[1] = hi;
+            }
         }
     }
 }
@@ -377,7 +383,7 @@ extern "C" int jtk_build_tiles(const int32_t *off, const int32_t *tile_off, int 
 }
 
 extern "C" int jtk_quant_dispatch(const float *x, int T, int d, int k, const int32_t *pos,
-                                  const float *wfin, int8_t *xq, float *xs, int8_t *xd,
+                                  const float *wfin, int8_t *xq, float *xs, uint16_t *xd,
                                   float4 *row_meta, float4 *sh_meta, cudaStream_t stream) {
     if (T <= 0 || d <= 0 || (d % 16) != 0 || k > 64) return -1;
     k_quant_dispatch<<<T, 256, 0, stream>>>(x, T, d, k, pos, wfin, xq, xs, xd, row_meta, sh_meta,

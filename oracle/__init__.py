@@ -118,3 +118,33 @@ def ref() -> C.CDLL:
             fn.argtypes = a
         _REF = h
     return _REF
+
+
+# Tolerances of the routed gate/up output h against this restatement.  The
+# CUDA path accumulates x * fp16_rn(code * scale) in fp32 on the tensor cores
+# (order chosen by the hardware), the restatement in double, so g and u agree
+# to a few fp32 ulps and h's requantization agrees except where a value lies
+# within that distance of a rounding tie.
+H_SCALE_RTOL = 1e-5
+H_FLIP_FRAC = 1e-3
+# The layer output then carries those rare one-step code differences through
+# the down projection: the north_star fp32 tolerance, relative to max |y|.
+Y_RTOL = 1e-3
+
+
+def h_mismatch(hq_got, hs_got, hq_want, hs_want) -> str | None:
+    """None when the requantized h (int8 codes, per-64 scales) agrees within
+    the tolerances above: every scale within H_SCALE_RTOL, every code within
+    one step, and at most H_FLIP_FRAC of the codes differing at all; else a
+    one-line description of the disagreement."""
+    hs_g = np.asarray(hs_got, np.float64).ravel()
+    hs_w = np.asarray(hs_want, np.float64).ravel()
+    if hs_g.shape != hs_w.shape or np.asarray(hq_got).shape != np.asarray(hq_want).shape:
+        return "shape differs"
+    rel = float((np.abs(hs_g - hs_w) / np.maximum(np.abs(hs_w), 1e-30)).max()) if hs_g.size else 0.0
+    dq = np.abs(np.asarray(hq_got, np.int32) - np.asarray(hq_want, np.int32))
+    big = int(dq.max()) if dq.size else 0
+    frac = float((dq != 0).mean()) if dq.size else 0.0
+    if rel > H_SCALE_RTOL or big > 1 or frac > H_FLIP_FRAC:
+        return f"h scales rel {rel:.3g}, max code step {big}, differing codes {frac:.3g}"
+    return None

@@ -371,8 +371,35 @@ void jto_lowbit_gemv(const int8_t *a, float sa, const uint8_t *packed, const uin
 
 /* ------------------------------------------------------------ MoE layer */
 
+/* The gate/up weight of code c (in {-3, -1, 1, 3}) in a group with fp16
+ * scale s: fp16_rn(c * s) (c * s is exact in fp32; +-s needs no rounding). */
+static float gu_weight16(int c, uint16_t s) {
+    return jto_half_to_float(jto_float_to_half((float)c * jto_half_to_float(s)));
+}
+
+/* sum_k x[k] * w16[k] of one packed INT2 row in double (every product and
+ * partial sum exact up to the final rounding: 18-bit products, |sum| < 2^40),
+ * rounded once to fp32: the value the tensor core's fp32 accumulation
+ * approximates. */
+static float gu_dot16(const int8_t *xq, const uint8_t *row, const uint16_t *s_col, int d, int f) {
+    double acc = 0.0;
+    for (int g = 0; g < d / 64; g++) {
+        const uint16_t sg = s_col[(size_t)g * f];
+        float wv[4];
+        for (int li = 0; li < 4; li++) wv[li] = gu_weight16(2 * li - 3, sg);
+        for (int i = 0; i < 64; i++) {
+            const int k = g * 64 + i;
+            const int li = (row[k / 4] >> (2 * (k % 4))) & 3;
+            acc += (double)xq[k] * (double)wv[li];
+        }
+    }
+    return (float)acc;
+}
+
 /* Routed expert e on one quantized token row:
- *   gate/up: fold over 64-groups of fmaf((float)P, s_g, r), then * sa
+ *   gate/up: g = fl32(dot16 * sa) with dot16 = sum_k x[k] * fp16_rn(c_k * s_g(k))
+ *     (gu_dot16; the CUDA path accumulates the same products in fp32 on the
+ *     tensor cores, so it agrees to rounding, not bit for bit)
  *   h = SwiGLU(gate, up); requantize h per 64-channel group (w8a8.c:688-747)
  *   down: per 64-group g: t = (float)P_g * s_g; r = fmaf(t, hs_g, r). */
 static void routed_expert(const jto_moe_dims *dm, const jto_moe_weights *w, int e,
@@ -387,14 +414,8 @@ static void routed_expert(const jto_moe_dims *dm, const jto_moe_weights *w, int 
     const uint16_t *sd = w->sd + (size_t)e * gf * d; /* [g][o] */
     int32_t P[64];
     for (int c = 0; c < f; c++) {
-        jto_lowbit_partials(xq, wg + (size_t)c * (d / 4), 1, d, 2, P);
-        float r = 0.0f;
-        for (int g = 0; g < gd; g++) r = fmaf((float)P[g], jto_half_to_float(sg[(size_t)g * f + c]), r);
-        gbuf[c] = r * xs;
-        jto_lowbit_partials(xq, wu + (size_t)c * (d / 4), 1, d, 2, P);
-        r = 0.0f;
-        for (int g = 0; g < gd; g++) r = fmaf((float)P[g], jto_half_to_float(su[(size_t)g * f + c]), r);
-        ubuf[c] = r * xs;
+        gbuf[c] = gu_dot16(xq, wg + (size_t)c * (d / 4), sg + c, d, f) * xs;
+        ubuf[c] = gu_dot16(xq, wu + (size_t)c * (d / 4), su + c, d, f) * xs;
         hbuf[c] = jto_swiglu(gbuf[c], ubuf[c]);
     }
     jto_quant_blocks(hbuf, 1, f, 64, hq, hs);

@@ -1,7 +1,9 @@
 """Expert-parallel layer on 2 GPUs (NCCL dispatch/combine) against the
 single-GPU layer on the whole batch: routing ids, drops and renormalized
-weights bit-exact, layer output within 1e-5 relative (fp32 atomics; the
-north_star tolerance is 1e-3).  Needs at least two GPUs."""
+weights bit-exact, layer output within the north_star tolerance 1e-3
+relative (fp32 atomics in no fixed order; the tensor cores' fp32 sums of
+the routed gate/up may round differently when a row sits at another
+position of another tile).  Needs at least two GPUs."""
 import json
 import os
 import subprocess
@@ -31,6 +33,6 @@ def test_ep_two_ranks_match_single_gpu(tmp_path, Tl, cf):
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     res = json.loads(out.read_text())
     assert res["ids"] and res["drop"] and res["w"], res
-    assert res["err"] < 1e-5, res
+    assert res["err"] < 1e-3, res
     if cf == 1.0:
         assert res["drops"] > 0

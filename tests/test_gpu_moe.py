@@ -2,11 +2,12 @@
 
 Bit-exact: routing ids, renormalized weights, perm / off / drop (the
 reference's jt_routing_topk + jt_moe_batch_sort semantics), per-token codes
-and scales, and the requantized SwiGLU output h (codes + scales) of every
-kept (token, slot) row - which pins the int32 group partials of gate/up,
-their fp32 fold and the SwiGLU.  The layer output is compared within a
-relative tolerance because the combine adds the k slot contributions with
-fp32 atomics in arbitrary order (north_star tolerance 1e-3; asserted 1e-5).
+and scales.  Within oracle.h_mismatch's tolerances: the requantized SwiGLU
+output h (codes + scales) of every kept (token, slot) row, whose gate/up
+sums of x * fp16 weight the tensor cores (batched) or the integer partials
+(batch-1) form in fp32 in their own order.  The layer output within the
+north_star tolerance 1e-3 of its largest magnitude (the combine also adds
+the k slot contributions with fp32 atomics in arbitrary order).
 """
 import ctypes as C
 
@@ -110,12 +111,11 @@ def test_moe_layer_matches_oracle(T, d, f, E, k, S, fs, cap, zipf):
     assert np.array_equal(got["w"].view(np.uint32), tr["w"].view(np.uint32))
     assert np.array_equal(got["xq"], tr["xq"])
     assert np.array_equal(got["xs"].view(np.uint32), tr["xs"].view(np.uint32))
-    assert np.array_equal(got["hq"], tr["hq"][:kept * f]), \
-        f"hq mismatches {(got['hq'] != tr['hq'][:kept * f]).sum()}"
-    assert np.array_equal(got["hs"].view(np.uint32), tr["hs"][:kept * (f // 64)].view(np.uint32))
+    bad = oracle.h_mismatch(got["hq"], got["hs"], tr["hq"][:kept * f], tr["hs"][:kept * (f // 64)])
+    assert bad is None, bad
     scale = max(float(np.abs(y_ref).max()), 1e-30)
     err = float(np.abs(y_gpu - y_ref).max()) / scale
-    assert err < 1e-5, err
+    assert err < oracle.Y_RTOL, err
     if zipf is not None and cap == 1.0:
         assert tr["drop"].sum() > 0  # the case exercises drops
 

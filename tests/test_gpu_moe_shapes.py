@@ -8,15 +8,15 @@ exactly the values of the full form (tests/test_oracle_pins.py checks that):
 * in full and bit for bit: routing ids and renormalized weights, the
   capacity sort (perm / off / drop, kept count) and the per-token int8
   codes and scales of the activations;
-* bit for bit on a seeded sample of kept (token, slot) rows: the
-  requantized SwiGLU output h (int8 codes and per-64-channel scales), which
-  pins the int32 group partials of the routed gate/up GEMM, their fp32 fold
-  and the SwiGLU of those rows;
+* on a seeded sample of kept (token, slot) rows, within oracle.h_mismatch's
+  tolerances: the requantized SwiGLU output h (int8 codes and per-64-channel
+  scales) of the routed gate/up GEMM, whose fp16-weight products the tensor
+  cores sum in fp32 in their own order (scales within 1e-5, codes within one
+  step, at most 0.1 % of them differing);
 * within tolerance on a seeded sample of tokens: the layer output (routed
-  down projection, weighted combine and shared experts), 1e-5 of the
-  sample's largest magnitude for fp32 output (the combine adds in fp32 in no
-  fixed order) and 1e-2 for bf16 output; the north_star tolerances are 1e-3
-  and 1e-2.
+  down projection, weighted combine and shared experts), the north_star
+  tolerances 1e-3 of the sample's largest magnitude for fp32 output and
+  1e-2 for bf16 output.
 
 Cases: configuration 3 in full (T=4096, d=2048, 256 experts of ffn 1024,
 two shared experts of ffn 2048, Zipf-skewed routing with drops, bf16 and
@@ -128,11 +128,11 @@ def test_moe_layer_benchmarked_shape(name):
         assert np.array_equal(got[n].view(np.uint32), tr[n].view(np.uint32)), n
     if zipf is not None:
         assert tr["drop"].sum() > 0  # the skewed case exercises drops and renormalization
-    assert np.array_equal(got["hq"][rows], hq_ref), f"hq mismatches {(got['hq'][rows] != hq_ref).sum()}"
-    assert np.array_equal(got["hs"][rows].view(np.uint32), hs_ref.view(np.uint32))
+    bad = oracle.h_mismatch(got["hq"][rows], got["hs"][rows], hq_ref, hs_ref)
+    assert bad is None, bad
     scale = max(float(np.abs(y_ref).max()), 1e-30)
     err = float(np.abs(y_gpu[toks] - y_ref).max()) / scale
-    assert err < 1e-5, err
+    assert err < oracle.Y_RTOL, err
 
     if name == "cfg3":  # the configuration's own output type
         y16, _ = gpu_forward(torch, dm, wp, dx, dl, db, bf16=True)
