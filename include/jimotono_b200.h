@@ -384,8 +384,7 @@ enum {
     JT_B200_DBG_DROP = 4,    /* uint8 [T][k] dropped flags */
     JT_B200_DBG_XQ = 5,      /* int8 [T][d] per-token codes */
     JT_B200_DBG_XS = 6,      /* fp32 [T] per-token scales */
-    JT_B200_DBG_HQ = 7,      /* int8 [kept][f] requantized SwiGLU output, perm order */
-    JT_B200_DBG_HS = 8,      /* fp32 [kept][f/64] its scales */
+    JT_B200_DBG_H = 7,       /* bf16 [kept][f] routed SwiGLU output, perm order */
     JT_B200_DBG_META = 9     /* int32 [4]: kept, token tiles, max kept per expert */
 };
 int jt_b200_moe_debug_copy(jt_b200_moe_plan *plan, int what, void *host_dst, size_t bytes);

@@ -85,7 +85,7 @@ struct DecParams {
     const int8_t *wsd;       // [S][d][fs]
     const float *ssd;        // [S][d]
     int d, f, E, k, S, fs;
-    int hs_ld, hs_ld_s;      // row strides of the h scales (routed, shared)
+    int hs_ld_s;             // row stride of the shared h scales
     int n_routed_units;      // k * (f / 64)
     int ksplit;              // K parts of a shared-expert row
     int32_t *acc_s;          // [S][2][fs] shared partial dots (zero between calls)
@@ -93,8 +93,7 @@ struct DecParams {
     // outputs of the gate/up kernel (and debug copies of the batched path)
     int8_t *xq;
     float *xs;
-    int8_t *hq;              // [k][f] routed h codes, rows in expert order
-    float *hs;               // [k][hs_ld]
+    uint16_t *h;             // [k][f] routed h, bf16, rows in expert order
     int8_t *hq_s;            // [S][fs]
     float *hs_s;             // [S][hs_ld_s]
     int32_t *perm, *pos, *off, *tile_off, *meta;
@@ -180,6 +179,18 @@ __device__ __forceinline__ float int2_fold(float acc, int2 pa, __half sg) {
     const float s3 = 3.0f * s;
     const float dt = __half2float(__float2half_rn(s3)) - s3;
     return fmaf((float)pa.y, dt, fmaf((float)pa.x, s, acc));
+}
+
+// SwiGLU of the 64 channels staged in gu, rounded to bf16 into h[0..63]
+// (the routed experts' h).  Warp 0 only.
+__device__ __forceinline__ void swiglu_bf16_64(const float (&gu)[2][64], uint16_t *h, int *err) {
+    const int lane = threadIdx.x & 31;
+    const float h0 = jt::swiglu(gu[0][2 * lane], gu[1][2 * lane]);
+    const float h1 = jt::swiglu(gu[0][2 * lane + 1], gu[1][2 * lane + 1]);
+    const bool bad = !isfinite(h0) || !isfinite(h1);
+    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicExch(err, JT_KERR_NONFINITE);
+    const __nv_bfloat162 v = __floats2bfloat162_rn(h0, h1);
+    reinterpret_cast<uint32_t *>(h)[lane] = *reinterpret_cast<const uint32_t *>(&v);
 }
 
 // grid n_routed_units + S * (fs/64) * ksplit, kGuThreads threads.
@@ -420,7 +431,7 @@ __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant
         __syncthreads();
         if (warp == 0) {
             const int row = slot_rank(sids, p.k, slot);
-            swiglu_requant64(gu, p.hq + (size_t)row * p.f + cb * 64, p.hs + (size_t)row * p.hs_ld + cb, p.err);
+            swiglu_bf16_64(gu, p.h + (size_t)row * p.f + cb * 64, p.err);
         }
         if (blockIdx.x == 0) {
             // the batched path's per-token results for one token
@@ -492,7 +503,7 @@ __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant
 // are padded by 16 bytes so that rows read by neighbouring threads start in
 // different banks.
 struct DnLayout {
-    uint32_t wr, wsc, ws, ssc, hp, hsum, hsr, hqs, hss, racc, sp, bar, total;
+    uint32_t wr, wsc, ws, ssc, hr, hqs, hss, racc, sp, bar, total;
 };
 
 __host__ __device__ inline uint32_t dn_take(uint32_t &o, uint32_t bytes) {
@@ -508,9 +519,7 @@ __host__ __device__ inline DnLayout dn_layout(int k, int f, int S, int fs) {
     L.wsc = dn_take(o, (uint32_t)k * (f / 64) * kDnWarps * 2);     // their fp16 scales [k][f/64][8]
     L.ws = dn_take(o, (uint32_t)S * kDnWarps * (fs + 16));         // shared down rows [S][8], padded
     L.ssc = dn_take(o, (uint32_t)S * kDnWarps * 4);                // their channel scales [S][8]
-    L.hp = dn_take(o, (uint32_t)k * (f / 4 + 4) * 4);              // routed h, permuted words [k], padded
-    L.hsum = dn_take(o, (uint32_t)k * (f / 64) * 4);               // per (row, group) code sums
-    L.hsr = dn_take(o, (uint32_t)k * (f / 64) * 4);                // routed h scales [k][f/64]
+    L.hr = dn_take(o, (uint32_t)k * (2 * f + 16));                 // routed h rows, bf16 [k], padded
     L.hqs = dn_take(o, (uint32_t)S * fs);                          // shared h codes [S][fs]
     L.hss = dn_take(o, (uint32_t)S * (fs / 64) * 4);               // shared h scales [S][fs/64]
     L.racc = dn_take(o, (uint32_t)kDnWarps * k * 4);               // folded routed rows [8][k]
@@ -589,77 +598,47 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constan
         }
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    // ---- h of the routed rows (rank order) permuted for INT4 words: for
-    // packed word w (codes 8w .. 8w+7, even k in the low nibbles) the even
-    // codes {h[8w], h[8w+2], h[8w+4], h[8w+6]} at hp[2w], the odd ones at
-    // hp[2w+1]; per (row, group) code sums; the shared h as stored.  One
-    // pass over 16-byte chunks, every load issued before it is used.
-    uint32_t *hp = reinterpret_cast<uint32_t *>(dsm + L.hp);
-    int *hsum = reinterpret_cast<int *>(dsm + L.hsum);
-    float *hsr = reinterpret_cast<float *>(dsm + L.hsr);
+    // ---- h of the routed rows (bf16, rank order) and the shared h codes
+    // and scales into shared memory: every global load of this phase first,
+    // then the shared-memory writes (one round trip to L2)
+    uint8_t *hr = dsm + L.hr;
     int8_t *hqs = reinterpret_cast<int8_t *>(dsm + L.hqs);
     float *hss = reinterpret_cast<float *>(dsm + L.hss);
-    const int nw = f / 8;    // packed INT4 words per routed row
-    const int nck = f / 16;  // 16-byte chunks of h per routed row (4 per group)
-    // every global load of this phase first, then the shared-memory writes
-    // (one round trip to L2)
-    constexpr int kHq = 4;   // routed h chunks per thread (k * f / 16 <= 1024 below)
-    uint4 hv[kHq];
-    float hsv[2];
+    const int nck = f / 8;   // 16-byte chunks of a routed h row
+    constexpr int kHr = 6;   // routed h chunks per thread (k * f / 8 <= 1536 below)
+    uint4 hv[kHr];
     int4 hqv[2];
     float hssv[2];
-    const int n_hq = k * nck, n_hs = k * gf, n_hqs = S * fs / 16, n_hss = S * (fs / 64);
+    const int n_hr = k * nck, n_hqs = S * fs / 16, n_hss = S * (fs / 64);
 #pragma unroll
-    for (int t = 0; t < kHq; ++t) {
+    for (int t = 0; t < kHr; ++t) {
         const int i = threadIdx.x + t * (int)blockDim.x;
-        const int ii = i < n_hq ? i : 0;
-        hv[t] = *reinterpret_cast<const uint4 *>(p.hq + (size_t)(ii / nck) * f + 16 * (ii % nck));
+        const int ii = i < n_hr ? i : 0;
+        hv[t] = reinterpret_cast<const uint4 *>(p.h + (size_t)(ii / nck) * f)[ii % nck];
     }
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
         const int i = threadIdx.x + t * (int)blockDim.x;
-        if (i < n_hs) hsv[t] = p.hs[(size_t)(i / gf) * p.hs_ld + i % gf];
         if (i < n_hqs) hqv[t] = reinterpret_cast<const int4 *>(p.hq_s + (size_t)(i / (fs / 16)) * fs)[i % (fs / 16)];
         if (i < n_hss) hssv[t] = p.hs_s[(size_t)(i / (fs / 64)) * p.hs_ld_s + i % (fs / 64)];
     }
-    // routed h permuted for INT4 words: for packed word w (codes 8w .. 8w+7,
-    // even k in the low nibbles) the even codes {h[8w], h[8w+2], h[8w+4],
-    // h[8w+6]} at hp[2w], the odd ones at hp[2w+1]; per (row, group) code
-    // sums from the four chunks of a group (four neighbouring lanes)
 #pragma unroll
-    for (int t = 0; t < kHq; ++t) {
+    for (int t = 0; t < kHr; ++t) {
         const int i = threadIdx.x + t * (int)blockDim.x;
-        if (t * (int)blockDim.x >= n_hq) break;  // uniform over the block
-        const uint4 v = hv[t];
-        int sm = __dp4a((int)v.x, 0x01010101, 0);
-        sm = __dp4a((int)v.y, 0x01010101, sm);
-        sm = __dp4a((int)v.z, 0x01010101, sm);
-        sm = __dp4a((int)v.w, 0x01010101, sm);
-        sm += __shfl_xor_sync(0xffffffffu, sm, 1);
-        sm += __shfl_xor_sync(0xffffffffu, sm, 2);
-        if (i < n_hq) {
-            const int rr = i / nck, c = i % nck;
-            uint4 o;
-            o.x = __byte_perm(v.x, v.y, 0x6420);
-            o.y = __byte_perm(v.x, v.y, 0x7531);
-            o.z = __byte_perm(v.z, v.w, 0x6420);
-            o.w = __byte_perm(v.z, v.w, 0x7531);
-            reinterpret_cast<uint4 *>(hp + (size_t)rr * (2 * nw + 4))[c] = o;
-            if ((c & 3) == 0) hsum[rr * gf + c / 4] = sm;
-        }
+        if (i < n_hr) reinterpret_cast<uint4 *>(hr + (size_t)(i / nck) * (2 * f + 16))[i % nck] = hv[t];
     }
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
         const int i = threadIdx.x + t * (int)blockDim.x;
-        if (i < n_hs) hsr[i] = hsv[t];
         if (i < n_hqs) reinterpret_cast<int4 *>(hqs)[i] = hqv[t];
         if (i < n_hss) hss[i] = hssv[t];
     }
     __syncthreads();
     if (!jt::mbar_wait(bar, 0, &abort_flag, p.err)) return;
     // ---- one thread per dot product.  Routed item (slot q, channel j): the
-    // whole INT4 row against its h row, folded over the groups in order
-    // (t = (float)P * s_g; r = fmaf(t, hs_g, r)).  Shared item (128-byte
+    // whole INT4 row, as the bf16 weights bf16_rn(code * bf16_rn(s_g)) of the
+    // batched kernel (jt_moe_dn16.cu), against its bf16 h row, summed in fp32
+    // in k order.  Shared item (128-byte
     // part, expert sh, channel j): the int32 partials of its two groups.
     // Neighbouring threads take neighbouring (padded) rows.
     const uint32_t *wr = reinterpret_cast<const uint32_t *>(dsm + L.wr);
@@ -674,27 +653,30 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constan
         if (it < n_r) {
             const int q = it / kDnWarps, j = it % kDnWarps;
             const int rr = srank[q];
-            const uint4 *row = reinterpret_cast<const uint4 *>(wr + ((size_t)q * kDnWarps + j) * (nw + 4));
-            const uint4 *hrow = reinterpret_cast<const uint4 *>(hp + (size_t)rr * (2 * nw + 4));
+            const uint4 *row = reinterpret_cast<const uint4 *>(wr + ((size_t)q * kDnWarps + j) * (f / 8 + 4));
+            const uint4 *hrow = reinterpret_cast<const uint4 *>(hr + (size_t)rr * (2 * f + 16));
             float acc = 0.0f;
             for (int g = 0; g < gf; ++g) {
-                int part = 0;
+                const __nv_bfloat162 s2 = __bfloat162bfloat162(
+                    __float2bfloat16_rn(__half2float(wsc[((size_t)q * gf + g) * kDnWarps + j])));
 #pragma unroll
-                for (int c = 0; c < 2; ++c) {  // 8 words = 64 codes = one group
+                for (int c = 0; c < 2; ++c) {  // 4 words = 32 codes
                     const uint4 v = row[2 * g + c];
-                    const uint4 h0 = hrow[4 * g + 2 * c], h1 = hrow[4 * g + 2 * c + 1];
-                    part = __dp4a((int)(v.x & 0x0F0F0F0Fu), (int)h0.x, part);
-                    part = __dp4a((int)((v.x >> 4) & 0x0F0F0F0Fu), (int)h0.y, part);
-                    part = __dp4a((int)(v.y & 0x0F0F0F0Fu), (int)h0.z, part);
-                    part = __dp4a((int)((v.y >> 4) & 0x0F0F0F0Fu), (int)h0.w, part);
-                    part = __dp4a((int)(v.z & 0x0F0F0F0Fu), (int)h1.x, part);
-                    part = __dp4a((int)((v.z >> 4) & 0x0F0F0F0Fu), (int)h1.y, part);
-                    part = __dp4a((int)(v.w & 0x0F0F0F0Fu), (int)h1.z, part);
-                    part = __dp4a((int)((v.w >> 4) & 0x0F0F0F0Fu), (int)h1.w, part);
+                    const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {  // 8 codes against 8 h values
+                        uint32_t wb[4];
+                        jt::int4_bf16x8(wv[i], s2, wb);
+                        const uint4 h8 = hrow[8 * g + 4 * c + i];
+                        const uint32_t hb[4] = {h8.x, h8.y, h8.z, h8.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            acc = fmaf(__uint_as_float(hb[e] << 16), __uint_as_float(wb[e] << 16), acc);
+                            acc = fmaf(__uint_as_float(hb[e] & 0xFFFF0000u), __uint_as_float(wb[e] & 0xFFFF0000u),
+                                       acc);
+                        }
+                    }
                 }
-                const int P = 2 * part - 15 * hsum[rr * gf + g];
-                const float t = __fmul_rn((float)P, __half2float(wsc[((size_t)q * gf + g) * kDnWarps + j]));
-                acc = fmaf(t, hsr[rr * gf + g], acc);
             }
             racc[j * k + q] = acc;
         } else {
@@ -746,8 +728,8 @@ extern "C" int jtk_moe_decode(const float *x, const float *logits, const float *
                               const uint8_t *wg, const uint8_t *wu, const void *sg, const void *su,
                               const uint8_t *wd, const void *sd, const int8_t *wsg, const int8_t *wsu,
                               const float *ssg, const float *ssu, const int8_t *wsd, const float *ssd, int d,
-                              int f, int E, int k, int S, int fs, int8_t *xq, float *xs, int8_t *hq, float *hs,
-                              int hs_ld, int8_t *hq_s, float *hs_s, int hs_ld_s, int32_t *acc_s,
+                              int f, int E, int k, int S, int fs, int8_t *xq, float *xs, uint16_t *h,
+                              int8_t *hq_s, float *hs_s, int hs_ld_s, int32_t *acc_s,
                               int32_t *cnt_s, int32_t *perm, int32_t *pos, int32_t *off, int32_t *tile_off,
                               int32_t *meta, uint8_t *drop, float *w_fin, float *y, uint16_t *y_bf16,
                               cudaStream_t stream) {
@@ -758,15 +740,15 @@ extern "C" int jtk_moe_decode(const float *x, const float *logits, const float *
     // bulk copies and 16-byte loads need 16-byte aligned bases
     if (!aligned16(x) || !aligned16(wg) || !aligned16(wu) || !aligned16(sg) || !aligned16(su) ||
         !aligned16(wd) || !aligned16(sd) ||
-        !aligned16(hq) ||
+        !aligned16(h) ||
         (S > 0 && (!aligned16(wsg) || !aligned16(wsu) || !aligned16(wsd) || !aligned16(ssd) || !aligned16(hq_s))))
         return -1;
     const DnLayout L = dn_layout(k, f, S, fs_eff);
     if (L.total > kDnSmemMax) return -1;
-    // the down kernel stages h in one pass of its 256 threads: at most 4
+    // the down kernel stages h in one pass of its 256 threads: at most 6
     // routed chunks and 2 of each shared piece per thread
-    if (k * (f / 16) > 4 * kDnWarps * 32 || k * (f / 64) > 2 * kDnWarps * 32 ||
-        S * fs_eff / 16 > 2 * kDnWarps * 32)
+    if (k * (f / 8) > 6 * kDnWarps * 32 || S * fs_eff / 16 > 2 * kDnWarps * 32 ||
+        S * (fs_eff / 64) > 2 * kDnWarps * 32)
         return -1;
     DecParams p{};
     p.tma = d % 512 == 0;
@@ -797,7 +779,6 @@ extern "C" int jtk_moe_decode(const float *x, const float *logits, const float *
     p.k = k;
     p.S = S;
     p.fs = fs_eff;
-    p.hs_ld = hs_ld;
     p.hs_ld_s = hs_ld_s;
     p.n_routed_units = k * (f / 64);
     // K parts of kSharedPart bytes (half that when d is an odd multiple of 128)
@@ -806,8 +787,7 @@ extern "C" int jtk_moe_decode(const float *x, const float *logits, const float *
     p.cnt_s = cnt_s;
     p.xq = xq;
     p.xs = xs;
-    p.hq = hq;
-    p.hs = hs;
+    p.h = h;
     p.hq_s = hq_s;
     p.hs_s = hs_s;
     p.perm = perm;

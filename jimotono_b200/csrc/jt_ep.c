@@ -65,10 +65,11 @@ struct jt_b200_moe_ep_plan {
     /* exchange: cnt = E expert counts then N token-row counts */
     int32_t *cnt, *cnt_all, *gbase, *own_off, *own_tile_off, *trow, *tsoff;
     int4 *gather, *own_tiles;
-    int8_t *send_tok, *rtok, *own_hq;
+    int8_t *send_tok, *rtok;
+    uint16_t *own_h; /* owned pairs' routed SwiGLU output, bf16 */
     uint16_t *own_x; /* owned pairs' token rows, fp16, expert order (jtk_ep_gather) */
     float4 *rmeta, *own_meta;
-    float *own_hs, *ret, *back;
+    float *ret, *back;
     int R_tok; /* received token rows capacity (T * N) */
     cudaEvent_t ev_counts; /* the gathered counts reached the host buffer */
     /* host (pinned) */
@@ -209,8 +210,8 @@ int jt_b200_moe_ep_plan_create(const jt_b200_moe_dims *dims, jt_b200_ep_comm *co
         {(void **)&p->own_tile_off, (El + 1) * 4},
         {(void **)&p->gather, Nn * El * 16}, {(void **)&p->own_tiles, (R / JT_TILE_ROWS + El + 1) * 16},
         {(void **)&p->rtok, RT * d},         {(void **)&p->own_x, R * d * 2},
-        {(void **)&p->own_hq, R * f},        {(void **)&p->rmeta, R * 16},
-        {(void **)&p->own_meta, R * 16},     {(void **)&p->own_hs, R * (size_t)hs_ld((int)f) * 4},
+        {(void **)&p->own_h, R * f * 2},     {(void **)&p->rmeta, R * 16},
+        {(void **)&p->own_meta, R * 16},
         {(void **)&p->ret, RT * d * 4},      {(void **)&p->back, Tdst * d * 4},
     };
     const size_t nparts = sizeof(parts) / sizeof(parts[0]);
@@ -429,13 +430,12 @@ int jt_b200_moe_ep_forward(jt_b200_moe_ep_plan *p, const jt_b200_moe_weights *w,
     if (own_rows > 0) {
         LAUNCH(jtk_ep_gather(p->gather, N * El, p->rtok, p->rmeta, d, p->own_x, p->own_meta, st));
         LAUNCH(jtk_build_tiles(p->own_off, p->own_tile_off, El, p->own_tiles, st));
-        const int gu_hint = own_tiles * (f / 128), dn_hint = own_tiles * (d / 128);
+        const int gu_hint = own_tiles * (f / 128), dn_hint = own_tiles * ((d + 255) / 256);
         LAUNCH(jtk_moe_gateup_routed(w->wg, w->wu, w->sg, w->su, El, f, d, p->own_x, p->R_max,
-                                     p->own_meta, p->own_tiles, p->own_tile_off + El, p->own_hq,
-                                     p->own_hs, gu_hint, st));
-        LAUNCH(jtk_moe_down_routed(w->wd, w->sd, El, d, f, p->own_hq, p->R_max, p->own_hs,
-                                   p->own_meta, p->own_tiles, p->own_tile_off + El, p->ret, 1,
-                                   dn_hint, st));
+                                     p->own_meta, p->own_tiles, p->own_tile_off + El, p->own_h,
+                                     gu_hint, st));
+        LAUNCH(jtk_moe_down_routed(w->wd, w->sd, El, d, f, p->own_h, p->R_max, p->own_meta,
+                                   p->own_tiles, p->own_tile_off + El, p->ret, 1, dn_hint, st));
     }
 
     /* 5. combine: token rows back to their sources, added into y */
@@ -467,7 +467,7 @@ int jt_b200_moe_ep_debug_copy(jt_b200_moe_ep_plan *p, int what, void *host_dst, 
     case JT_B200_DBG_XQ: src = p->xq; have = (size_t)p->dm.T * p->dm.d; break;
     case JT_B200_DBG_XS: src = p->xs; have = (size_t)p->dm.T * 4; break;
     case JT_B200_DBG_PERM: src = p->perm; have = Tk * 4; break;
-    case JT_B200_DBG_HQ: src = p->own_hq; have = (size_t)p->R_max * p->dm.f; break;
+    case JT_B200_DBG_H: src = p->own_h; have = (size_t)p->R_max * p->dm.f * 2; break;
     case JT_B200_DBG_META: {
         /* kept local pairs, owned rows, owned token tiles, capacity */
         int32_t m[4] = {0, 0, 0, p->cap};

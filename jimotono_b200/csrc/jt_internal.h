@@ -108,18 +108,21 @@ int jtk_quant_dispatch(const float *x, int T, int d, int k, const int32_t *pos,
                        const float *wfin, int8_t *xq, float *xs, uint16_t *xd, float4 *row_meta,
                        float4 *sh_meta, cudaStream_t stream);
 
-/* Expert GEMMs (jt_moe_gemm.cu), JT_TILE_ROWS-row token tiles.  tiles / ntiles: tile
- * table and its length (device).  row_meta [rows]: float4 records above.
- * Group scales fp16 [E][K/64][n_ch]; h scales hs [rows][hs_ld] with
- * hs_ld = round_up(n_ch/64, 4). */
+/* Expert GEMMs, JT_TILE_ROWS-row token tiles.  tiles / ntiles: tile table
+ * and its length (device).  row_meta [rows]: float4 records above.  Group
+ * scales fp16 [E][K/64][n_ch].  Routed gate/up (jt_moe_gu16.cu) writes the
+ * bf16 SwiGLU output h [rows][f]; the shared experts (jt_moe_gemm.cu,
+ * jt_shared_pair.cu) requantize h per (token, 64 channels) with hs
+ * group-major [fs/64][round_up(T, 4)]. */
 int jtk_moe_gateup_routed(const uint8_t *wg, const uint8_t *wu, const void *gs, const void *us,
                           int E, int f, int d, const uint16_t *xd, int rows_cap,
                           const float4 *row_meta, const int4 *tiles, const int32_t *ntiles,
-                          int8_t *hq, float *hs, int max_tiles_hint, cudaStream_t stream);
-/* y_accumulate 1: y[token][:] += w * row (combine into the layer output);
+                          uint16_t *h, int max_tiles_hint, cudaStream_t stream);
+/* Routed down projection (jt_moe_dn16.cu) of the bf16 h rows [rows][f].
+ * y_accumulate 1: y[token][:] += w * row (combine into the layer output);
  * 0: y[row_meta.z][:] = w * row (one output row per routed row). */
-int jtk_moe_down_routed(const uint8_t *wd, const void *ds, int E, int d, int f, const int8_t *hq,
-                        int rows_cap, const float *hs, const float4 *row_meta, const int4 *tiles,
+int jtk_moe_down_routed(const uint8_t *wd, const void *ds, int E, int d, int f, const uint16_t *h,
+                        int rows_cap, const float4 *row_meta, const int4 *tiles,
                         const int32_t *ntiles, float *y, int y_accumulate, int max_tiles_hint,
                         cudaStream_t stream);
 int jtk_moe_gateup_shared(const int8_t *wsg, const int8_t *wsu, const float *ssg,
@@ -172,8 +175,8 @@ int jtk_moe_decode(const float *x, const float *logits, const float *bias, int32
                    const uint8_t *wg, const uint8_t *wu,
                    const void *sg, const void *su, const uint8_t *wd, const void *sd, const int8_t *wsg,
                    const int8_t *wsu, const float *ssg, const float *ssu, const int8_t *wsd, const float *ssd,
-                   int d, int f, int E, int k, int S, int fs, int8_t *xq, float *xs, int8_t *hq, float *hs,
-                   int hs_ld, int8_t *hq_s, float *hs_s, int hs_ld_s, int32_t *acc_s, int32_t *cnt_s,
+                   int d, int f, int E, int k, int S, int fs, int8_t *xq, float *xs, uint16_t *h,
+                   int8_t *hq_s, float *hs_s, int hs_ld_s, int32_t *acc_s, int32_t *cnt_s,
                    int32_t *perm, int32_t *pos, int32_t *off, int32_t *tile_off, int32_t *meta,
                    uint8_t *drop, float *w_fin, float *y, uint16_t *y_bf16, cudaStream_t stream);
 

@@ -47,9 +47,10 @@ struct jt_b200_moe_plan {
     int32_t *ids, *perm, *pos, *hist, *off, *tile_off, *meta, *sh_ntiles;
     int4 *tiles, *sh_tiles;
     float4 *row_meta, *sh_meta;
-    float *w_raw, *w_fin, *xs, *hs, *hs_s, *y32;
+    float *w_raw, *w_fin, *xs, *hs_s, *y32;
     uint8_t *drop;
-    int8_t *xq, *hq, *hq_s;
+    int8_t *xq, *hq_s;
+    uint16_t *h;  /* routed SwiGLU output, bf16 [kept][f] */
     uint16_t *xd; /* kept token rows, fp16, expert order (jtk_quant_dispatch) */
     /* batch-1 path: h codes and scales of every shared expert at once */
     int8_t *hq_d;
@@ -105,11 +106,11 @@ int jt_b200_moe_plan_create(const jt_b200_moe_dims *dims, jt_b200_moe_plan **out
         {(void **)&p->tiles, max_tiles * 16}, {(void **)&p->sh_tiles, (T / JT_TILE_ROWS + 1) * 16},
         {(void **)&p->row_meta, Tk * 16},    {(void **)&p->sh_meta, T * 16},
         {(void **)&p->w_raw, Tk * 4},        {(void **)&p->w_fin, Tk * 4},
-        {(void **)&p->xs, T * 4},            {(void **)&p->hs, Tk * (size_t)hs_ld((int)f) * 4},
+        {(void **)&p->xs, T * 4},
         {(void **)&p->hs_s, ((T + 3) & ~(size_t)3) * (size_t)hs_ld((int)fs) * 4},
         {(void **)&p->y32, T * d * 4},       {(void **)&p->drop, Tk},
         {(void **)&p->xq, T * d},            {(void **)&p->xd, Tk * d * 2},
-        {(void **)&p->hq, Tk * f},           {(void **)&p->hq_s, T * fs},
+        {(void **)&p->h, Tk * f * 2},        {(void **)&p->hq_s, T * fs},
         {(void **)&p->hq_d, (size_t)(dims->S > 0 ? dims->S : 1) * fs},
         {(void **)&p->hs_d, (size_t)(dims->S > 0 ? dims->S : 1) * (size_t)hs_ld((int)fs) * 4},
         {(void **)&p->dec_acc, (size_t)(dims->S > 0 ? dims->S : 1) * 2 * fs * 4},
@@ -291,7 +292,7 @@ int jt_b200_moe_forward(jt_b200_moe_plan *plan, const jt_b200_moe_weights *w, co
         MARK(JT_B200_STAGE_GATEUP);
         const int r = jtk_moe_decode(x, logits, bias, plan->ids, plan->w_raw, w->wg, w->wu, w->sg, w->su, w->wd, w->sd,
                                      w->wsg, w->wsu, w->ssg, w->ssu, w->wsd, w->ssd, d, f, E, k, S, fs,
-                                     plan->xq, plan->xs, plan->hq, plan->hs, hs_ld(f), plan->hq_d,
+                                     plan->xq, plan->xs, plan->h, plan->hq_d,
                                      plan->hs_d, hs_ld(S > 0 ? fs : 64), plan->dec_acc, plan->dec_cnt,
                                      plan->perm, plan->pos, plan->off,
                                      plan->tile_off, plan->meta, plan->drop, plan->w_fin,
@@ -342,16 +343,15 @@ int jt_b200_moe_forward(jt_b200_moe_plan *plan, const jt_b200_moe_weights *w, co
         const long long ne = pairs < E ? pairs : E;
         const long long tl = ne + pairs / JT_TILE_ROWS;
         gu_hint = tl * (f / 128) > 0x7fffffffLL ? 0 : (int)(tl * (f / 128));
-        dn_hint = tl * (d / 128) > 0x7fffffffLL ? 0 : (int)(tl * (d / 128));
+        dn_hint = tl * ((d + 255) / 256) > 0x7fffffffLL ? 0 : (int)(tl * ((d + 255) / 256));
     }
     MARK(JT_B200_STAGE_GATEUP);
     LAUNCH(jtk_moe_gateup_routed(w->wg, w->wu, w->sg, w->su, E, f, d, plan->xd, rows_cap,
-                                 plan->row_meta, plan->tiles, plan->tile_off + E, plan->hq,
-                                 plan->hs, gu_hint, st));
+                                 plan->row_meta, plan->tiles, plan->tile_off + E, plan->h, gu_hint,
+                                 st));
     MARK(JT_B200_STAGE_DOWN);
-    LAUNCH(jtk_moe_down_routed(w->wd, w->sd, E, d, f, plan->hq, rows_cap, plan->hs,
-                               plan->row_meta, plan->tiles, plan->tile_off + E, yf, 1, dn_hint,
-                               st));
+    LAUNCH(jtk_moe_down_routed(w->wd, w->sd, E, d, f, plan->h, rows_cap, plan->row_meta, plan->tiles,
+                               plan->tile_off + E, yf, 1, dn_hint, st));
     MARK(JT_B200_STAGE_OUTPUT);
     if (y_bf16) LAUNCH(jtk_f32_to_bf16(yf, (uint16_t *)y, (size_t)T * d, st));
     MARK(JT_B200_MOE_NSTAGE);
@@ -376,23 +376,7 @@ int jt_b200_moe_debug_copy(jt_b200_moe_plan *plan, int what, void *host_dst, siz
         case JT_B200_DBG_DROP: src = plan->drop; cap = T * k; break;
         case JT_B200_DBG_XQ: src = plan->xq; cap = T * d; break;
         case JT_B200_DBG_XS: src = plan->xs; cap = T * 4; break;
-        case JT_B200_DBG_HQ: src = plan->hq; cap = T * k * f; break;
-        case JT_B200_DBG_HS: {
-            /* stored with a padded row stride; return [rows][f/64] */
-            const size_t G = f / 64, ld = (size_t)hs_ld((int)f);
-            if (bytes % (G * 4) || bytes / (G * 4) > T * k) {
-                errno = EINVAL;
-                return JT_ERR_INVAL;
-            }
-            const size_t rows = bytes / (G * 4);
-            if (cudaDeviceSynchronize() != cudaSuccess ||
-                cudaMemcpy2D(host_dst, G * 4, plan->hs, ld * 4, G * 4, rows,
-                             cudaMemcpyDeviceToHost) != cudaSuccess) {
-                errno = EIO;
-                return JT_ERR_CUDA;
-            }
-            return JT_OK;
-        }
+        case JT_B200_DBG_H: src = plan->h; cap = T * k * f * 2; break;
         case JT_B200_DBG_META: src = plan->meta; cap = 16; break;
         default:
             errno = EINVAL;

@@ -782,35 +782,6 @@ bool meta_map(CUtensorMap *m, const float4 *row_meta, int rows) {
 
 }  // namespace
 
-// Routed down: wd packed INT4 [E][d][f/2], ds fp16 [E][f/64][d]; hq [rows][f]
-// with hs [rows][round_up(f/64, 4)]; y[tok][d] += w_row * y_pair (atomic).
-extern "C" int jtk_moe_down_routed(const uint8_t *wd, const void *ds, int E, int d, int f,
-                                   const int8_t *hq, int rows_cap, const float *hs,
-                                   const float4 *row_meta, const int4 *tiles,
-                                   const int32_t *ntiles, float *y, int y_accumulate,
-                                   int max_tiles_hint, cudaStream_t stream) {
-    if (d % kBM || f % kBK || f / 64 > kMaxGroups || E <= 0 || rows_cap <= 0) return -1;
-    MoeGemmParams p{};
-    const uint32_t prow = f / 2, G = f / 64;
-    const int hs_ld = hs_stride(f);
-    if (!jt::make_tmap_2d_u8(&p.tmA0, wd, prow, (uint64_t)E * d, prow, 64, kBM, false) ||
-        !jt::make_tmap_2d_u8(&p.tmX, hq, f, rows_cap, f, kBK, kBN, true) ||
-        !jt::make_tmap_2d_u8(&p.tmS0, ds, (uint64_t)d * 2, (uint64_t)E * G, (uint64_t)d * 2, 256, G, false) ||
-        !meta_map(&p.tmM, row_meta, rows_cap) ||
-        !jt::make_tmap_2d_u8(&p.tmH, hs, (uint64_t)hs_ld * 4, rows_cap, (uint64_t)hs_ld * 4, hs_ld * 4, kBN, false))
-        return -2;
-    p.tmA1 = p.tmA0;
-    p.tmS1 = p.tmS0;
-    p.tiles = tiles;
-    p.ntiles = ntiles;
-    p.n_ch = d;
-    p.K = f;
-    p.hs_ld = hs_ld;
-    p.y = y;
-    p.y_accumulate = y_accumulate;
-    return launch<DN_ROUTED>(p, max_tiles_hint, stream);
-}
-
 // Shared gate/up (one shared expert): wsg, wsu int8 [fs][d] with per-channel
 // ssg, ssu; x int8 [T][d], sh_meta [T]; writes hq [T][fs] and hs group-major
 // [fs/64][round_up(T, 4)].

@@ -1,7 +1,6 @@
 // jt_moe_gu16.cu - gate/up projection of the routed experts on the sm_100a
 // tensor cores with fp16 operands (tcgen05.mma kind::f16, fp32 TMEM
-// accumulators, TMA operand feed), fused with SwiGLU and the per-(row,
-// 64-channel) requantization of h.
+// accumulators, TMA operand feed), fused with SwiGLU; h leaves as bf16.
 //
 // Arithmetic, for kept row r (token t) of expert e and gate channel c:
 //   w16[c][k] = fp16_rn(code(c, k) * s[k/64][c])   code in {-3, -1, 1, 3}
@@ -10,15 +9,14 @@
 // the weight before the MMA (the product of a code and an fp16 scale is
 // rounded once to fp16; +-1 times the scale is exact), x are the token's
 // int8 codes (exact in fp16), and the K sum runs in fp32 inside the tensor
-// core in an order the hardware chooses.  Then h = SwiGLU(g, u)
-// (moe_layer.c:146-148, jt_swiglu.cuh) and h is requantized per (row, 64
-// channels) with the symmetric int8 rule of w8a8.c:688-747.
+// core in an order the hardware chooses.  Then h = bf16_rn(SwiGLU(g, u))
+// (moe_layer.c:146-148, jt_swiglu.cuh), the routed down projection's input
+// (jt_moe_dn16.cu).
 //
 // Tile: 128 token rows of one expert (MMA M, TMEM lane = token row) x 128
 // channels (MMA N = 256: the 128 gate rows, then the same 128 up rows), so
 // a thread of the epilogue holds the gate and up sums of its token for
-// the same channels and forms SwiGLU and the 64-channel requantization in
-// registers.  One pipeline stage is one 64-K scale group: the token rows as
+// the same channels and forms SwiGLU in registers.  One pipeline stage is one 64-K scale group: the token rows as
 // fp16 (16 KB, 128-byte swizzle), the packed INT2 codes of the 256 weight
 // rows (4 KB) and their fp16 group scales (512 B) arrive by TMA (seven
 // stages in flight); eight unpack warps turn the codes into fp16 weights in
@@ -41,6 +39,7 @@
 // weight row per thread), w10-17 epilogue (two warps per TMEM lane quarter,
 // 64 channels each).  Every wait is a bounded mbarrier wait.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -85,9 +84,7 @@ struct Gu16Params {
     const int4 *tiles;       // {e, row0, row_end, 0}
     const int32_t *ntiles;
     int f, d, G, stages;
-    int hs_ld;
-    int8_t *hq;              // [rows][f]
-    float *hs;               // [rows][hs_ld]
+    uint16_t *h;             // [rows][f] bf16
     int *err;
 };
 
@@ -389,10 +386,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gu16(const __grid_constant_
             }
             jt::tc_fence_after();
             const uint32_t acc = tq + buf * kBN + ch0;
-            // pass 1: h = SwiGLU(g xs, u xs) eight channels at a time, written
-            // back over the gate columns (the accumulator stays held until the
-            // codes are out), and the 64-channel maximum
-            float m = 0.0f;
+            // h = SwiGLU(g xs, u xs) eight channels at a time, stored as bf16
+            uint4 *dst = reinterpret_cast<uint4 *>(p.h + (size_t)(info.y + j) * p.f + info.w + ch0);
             bool bad = false;
 #pragma unroll 2
             for (int c = 0; c < 64; c += 8) {
@@ -401,52 +396,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gu16(const __grid_constant_
                 jt::tmem_ld8(acc + kCh + c, ua);
                 jt::tmem_wait_ld8(ga);
                 jt::tmem_wait_ld8(ua);
+                uint32_t hw[4];
 #pragma unroll
                 for (int i = 0; i < 8; i += 2) {
                     const float2 g2 = make_float2(__fmul_rn(__uint_as_float(ga[i]), xs),
                                                   __fmul_rn(__uint_as_float(ga[i + 1]), xs));
                     const float2 u2 = make_float2(__fmul_rn(__uint_as_float(ua[i]), xs),
                                                   __fmul_rn(__uint_as_float(ua[i + 1]), xs));
-                    float2 hv = jt::swiglu2(g2, u2);
-                    if (!live) hv = make_float2(0.0f, 0.0f);  // rows past the tile: no slow paths
-                    ga[i] = __float_as_uint(hv.x);
-                    ga[i + 1] = __float_as_uint(hv.y);
-                    bad |= !isfinite(hv.x) | !isfinite(hv.y);  // (zero on rows past the tile)
-                    m = fmaxf(m, fmaxf(fabsf(hv.x), fabsf(hv.y)));
+                    const float2 hv = jt::swiglu2(g2, u2);
+                    bad |= live & (!isfinite(hv.x) | !isfinite(hv.y));
+                    const __nv_bfloat162 hb = __floats2bfloat162_rn(hv.x, hv.y);
+                    hw[i / 2] = *reinterpret_cast<const uint32_t *>(&hb);
                 }
-                jt::tmem_st8(acc + c, ga);
-            }
-            jt::tmem_wait_st();
-            if (__any_sync(0xffffffffu, bad) && lane == 0) atomicExch(err, JT_KERR_NONFINITE);
-            // pass 2: the 64 codes of the row, 16 per 16-byte store
-            const jt::QuantBlockF qb = jt::quant_block_f(m);
-            const int row = info.y + j;
-            uint4 *dst = reinterpret_cast<uint4 *>(p.hq + (size_t)row * p.f + info.w + ch0);
-#pragma unroll 1
-            for (int c = 0; c < 64; c += 16) {
-                uint32_t ha[8], hb[8];
-                jt::tmem_ld8(acc + c, ha);
-                jt::tmem_ld8(acc + c + 8, hb);
-                jt::tmem_wait_ld8(ha);
-                jt::tmem_wait_ld8(hb);
-                uint32_t wd[4];
-#pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    wd[i] = (uint32_t)(uint8_t)(int8_t)jt::quant_code_f(__uint_as_float(ha[4 * i]), qb) |
-                            ((uint32_t)(uint8_t)(int8_t)jt::quant_code_f(__uint_as_float(ha[4 * i + 1]), qb) << 8) |
-                            ((uint32_t)(uint8_t)(int8_t)jt::quant_code_f(__uint_as_float(ha[4 * i + 2]), qb) << 16) |
-                            ((uint32_t)(uint8_t)(int8_t)jt::quant_code_f(__uint_as_float(ha[4 * i + 3]), qb) << 24);
-                    wd[2 + i] = (uint32_t)(uint8_t)(int8_t)jt::quant_code_f(__uint_as_float(hb[4 * i]), qb) |
-                                ((uint32_t)(uint8_t)(int8_t)jt::quant_code_f(__uint_as_float(hb[4 * i + 1]), qb) << 8) |
-                                ((uint32_t)(uint8_t)(int8_t)jt::quant_code_f(__uint_as_float(hb[4 * i + 2]), qb) << 16) |
-                                ((uint32_t)(uint8_t)(int8_t)jt::quant_code_f(__uint_as_float(hb[4 * i + 3]), qb) << 24);
-                }
-                if (live) dst[c / 16] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+                if (live) dst[c / 8] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
             }
             jt::tc_fence_before();
             __syncwarp();
             if (lane == 0) jt::mbar_arrive(&tempty[buf]);
-            if (live) p.hs[(size_t)row * p.hs_ld + (info.w + ch0) / 64] = qb.scale_f;
+            if (__any_sync(0xffffffffu, bad) && lane == 0) atomicExch(err, JT_KERR_NONFINITE);
         }
     }
     __syncthreads();
@@ -456,18 +423,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_gu16(const __grid_constant_
     }
 }
 
-int hs_stride(int n_ch) { return ((n_ch / 64) + 3) & ~3; }
-
 }  // namespace
 
 // Routed gate/up: wg, wu packed INT2 [E][f][d/4]; gs, us fp16 [E][d/64][f];
 // xd fp16 [rows][d] in expert order (jt::kX16Order inside every 16-element
-// block); writes hq [rows][f] and hs [rows][round_up(f/64, 4)].
+// block); writes h [rows][f] bf16.
 extern "C" int jtk_moe_gateup_routed(const uint8_t *wg, const uint8_t *wu, const void *gs,
                                      const void *us, int E, int f, int d, const uint16_t *xd,
                                      int rows_cap, const float4 *row_meta, const int4 *tiles,
-                                     const int32_t *ntiles, int8_t *hq, float *hs,
-                                     int max_tiles_hint, cudaStream_t stream) {
+                                     const int32_t *ntiles, uint16_t *h, int max_tiles_hint,
+                                     cudaStream_t stream) {
     if (f % kCh || d % 64 || d / 64 > kMaxGroups || E <= 0 || rows_cap <= 0) return -1;
     const int G = d / 64;
     Gu16Params p{};
@@ -490,9 +455,7 @@ extern "C" int jtk_moe_gateup_routed(const uint8_t *wg, const uint8_t *wu, const
     p.d = d;
     p.G = G;
     p.stages = stages;
-    p.hs_ld = hs_stride(f);
-    p.hq = hq;
-    p.hs = hs;
+    p.h = h;
     p.err = jtk_error_word();
     static bool attr = false;
     if (!attr) {

@@ -11,6 +11,7 @@
 // (FMA pipe) rather than floor/convert instructions, which issue at a
 // fraction of the FMA rate.
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <cstdint>
@@ -40,6 +41,27 @@ __device__ __forceinline__ void x16_block(uint32_t w0, uint32_t w1, uint32_t w2,
                                           uint4 &hi) {
     lo = make_uint4(x16_pair(w0, w1, 0), x16_pair(w2, w3, 0), x16_pair(w0, w1, 1), x16_pair(w2, w3, 1));
     hi = make_uint4(x16_pair(w0, w1, 2), x16_pair(w2, w3, 2), x16_pair(w0, w1, 3), x16_pair(w2, w3, 3));
+}
+
+// Eight INT4 codes (one packed word: element 2b in the low nibble of byte
+// b, 2b + 1 in the high nibble) -> the eight bf16 weights
+// bf16_rn((2 li - 15) * s) in order, as four words, for a scale s already in
+// bf16 (s2 = (s, s)): 2 li is moved into the low byte of each 16-bit lane of
+// 0x4300 (bf16 128 + 2 li, exact), minus 143 gives the code exactly, and one
+// bf16 multiply rounds the product.
+__device__ __forceinline__ void int4_bf16x8(uint32_t w, __nv_bfloat162 s2, uint32_t (&o)[4]) {
+    const uint32_t lo2 = (w << 1) & 0x1E1E1E1Eu;  // 2 li of the even elements, one per byte
+    const uint32_t hi2 = (w >> 3) & 0x1E1E1E1Eu;  // 2 li of the odd elements
+    const uint32_t k143u = 0x430F430Fu;           // bf16 (143, 143)
+    const __nv_bfloat162 k143 = *reinterpret_cast<const __nv_bfloat162 *>(&k143u);
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+        // lanes (low 16 bits, high 16 bits) = bf16 (128 + 2 li_2b, 128 + 2 li_2b+1)
+        const uint32_t t = (__byte_perm(lo2, hi2, b | ((4 + b) << 8)) & 0x00FF00FFu) | 0x43004300u;
+        const __nv_bfloat162 c = __hsub2(*reinterpret_cast<const __nv_bfloat162 *>(&t), k143);
+        const __nv_bfloat162 v = __hmul2(c, s2);
+        o[b] = *reinterpret_cast<const uint32_t *>(&v);
+    }
 }
 
 struct QuantBlock {

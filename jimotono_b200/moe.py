@@ -31,7 +31,8 @@ class MoeWeights(C.Structure):
 
 WEIGHT_FIELDS = ("wg", "wu", "sg", "su", "wd", "sd", "wsg", "wsu", "ssg", "ssu", "wsd", "ssd")
 
-DBG_IDS, DBG_WEIGHTS, DBG_PERM, DBG_OFF, DBG_DROP, DBG_XQ, DBG_XS, DBG_HQ, DBG_HS, DBG_META = range(10)
+DBG_IDS, DBG_WEIGHTS, DBG_PERM, DBG_OFF, DBG_DROP, DBG_XQ, DBG_XS, DBG_H = range(8)
+DBG_META = 9
 
 
 @dataclass

@@ -251,6 +251,21 @@ uint16_t jto_float_to_half(float f) {
     return (uint16_t)(sign | ((uint32_t)he << 10) | (m & 1023u));
 }
 
+float jto_bf16_to_float(uint16_t h) {
+    const uint32_t x = (uint32_t)h << 16;
+    float f;
+    memcpy(&f, &x, 4);
+    return f;
+}
+
+uint16_t jto_float_to_bf16(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    if (isnan(f)) return (uint16_t)((x >> 16) | 0x40u);
+    x += 0x7FFFu + ((x >> 16) & 1u); /* round to nearest even (overflow to inf) */
+    return (uint16_t)(x >> 16);
+}
+
 /* ------------------------------------------------------------ low-bit format */
 
 /* Level rule of lowbit.c:78-88 applied per `group` elements along K. */
@@ -396,14 +411,23 @@ static float gu_dot16(const int8_t *xq, const uint8_t *row, const uint16_t *s_co
     return (float)acc;
 }
 
+/* The down weight of INT4 code li (c = 2 li - 15) in a group with fp16
+ * scale s: bf16_rn(c * bf16_rn(s)) (the product is exact in fp32). */
+static float dn_weight16(int li, uint16_t s) {
+    const float sb = jto_bf16_to_float(jto_float_to_bf16(jto_half_to_float(s)));
+    return jto_bf16_to_float(jto_float_to_bf16((float)(2 * li - 15) * sb));
+}
+
 /* Routed expert e on one quantized token row:
  *   gate/up: g = fl32(dot16 * sa) with dot16 = sum_k x[k] * fp16_rn(c_k * s_g(k))
  *     (gu_dot16; the CUDA path accumulates the same products in fp32 on the
  *     tensor cores, so it agrees to rounding, not bit for bit)
- *   h = SwiGLU(gate, up); requantize h per 64-channel group (w8a8.c:688-747)
- *   down: per 64-group g: t = (float)P_g * s_g; r = fmaf(t, hs_g, r). */
+ *   h = bf16_rn(SwiGLU(gate, up))  (hb: bf16 bits [f])
+ *   down: y[o] = fl32(sum_k h[k] * bf16_rn(c_ok * bf16_rn(s_g(k)[o]))) accumulated in
+ *     double (bf16 x bf16 products are exact), the value the tensor core's
+ *     fp32 accumulation approximates. */
 static void routed_expert(const jto_moe_dims *dm, const jto_moe_weights *w, int e,
-                          const int8_t *xq, float xs, int8_t *hq, float *hs, float *yout,
+                          const int8_t *xq, float xs, uint16_t *hb, float *yout,
                           float *gbuf, float *ubuf, float *hbuf) {
     const int d = dm->d, f = dm->f, gd = d / 64, gf = f / 64;
     const uint8_t *wg = w->wg + (size_t)e * f * (d / 4);
@@ -412,21 +436,25 @@ static void routed_expert(const jto_moe_dims *dm, const jto_moe_weights *w, int 
     const uint16_t *su = w->su + (size_t)e * gd * f;
     const uint8_t *wd = w->wd + (size_t)e * d * (f / 2);
     const uint16_t *sd = w->sd + (size_t)e * gf * d; /* [g][o] */
-    int32_t P[64];
     for (int c = 0; c < f; c++) {
         gbuf[c] = gu_dot16(xq, wg + (size_t)c * (d / 4), sg + c, d, f) * xs;
         ubuf[c] = gu_dot16(xq, wu + (size_t)c * (d / 4), su + c, d, f) * xs;
-        hbuf[c] = jto_swiglu(gbuf[c], ubuf[c]);
+        hb[c] = jto_float_to_bf16(jto_swiglu(gbuf[c], ubuf[c]));
+        hbuf[c] = jto_bf16_to_float(hb[c]);
     }
-    jto_quant_blocks(hbuf, 1, f, 64, hq, hs);
     for (int o = 0; o < d; o++) {
-        jto_lowbit_partials(hq, wd + (size_t)o * (f / 2), 1, f, 4, P);
-        float r = 0.0f;
+        const uint8_t *row = wd + (size_t)o * (f / 2);
+        double acc = 0.0;
         for (int g = 0; g < gf; g++) {
-            const float t = (float)P[g] * jto_half_to_float(sd[(size_t)g * d + o]);
-            r = fmaf(t, hs[g], r);
+            float wv[16];
+            for (int li = 0; li < 16; li++) wv[li] = dn_weight16(li, sd[(size_t)g * d + o]);
+            for (int i = 0; i < 64; i++) {
+                const int k = g * 64 + i;
+                const int li = (row[k / 2] >> (4 * (k % 2))) & 15;
+                acc += (double)hbuf[k] * (double)wv[li];
+            }
         }
-        yout[o] = r;
+        yout[o] = (float)acc;
     }
 }
 
@@ -486,12 +514,13 @@ int jto_moe_forward(const jto_moe_dims *dm, const jto_moe_weights *w, const floa
     float *hbuf = malloc((size_t)fmax_ * sizeof(float));
     int8_t *hqtmp = malloc((size_t)fmax_);
     float *hstmp = malloc((size_t)(fmax_ / 64 + 1) * sizeof(float));
+    uint16_t *hbtmp = malloc((size_t)fmax_ * sizeof(uint16_t));
     float *ypair = malloc(Tk * (size_t)d * sizeof(float));
     float *ys = malloc((size_t)(S > 0 ? S : 1) * T * (size_t)d * sizeof(float));
     double *yacc = calloc((size_t)T * d, sizeof(double));
     int kept = 0;
     if (!ids || !wt || !perm || !off || !drop || !xq || !xs || !gbuf || !ubuf || !hbuf ||
-        !hqtmp || !hstmp || !ypair || !ys || !yacc) {
+        !hqtmp || !hstmp || !hbtmp || !ypair || !ys || !yacc) {
         rc = 1;
         goto out;
     }
@@ -501,10 +530,9 @@ int jto_moe_forward(const jto_moe_dims *dm, const jto_moe_weights *w, const floa
     if (jto_quant_blocks(x, T, d, d, xq, xs)) goto out;
     for (int i = 0; i < kept; i++) {
         const int q = perm[i], t = q / k, e = ids[q];
-        routed_expert(dm, w, e, xq + (size_t)t * d, xs[t], hqtmp, hstmp,
-                      ypair + (size_t)i * d, gbuf, ubuf, hbuf);
-        if (tr && tr->hq) memcpy(tr->hq + (size_t)i * f, hqtmp, (size_t)f);
-        if (tr && tr->hs) memcpy(tr->hs + (size_t)i * (f / 64), hstmp, (size_t)(f / 64) * sizeof(float));
+        routed_expert(dm, w, e, xq + (size_t)t * d, xs[t], hbtmp, ypair + (size_t)i * d, gbuf, ubuf,
+                      hbuf);
+        if (tr && tr->h) memcpy(tr->h + (size_t)i * f, hbtmp, (size_t)f * sizeof(uint16_t));
     }
     for (int s = 0; s < S; s++)
         for (int t = 0; t < T; t++)
@@ -567,6 +595,7 @@ out:
     free(hbuf);
     free(hqtmp);
     free(hstmp);
+    free(hbtmp);
     free(ypair);
     free(ys);
     free(yacc);
@@ -587,8 +616,8 @@ out:
  * token. */
 int jto_moe_forward_sampled(const jto_moe_dims *dm, const jto_moe_weights *w, const float *x,
                             const float *logits, const float *bias, int32_t *rows, int n_rows,
-                            int8_t *hq_rows, float *hs_rows, const int32_t *toks, int n_tok,
-                            float *y_tok, jto_moe_trace *tr) {
+                            uint16_t *h_rows, const int32_t *toks, int n_tok, float *y_tok,
+                            jto_moe_trace *tr) {
     const int T = dm->T, d = dm->d, f = dm->f, E = dm->E, k = dm->k, S = dm->S, fs = dm->fs;
     if (T <= 0 || d <= 0 || f <= 0 || E <= 0 || k <= 0 || k > E || S < 0) return 2;
     if (d % 128 || f % 128 || (S > 0 && fs % 128)) return 2;
@@ -610,10 +639,11 @@ int jto_moe_forward_sampled(const jto_moe_dims *dm, const jto_moe_weights *w, co
     float *hbuf = malloc((size_t)fmax_ * sizeof(float));
     int8_t *hqtmp = malloc((size_t)fmax_);
     float *hstmp = malloc((size_t)(fmax_ / 64 + 1) * sizeof(float));
+    uint16_t *hbtmp = malloc((size_t)fmax_ * sizeof(uint16_t));
     float *yrow = malloc((size_t)d * sizeof(float));
     double *yacc = malloc((size_t)d * sizeof(double));
     if (!ids || !wt || !perm || !off || !drop || !xq || !xs || !gbuf || !ubuf || !hbuf ||
-        !hqtmp || !hstmp || !yrow || !yacc) {
+        !hqtmp || !hstmp || !hbtmp || !yrow || !yacc) {
         rc = 1;
         goto out;
     }
@@ -625,8 +655,7 @@ int jto_moe_forward_sampled(const jto_moe_dims *dm, const jto_moe_weights *w, co
         const int r = (int)((uint32_t)rows[i] % (uint32_t)kept);
         rows[i] = r;
         const int q = perm[r], t = q / k, e = ids[q];
-        routed_expert(dm, w, e, xq + (size_t)t * d, xs[t], hq_rows + (size_t)i * f,
-                      hs_rows + (size_t)i * (f / 64), yrow, gbuf, ubuf, hbuf);
+        routed_expert(dm, w, e, xq + (size_t)t * d, xs[t], h_rows + (size_t)i * f, yrow, gbuf, ubuf, hbuf);
     }
     for (int i = 0; i < n_tok; i++) {
         const int t = toks[i];
@@ -634,8 +663,7 @@ int jto_moe_forward_sampled(const jto_moe_dims *dm, const jto_moe_weights *w, co
         for (int p = 0; p < k; p++) {
             const size_t q = (size_t)t * k + p;
             if (drop[q]) continue;
-            routed_expert(dm, w, ids[q], xq + (size_t)t * d, xs[t], hqtmp, hstmp, yrow, gbuf, ubuf,
-                          hbuf);
+            routed_expert(dm, w, ids[q], xq + (size_t)t * d, xs[t], hbtmp, yrow, gbuf, ubuf, hbuf);
             for (int o = 0; o < d; o++) yacc[o] += (double)wt[q] * (double)yrow[o];
         }
         for (int s = 0; s < S; s++) {
@@ -668,6 +696,7 @@ out:
     free(hbuf);
     free(hqtmp);
     free(hstmp);
+    free(hbtmp);
     free(yrow);
     free(yacc);
     return rc;

@@ -57,6 +57,9 @@ int jto_renorm(float *w, const uint8_t *drop, int T, int k);
 /* fp16 <-> fp32 (IEEE binary16, round to nearest even). */
 float jto_half_to_float(uint16_t h);
 uint16_t jto_float_to_half(float f);
+/* bf16 <-> fp32 (round to nearest even; NaN stays NaN). */
+float jto_bf16_to_float(uint16_t h);
+uint16_t jto_float_to_bf16(float f);
 
 /* Pack fp32 weights W [rows][K] into odd-symmetric `bits`-bit codes with
  * one fp16 scale per `group` elements: per group maxa = max|w|, level rule
@@ -108,8 +111,7 @@ typedef struct jto_moe_trace {
     uint8_t *drop;    /* [T*k] */
     int8_t *xq;       /* [T][d] */
     float *xs;        /* [T] */
-    int8_t *hq;       /* [kept][f]   (perm order) */
-    float *hs;        /* [kept][f/64] */
+    uint16_t *h;      /* [kept][f] routed SwiGLU output, bf16 bits (perm order) */
     float *ypair;     /* [kept][d]  expert output before weighting */
     float *yshared;   /* [T][d]     sum of shared experts */
     int kept;
@@ -121,13 +123,14 @@ int jto_moe_forward(const jto_moe_dims *dm, const jto_moe_weights *w, const floa
 
 /* Sampled form for the benchmarked shapes: routing, sort, renormalization
  * and token quantization in full (trace ids/w/perm/off/drop/xq/xs/kept);
- * hq/hs only for the kept rows rows[i] % kept (index written back), the
- * output only for the tokens toks[i] (y_tok [n_tok][d]).  Same values as
- * jto_moe_forward for those rows and tokens. */
+ * the routed h (bf16) only for the kept rows rows[i] % kept (index written
+ * back) -> h_rows [n_rows][f], the output only for the tokens toks[i]
+ * (y_tok [n_tok][d]).  Same values as jto_moe_forward for those rows and
+ * tokens. */
 int jto_moe_forward_sampled(const jto_moe_dims *dm, const jto_moe_weights *w, const float *x,
                             const float *logits, const float *bias, int32_t *rows, int n_rows,
-                            int8_t *hq_rows, float *hs_rows, const int32_t *toks, int n_tok,
-                            float *y_tok, jto_moe_trace *trace);
+                            uint16_t *h_rows, const int32_t *toks, int n_tok, float *y_tok,
+                            jto_moe_trace *trace);
 
 #ifdef __cplusplus
 }

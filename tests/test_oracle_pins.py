@@ -302,9 +302,9 @@ def test_sampled_layer_equals_full_layer():
     full = {"ids": np.zeros(Tk, np.int32), "w": np.zeros(Tk, np.float32), "perm": np.zeros(Tk, np.int32),
             "off": np.zeros(dm.E + 1, np.int32), "drop": np.zeros(Tk, np.uint8),
             "xq": np.zeros(dm.T * dm.d, np.int8), "xs": np.zeros(dm.T, np.float32),
-            "hq": np.zeros(Tk * dm.f, np.int8), "hs": np.zeros(Tk * dm.f // 64, np.float32)}
+            "h": np.zeros(Tk * dm.f, np.uint16)}
     ft = oracle.MoeTrace(*[full[n].ctypes.data for n in ("ids", "w", "perm", "off", "drop", "xq", "xs",
-                                                         "hq", "hs")], None, None, 0)
+                                                         "h")], None, None, 0)
     y = np.zeros((dm.T, dm.d), np.float32)
     o = oracle.oracle()
     assert o.jto_moe_forward(C.byref(od), C.byref(ow), P(x), P(logits), P(bias), P(y), C.byref(ft)) == 0
@@ -312,21 +312,18 @@ def test_sampled_layer_equals_full_layer():
     assert full["drop"].sum() > 0
     samp = {n: np.zeros_like(full[n]) for n in ("ids", "w", "perm", "off", "drop", "xq", "xs")}
     st = oracle.MoeTrace(*[samp[n].ctypes.data for n in ("ids", "w", "perm", "off", "drop", "xq", "xs")],
-                         None, None, None, None, 0)
+                         None, None, None, 0)
     rows = np.array([0, 5, kept - 1, kept + 3, 2**31 - 2], np.int32)
     toks = np.array([0, 17, dm.T - 1], np.int32)
-    hq = np.zeros((len(rows), dm.f), np.int8)
-    hs = np.zeros((len(rows), dm.f // 64), np.float32)
+    h = np.zeros((len(rows), dm.f), np.uint16)
     ys = np.zeros((len(toks), dm.d), np.float32)
     assert o.jto_moe_forward_sampled(C.byref(od), C.byref(ow), P(x), P(logits), P(bias), P(rows), len(rows),
-                                     P(hq), P(hs), P(toks), len(toks), P(ys), C.byref(st)) == 0
+                                     P(h), P(toks), len(toks), P(ys), C.byref(st)) == 0
     assert st.kept == kept
     for n in ("ids", "w", "off", "drop", "xq", "xs"):
         assert np.array_equal(samp[n], full[n]), n
     assert np.array_equal(samp["perm"][:kept], full["perm"][:kept])
     assert list(rows) == [0, 5, kept - 1, 3, (2**31 - 2) % kept]
-    fhq = full["hq"].reshape(Tk, dm.f)
-    fhs = full["hs"].reshape(Tk, dm.f // 64)
-    assert np.array_equal(hq, fhq[rows])
-    assert np.array_equal(hs.view(np.uint32), fhs[rows].view(np.uint32))
+    fh = full["h"].reshape(Tk, dm.f)
+    assert np.array_equal(h, fh[rows])
     assert np.array_equal(ys.view(np.uint32), y[toks].view(np.uint32))
