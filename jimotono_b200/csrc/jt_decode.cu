@@ -85,7 +85,6 @@ struct DecParams {
     const int8_t *wsd;       // [S][d][fs]
     const float *ssd;        // [S][d]
     int d, f, E, k, S, fs;
-    int hs_ld_s;             // row stride of the shared h scales
     int n_routed_units;      // k * (f / 64)
     int ksplit;              // K parts of a shared-expert row
     int32_t *acc_s;          // [S][2][fs] shared partial dots (zero between calls)
@@ -94,8 +93,7 @@ struct DecParams {
     int8_t *xq;
     float *xs;
     uint16_t *h;             // [k][f] routed h, bf16, rows in expert order
-    int8_t *hq_s;            // [S][fs]
-    float *hs_s;             // [S][hs_ld_s]
+    uint16_t *hb_s;          // [S][fs] shared h, bf16
     int32_t *perm, *pos, *off, *tile_off, *meta;
     uint8_t *drop;
     float *w_fin;
@@ -120,25 +118,6 @@ __device__ __forceinline__ int slot_rank(const int32_t *ids, int k, int p) {
     int r = 0;
     for (int q = 0; q < k; ++q) r += ids[q] < e;
     return r;
-}
-
-// SwiGLU of the 64 channels staged in gu (scaled gate, scaled up), the
-// requantization of h over the 64 channels (w8a8.c:688-747), codes to
-// hq[0..63] and the scale to *hs.  Warp 0 only.
-__device__ __forceinline__ void swiglu_requant64(const float (&gu)[2][64], int8_t *hq, float *hs, int *err) {
-    const int lane = threadIdx.x & 31;
-    const float h0 = jt::swiglu(gu[0][2 * lane], gu[1][2 * lane]);
-    const float h1 = jt::swiglu(gu[0][2 * lane + 1], gu[1][2 * lane + 1]);
-    const bool bad = !isfinite(h0) || !isfinite(h1);
-    float m = fmaxf(fabsf(h0), fabsf(h1));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicExch(err, JT_KERR_NONFINITE);
-    const jt::QuantBlockF qb = jt::quant_block_f(m);
-    const int q0 = jt::quant_code_f(h0, qb), q1 = jt::quant_code_f(h1, qb);
-    *reinterpret_cast<uint16_t *>(hq + 2 * lane) =
-        (uint16_t)(uint8_t)(int8_t)q0 | ((uint16_t)(uint8_t)(int8_t)q1 << 8);
-    if (lane == 0) *hs = qb.scale_f;
 }
 
 // Group partials of one INT2 group (16 packed bytes, codes li little-endian
@@ -496,7 +475,7 @@ __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant
     gu[up][r & 63] = __fmul_rn(__fmul_rn(__int2float_rn(total), xs), cs);
     __syncthreads();
     if (warp == 0)
-        swiglu_requant64(gu, p.hq_s + (size_t)s * p.fs + cb * 64, p.hs_s + (size_t)s * p.hs_ld_s + cb, p.err);
+        swiglu_bf16_64(gu, p.hb_s + (size_t)s * p.fs + cb * 64, p.err);
 }
 
 // Layout of the down kernel's dynamic shared memory (byte offsets).  Rows
@@ -521,7 +500,7 @@ __host__ __device__ inline DnLayout dn_layout(int k, int f, int S, int fs) {
     L.ssc = dn_take(o, (uint32_t)S * kDnWarps * 4);                // their channel scales [S][8]
     L.hr = dn_take(o, (uint32_t)k * (2 * f + 16));                 // routed h rows, bf16 [k], padded
     L.hqs = dn_take(o, (uint32_t)S * fs);                          // shared h codes [S][fs]
-    L.hss = dn_take(o, (uint32_t)S * (fs / 64) * 4);               // shared h scales [S][fs/64]
+    L.hss = dn_take(o, (uint32_t)S * 4);                           // shared h row scales [S]
     L.racc = dn_take(o, (uint32_t)kDnWarps * k * 4);               // folded routed rows [8][k]
     L.sp = dn_take(o, (uint32_t)kDnWarps * S * (fs / 64) * 4);     // shared group partials [8][S][fs/64]
     L.bar = dn_take(o, 8);
@@ -538,6 +517,7 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constan
     __shared__ uint32_t taken[kMaxE / 32];
     __shared__ int32_t sids[64], ssel[64], srank[64];
     __shared__ float sw[64], sselv[64];
+    __shared__ unsigned smax[8];  // shared h row maxima (float bits), S <= 8
     __shared__ int abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int d = p.d, f = p.f, fs = p.fs, k = p.k, S = p.S, gf = f / 64;
@@ -548,6 +528,7 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constan
         sids[threadIdx.x] = threadIdx.x;
         sw[threadIdx.x] = 0.0f;
     }
+    if (threadIdx.x < 8) smax[threadIdx.x] = 0u;
     if (threadIdx.x == 0) {
         abort_flag = 0;
         jt::mbar_init(bar, 1);
@@ -598,18 +579,18 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constan
         }
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    // ---- h of the routed rows (bf16, rank order) and the shared h codes
-    // and scales into shared memory: every global load of this phase first,
-    // then the shared-memory writes (one round trip to L2)
+    // ---- h of the routed rows (bf16, rank order) into shared memory; the
+    // shared h rows (bf16) quantized per row (w8a8.c:688-747 over the fs
+    // channels, one scale per shared expert) into shared memory.  Every
+    // global load of this phase first (one round trip to L2).
     uint8_t *hr = dsm + L.hr;
     int8_t *hqs = reinterpret_cast<int8_t *>(dsm + L.hqs);
     float *hss = reinterpret_cast<float *>(dsm + L.hss);
     const int nck = f / 8;   // 16-byte chunks of a routed h row
     constexpr int kHr = 6;   // routed h chunks per thread (k * f / 8 <= 1536 below)
-    uint4 hv[kHr];
-    int4 hqv[2];
-    float hssv[2];
-    const int n_hr = k * nck, n_hqs = S * fs / 16, n_hss = S * (fs / 64);
+    constexpr int kHs = 4;   // shared h chunks per thread (S * fs / 8 <= 1024 below)
+    uint4 hv[kHr], sv[kHs];
+    const int n_hr = k * nck, n_hs = S * fs / 8;
 #pragma unroll
     for (int t = 0; t < kHr; ++t) {
         const int i = threadIdx.x + t * (int)blockDim.x;
@@ -617,21 +598,46 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constan
         hv[t] = reinterpret_cast<const uint4 *>(p.h + (size_t)(ii / nck) * f)[ii % nck];
     }
 #pragma unroll
-    for (int t = 0; t < 2; ++t) {
+    for (int t = 0; t < kHs; ++t) {
         const int i = threadIdx.x + t * (int)blockDim.x;
-        if (i < n_hqs) hqv[t] = reinterpret_cast<const int4 *>(p.hq_s + (size_t)(i / (fs / 16)) * fs)[i % (fs / 16)];
-        if (i < n_hss) hssv[t] = p.hs_s[(size_t)(i / (fs / 64)) * p.hs_ld_s + i % (fs / 64)];
+        if (i < n_hs) sv[t] = reinterpret_cast<const uint4 *>(p.hb_s)[i];
     }
 #pragma unroll
     for (int t = 0; t < kHr; ++t) {
         const int i = threadIdx.x + t * (int)blockDim.x;
         if (i < n_hr) reinterpret_cast<uint4 *>(hr + (size_t)(i / nck) * (2 * f + 16))[i % nck] = hv[t];
     }
+    // row maxima of the shared h (|bf16| as float bits order like the values)
 #pragma unroll
-    for (int t = 0; t < 2; ++t) {
+    for (int t = 0; t < kHs; ++t) {
         const int i = threadIdx.x + t * (int)blockDim.x;
-        if (i < n_hqs) reinterpret_cast<int4 *>(hqs)[i] = hqv[t];
-        if (i < n_hss) hss[i] = hssv[t];
+        if (i < n_hs) {
+            const uint32_t w4[4] = {sv[t].x, sv[t].y, sv[t].z, sv[t].w};
+            float m = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                m = fmaxf(m, fmaxf(fabsf(__uint_as_float(w4[e] << 16)), fabsf(__uint_as_float(w4[e] & 0xFFFF0000u))));
+            atomicMax(&smax[i / (fs / 8)], __float_as_uint(m));
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < kHs; ++t) {
+        const int i = threadIdx.x + t * (int)blockDim.x;
+        if (i < n_hs) {
+            const int sh = i / (fs / 8);
+            const jt::QuantBlock qb = jt::quant_block(__uint_as_float(smax[sh]));
+            const uint32_t w4[4] = {sv[t].x, sv[t].y, sv[t].z, sv[t].w};
+            uint32_t q[2] = {0u, 0u};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int q0 = jt::quant_code(__uint_as_float(w4[e] << 16), qb);
+                const int q1 = jt::quant_code(__uint_as_float(w4[e] & 0xFFFF0000u), qb);
+                q[e >> 1] |= ((uint32_t)(uint8_t)(int8_t)q0 | ((uint32_t)(uint8_t)(int8_t)q1 << 8)) << (16 * (e & 1));
+            }
+            reinterpret_cast<uint2 *>(hqs)[i] = make_uint2(q[0], q[1]);
+            if (i % (fs / 8) == 0) hss[sh] = qb.scale_f;
+        }
     }
     __syncthreads();
     if (!jt::mbar_wait(bar, 0, &abort_flag, p.err)) return;
@@ -702,16 +708,17 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constan
     __syncthreads();
     // ---- one thread per output channel: the combine in double, routed rows
     // in slot order (moe_layer.c:1443-1463), then the shared experts in s
-    // order, each folded over its groups (moe_layer.c:1549-1559)
+    // order (moe_layer.c:1549-1559), each ((float)acc * hs) * ssd[o] with its
+    // exact int32 dot summed over the groups
     if (threadIdx.x >= kDnWarps) return;
     const int j = threadIdx.x, o = o0 + j;
     if (o >= d) return;
     double ya = 0.0;
     for (int q = 0; q < k; ++q) ya = __dadd_rn(ya, __dmul_rn((double)sw[q], (double)racc[j * k + q]));
     for (int sh = 0; sh < S; ++sh) {
-        float acc = 0.0f;
-        for (int g = 0; g < gs; ++g) acc = fmaf((float)sp[(j * S + sh) * gs + g], hss[sh * gs + g], acc);
-        ya = __dadd_rn(ya, (double)__fmul_rn(acc, ssc[sh * kDnWarps + j]));
+        int acc = 0;
+        for (int g = 0; g < gs; ++g) acc += sp[(j * S + sh) * gs + g];
+        ya = __dadd_rn(ya, (double)__fmul_rn(__fmul_rn((float)acc, hss[sh]), ssc[sh * kDnWarps + j]));
     }
     const float yv = (float)ya;
     if (p.y) p.y[o] = yv;
@@ -729,7 +736,7 @@ extern "C" int jtk_moe_decode(const float *x, const float *logits, const float *
                               const uint8_t *wd, const void *sd, const int8_t *wsg, const int8_t *wsu,
                               const float *ssg, const float *ssu, const int8_t *wsd, const float *ssd, int d,
                               int f, int E, int k, int S, int fs, int8_t *xq, float *xs, uint16_t *h,
-                              int8_t *hq_s, float *hs_s, int hs_ld_s, int32_t *acc_s,
+                              uint16_t *hb_s, int32_t *acc_s,
                               int32_t *cnt_s, int32_t *perm, int32_t *pos, int32_t *off, int32_t *tile_off,
                               int32_t *meta, uint8_t *drop, float *w_fin, float *y, uint16_t *y_bf16,
                               cudaStream_t stream) {
@@ -741,15 +748,13 @@ extern "C" int jtk_moe_decode(const float *x, const float *logits, const float *
     if (!aligned16(x) || !aligned16(wg) || !aligned16(wu) || !aligned16(sg) || !aligned16(su) ||
         !aligned16(wd) || !aligned16(sd) ||
         !aligned16(h) ||
-        (S > 0 && (!aligned16(wsg) || !aligned16(wsu) || !aligned16(wsd) || !aligned16(ssd) || !aligned16(hq_s))))
+        (S > 0 && (!aligned16(wsg) || !aligned16(wsu) || !aligned16(wsd) || !aligned16(ssd) || !aligned16(hb_s))))
         return -1;
     const DnLayout L = dn_layout(k, f, S, fs_eff);
     if (L.total > kDnSmemMax) return -1;
     // the down kernel stages h in one pass of its 256 threads: at most 6
-    // routed chunks and 2 of each shared piece per thread
-    if (k * (f / 8) > 6 * kDnWarps * 32 || S * fs_eff / 16 > 2 * kDnWarps * 32 ||
-        S * (fs_eff / 64) > 2 * kDnWarps * 32)
-        return -1;
+    // routed and 4 shared 16-byte chunks per thread
+    if (k * (f / 8) > 6 * kDnWarps * 32 || S * fs_eff / 8 > 4 * kDnWarps * 32 || S > 8) return -1;
     DecParams p{};
     p.tma = d % 512 == 0;
     if (p.tma && (!jt::make_tmap_2d_u8(&p.tmG, wg, (uint64_t)(d / 4), (uint64_t)E * f, (uint64_t)(d / 4), 128, 64, true) ||
@@ -779,7 +784,6 @@ extern "C" int jtk_moe_decode(const float *x, const float *logits, const float *
     p.k = k;
     p.S = S;
     p.fs = fs_eff;
-    p.hs_ld_s = hs_ld_s;
     p.n_routed_units = k * (f / 64);
     // K parts of kSharedPart bytes (half that when d is an odd multiple of 128)
     p.ksplit = d % kSharedPart == 0 ? d / kSharedPart : d / (kSharedPart / 2);
@@ -788,8 +792,7 @@ extern "C" int jtk_moe_decode(const float *x, const float *logits, const float *
     p.xq = xq;
     p.xs = xs;
     p.h = h;
-    p.hq_s = hq_s;
-    p.hs_s = hs_s;
+    p.hb_s = hb_s;
     p.perm = perm;
     p.pos = pos;
     p.off = off;

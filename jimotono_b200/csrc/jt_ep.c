@@ -56,12 +56,14 @@ struct jt_b200_moe_ep_plan {
     void *arena;
     size_t arena_bytes;
     /* local routing and dispatch */
-    int32_t *ids, *perm, *pos, *hist, *off, *tile_off, *meta, *sh_ntiles;
-    int4 *tiles, *sh_tiles;
+    int32_t *ids, *perm, *pos, *hist, *off, *tile_off, *meta;
+    int4 *tiles;
     float4 *row_meta, *sh_meta;
     float *w_raw, *w_fin, *xs, *hs_s, *y32;
     uint8_t *drop;
     int8_t *xq, *hq_s;
+    uint16_t *hb_s;   /* shared experts' SwiGLU output, bf16 [T][fs] */
+    float *g32, *u32; /* shared gate / up in fp32 [min(T, 255)][fs] (T < 256 only) */
     /* exchange: cnt = E expert counts then N token-row counts */
     int32_t *cnt, *cnt_all, *gbase, *own_off, *own_tile_off, *trow, *tsoff;
     int4 *gather, *own_tiles;
@@ -78,7 +80,6 @@ struct jt_b200_moe_ep_plan {
 };
 
 static size_t align_up(size_t v) { return (v + 255) & ~(size_t)255; }
-static int hs_ld(int n_ch) { return ((n_ch / 64) + 3) & ~3; }
 
 static int nccl_fail(const char *what, int r) {
     const jt_nccl_api *nc = jt_nccl();
@@ -195,12 +196,13 @@ int jt_b200_moe_ep_plan_create(const jt_b200_moe_dims *dims, jt_b200_ep_comm *co
         {(void **)&p->ids, Tk * 4},          {(void **)&p->perm, Tk * 4},
         {(void **)&p->pos, Tk * 4},          {(void **)&p->hist, nch * E * 4},
         {(void **)&p->off, (E + 1) * 4},     {(void **)&p->tile_off, (E + 1) * 4},
-        {(void **)&p->meta, 64},             {(void **)&p->sh_ntiles, 64},
+        {(void **)&p->meta, 64},
         {(void **)&p->tiles, (Tk / JT_TILE_ROWS + E + 1) * 16},
-        {(void **)&p->sh_tiles, (T / JT_TILE_ROWS + 1) * 16},
         {(void **)&p->row_meta, Tk * 16},    {(void **)&p->sh_meta, T * 16},
         {(void **)&p->w_raw, Tk * 4},        {(void **)&p->w_fin, Tk * 4},
-        {(void **)&p->xs, T * 4},            {(void **)&p->hs_s, ((T + 3) & ~(size_t)3) * (size_t)hs_ld((int)fs) * 4},
+        {(void **)&p->xs, T * 4},            {(void **)&p->hs_s, T * 4},
+        {(void **)&p->hb_s, T * fs * 2},
+        {(void **)&p->g32, (T < 255 ? T : 255) * fs * 4}, {(void **)&p->u32, (T < 255 ? T : 255) * fs * 4},
         {(void **)&p->y32, T * d * 4},       {(void **)&p->drop, Tk},
         {(void **)&p->xq, T * d},            {(void **)&p->send_tok, Tdst * d},
         {(void **)&p->hq_s, T * fs},
@@ -339,16 +341,8 @@ int jt_b200_moe_ep_forward(jt_b200_moe_ep_plan *p, const jt_b200_moe_weights *w,
     LAUNCH(jtk_quant_dispatch(x, T, d, k, NULL, p->w_raw, p->xq, p->xs, NULL, NULL,
                               S > 0 ? p->sh_meta : NULL, st));
     if (S > 0) {
-        LAUNCH(jtk_fill_single_tiles(p->sh_tiles, p->sh_ntiles, T, st));
-        for (int s = 0; s < S; s++) {
-            LAUNCH(jtk_moe_gateup_shared(w->wsg + (size_t)s * fs * d, w->wsu + (size_t)s * fs * d,
-                                         w->ssg + (size_t)s * fs, w->ssu + (size_t)s * fs, fs, d,
-                                         p->xq, T, p->sh_meta, p->sh_tiles, p->sh_ntiles, p->hq_s,
-                                         p->hs_s, st));
-            LAUNCH(jtk_moe_down_shared(w->wsd + (size_t)s * d * fs, w->ssd + (size_t)s * d, d, fs,
-                                       p->hq_s, T, p->hs_s, p->sh_meta, p->sh_tiles, p->sh_ntiles,
-                                       yf, s > 0, st));
-        }
+        LAUNCH(jtk_moe_shared(w->wsg, w->wsu, w->ssg, w->ssu, w->wsd, w->ssd, S, fs, d, p->xq, p->xs,
+                              p->sh_meta, T, p->hb_s, p->hq_s, p->hs_s, p->g32, p->u32, yf, st));
     } else {
         CUDA(cudaMemsetAsync(yf, 0, (size_t)T * d * sizeof(float), st));
     }

@@ -21,7 +21,8 @@ extern "C" {
 enum jtk_w8a8_epi {
     JTK_EPI_TOKEN_CHANNEL_F32 = 0, /* C = ((float)acc * sx[m]) * sw[n] */
     JTK_EPI_TENSOR_CHANNEL_F64 = 1, /* C = (float)((double)acc * ((double)sA * sw[n])) */
-    JTK_EPI_RAW_I32 = 2            /* C = acc (int32) */
+    JTK_EPI_RAW_I32 = 2,           /* C = acc (int32) */
+    JTK_EPI_TOKEN_CHANNEL_F32_ACC = 3 /* C += ((float)acc * sx[m]) * sw[n] (one writer per element) */
 };
 
 /* C[M][N] from X int8 [M][K] (row stride ldx bytes) and W int8 [N][K]
@@ -53,10 +54,6 @@ int jtk_dequant_rows(const int8_t *src, const float *scales, size_t rows, size_t
 /* fp32 -> bf16 (round to nearest even). */
 int jtk_f32_to_bf16(const float *src, uint16_t *dst, size_t n, cudaStream_t stream);
 
-/* Shared-expert tile table: tiles[j] = {0, JT_TILE_ROWS j, T, 0},
- * ntiles[0] = ceil(T / JT_TILE_ROWS). */
-int jtk_fill_single_tiles(int4 *tiles, int32_t *ntiles, int T, cudaStream_t stream);
-
 /* Router logits (jt_router.cu): logits[t][e] = (float) 4-lane double dot of
  * x[t] and wgate[e]; d % 32 == 0, x and wgate 16-byte aligned. */
 int jtk_router_logits(const float *x, const float *wgate, int T, int d, int E, float *logits,
@@ -82,10 +79,21 @@ int jtk_moe_sort(const int32_t *ids, const float *w_in, int T, int k, int E, int
 int jtk_build_tiles(const int32_t *off, const int32_t *tile_off, int E, int4 *tiles,
                     cudaStream_t stream);
 
-/* Expert-parallel exchange kernels (jt_ep.cu). */
+/* Shared gate/up of one shared expert on CTA-pair tiles (jt_shared_pair.cu):
+ * hb [T][fs] bf16 SwiGLU output, rowmax [T] its row maxima (atomic max on
+ * the bits: zero before the call).  -1: shape outside the kernel. */
 int jtk_shared_gu_pair(const int8_t *wsg, const int8_t *wsu, const float *ssg, const float *ssu, int fs,
-                       int d, const int8_t *xq, const float4 *sh_meta, int T, int8_t *hq, float *hs,
+                       int d, const int8_t *xq, const float4 *sh_meta, int T, uint16_t *hb, float *rowmax,
                        cudaStream_t stream);
+/* The S shared experts on T token rows into y (jt_shared.cu): stored by the
+ * first expert, added by the others.  Scratch hb [T][fs] bf16, hq [T][fs],
+ * hs [T]; g32 / u32 [T][fs] fp32 used only when T < 256. */
+int jtk_moe_shared(const int8_t *wsg, const int8_t *wsu, const float *ssg, const float *ssu,
+                   const int8_t *wsd, const float *ssd, int S, int fs, int d, const int8_t *xq,
+                   const float *xs, const float4 *sh_meta, int T, uint16_t *hb, int8_t *hq, float *hs,
+                   float *g32, float *u32, float *y, cudaStream_t stream);
+
+/* Expert-parallel exchange kernels (jt_ep.cu). */
 int jtk_ep_count(const int32_t *ids, int n, int E, int32_t *cnt, cudaStream_t stream);
 int jtk_ep_tokens(const int32_t *ids, int T, int k, int El, int N, int32_t *trow, int32_t *ntok,
                   cudaStream_t stream);
@@ -111,9 +119,7 @@ int jtk_quant_dispatch(const float *x, int T, int d, int k, const int32_t *pos,
 /* Expert GEMMs, JT_TILE_ROWS-row token tiles.  tiles / ntiles: tile table
  * and its length (device).  row_meta [rows]: float4 records above.  Group
  * scales fp16 [E][K/64][n_ch].  Routed gate/up (jt_moe_gu16.cu) writes the
- * bf16 SwiGLU output h [rows][f]; the shared experts (jt_moe_gemm.cu,
- * jt_shared_pair.cu) requantize h per (token, 64 channels) with hs
- * group-major [fs/64][round_up(T, 4)]. */
+ * bf16 SwiGLU output h [rows][f]; the routed down (jt_moe_dn16.cu) reads it. */
 int jtk_moe_gateup_routed(const uint8_t *wg, const uint8_t *wu, const void *gs, const void *us,
                           int E, int f, int d, const uint16_t *xd, int rows_cap,
                           const float4 *row_meta, const int4 *tiles, const int32_t *ntiles,
@@ -125,13 +131,6 @@ int jtk_moe_down_routed(const uint8_t *wd, const void *ds, int E, int d, int f, 
                         int rows_cap, const float4 *row_meta, const int4 *tiles,
                         const int32_t *ntiles, float *y, int y_accumulate, int max_tiles_hint,
                         cudaStream_t stream);
-int jtk_moe_gateup_shared(const int8_t *wsg, const int8_t *wsu, const float *ssg,
-                          const float *ssu, int fs, int d, const int8_t *xq, int T,
-                          const float4 *sh_meta, const int4 *tiles, const int32_t *ntiles,
-                          int8_t *hq, float *hs, cudaStream_t stream);
-int jtk_moe_down_shared(const int8_t *wsd, const float *ssd, int d, int fs, const int8_t *hq,
-                        int T, const float *hs, const float4 *sh_meta, const int4 *tiles,
-                        const int32_t *ntiles, float *y, int accumulate, cudaStream_t stream);
 
 /* Batch-1 low-bit GEMV (jt_gemv.cu): y[0..n2) from INT2 rows w2 [n2][K/4],
  * y[n2..n2+n4) from INT4 rows w4 [n4][K/2]; fp16 scales s [rows][K/64]. */
@@ -176,7 +175,7 @@ int jtk_moe_decode(const float *x, const float *logits, const float *bias, int32
                    const void *sg, const void *su, const uint8_t *wd, const void *sd, const int8_t *wsg,
                    const int8_t *wsu, const float *ssg, const float *ssu, const int8_t *wsd, const float *ssd,
                    int d, int f, int E, int k, int S, int fs, int8_t *xq, float *xs, uint16_t *h,
-                   int8_t *hq_s, float *hs_s, int hs_ld_s, int32_t *acc_s, int32_t *cnt_s,
+                   uint16_t *hb_s, int32_t *acc_s, int32_t *cnt_s,
                    int32_t *perm, int32_t *pos, int32_t *off, int32_t *tile_off, int32_t *meta,
                    uint8_t *drop, float *w_fin, float *y, uint16_t *y_bf16, cudaStream_t stream);
 

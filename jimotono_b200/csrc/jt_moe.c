@@ -44,17 +44,18 @@ struct jt_b200_moe_plan {
     int dev;
     void *arena;
     size_t arena_bytes;
-    int32_t *ids, *perm, *pos, *hist, *off, *tile_off, *meta, *sh_ntiles;
-    int4 *tiles, *sh_tiles;
+    int32_t *ids, *perm, *pos, *hist, *off, *tile_off, *meta;
+    int4 *tiles;
     float4 *row_meta, *sh_meta;
     float *w_raw, *w_fin, *xs, *hs_s, *y32;
     uint8_t *drop;
     int8_t *xq, *hq_s;
+    uint16_t *hb_s;    /* shared experts' SwiGLU output, bf16 [T][fs] */
+    float *g32, *u32;  /* shared gate / up in fp32 [min(T, 255)][fs] (T < 256 only) */
     uint16_t *h;  /* routed SwiGLU output, bf16 [kept][f] */
     uint16_t *xd; /* kept token rows, fp16, expert order (jtk_quant_dispatch) */
     /* batch-1 path: h codes and scales of every shared expert at once */
-    int8_t *hq_d;
-    float *hs_d;
+    uint16_t *hb_d;    /* batch-1 path: shared h of every shared expert, bf16 [S][fs] */
     int32_t *dec_acc, *dec_cnt; /* K-split partial dots of the shared experts (zero between calls) */
     /* optional per-stage profiling: events[step][JT_B200_MOE_NSTAGE + 1] */
     cudaEvent_t *prof_ev;
@@ -63,7 +64,6 @@ struct jt_b200_moe_plan {
 
 /* Row stride (floats) of the per-(row, 64-channel group) h scales: padded to
  * 16 bytes so a token tile's scales are one TMA box. */
-static int hs_ld(int n_ch) { return ((n_ch / 64) + 3) & ~3; }
 
 static size_t align_up(size_t v) { return (v + 255u) & ~(size_t)255u; }
 
@@ -102,17 +102,18 @@ int jt_b200_moe_plan_create(const jt_b200_moe_dims *dims, jt_b200_moe_plan **out
         {(void **)&p->ids, Tk * 4},          {(void **)&p->perm, Tk * 4},
         {(void **)&p->pos, Tk * 4},          {(void **)&p->hist, nch * E * 4},
         {(void **)&p->off, (E + 1) * 4},     {(void **)&p->tile_off, (E + 1) * 4},
-        {(void **)&p->meta, 64},             {(void **)&p->sh_ntiles, 64},
-        {(void **)&p->tiles, max_tiles * 16}, {(void **)&p->sh_tiles, (T / JT_TILE_ROWS + 1) * 16},
+        {(void **)&p->meta, 64},
+        {(void **)&p->tiles, max_tiles * 16},
         {(void **)&p->row_meta, Tk * 16},    {(void **)&p->sh_meta, T * 16},
         {(void **)&p->w_raw, Tk * 4},        {(void **)&p->w_fin, Tk * 4},
         {(void **)&p->xs, T * 4},
-        {(void **)&p->hs_s, ((T + 3) & ~(size_t)3) * (size_t)hs_ld((int)fs) * 4},
+        {(void **)&p->hs_s, T * 4},
+        {(void **)&p->hb_s, T * fs * 2},
+        {(void **)&p->g32, (T < 255 ? T : 255) * fs * 4}, {(void **)&p->u32, (T < 255 ? T : 255) * fs * 4},
         {(void **)&p->y32, T * d * 4},       {(void **)&p->drop, Tk},
         {(void **)&p->xq, T * d},            {(void **)&p->xd, Tk * d * 2},
         {(void **)&p->h, Tk * f * 2},        {(void **)&p->hq_s, T * fs},
-        {(void **)&p->hq_d, (size_t)(dims->S > 0 ? dims->S : 1) * fs},
-        {(void **)&p->hs_d, (size_t)(dims->S > 0 ? dims->S : 1) * (size_t)hs_ld((int)fs) * 4},
+        {(void **)&p->hb_d, (size_t)(dims->S > 0 ? dims->S : 1) * fs * 2},
         {(void **)&p->dec_acc, (size_t)(dims->S > 0 ? dims->S : 1) * 2 * fs * 4},
         {(void **)&p->dec_cnt, (size_t)(dims->S > 0 ? dims->S : 1) * (fs / 64) * 4},
     };
@@ -292,8 +293,7 @@ int jt_b200_moe_forward(jt_b200_moe_plan *plan, const jt_b200_moe_weights *w, co
         MARK(JT_B200_STAGE_GATEUP);
         const int r = jtk_moe_decode(x, logits, bias, plan->ids, plan->w_raw, w->wg, w->wu, w->sg, w->su, w->wd, w->sd,
                                      w->wsg, w->wsu, w->ssg, w->ssu, w->wsd, w->ssd, d, f, E, k, S, fs,
-                                     plan->xq, plan->xs, plan->h, plan->hq_d,
-                                     plan->hs_d, hs_ld(S > 0 ? fs : 64), plan->dec_acc, plan->dec_cnt,
+                                     plan->xq, plan->xs, plan->h, plan->hb_d, plan->dec_acc, plan->dec_cnt,
                                      plan->perm, plan->pos, plan->off,
                                      plan->tile_off, plan->meta, plan->drop, plan->w_fin,
                                      y_bf16 ? NULL : (float *)y, y_bf16 ? (uint16_t *)y : NULL, st);
@@ -320,16 +320,9 @@ int jt_b200_moe_forward(jt_b200_moe_plan *plan, const jt_b200_moe_weights *w, co
                               plan->row_meta, S > 0 ? plan->sh_meta : NULL, st));
     MARK(JT_B200_STAGE_SHARED);
     if (S > 0) {
-        LAUNCH(jtk_fill_single_tiles(plan->sh_tiles, plan->sh_ntiles, T, st));
-        for (int s = 0; s < S; s++) {
-            LAUNCH(jtk_moe_gateup_shared(w->wsg + (size_t)s * fs * d, w->wsu + (size_t)s * fs * d,
-                                         w->ssg + (size_t)s * fs, w->ssu + (size_t)s * fs, fs, d,
-                                         plan->xq, T, plan->sh_meta, plan->sh_tiles,
-                                         plan->sh_ntiles, plan->hq_s, plan->hs_s, st));
-            LAUNCH(jtk_moe_down_shared(w->wsd + (size_t)s * d * fs, w->ssd + (size_t)s * d, d, fs,
-                                       plan->hq_s, T, plan->hs_s, plan->sh_meta, plan->sh_tiles,
-                                       plan->sh_ntiles, yf, s > 0, st));
-        }
+        LAUNCH(jtk_moe_shared(w->wsg, w->wsu, w->ssg, w->ssu, w->wsd, w->ssd, S, fs, d, plan->xq, plan->xs,
+                              plan->sh_meta, T, plan->hb_s, plan->hq_s, plan->hs_s, plan->g32, plan->u32, yf,
+                              st));
     } else {
         if (cudaMemsetAsync(yf, 0, (size_t)T * d * sizeof(float), st) != cudaSuccess) {
             errno = EIO;

@@ -1,14 +1,15 @@
 // jt_shared_pair.cu - gate/up projection of a shared expert, fused with
-// SwiGLU and the per-(token, 64-channel) requantization of h, on the
-// CTA-pair tensor-core pipeline (jt_pair.cuh, tcgen05 cta_group::2).
+// SwiGLU, on the CTA-pair tensor-core pipeline (jt_pair.cuh, tcgen05
+// cta_group::2).  h leaves as bf16 with the running maximum of |h| of every
+// token row (the row's requantization scale, jt_shared.cu).
 //
 // Arithmetic (identical to the single-CTA form in jt_moe_gemm.cu, which is
 // the restatement of moe_layer.c:129-157 with the W8A8 projections of
-// w8a8.c:1021-1072 and the QuantBlockF requantization of w8a8.c:688-747):
+// w8a8.c:1021-1072):
 //   g[t][c] = ((float)acc_gate[t][c] * xs[t]) * sg[c]     (xs[t] = meta[t].x)
 //   u[t][c] = ((float)acc_up[t][c]   * xs[t]) * su[c]
 //   h[t][c] = SwiGLU(g, u)                      (jt_swiglu.cuh)
-//   hq[t][c0..c0+63], hs[c0/64][t] = QuantBlockF(h[t][c0..c0+63])
+//   hb[t][c] = bf16_rn(h[t][c]);  rowmax[t] = max(rowmax[t], max_c |hb[t][c]|)
 //
 // Tiles: a pair covers 128 output channels x 256 tokens; rank r's 128 weight
 // rows are gate rows c0 + 64r .. +63 over up rows c0 + 64r .. +63 (two
@@ -29,6 +30,7 @@
 // The readers release the accumulator as soon as a tile is staged, so the
 // SwiGLU of one tile overlaps the TMEM reads of the next.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include "jt_internal.h"
@@ -56,9 +58,8 @@ struct SharedGuParams {
     int T, fs, d;
     const float4 *meta;         // per-token {activation scale, 1, t, 0} [T]
     const float *sg, *su;       // per-channel weight scales [fs]
-    int8_t *hq;                 // [T][fs]
-    float *hs;                  // group-major [fs/64][hs_rows]
-    int hs_rows;
+    uint16_t *hb;               // [T][fs] bf16
+    float *rowmax;              // [T], max |hb| of the row (atomic max on the bits; zero before)
     int *err;
 };
 
@@ -189,15 +190,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_shared_gu_pair(const __grid_con
                     m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
                     if (__any_sync(0xffffffffu, bad) && c.lane == 0) atomicExch(p.err, JT_KERR_NONFINITE);
                     if (live) {
-                        const jt::QuantBlockF qb = jt::quant_block_f(m);
-                        uint32_t wd[2] = {0u, 0u};
+                        uint32_t hw[4];
 #pragma unroll
-                        for (int i = 0; i < 8; ++i)
-                            wd[i >> 2] |= (uint32_t)(uint8_t)(int8_t)jt::quant_code_f(h[i], qb) << (8 * (i & 3));
+                        for (int i = 0; i < 4; ++i) {
+                            const __nv_bfloat162 v = __floats2bfloat162_rn(h[2 * i], h[2 * i + 1]);
+                            hw[i] = *reinterpret_cast<const uint32_t *>(&v);
+                        }
                         const int tok = tok0 + j;
-                        *reinterpret_cast<uint2 *>(p.hq + (size_t)tok * p.fs + cbase + 8 * sl) =
-                            make_uint2(wd[0], wd[1]);
-                        if (sl == 0) p.hs[(size_t)(cbase / 64) * p.hs_rows + tok] = qb.scale_f;
+                        *reinterpret_cast<uint4 *>(p.hb + (size_t)tok * p.fs + cbase + 8 * sl) =
+                            make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                        // |bf16(v)| is the bf16 rounding of |v|: the row maximum of the stored values
+                        if (sl == 0)
+                            atomicMax(reinterpret_cast<unsigned int *>(p.rowmax) + tok,
+                                      __float_as_uint(__bfloat162float(__float2bfloat16_rn(m))));
                     }
                 }
                 __syncwarp();
@@ -214,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_shared_gu_pair(const __grid_con
 // (the caller then uses the single-CTA form).
 extern "C" int jtk_shared_gu_pair(const int8_t *wsg, const int8_t *wsu, const float *ssg,
                                   const float *ssu, int fs, int d, const int8_t *xq,
-                                  const float4 *sh_meta, int T, int8_t *hq, float *hs,
+                                  const float4 *sh_meta, int T, uint16_t *hb, float *rowmax,
                                   cudaStream_t stream) {
     if (fs % 128 || d % jp::kBK || T < 256 || fs <= 0 || d <= 0) return -1;
     SharedGuParams p{};
@@ -228,9 +233,8 @@ extern "C" int jtk_shared_gu_pair(const int8_t *wsg, const int8_t *wsu, const fl
     p.meta = sh_meta;
     p.sg = ssg;
     p.su = ssu;
-    p.hq = hq;
-    p.hs = hs;
-    p.hs_rows = (T + 3) & ~3;
+    p.hb = hb;
+    p.rowmax = rowmax;
     p.err = jtk_error_word();
     static bool attr_done = false;
     if (!attr_done) {

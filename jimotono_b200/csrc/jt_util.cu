@@ -127,18 +127,5 @@ extern "C" int jtk_f32_to_bf16(const float *src, uint16_t *dst, size_t n, cudaSt
 }
 
 namespace {
-// Tile table of a single "expert" covering rows [0, T) (shared experts):
-// entry j = {0, 64 j, T, 0}; ntiles[0] = ceil(T / 64).
-__global__ void k_fill_single_tiles(int4 *tiles, int32_t *ntiles, int T) {
-    const int n = (T + JT_TILE_ROWS - 1) / JT_TILE_ROWS;
-    for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x)
-        tiles[j] = make_int4(0, JT_TILE_ROWS * j, T, 0);
-    if (blockIdx.x == 0 && threadIdx.x == 0) ntiles[0] = n;
-}
 }  // namespace
 
-extern "C" int jtk_fill_single_tiles(int4 *tiles, int32_t *ntiles, int T, cudaStream_t stream) {
-    k_fill_single_tiles<<<((T + JT_TILE_ROWS - 1) / JT_TILE_ROWS + 255) / 256, 256, 0, stream>>>(
-        tiles, ntiles, T);
-    return cudaGetLastError() == cudaSuccess ? 0 : -4;
-}

@@ -7,6 +7,8 @@
 //   acc[m][n] = sum_k X[m][k] * W[n][k]            (int32, exact)
 // and one of three epilogues:
 //   TOKEN_CHANNEL_F32 : C = ((float)acc * sx[m]) * sw[n]          (per-token x per-channel)
+//   TOKEN_CHANNEL_F32_ACC: C += the same (the shared experts' down projections
+//                      adding into the layer output)
 //   TENSOR_CHANNEL_F64: C = (float)((double)acc * (sA * (double)sw[n]))  (w8a8.c:664,676-677)
 //   RAW_I32           : C = acc
 //
@@ -71,17 +73,21 @@ __device__ __forceinline__ void epi_chunk(const uint32_t (&v)[NCOL], int tok0, i
                                           int ldo, int lane) {
     const int nvalid = (M - tok0) < NCOL ? (M - tok0) : NCOL;
     float sxl = 0.f;
-    if (EPI == JTK_EPI_TOKEN_CHANNEL_F32 && lane < nvalid) sxl = __ldg(&sx[tok0 + lane]);
+    constexpr bool kTC = EPI == JTK_EPI_TOKEN_CHANNEL_F32 || EPI == JTK_EPI_TOKEN_CHANNEL_F32_ACC;
+    if (kTC && lane < nvalid) sxl = __ldg(&sx[tok0 + lane]);
     const size_t base = static_cast<size_t>(tok0) * ldo + ch;
 #pragma unroll
     for (int j = 0; j < NCOL; ++j) {
         const int32_t acc = static_cast<int32_t>(v[j]);
         const bool live = ch_ok && j < nvalid;
         const size_t o = base + static_cast<size_t>(j) * ldo;
-        if (EPI == JTK_EPI_TOKEN_CHANNEL_F32) {
+        if (kTC) {
             const float sj = __shfl_sync(0xffffffffu, sxl, j);
             const float r = __fmul_rn(__fmul_rn(__int2float_rn(acc), sj), swf);
-            if (live) static_cast<float *>(out)[o] = r;
+            if (live) {
+                float *dst = static_cast<float *>(out) + o;
+                *dst = EPI == JTK_EPI_TOKEN_CHANNEL_F32_ACC ? __fadd_rn(*dst, r) : r;
+            }
         } else if (EPI == JTK_EPI_TENSOR_CHANNEL_F64) {
             if (live) static_cast<float *>(out)[o] = __double2float_rn(__dmul_rn((double)acc, ss));
         } else {
@@ -250,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool ch_ok = ch < N;
             float swf = 0.f;
             double ss = 0.0;
-            if (EPI == JTK_EPI_TOKEN_CHANNEL_F32) swf = ch_ok ? sw[ch] : 0.f;
+            if (EPI == JTK_EPI_TOKEN_CHANNEL_F32 || EPI == JTK_EPI_TOKEN_CHANNEL_F32_ACC) swf = ch_ok ? sw[ch] : 0.f;
             if (EPI == JTK_EPI_TENSOR_CHANNEL_F64) ss = ch_ok ? sA * (double)sw[ch] : 0.0;
             const uint32_t trow = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
             const int cols = (M - m0) < BN ? (M - m0) : BN;
@@ -322,7 +328,7 @@ __global__ void __launch_bounds__(jt::pair::kThreads, 1)
             const bool ch_ok = ch < N;
             float swf = 0.f;
             double ss = 0.0;
-            if (EPI == JTK_EPI_TOKEN_CHANNEL_F32) swf = ch_ok ? sw[ch] : 0.f;
+            if (EPI == JTK_EPI_TOKEN_CHANNEL_F32 || EPI == JTK_EPI_TOKEN_CHANNEL_F32_ACC) swf = ch_ok ? sw[ch] : 0.f;
             if (EPI == JTK_EPI_TENSOR_CHANNEL_F64) ss = ch_ok ? sA * (double)sw[ch] : 0.0;
             const int cols = (M - m0) < 256 ? (M - m0) : 256;
             const int ce = (colh + 128) < cols ? (colh + 128) : cols;
@@ -432,6 +438,10 @@ extern "C" int jtk_w8a8_gemm(const int8_t *X, int ldx, const int8_t *W, int ldw,
             if (!sx || !sw) return -1;
             return launch_epi<JTK_EPI_TOKEN_CHANNEL_F32>(X, ldx, W, ldw, M, N, K, sx, sw, sA, out,
                                                          ldo, stream);
+        case JTK_EPI_TOKEN_CHANNEL_F32_ACC:
+            if (!sx || !sw) return -1;
+            return launch_epi<JTK_EPI_TOKEN_CHANNEL_F32_ACC>(X, ldx, W, ldw, M, N, K, sx, sw, sA, out,
+                                                             ldo, stream);
         case JTK_EPI_TENSOR_CHANNEL_F64:
             if (!sw) return -1;
             return launch_epi<JTK_EPI_TENSOR_CHANNEL_F64>(X, ldx, W, ldw, M, N, K, sx, sw, sA,

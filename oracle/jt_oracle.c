@@ -459,9 +459,11 @@ static void routed_expert(const jto_moe_dims *dm, const jto_moe_weights *w, int 
 }
 
 /* Shared expert s on token t:
- *   gate = ((float)acc * xs) * ssg[c]; up likewise; h = SwiGLU;
- *   requantize per 64-channel group; down: r = fmaf((float)P_g, hs_g, r)
- *   over 64-groups, y = r * ssd[o]. */
+ *   gate = ((float)acc * xs) * ssg[c]; up likewise; h = bf16_rn(SwiGLU);
+ *   h requantized per token row (one scale over all fs channels,
+ *   w8a8.c:688-747 on the row); down: y = ((float)acc * hs) * ssd[o] with
+ *   acc = sum_k hq[k] * wsd[o][k] (int32, exact) - the per-token x
+ *   per-channel W8A8 of w8a8.c:1021-1072. */
 static void shared_expert(const jto_moe_dims *dm, const jto_moe_weights *w, int s,
                           const int8_t *xq, float xs, float *yout, float *hbuf, int8_t *hq,
                           float *hs) {
@@ -477,20 +479,13 @@ static void shared_expert(const jto_moe_dims *dm, const jto_moe_weights *w, int 
         }
         float g = ((float)ag * xs) * w->ssg[(size_t)s * fs + c];
         float u = ((float)au * xs) * w->ssu[(size_t)s * fs + c];
-        hbuf[c] = jto_swiglu(g, u);
+        hbuf[c] = jto_bf16_to_float(jto_float_to_bf16(jto_swiglu(g, u)));
     }
-    jto_quant_blocks(hbuf, 1, fs, 64, hq, hs);
+    jto_quant_blocks(hbuf, 1, fs, fs, hq, hs);
     for (int o = 0; o < d; o++) {
-        float r = 0.0f;
-        for (int b = 0; b < fs / 64; b++) {
-            int32_t P = 0;
-            for (int i = 0; i < 64; i++) {
-                const int k = b * 64 + i;
-                P += (int32_t)hq[k] * (int32_t)wsd[(size_t)o * fs + k];
-            }
-            r = fmaf((float)P, hs[b], r);
-        }
-        yout[o] = r * w->ssd[(size_t)s * d + o];
+        int32_t acc = 0;
+        for (int k = 0; k < fs; k++) acc += (int32_t)hq[k] * (int32_t)wsd[(size_t)o * fs + k];
+        yout[o] = ((float)acc * hs[0]) * w->ssd[(size_t)s * d + o];
     }
 }
 
