@@ -48,8 +48,8 @@ DEC_ROT = 48
 CFG5_SMALL = dict(T=2048, d=2048, f=1536, E=128, k=8, S=2, fs=4096, cap=1.5)
 METRIC = "MoE-layer tokens/s at 1/2/4/8 B200; W8A8 TOPS; decode HBM GB/s vs peak"
 # DRAM bytes (read + write) of one routed gate/up launch at config 5: the ncu
-# capture of `bench.py --small` (1/8 of config 5) gave 282.6 MB, scaled by 8.
-GU_TRAFFIC_BYTES = 8 * 282_609_920
+# capture of `bench.py --small` (1/8 of config 5) gave 294.3 + 43.0 MB, scaled by 8.
+GU_TRAFFIC_BYTES = 8 * 337_319_680
 
 
 def peaks():
@@ -59,6 +59,17 @@ def peaks():
         return float(p["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
+
+
+def tensor_peak():
+    """Dense bf16/fp16 tensor-core peak (TFLOP/s) for the kind::f16 expert
+    GEMMs: the measured cuBLAS bf16 burst figure (a kernel of a few ms timed
+    inside a forward of a few ms, not a seconds-long loop)."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            return float(json.load(fh)["bf16_tflops"]), "measured (cuBLAS bf16 burst)"
+    except Exception:
+        return 1590.0, "fallback"
 
 
 # ----------------------------------------------------------------- clocks
@@ -638,24 +649,26 @@ def main():
     clocks = clk.summary()
     if rank == 0:
         gu_ms = stage[4]
+        t_peak, t_peak_kind = tensor_peak()
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded; random-init packed weights)",
+            "vs_baseline": None, "dtype": "f16/bf16 products of int8, INT2, INT4 codes; fp32 accumulate",
+            "data": "synthetic (seeded; random-init packed weights)",
             "config": {"workload": "cfg5 EP MoE layer: T=16384 d=2048 E=1024 f=1536 top-8 INT2/INT4 g64 + 2 shared INT8 f=4096, cap 1.5",
                        "tokens": tokens, "parallelism": f"replicas{world}" if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (3.6 GB weights, 134 MB activations)"},
             "e2e": {"value": round(tokens / (e2e_ms / 1e3) if world == 1 else st["T"] / (e2e_ms / 1e3), 1),
                     "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": args.steps * (9 + 2 * dm.S),
+            "gpu_launches": args.steps * (8 + 3 * dm.S),
             "stage_ms": {n: round(v, 4) for n, v in zip(
                 ["route", "sort", "dispatch", "shared", "gateup", "down", "output"], stage)},
             "kept_pairs": kept,
-            "roofline": {"bound": "tensor", "kernel": "routed gate/up (k_moe_gemm mode 0)",
-                         "achieved": round(ops_gu / (gu_ms / 1e3) / 1e12, 2), "peak": 4500.0,
-                         "unit": "TOPS", "frac": round(ops_gu / (gu_ms / 1e3) / 1e12 / 4500.0, 4),
-                         "peak_kind": "nominal dense int8 (MEASURED_PEAKS has no int8 entry)",
+            "roofline": {"bound": "tensor", "kernel": "routed gate/up (k_moe_gu16, tcgen05 kind::f16)",
+                         "achieved": round(ops_gu / (gu_ms / 1e3) / 1e12, 2), "peak": t_peak,
+                         "unit": "TFLOP/s", "frac": round(ops_gu / (gu_ms / 1e3) / 1e12 / t_peak, 4),
+                         "peak_kind": t_peak_kind,
                          "traffic": GU_TRAFFIC_BYTES,
                          "traffic_note": "ncu dram read+write of one launch at 1/8 of config 5, x8"},
             "layer_TOPS": round((ops_gu + ops_dn + ops_sh) / (ms / 1e3) / 1e12, 1),

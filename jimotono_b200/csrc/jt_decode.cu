@@ -501,7 +501,7 @@ __host__ __device__ inline DnLayout dn_layout(int k, int f, int S, int fs) {
     L.hr = dn_take(o, (uint32_t)k * (2 * f + 16));                 // routed h rows, bf16 [k], padded
     L.hqs = dn_take(o, (uint32_t)S * fs);                          // shared h codes [S][fs]
     L.hss = dn_take(o, (uint32_t)S * 4);                           // shared h row scales [S]
-    L.racc = dn_take(o, (uint32_t)kDnWarps * k * 4);               // folded routed rows [8][k]
+    L.racc = dn_take(o, (uint32_t)kDnWarps * k * (f / 64) * 4);    // routed group dots [8][k][f/64]
     L.sp = dn_take(o, (uint32_t)kDnWarps * S * (fs / 64) * 4);     // shared group partials [8][S][fs/64]
     L.bar = dn_take(o, 8);
     L.total = o;
@@ -607,18 +607,23 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constan
         const int i = threadIdx.x + t * (int)blockDim.x;
         if (i < n_hr) reinterpret_cast<uint4 *>(hr + (size_t)(i / nck) * (2 * f + 16))[i % nck] = hv[t];
     }
-    // row maxima of the shared h (|bf16| as float bits order like the values)
+    // row maxima of the shared h (|bf16| as float bits order like the values):
+    // 16 consecutive chunks lie in one row (fs / 8 is a multiple of 16), so
+    // one shared-memory atomic per half warp and chunk round
 #pragma unroll
     for (int t = 0; t < kHs; ++t) {
         const int i = threadIdx.x + t * (int)blockDim.x;
+        if (t * (int)blockDim.x >= n_hs) break;  // uniform over the block
+        float m = 0.0f;
         if (i < n_hs) {
             const uint32_t w4[4] = {sv[t].x, sv[t].y, sv[t].z, sv[t].w};
-            float m = 0.0f;
 #pragma unroll
             for (int e = 0; e < 4; ++e)
                 m = fmaxf(m, fmaxf(fabsf(__uint_as_float(w4[e] << 16)), fabsf(__uint_as_float(w4[e] & 0xFFFF0000u))));
-            atomicMax(&smax[i / (fs / 8)], __float_as_uint(m));
         }
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if ((lane & 15) == 0 && i < n_hs) atomicMax(&smax[i / (fs / 8)], __float_as_uint(m));
     }
     __syncthreads();
 #pragma unroll
@@ -626,13 +631,13 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constan
         const int i = threadIdx.x + t * (int)blockDim.x;
         if (i < n_hs) {
             const int sh = i / (fs / 8);
-            const jt::QuantBlock qb = jt::quant_block(__uint_as_float(smax[sh]));
+            const jt::QuantBlockF qb = jt::quant_block_f(__uint_as_float(smax[sh]));
             const uint32_t w4[4] = {sv[t].x, sv[t].y, sv[t].z, sv[t].w};
             uint32_t q[2] = {0u, 0u};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const int q0 = jt::quant_code(__uint_as_float(w4[e] << 16), qb);
-                const int q1 = jt::quant_code(__uint_as_float(w4[e] & 0xFFFF0000u), qb);
+                const int q0 = jt::quant_code_f(__uint_as_float(w4[e] << 16), qb);
+                const int q1 = jt::quant_code_f(__uint_as_float(w4[e] & 0xFFFF0000u), qb);
                 q[e >> 1] |= ((uint32_t)(uint8_t)(int8_t)q0 | ((uint32_t)(uint8_t)(int8_t)q1 << 8)) << (16 * (e & 1));
             }
             reinterpret_cast<uint2 *>(hqs)[i] = make_uint2(q[0], q[1]);
@@ -642,9 +647,10 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constan
     __syncthreads();
     if (!jt::mbar_wait(bar, 0, &abort_flag, p.err)) return;
     // ---- one thread per dot product.  Routed item (slot q, channel j): the
-    // whole INT4 row, as the bf16 weights bf16_rn(code * bf16_rn(s_g)) of the
-    // batched kernel (jt_moe_dn16.cu), against its bf16 h row, summed in fp32
-    // in k order.  Shared item (128-byte
+    // INT4 row's 64 codes of group g, as the bf16 weights
+    // bf16_rn(code * bf16_rn(s_g)) of the batched kernel (jt_moe_dn16.cu),
+    // against its bf16 h, summed in fp32 (the row's group dots are added in
+    // group order in the combine).  Shared item (128-byte
     // part, expert sh, channel j): the int32 partials of its two groups.
     // Neighbouring threads take neighbouring (padded) rows.
     const uint32_t *wr = reinterpret_cast<const uint32_t *>(dsm + L.wr);
@@ -654,37 +660,34 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constan
     float *racc = reinterpret_cast<float *>(dsm + L.racc);
     int *sp = reinterpret_cast<int *>(dsm + L.sp);
     const int gs = fs / 64;
-    const int n_r = kDnWarps * k, n_s = kDnWarps * S * (fs / 128);
+    const int n_rows = kDnWarps * k, n_r = n_rows * gf, n_s = kDnWarps * S * (fs / 128);
     for (int it = threadIdx.x; it < n_r + n_s; it += blockDim.x) {
-        if (it < n_r) {
-            const int q = it / kDnWarps, j = it % kDnWarps;
+        if (it < n_r) {  // routed item: group g of row (slot q, channel j)
+            const int g = it / n_rows, q = (it % n_rows) / kDnWarps, j = it % kDnWarps;
             const int rr = srank[q];
             const uint4 *row = reinterpret_cast<const uint4 *>(wr + ((size_t)q * kDnWarps + j) * (f / 8 + 4));
             const uint4 *hrow = reinterpret_cast<const uint4 *>(hr + (size_t)rr * (2 * f + 16));
-            float acc = 0.0f;
-            for (int g = 0; g < gf; ++g) {
-                const __nv_bfloat162 s2 = __bfloat162bfloat162(
-                    __float2bfloat16_rn(__half2float(wsc[((size_t)q * gf + g) * kDnWarps + j])));
+            const __nv_bfloat162 s2 = __bfloat162bfloat162(
+                __float2bfloat16_rn(__half2float(wsc[((size_t)q * gf + g) * kDnWarps + j])));
+            float acc0 = 0.0f, acc1 = 0.0f;
 #pragma unroll
-                for (int c = 0; c < 2; ++c) {  // 4 words = 32 codes
-                    const uint4 v = row[2 * g + c];
-                    const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+            for (int c = 0; c < 2; ++c) {  // 4 words = 32 codes
+                const uint4 v = row[2 * g + c];
+                const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {  // 8 codes against 8 h values
-                        uint32_t wb[4];
-                        jt::int4_bf16x8(wv[i], s2, wb);
-                        const uint4 h8 = hrow[8 * g + 4 * c + i];
-                        const uint32_t hb[4] = {h8.x, h8.y, h8.z, h8.w};
+                for (int i = 0; i < 4; ++i) {  // 8 codes against 8 h values
+                    uint32_t wb[4];
+                    jt::int4_bf16x8(wv[i], s2, wb);
+                    const uint4 h8 = hrow[8 * g + 4 * c + i];
+                    const uint32_t hb[4] = {h8.x, h8.y, h8.z, h8.w};
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            acc = fmaf(__uint_as_float(hb[e] << 16), __uint_as_float(wb[e] << 16), acc);
-                            acc = fmaf(__uint_as_float(hb[e] & 0xFFFF0000u), __uint_as_float(wb[e] & 0xFFFF0000u),
-                                       acc);
-                        }
+                    for (int e = 0; e < 4; ++e) {
+                        acc0 = fmaf(__uint_as_float(hb[e] << 16), __uint_as_float(wb[e] << 16), acc0);
+                        acc1 = fmaf(__uint_as_float(hb[e] & 0xFFFF0000u), __uint_as_float(wb[e] & 0xFFFF0000u), acc1);
                     }
                 }
             }
-            racc[j * k + q] = acc;
+            racc[(j * k + q) * gf + g] = acc0 + acc1;
         } else {
             const int u = it - n_r;
             const int pt = u / (S * kDnWarps), sh = (u / kDnWarps) % S, j = u % kDnWarps;
@@ -714,7 +717,11 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constan
     const int j = threadIdx.x, o = o0 + j;
     if (o >= d) return;
     double ya = 0.0;
-    for (int q = 0; q < k; ++q) ya = __dadd_rn(ya, __dmul_rn((double)sw[q], (double)racc[j * k + q]));
+    for (int q = 0; q < k; ++q) {
+        float yp = 0.0f;  // the row's group dots in group order
+        for (int g = 0; g < gf; ++g) yp += racc[(j * k + q) * gf + g];
+        ya = __dadd_rn(ya, __dmul_rn((double)sw[q], (double)yp));
+    }
     for (int sh = 0; sh < S; ++sh) {
         int acc = 0;
         for (int g = 0; g < gs; ++g) acc += sp[(j * S + sh) * gs + g];

@@ -70,7 +70,7 @@ __global__ void __launch_bounds__(256) k_shared_swiglu(const float *__restrict__
 __global__ void __launch_bounds__(256) k_shared_quant(const uint16_t *__restrict__ hb, float *rowmax, int fs,
                                                       int8_t *__restrict__ hq) {
     const size_t row = blockIdx.x;
-    const jt::QuantBlock qb = jt::quant_block(rowmax[row]);
+    const jt::QuantBlockF qb = jt::quant_block_f(rowmax[row]);
     for (int c = threadIdx.x * 16; c < fs; c += blockDim.x * 16) {
         const uint4 *src = reinterpret_cast<const uint4 *>(hb + row * fs + c);
         const uint4 a = src[0], b = src[1];
@@ -78,8 +78,8 @@ __global__ void __launch_bounds__(256) k_shared_quant(const uint16_t *__restrict
         uint32_t q[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const int q0 = jt::quant_code(__uint_as_float(hw[i] << 16), qb);
-            const int q1 = jt::quant_code(__uint_as_float(hw[i] & 0xFFFF0000u), qb);
+            const int q0 = jt::quant_code_f(__uint_as_float(hw[i] << 16), qb);
+            const int q1 = jt::quant_code_f(__uint_as_float(hw[i] & 0xFFFF0000u), qb);
             q[i >> 1] |= ((uint32_t)(uint8_t)(int8_t)q0 | ((uint32_t)(uint8_t)(int8_t)q1 << 8)) << (16 * (i & 1));
         }
         *reinterpret_cast<uint4 *>(hq + row * fs + c) = make_uint4(q[0], q[1], q[2], q[3]);

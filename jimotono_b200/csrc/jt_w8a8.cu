@@ -86,7 +86,12 @@ __device__ __forceinline__ void epi_chunk(const uint32_t (&v)[NCOL], int tok0, i
             const float r = __fmul_rn(__fmul_rn(__int2float_rn(acc), sj), swf);
             if (live) {
                 float *dst = static_cast<float *>(out) + o;
-                *dst = EPI == JTK_EPI_TOKEN_CHANNEL_F32_ACC ? __fadd_rn(*dst, r) : r;
+                // the add happens in L2 (no load to wait for); one writer per
+                // element, so it is the same single rounding as *dst + r
+                if (EPI == JTK_EPI_TOKEN_CHANNEL_F32_ACC)
+                    atomicAdd(dst, r);
+                else
+                    *dst = r;
             }
         } else if (EPI == JTK_EPI_TENSOR_CHANNEL_F64) {
             if (live) static_cast<float *>(out)[o] = __double2float_rn(__dmul_rn((double)acc, ss));
