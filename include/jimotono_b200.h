@@ -398,8 +398,14 @@ int jt_b200_moe_debug_copy(jt_b200_moe_plan *plan, int what, void *host_dst, siz
  * replicated.  Routing, capacity and drop follow the reference over the
  * whole batch: a pair of expert e is kept when fewer than cap pairs of e
  * precede it in the global q = t*k + p order (moe_layer.c:931-970).
- * Dispatch and combine are NCCL send/recv; each forward synchronizes its
- * stream once (to size the exchange from the gathered expert counts).
+ * Dispatch and combine are NCCL send/recv; each forward waits once on the
+ * host for the gathered expert counts (to size the exchange).  That wait is
+ * bounded (jt_b200_ep_comm_set_timeout, default 60 s, or the environment
+ * variable JT_B200_EP_TIMEOUT_MS): when a peer reports an error or the
+ * deadline passes, the communicator is aborted (its in-flight NCCL work
+ * ends) and the forward returns JT_ERR_CUDA with jt_b200_last_error naming
+ * the cause; the communicator then stays dead (later forwards fail at
+ * once) and is freed by jt_b200_ep_comm_destroy.
  * NCCL is loaded at run time (libnccl.so.2); without it the calls return
  * JT_ERR_NOSUP. */
 typedef struct jt_b200_ep_comm jt_b200_ep_comm;
@@ -409,6 +415,15 @@ int jt_b200_ep_unique_id(void *id128);
 /* Communicator of the current CUDA device (collective over the N ranks). */
 int jt_b200_ep_comm_create(const void *id128, int nranks, int rank, jt_b200_ep_comm **out);
 int jt_b200_ep_comm_destroy(jt_b200_ep_comm *comm);
+/* Deadline of the forward's host wait, in milliseconds (> 0). */
+int jt_b200_ep_comm_set_timeout(jt_b200_ep_comm *comm, int timeout_ms);
+/* 1 when the communicator was aborted by the watchdog, else 0. */
+int jt_b200_ep_comm_failed(const jt_b200_ep_comm *comm);
+/* The watchdog's polling loop against fake operations, without a GPU:
+ * scenario 0 completes after a few polls, 1 reports an asynchronous error,
+ * 2 never completes (the deadline timeout_ms runs out).  Returns 0
+ * (completed), 1 (error) or 2 (timeout); *out_aborted = whether it aborted. */
+int jt_b200_watchdog_selftest(int scenario, int timeout_ms, int *out_aborted);
 int jt_b200_moe_ep_plan_create(const jt_b200_moe_dims *dims, jt_b200_ep_comm *comm,
                                jt_b200_moe_ep_plan **out);
 int jt_b200_moe_ep_plan_destroy(jt_b200_moe_ep_plan *plan);
@@ -417,8 +432,8 @@ int jt_b200_moe_ep_forward(jt_b200_moe_ep_plan *plan, const jt_b200_moe_weights 
                            const float *logits, const float *bias, void *y, int y_bf16,
                            void *stream);
 /* Intermediates of the last forward (synchronizes): local JT_B200_DBG_IDS,
- * _WEIGHTS, _DROP, _XQ, _XS, _PERM (kept local pairs in send order); _HQ
- * the requantized SwiGLU rows of the owned experts (expert-contiguous);
+ * _WEIGHTS, _DROP, _XQ, _XS, _PERM (kept local pairs in send order); _H
+ * the bf16 SwiGLU rows of the owned experts (expert-contiguous);
  * _META int32 [4] {kept local pairs, owned rows, owned token tiles, cap}. */
 int jt_b200_moe_ep_debug_copy(jt_b200_moe_ep_plan *plan, int what, void *host_dst, size_t bytes);
 /* cap = ceil(cap_factor * T_global * k / E) in double (moe_layer.c:931-943);

@@ -67,6 +67,9 @@ PROTOTYPES = {
     "jt_b200_ep_unique_id": (I, [P]),
     "jt_b200_ep_comm_create": (I, [P, I, I, P]),
     "jt_b200_ep_comm_destroy": (I, [P]),
+    "jt_b200_ep_comm_set_timeout": (I, [P, I]),
+    "jt_b200_ep_comm_failed": (I, [P]),
+    "jt_b200_watchdog_selftest": (I, [I, I, P]),
     "jt_b200_moe_ep_plan_create": (I, [P, P, P]),
     "jt_b200_moe_ep_plan_destroy": (I, [P]),
     "jt_b200_moe_ep_forward": (I, [P, P, P, P, P, P, I, P]),

@@ -47,6 +47,8 @@ void jt_set_last_error(const char *what, int code);
 struct jt_b200_ep_comm {
     jt_nccl_comm comm;
     int nranks, rank, dev;
+    int timeout_ms; /* deadline of the forward's host wait */
+    int failed;     /* aborted by the watchdog */
 };
 
 struct jt_b200_moe_ep_plan {
@@ -138,8 +140,49 @@ int jt_b200_ep_comm_create(const void *id128, int nranks, int rank, jt_b200_ep_c
     }
     c->nranks = nranks;
     c->rank = rank;
+    c->timeout_ms = 60000;
+    const char *env = getenv("JT_B200_EP_TIMEOUT_MS");
+    if (env && atoi(env) > 0) c->timeout_ms = atoi(env);
     *out = c;
     return JT_OK;
+}
+
+int jt_b200_ep_comm_set_timeout(jt_b200_ep_comm *c, int timeout_ms) {
+    if (c == NULL || timeout_ms <= 0) {
+        errno = EINVAL;
+        return JT_ERR_INVAL;
+    }
+    c->timeout_ms = timeout_ms;
+    return JT_OK;
+}
+
+int jt_b200_ep_comm_failed(const jt_b200_ep_comm *c) { return c != NULL && c->failed; }
+
+/* watchdog operations of one forward: the counts' event, the communicator */
+typedef struct {
+    cudaEvent_t ev;
+    jt_b200_ep_comm *c;
+} wd_ctx;
+
+static int wd_done(void *p) {
+    const cudaError_t e = cudaEventQuery(((wd_ctx *)p)->ev);
+    return e == cudaSuccess ? 1 : (e == cudaErrorNotReady ? 0 : -1);
+}
+
+static int wd_async_error(void *p) {
+    const jt_nccl_api *nc = jt_nccl();
+    int err = 0;
+    if (nc && nc->comm_get_async_error && nc->comm_get_async_error(((wd_ctx *)p)->c->comm, &err) != 0)
+        return 1;
+    return err != 0 && err != 7; /* 7: ncclInProgress */
+}
+
+static void wd_abort(void *p) {
+    jt_b200_ep_comm *c = ((wd_ctx *)p)->c;
+    const jt_nccl_api *nc = jt_nccl();
+    if (nc && nc->comm_abort && c->comm) nc->comm_abort(c->comm);
+    c->comm = NULL; /* aborted: destroy must not touch it again */
+    c->failed = 1;
 }
 
 int jt_b200_ep_comm_destroy(jt_b200_ep_comm *c) {
@@ -323,6 +366,11 @@ int jt_b200_moe_ep_forward(jt_b200_moe_ep_plan *p, const jt_b200_moe_weights *w,
         errno = EINVAL;
         return JT_ERR_INVAL;
     }
+    if (p->comm->failed) {
+        jt_set_last_error("expert-parallel communicator aborted by the watchdog", 0);
+        errno = EIO;
+        return JT_ERR_CUDA;
+    }
     cudaStream_t st = (cudaStream_t)stream;
     jt_nccl_comm comm = p->comm->comm;
     float *yf = y_bf16 ? p->y32 : (float *)y;
@@ -346,7 +394,18 @@ int jt_b200_moe_ep_forward(jt_b200_moe_ep_plan *p, const jt_b200_moe_weights *w,
     } else {
         CUDA(cudaMemsetAsync(yf, 0, (size_t)T * d * sizeof(float), st));
     }
-    CUDA(cudaEventSynchronize(p->ev_counts));
+    {   /* bounded wait for the gathered counts (jt_watchdog.c) */
+        wd_ctx wc = {p->ev_counts, p->comm};
+        const jt_watchdog_ops ops = {wd_done, wd_async_error, wd_abort, &wc};
+        const int wr = jt_watchdog_wait(&ops, p->comm->timeout_ms, NULL);
+        if (wr != JT_WD_DONE) {
+            jt_set_last_error(wr == JT_WD_TIMEOUT ? "expert counts all-gather: deadline passed, communicator aborted"
+                                                  : "expert counts all-gather: NCCL error, communicator aborted",
+                              wr);
+            errno = wr == JT_WD_TIMEOUT ? ETIMEDOUT : EIO;
+            return JT_ERR_CUDA;
+        }
+    }
     for (int s = 0; s < N; s++)
         memcpy(p->h_cnt_all + (size_t)s * E, p->h_ext + (size_t)s * (E + N), (size_t)E * sizeof(int32_t));
 

@@ -179,6 +179,19 @@ int jtk_moe_decode(const float *x, const float *logits, const float *bias, int32
                    int32_t *perm, int32_t *pos, int32_t *off, int32_t *tile_off, int32_t *meta,
                    uint8_t *drop, float *w_fin, float *y, uint16_t *y_bf16, cudaStream_t stream);
 
+/* Bounded host wait (jt_watchdog.c): polls done() (> 0 done, < 0 failed)
+ * and async_error() (!= 0: the communicator reported an error) until done
+ * or timeout_ms; on an error or the deadline calls abort_comm().  Returns
+ * JT_WD_DONE, JT_WD_ERROR or JT_WD_TIMEOUT; *polls (may be NULL) = polls made. */
+typedef struct {
+    int (*done)(void *ctx);
+    int (*async_error)(void *ctx);
+    void (*abort_comm)(void *ctx);
+    void *ctx;
+} jt_watchdog_ops;
+enum { JT_WD_DONE = 0, JT_WD_ERROR = 1, JT_WD_TIMEOUT = 2 };
+int jt_watchdog_wait(const jt_watchdog_ops *ops, int timeout_ms, int *polls);
+
 /* Device error word shared by all kernels of the library (0 = clean). */
 int jtk_read_and_clear_error(int *out_code);
 int *jtk_error_word(void);

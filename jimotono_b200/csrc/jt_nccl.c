@@ -29,6 +29,8 @@ static void load(void) {
     SYM(recv, "ncclRecv");
     SYM(error_string, "ncclGetErrorString");
 #undef SYM
+    *(void **)(&g_api.comm_get_async_error) = dlsym(h, "ncclCommGetAsyncError");
+    *(void **)(&g_api.comm_abort) = dlsym(h, "ncclCommAbort");
     g_ok = 1;
 }
 

@@ -27,6 +27,8 @@ typedef struct {
     int (*send)(const void *, size_t, int, int, jt_nccl_comm, cudaStream_t);
     int (*recv)(void *, size_t, int, int, jt_nccl_comm, cudaStream_t);
     const char *(*error_string)(int);
+    int (*comm_get_async_error)(jt_nccl_comm, int *);  /* may be NULL (old NCCL) */
+    int (*comm_abort)(jt_nccl_comm);                   /* may be NULL (old NCCL) */
 } jt_nccl_api;
 
 /* NULL when no NCCL library can be loaded. */
