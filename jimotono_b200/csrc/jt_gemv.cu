@@ -35,32 +35,28 @@
 
 namespace {
 
-constexpr int kConsumers = 8;
+constexpr int kConsumers = 7;
 constexpr int kThreads = (kConsumers + 1) * 32;
-// One ring stage per consumer warp: stage i % 8 is always consumed by warp
-// i % 8, so each warp waits for every fill of its stage in order and the
-// mbarrier phase parity is never ambiguous.
+// One ring stage per consumer warp: stage i % kStages is always consumed by
+// warp i % kConsumers, so each warp waits for every fill of its stage in
+// order and the mbarrier phase parity is never ambiguous.
 constexpr int kStages = kConsumers;
-constexpr uint32_t kStageBytes = 10240;
+constexpr uint32_t kStageBytes = 9216;  // 16 INT2 or 8 INT4 rows of K = 2048 with their scales
 constexpr int kMaxG = 64;  // K <= 4096
 constexpr int kSub = 16;   // rows per fold batch
 
 // shared memory: ring (codes, then the chunk's scales when they are copied
 // too) | activation words [2 formats][kMaxG][16] | group sums [kMaxG] |
-// activations [K] | partials per consumer [kSub][33] (32 groups per pass) |
-// barriers
+// partials per consumer [kSub][kPld] (32 groups per pass) | row scales per
+// consumer, fp32 [kSub][kPld] (the K = 2048 path) | barriers
 constexpr size_t kOffAct = (size_t)kStages * kStageBytes;
 constexpr size_t kOffSum = kOffAct + 2 * kMaxG * 16 * 4;
-constexpr size_t kOffA = kOffSum + kMaxG * 4;          // activations, K bytes
-constexpr size_t kOffP = kOffA + 64 * kMaxG;
+constexpr size_t kOffP = kOffSum + kMaxG * 4;
 constexpr int kPld = 36;  // partial-row stride (words): lane-per-row 16-byte reads without bank conflicts
-constexpr size_t kOffBar = kOffP + (size_t)kConsumers * kSub * kPld * 4;
+constexpr size_t kOffS = kOffP + (size_t)kConsumers * kSub * kPld * 4;
+constexpr size_t kOffBar = kOffS + (size_t)kConsumers * kSub * kPld * 4;
 constexpr size_t kSmem = kOffBar + 2 * kStages * 8 + 16;
 static_assert(kSmem <= 113 * 1024, "two CTAs per SM");
-
-__device__ __forceinline__ uint32_t ubyte(const int8_t *a, int k) {
-    return static_cast<uint32_t>(static_cast<uint8_t>(a[k]));
-}
 
 // Rows per chunk: as many as fit in a stage (codes + optional scales), a
 // multiple of 8 when at least 8 fit, at most 64.
@@ -126,12 +122,45 @@ __device__ __forceinline__ int group_partial(const uint8_t *codes, const uint32_
 // trip counts (rows past nrows hold stale bytes and are not stored), the
 // codes are masked in place into four (INT2) or two (INT4) independent
 // unsigned x signed dp4a chains whose 4^j / 16 factors are shifted out.
+// The lane's codes of every row go to registers and the row scales of the
+// fold, as fp32, to the warp's scale rows (Ss); then the stage is released
+// (`empty`), so the producer refills it while this warp computes.  The
+// partials are stored as fp32 (exact: |P| < 2^17) with every lane active:
+// 0x4B400000 + P is the bit pattern of 1.5 * 2^23 + P for |P| < 2^22, and
+// subtracting 1.5 * 2^23 leaves P, so the lane-per-row fold is FFMAs only.
 template <int BITS, int R>
 __device__ __forceinline__ void consume_k2048(const uint8_t *codes, int nrows, const uint32_t *act,
                                              const int *gsum, const uint16_t *sc, float sa, float *y,
-                                             int32_t *Ps) {
+                                             float *Ps, float *Ss, uint64_t *empty) {
     constexpr int kRowBytes = 2048 * BITS / 8;
+    constexpr int kW = BITS / 2;  // 16-byte words per lane and row
     const int lane = jt::lane_id();
+    uint4 q[R * kW];
+    const uint8_t *base = codes + lane * (64 * BITS / 8);
+#pragma unroll
+    for (int rr = 0; rr < R; ++rr)
+#pragma unroll
+        for (int h = 0; h < kW; ++h) q[rr * kW + h] = *reinterpret_cast<const uint4 *>(base + rr * kRowBytes + 16 * h);
+    // the R rows' 32 scales each, as fp32, to the scale rows (8 per step)
+#pragma unroll
+    for (int i = lane; i < R * 4; i += 32) {
+        const uint4 v = reinterpret_cast<const uint4 *>(sc)[i];
+        const uint32_t hv[4] = {v.x, v.y, v.z, v.w};
+        float f[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            __half2 h2;
+            memcpy(&h2, &hv[j], 4);
+            const float2 f2 = __half22float2(h2);
+            f[2 * j] = f2.x;
+            f[2 * j + 1] = f2.y;
+        }
+        float4 *dst = reinterpret_cast<float4 *>(Ss + (i / 4) * kPld + (i % 4) * 8);
+        dst[0] = make_float4(f[0], f[1], f[2], f[3]);
+        dst[1] = make_float4(f[4], f[5], f[6], f[7]);
+    }
+    __syncwarp();
+    if (lane == 0) jt::mbar_arrive(empty);
     const uint4 *a4 = reinterpret_cast<const uint4 *>(act + (BITS == 2 ? 0 : kMaxG * 16) + lane * 16);
     uint32_t ap[16];
 #pragma unroll
@@ -142,23 +171,22 @@ __device__ __forceinline__ void consume_k2048(const uint8_t *codes, int nrows, c
         ap[4 * i + 2] = v.z;
         ap[4 * i + 3] = v.w;
     }
-    const int asum = gsum[lane];
-    const uint8_t *base = codes + lane * (64 * BITS / 8);
+    // P = 2 sum(li a) - (2^BITS - 1) sum(a), carried as the biased pattern
+    const int bias = 0x4B400000 - (BITS == 2 ? 3 : 15) * gsum[lane];
 #pragma unroll
     for (int rr = 0; rr < R; ++rr) {
         int p;
         if (BITS == 2) {
-            const uint4 q = *reinterpret_cast<const uint4 *>(base + rr * kRowBytes);
-            const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+            const uint4 qq = q[rr * kW];
+            const uint32_t w[4] = {qq.x, qq.y, qq.z, qq.w};
             int acc[4] = {0, 0, 0, 0};  // acc[j] = 4^j * sum(li_j * a)
 #pragma unroll
             for (int i = 0; i < 4; ++i)
 #pragma unroll
                 for (int j = 0; j < 4; ++j) acc[j] = dp4a_us(w[i] & (0x03030303u << (2 * j)), ap[4 * i + j], acc[j]);
-            p = 2 * ((acc[0] + (acc[1] >> 2)) + ((acc[2] >> 4) + (acc[3] >> 6))) - 3 * asum;
+            p = 2 * ((acc[0] + (acc[1] >> 2)) + ((acc[2] >> 4) + (acc[3] >> 6))) + bias;
         } else {
-            const uint4 q0 = *reinterpret_cast<const uint4 *>(base + rr * kRowBytes);
-            const uint4 q1 = *reinterpret_cast<const uint4 *>(base + rr * kRowBytes + 16);
+            const uint4 q0 = q[rr * kW], q1 = q[rr * kW + kW - 1];
             const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
             int lo = 0, hi = 0;
 #pragma unroll
@@ -166,42 +194,24 @@ __device__ __forceinline__ void consume_k2048(const uint8_t *codes, int nrows, c
                 lo = dp4a_us(w[i] & 0x0F0F0F0Fu, ap[2 * i], lo);
                 hi = dp4a_us(w[i] & 0xF0F0F0F0u, ap[2 * i + 1], hi);
             }
-            p = 2 * (lo + (hi >> 4)) - 15 * asum;
+            p = 2 * (lo + (hi >> 4)) + bias;
         }
-        Ps[rr * kPld + lane] = p;
+        Ps[rr * kPld + lane] = __fsub_rn(__int_as_float(p), 12582912.0f);
     }
     __syncwarp();
     if (lane < nrows) {
-        // the row's 32 partials and 32 fp16 scales with 16-byte loads, then
-        // the fold in ascending group order
-        const uint4 *pp = reinterpret_cast<const uint4 *>(Ps + lane * kPld);
-        const uint4 *sp = reinterpret_cast<const uint4 *>(sc + lane * 32);
-        int32_t P[32];
-        uint32_t hs[16];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint4 v = pp[i];
-            P[4 * i] = (int32_t)v.x;
-            P[4 * i + 1] = (int32_t)v.y;
-            P[4 * i + 2] = (int32_t)v.z;
-            P[4 * i + 3] = (int32_t)v.w;
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const uint4 v = sp[i];
-            hs[4 * i] = v.x;
-            hs[4 * i + 1] = v.y;
-            hs[4 * i + 2] = v.z;
-            hs[4 * i + 3] = v.w;
-        }
+        // the row's 32 partials and 32 scales with 16-byte loads, then the
+        // fold in ascending group order
+        const float4 *pp = reinterpret_cast<const float4 *>(Ps + lane * kPld);
+        const float4 *sp = reinterpret_cast<const float4 *>(Ss + lane * kPld);
         float r = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {  // two scales per conversion (low half = even group)
-            __half2 h2;
-            memcpy(&h2, &hs[i], 4);
-            const float2 s2 = __half22float2(h2);
-            r = __fmaf_rn((float)P[2 * i], s2.x, r);
-            r = __fmaf_rn((float)P[2 * i + 1], s2.y, r);
+        for (int i = 0; i < 8; ++i) {
+            const float4 pv = pp[i], sv = sp[i];
+            r = __fmaf_rn(pv.x, sv.x, r);
+            r = __fmaf_rn(pv.y, sv.y, r);
+            r = __fmaf_rn(pv.z, sv.z, r);
+            r = __fmaf_rn(pv.w, sv.w, r);
         }
         y[lane] = __fmul_rn(r, sa);
     }
@@ -319,42 +329,48 @@ __global__ void __launch_bounds__(kThreads, 2)
             }
         }
     } else {
-        // ---------------- consumers: chunk i of this CTA (stage i % 8) goes to warp i % 8
-        // activation words permuted to the code order of the packed words
-        // (built while the producer's first copies are in flight):
-        // INT2 word w of a group holds k = 16w + 4b + j at bits 2j of byte b;
-        // INT4 word w holds k = 8w + 2b (low nibble) and 8w + 2b + 1 (high)
+        // ---------------- consumers: chunk i of this CTA (stage i % kStages) goes to warp i % kConsumers
+        // activation words permuted to the code order of the packed words:
+        // INT2 word t = 4w + j of a group holds k = 16w + 4b + j at byte b;
+        // INT4 word t = 2w + h holds k = 8w + h + 2b at byte b
         const int ct = threadIdx.x;  // consumer threads are 0..kConsumers*32-1
         // the activations (and y) may belong to the previous kernel of the
         // stream: wait for it here; the producer's weight copies (read-only
         // parameters) are already in flight
         asm volatile("griddepcontrol.wait;" ::: "memory");
-        int8_t *as = reinterpret_cast<int8_t *>(smem + kOffA);
-        for (int i = ct; i < K / 16; i += kConsumers * 32)
-            reinterpret_cast<uint4 *>(as)[i] = __ldg(reinterpret_cast<const uint4 *>(a) + i);
-        asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");
-        a = as;
-        for (int i = ct; i < G * 16; i += kConsumers * 32) {
-            const int g = i / 16, t = i % 16;
-            const int k0 = 64 * g;
-            {  // INT2: t = 4w + j
-                const int b0 = k0 + 16 * (t / 4) + (t % 4);
-                act[g * 16 + t] = ubyte(a, b0) | (ubyte(a, b0 + 4) << 8) | (ubyte(a, b0 + 8) << 16) | (ubyte(a, b0 + 12) << 24);
+        // thread i: 16-byte segment i = quarter qd of group g, which holds
+        // INT2 words 4 qd .. +3 (w = qd) and INT4 words 4 qd .. +3
+        // (w = 2 qd, 2 qd + 1); the group sum from the four segments by
+        // shuffles within the aligned lane quad (K / 16 is a multiple of 4
+        // and so is the thread count, so a quad is always active together)
+        for (int i = ct; i < K / 16; i += kConsumers * 32) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4 *>(a) + i);
+            const int g = i >> 2, qd = i & 3;
+            uint32_t w2[4], w4[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t sel = (uint32_t)j | ((4u + j) << 4);
+                w2[j] = __byte_perm(__byte_perm(v.x, v.y, sel), __byte_perm(v.z, v.w, sel), 0x5410);
             }
-            {  // INT4: t = 2w + h
-                const int b0 = k0 + 8 * (t / 2) + (t % 2);
-                act[kMaxG * 16 + g * 16 + t] =
-                    ubyte(a, b0) | (ubyte(a, b0 + 2) << 8) | (ubyte(a, b0 + 4) << 16) | (ubyte(a, b0 + 6) << 24);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t sel = (uint32_t)h | ((2u + h) << 4) | ((4u + h) << 8) | ((6u + h) << 12);
+                w4[h] = __byte_perm(v.x, v.y, sel);
+                w4[2 + h] = __byte_perm(v.z, v.w, sel);
             }
-        }
-        for (int g = ct; g < G; g += kConsumers * 32) {
-            int sum = 0;
-#pragma unroll 8
-            for (int i = 0; i < 64; ++i) sum += a[64 * g + i];
-            gsum[g] = sum;
+            reinterpret_cast<uint4 *>(act + g * 16)[qd] = make_uint4(w2[0], w2[1], w2[2], w2[3]);
+            reinterpret_cast<uint4 *>(act + kMaxG * 16 + g * 16)[qd] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+            int sum = __dp4a((int)v.x, 0x01010101, __dp4a((int)v.y, 0x01010101,
+                                                        __dp4a((int)v.z, 0x01010101, __dp4a((int)v.w, 0x01010101, 0))));
+            const unsigned quad = 0xFu << (jt::lane_id() & ~3);
+            sum += __shfl_xor_sync(quad, sum, 1);
+            sum += __shfl_xor_sync(quad, sum, 2);
+            if (qd == 0) gsum[g] = sum;
         }
         asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");
         int32_t *Ps = reinterpret_cast<int32_t *>(smem + kOffP) + warp * kSub * kPld;
+        float *Pf = reinterpret_cast<float *>(Ps);  // the K = 2048 path's fp32 partials
+        float *Ss = reinterpret_cast<float *>(smem + kOffS) + warp * kSub * kPld;
         int i = 0;
         for (int c = blockIdx.x; c < nchunks; c += gridDim.x, ++i) {
             if (i % kConsumers != warp) continue;
@@ -366,18 +382,20 @@ __global__ void __launch_bounds__(kThreads, 2)
             if (ch.bits == 2) {
                 const uint16_t *sc = sb ? reinterpret_cast<const uint16_t *>(codes + cr2 * rb2)
                                         : s2 + (size_t)ch.row0 * G;
-                if (K == 2048 && sb && cr2 == 16)
-                    consume_k2048<2, 16>(codes, ch.nrows, act, gsum, sc, sa, y + ch.row0, Ps);
-                else
-                    consume<2>(codes, ch.nrows, K, act, gsum, sc, sa, y + ch.row0, Ps);
+                if (K == 2048 && sb && cr2 == 16) {
+                    consume_k2048<2, 16>(codes, ch.nrows, act, gsum, sc, sa, y + ch.row0, Pf, Ss, &empty[st]);
+                    continue;
+                }
+                consume<2>(codes, ch.nrows, K, act, gsum, sc, sa, y + ch.row0, Ps);
             } else {
                 ch.nrows = min(cr4, n4 - ch.row0);
                 const uint16_t *sc = sb ? reinterpret_cast<const uint16_t *>(codes + cr4 * rb4)
                                         : s4 + (size_t)ch.row0 * G;
-                if (K == 2048 && sb && cr4 == 8)
-                    consume_k2048<4, 8>(codes, ch.nrows, act, gsum, sc, sa, y + n2 + ch.row0, Ps);
-                else
-                    consume<4>(codes, ch.nrows, K, act, gsum, sc, sa, y + n2 + ch.row0, Ps);
+                if (K == 2048 && sb && cr4 == 8) {
+                    consume_k2048<4, 8>(codes, ch.nrows, act, gsum, sc, sa, y + n2 + ch.row0, Pf, Ss, &empty[st]);
+                    continue;
+                }
+                consume<4>(codes, ch.nrows, K, act, gsum, sc, sa, y + n2 + ch.row0, Ps);
             }
             __syncwarp();
             if (lane == 0) jt::mbar_arrive(&empty[st]);

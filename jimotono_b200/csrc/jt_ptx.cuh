@@ -135,6 +135,16 @@ __device__ __forceinline__ void prefetch_l2(const void *gsrc, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gsrc), "r"(bytes) : "memory");
 }
 
+// L2 prefetch of the box of a 2-D tensor map at (x, y) (the box a
+// tma_load_2d at the same coordinates would copy); a hint with no effect on
+// the values later loads see, so it may run before the data's producer ends.
+__device__ __forceinline__ void prefetch_tile_2d(const CUtensorMap *map, int32_t x, int32_t y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y)
+                 : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -145,6 +145,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0 && lane == 0) {
         jt::prefetch_tmap(&tmW);
         jt::prefetch_tmap(&tmX);
+        // the first tile's first S k-blocks into L2 while the previous
+        // kernel of the stream may still run (a hint: the loads below still
+        // wait for that kernel and read what it wrote)
+        if (static_cast<int>(blockIdx.x) < ntiles) {
+            const int n0 = (blockIdx.x % n_ch_tiles) * kBM, m0 = (blockIdx.x / n_ch_tiles) * BN;
+            for (int kb = 0; kb < nk && kb < S; ++kb) {
+                jt::prefetch_tile_2d(&tmW, kb * kBK, n0);
+                jt::prefetch_tile_2d(&tmX, kb * kBK, m0);
+            }
+        }
     }
     if (warp == 1) {
         jt::tmem_alloc(tmem_slot, Cfg::kTmemCols);
