@@ -535,7 +535,7 @@ def main_ep(torch, args, rank, world, local, hbm_peak, peak_kind):
                        "l2": "inputs larger than L2 (weights per GPU > 126 MB)"},
             "e2e": {"value": round(T / (e2e_ms / 1e3), 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": st["h2d"] * world, "d2h_bytes_per_step": st["d2h"] * world},
-            "gpu_launches": args.steps * (14 + 3 * dm.S),
+            "gpu_launches": args.steps * (15 + 3 * dm.S),
             "kept_pairs": kept_all,
             "roofline": {"bound": "tensor", "kernel": "whole expert-parallel layer (flops of all GPUs)",
                          "achieved": round(ops / (ms / 1e3) / 1e12, 2), "peak": round(t_peak * world, 1),
@@ -663,7 +663,7 @@ def main():
                        "l2": "inputs larger than L2 (3.6 GB weights, 134 MB activations)"},
             "e2e": {"value": round(tokens / (e2e_ms / 1e3) if world == 1 else st["T"] / (e2e_ms / 1e3), 1),
                     "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": args.steps * (8 + 3 * dm.S),
+            "gpu_launches": args.steps * (9 + 3 * dm.S),
             "stage_ms": {n: round(v, 4) for n, v in zip(
                 ["route", "sort", "dispatch", "shared", "gateup", "down", "output"], stage)},
             "kept_pairs": kept,

@@ -68,7 +68,8 @@ struct jt_b200_moe_ep_plan {
     float *g32, *u32; /* shared gate / up in fp32 [min(T, 255)][fs] (T < 256 only) */
     /* exchange: cnt = E expert counts then N token-row counts */
     int32_t *cnt, *cnt_all, *gbase, *own_off, *own_tile_off, *trow, *tsoff;
-    int4 *gather, *own_tiles;
+    int4 *gather, *own_tiles, *own_sub_tiles; /* JT_TILE_ROWS- / JT_SUB_ROWS-row token tiles */
+    int32_t *own_nsub;
     int8_t *send_tok, *rtok;
     uint16_t *own_h; /* owned pairs' routed SwiGLU output, bf16 */
     uint16_t *own_x; /* owned pairs' token rows, fp16, expert order (jtk_ep_gather) */
@@ -254,6 +255,7 @@ int jt_b200_moe_ep_plan_create(const jt_b200_moe_dims *dims, jt_b200_ep_comm *co
         {(void **)&p->gbase, E * 4},         {(void **)&p->own_off, (El + 1) * 4},
         {(void **)&p->own_tile_off, (El + 1) * 4},
         {(void **)&p->gather, Nn * El * 16}, {(void **)&p->own_tiles, (R / JT_TILE_ROWS + El + 1) * 16},
+        {(void **)&p->own_sub_tiles, (R / JT_SUB_ROWS + El + 1) * 16}, {(void **)&p->own_nsub, 16},
         {(void **)&p->rtok, RT * d},         {(void **)&p->own_x, R * d * 2},
         {(void **)&p->own_h, R * f * 2},     {(void **)&p->rmeta, R * 16},
         {(void **)&p->own_meta, R * 16},
@@ -483,10 +485,11 @@ int jt_b200_moe_ep_forward(jt_b200_moe_ep_plan *p, const jt_b200_moe_weights *w,
     if (own_rows > 0) {
         LAUNCH(jtk_ep_gather(p->gather, N * El, p->rtok, p->rmeta, d, p->own_x, p->own_meta, st));
         LAUNCH(jtk_build_tiles(p->own_off, p->own_tile_off, El, p->own_tiles, st));
-        const int gu_hint = own_tiles * (f / 128), dn_hint = own_tiles * ((d + 255) / 256);
+        LAUNCH(jtk_split_tiles(p->own_tiles, p->own_tile_off + El, p->own_sub_tiles, p->own_nsub, st));
+        /* each JT_TILE_ROWS-row tile is at most two JT_SUB_ROWS-row ones */
+        const int gu_hint = 2 * own_tiles * (f / 128), dn_hint = own_tiles * ((d + 255) / 256);
         LAUNCH(jtk_moe_gateup_routed(w->wg, w->wu, w->sg, w->su, El, f, d, p->own_x, p->R_max,
-                                     p->own_meta, p->own_tiles, p->own_tile_off + El, p->own_h,
-                                     gu_hint, st));
+                                     p->own_meta, p->own_sub_tiles, p->own_nsub, p->own_h, gu_hint, st));
         LAUNCH(jtk_moe_down_routed(w->wd, w->sd, El, d, f, p->own_h, p->R_max, p->own_meta,
                                    p->own_tiles, p->own_tile_off + El, p->ret, 1, dn_hint, st));
     }

@@ -15,7 +15,9 @@ extern "C" {
 
 /* Token rows per tile of the expert GEMMs (the routed-expert tile table and
  * the shared-expert tiles are cut to this size). */
-#define JT_TILE_ROWS 128
+#define JT_TILE_ROWS 256
+/* Token rows of the routed gate/up GEMM's tiles (jtk_split_tiles). */
+#define JT_SUB_ROWS 128
 
 /* Epilogue modes of the dense int8 tensor-core GEMM. */
 enum jtk_w8a8_epi {
@@ -76,6 +78,11 @@ int jtk_moe_sort(const int32_t *ids, const float *w_in, int T, int k, int E, int
                  int32_t *perm, int32_t *pos, uint8_t *drop, float *w_out, cudaStream_t stream);
 /* Token-tile table from per-expert row offsets off [E+1] and tile offsets
  * tile_off [E+1] (one CTA list entry {e, row0, row_end, 0} per tile). */
+/* The JT_SUB_ROWS-row tile table of the JT_TILE_ROWS-row one (ntiles
+ * entries, read on the device): out [ntiles * JT_TILE_ROWS / JT_SUB_ROWS]
+ * in the same order, each entry {e, first row, expert's end row, 0}; nout
+ * its entry count.  One CTA. */
+int jtk_split_tiles(const int4 *tiles, const int32_t *ntiles, int4 *out, int32_t *nout, cudaStream_t stream);
 int jtk_build_tiles(const int32_t *off, const int32_t *tile_off, int E, int4 *tiles,
                     cudaStream_t stream);
 

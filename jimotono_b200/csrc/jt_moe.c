@@ -45,7 +45,9 @@ struct jt_b200_moe_plan {
     void *arena;
     size_t arena_bytes;
     int32_t *ids, *perm, *pos, *hist, *off, *tile_off, *meta;
-    int4 *tiles;
+    int4 *tiles;     /* JT_TILE_ROWS-row token tiles (routed down) */
+    int4 *sub_tiles; /* JT_SUB_ROWS-row token tiles (routed gate/up) */
+    int32_t *nsub;   /* entries of sub_tiles */
     float4 *row_meta, *sh_meta;
     float *w_raw, *w_fin, *xs, *hs_s, *y32;
     uint8_t *drop;
@@ -104,6 +106,7 @@ int jt_b200_moe_plan_create(const jt_b200_moe_dims *dims, jt_b200_moe_plan **out
         {(void **)&p->off, (E + 1) * 4},     {(void **)&p->tile_off, (E + 1) * 4},
         {(void **)&p->meta, 64},
         {(void **)&p->tiles, max_tiles * 16},
+        {(void **)&p->sub_tiles, (Tk / JT_SUB_ROWS + E + 1) * 16}, {(void **)&p->nsub, 16},
         {(void **)&p->row_meta, Tk * 16},    {(void **)&p->sh_meta, T * 16},
         {(void **)&p->w_raw, Tk * 4},        {(void **)&p->w_fin, Tk * 4},
         {(void **)&p->xs, T * 4},
@@ -315,6 +318,7 @@ int jt_b200_moe_forward(jt_b200_moe_plan *plan, const jt_b200_moe_weights *w, co
     LAUNCH(jtk_moe_sort(plan->ids, plan->w_raw, T, k, E, cap, NULL, plan->hist, plan->off,
                         plan->tile_off, plan->tiles, plan->meta, plan->perm, plan->pos, plan->drop,
                         plan->w_fin, st));
+    LAUNCH(jtk_split_tiles(plan->tiles, plan->tile_off + E, plan->sub_tiles, plan->nsub, st));
     MARK(JT_B200_STAGE_DISPATCH);
     LAUNCH(jtk_quant_dispatch(x, T, d, k, plan->pos, plan->w_fin, plan->xq, plan->xs, plan->xd,
                               plan->row_meta, S > 0 ? plan->sh_meta : NULL, st));
@@ -329,19 +333,18 @@ int jt_b200_moe_forward(jt_b200_moe_plan *plan, const jt_b200_moe_weights *w, co
             return JT_ERR_CUDA;
         }
     }
-    /* Upper bound of the device-side token-tile count: every non-empty
-     * expert adds at most one partial tile to (kept pairs)/JT_TILE_ROWS full ones. */
+    /* Upper bounds of the device-side token-tile counts: every non-empty
+     * expert adds at most one partial tile to (kept pairs)/(tile rows) full ones. */
     {
         const long long pairs = (long long)T * k;
         const long long ne = pairs < E ? pairs : E;
-        const long long tl = ne + pairs / JT_TILE_ROWS;
-        gu_hint = tl * (f / 128) > 0x7fffffffLL ? 0 : (int)(tl * (f / 128));
+        const long long tl = ne + pairs / JT_TILE_ROWS, ts = ne + pairs / JT_SUB_ROWS;
+        gu_hint = ts * (f / 128) > 0x7fffffffLL ? 0 : (int)(ts * (f / 128));
         dn_hint = tl * ((d + 255) / 256) > 0x7fffffffLL ? 0 : (int)(tl * ((d + 255) / 256));
     }
     MARK(JT_B200_STAGE_GATEUP);
     LAUNCH(jtk_moe_gateup_routed(w->wg, w->wu, w->sg, w->su, E, f, d, plan->xd, rows_cap,
-                                 plan->row_meta, plan->tiles, plan->tile_off + E, plan->h, gu_hint,
-                                 st));
+                                 plan->row_meta, plan->sub_tiles, plan->nsub, plan->h, gu_hint, st));
     MARK(JT_B200_STAGE_DOWN);
     LAUNCH(jtk_moe_down_routed(w->wd, w->sd, E, d, f, plan->h, rows_cap, plan->row_meta, plan->tiles,
                                plan->tile_off + E, yf, 1, dn_hint, st));

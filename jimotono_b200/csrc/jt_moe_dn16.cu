@@ -13,16 +13,17 @@
 // before the product so that the unpack forms each weight with one bf16
 // multiply (both roundings are part of the specification).
 //
-// Tile: 128 token rows of one expert (MMA M, TMEM lane = token row) x 256
-// output channels (MMA N).  One pipeline stage is one 64-K scale group: the
-// h rows (16 KB, 128-byte swizzle), the packed INT4 codes of the 256 weight
-// rows (8 KB) and their fp16 group scales (512 B) arrive by TMA; eight
-// unpack warps turn the codes into bf16 weights in the 128-byte-swizzled
-// K-major layout the MMA reads, in a separate ring of two 32 KB buffers.
-// The whole K accumulates in one TMEM accumulator of 256 columns; two of
-// them let the MMA run a tile ahead of the epilogue, whose threads each own
-// one token row and add 128 consecutive channels of it into the layer
-// output with 16-byte vector atomics.
+// Tile: up to 256 token rows of one expert, run as one or two sub-tiles of
+// 128 rows (MMA M, TMEM lane = token row), x 256 output channels (MMA N).
+// One pipeline stage is one 64-K scale group: the h rows (16 KB per
+// sub-tile, 128-byte swizzle), the packed INT4 codes of the 256 weight rows
+// (8 KB) and their fp16 group scales (512 B) arrive by TMA; eight unpack
+// warps turn the codes into bf16 weights in the 128-byte-swizzled K-major
+// layout the MMA reads, in a separate ring of two 32 KB buffers, which both
+// sub-tiles' MMAs read.  Each sub-tile accumulates the whole K in a TMEM
+// accumulator of 256 columns; the two accumulators are used in turn, and
+// the epilogue threads each own one token row and add 128 consecutive
+// channels of it into the layer output with 16-byte vector atomics.
 //
 // Unpack (jt::int4_bf16x8): four operations per pair of weights after two
 // masks per packed word.
@@ -44,7 +45,9 @@
 
 namespace {
 
-constexpr int kBM = JT_TILE_ROWS;         // token rows per tile (MMA M)
+constexpr int kBM = 128;                  // token rows per sub-tile (MMA M)
+constexpr int kTile = JT_TILE_ROWS;       // token rows per tile
+constexpr int kSubs = kTile / kBM;        // sub-tiles per tile
 constexpr int kBN = 256;                  // output channels per tile (MMA N)
 constexpr int kThreads = 576;             // 18 warps
 constexpr int kUnpack0 = 2;               // warps 2-9
@@ -52,20 +55,22 @@ constexpr int kUnpackWarps = 8;
 constexpr int kEpi0 = 10;                 // warps 10-17
 constexpr int kEpiWarps = 8;
 constexpr int kMaxStages = 8;
+static_assert(kSubs == 2, "two accumulators, one per sub-tile");
 constexpr int kBBufs = 2;
 constexpr int kMaxGroups = 64;            // f <= 4096
-constexpr uint32_t kX16 = kBM * 128;      // bf16 h rows of one 64-K group, 16 KB
-constexpr uint32_t kPk = kBN * 32;        // packed codes, 8 KB
+constexpr uint32_t kX16 = kBM * 128;      // bf16 h rows of one 64-K group, 16 KB per sub-tile
+constexpr uint32_t kOffPk = kSubs * kX16; // packed codes, 8 KB
+constexpr uint32_t kPk = kBN * 32;
 constexpr uint32_t kSc = kBN * 2;         // group scales, 512 B
-constexpr uint32_t kStage = 25600;        // X16 | packed | scales, 1024-aligned
+constexpr uint32_t kStage = 41984;        // X16 [kSubs] | packed | scales, 1024-aligned
 constexpr uint32_t kB16 = kBN * 128;      // bf16 weights of one 64-K group, 32 KB
-constexpr uint32_t kSlot = 3072;          // info | row meta [kBM] float4
+constexpr uint32_t kSlot = 5120;          // info | row meta [kTile] float4
 constexpr uint32_t kOffMeta = 128;
 constexpr uint32_t kBarBytes = 1024;
 constexpr size_t kSmemLimit = 232448;
 constexpr size_t kFixed = 1024 + kBBufs * (size_t)kB16 + 2 * (size_t)kSlot + kBarBytes;
-static_assert(kStage >= kX16 + kPk + kSc && kStage % 1024 == 0, "stage layout");
-static_assert(kOffMeta + kBM * 16 <= kSlot, "slot layout");
+static_assert(kStage >= kOffPk + kPk + kSc && kStage % 1024 == 0, "stage layout");
+static_assert(kOffMeta + kTile * 16 <= kSlot, "slot layout");
 
 struct Dn16Params {
     CUtensorMap tmA;   // packed INT4 rows [E*d][f/2], 32 B x 256 boxes
@@ -183,12 +188,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_dn16(const __grid_constant_
                     ok = false;
                     break;
                 }
+                const int nsub = min(te.z - te.y, kTile) > kBM ? 2 : 1;
                 uint8_t *sl = slot_base + ts * kSlot;
                 asm volatile("st.shared.v4.s32 [%0], {%1, %2, %3, %4};" ::"r"(jt::smem_u32(sl)), "r"(te.x),
                              "r"(te.y), "r"(te.z), "r"(c0)
                              : "memory");
-                jt::mbar_arrive_expect_tx(&pfull[ts], kBM * 16);
-                jt::tma_load_2d(sl + kOffMeta, &p.tmM, &pfull[ts], 0, te.y);
+                jt::mbar_arrive_expect_tx(&pfull[ts], nsub * kBM * 16);
+                for (int sb = 0; sb < nsub; ++sb)
+                    jt::tma_load_2d(sl + kOffMeta + sb * kBM * 16, &p.tmM, &pfull[ts], 0, te.y + sb * kBM);
                 t_issued |= 1u << ts;
                 t_phase = (t_phase & ~(1u << ts)) | (tphase << ts);
                 if (++ts == 2) {
@@ -201,11 +208,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_dn16(const __grid_constant_
                         break;
                     }
                     uint8_t *st = smem + (size_t)stage * kStage;
-                    jt::mbar_arrive_expect_tx(&full[stage], kX16 + kPk + kSc);
-                    jt::tma_load_2d(st, &p.tmH, &full[stage], kb * 128, te.y);
-                    jt::tma_load_2d(st + kX16, &p.tmA, &full[stage], kb * 32, wrow);
-                    jt::tma_load_2d(st + kX16 + kPk, &p.tmS, &full[stage], c0 * 2, te.x * G + kb);
-                    jt::tma_load_2d(st + kX16 + kPk + 256, &p.tmS, &full[stage], c0 * 2 + 256, te.x * G + kb);
+                    jt::mbar_arrive_expect_tx(&full[stage], nsub * kX16 + kPk + kSc);
+                    for (int sb = 0; sb < nsub; ++sb)
+                        jt::tma_load_2d(st + sb * kX16, &p.tmH, &full[stage], kb * 128, te.y + sb * kBM);
+                    jt::tma_load_2d(st + kOffPk, &p.tmA, &full[stage], kb * 32, wrow);
+                    jt::tma_load_2d(st + kOffPk + kPk, &p.tmS, &full[stage], c0 * 2, te.x * G + kb);
+                    jt::tma_load_2d(st + kOffPk + kPk + 256, &p.tmS, &full[stage], c0 * 2 + 256, te.x * G + kb);
                     issued_mask |= 1u << stage;
                     issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
                     if (++stage == (uint32_t)S) {
@@ -234,28 +242,32 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_dn16(const __grid_constant_
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
-            uint32_t stage = 0, phase = 0, bb = 0, bphase = 0, tc = 0;
+            // accumulator use n goes to buffer n % 2; a tile takes one use per sub-tile
+            uint32_t stage = 0, phase = 0, bb = 0, bphase = 0, n = 0;
             bool ok = true;
             constexpr uint32_t idesc = jt::idesc_bf16(kBM, kBN);
-            for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++tc) {
-                const uint32_t buf = tc & 1u;
-                if (!jt::mbar_wait(&tempty[buf], (tc >> 1) & 1u, abort_flag, err)) {
-                    ok = false;
-                    break;
-                }
+            for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+                const int4 te = __ldg(&p.tiles[u / nch]);
+                const uint32_t nsub = min(te.z - te.y, kTile) > kBM ? 2u : 1u;
+                for (uint32_t sb = 0; sb < nsub && ok; ++sb)
+                    ok = jt::mbar_wait(&tempty[(n + sb) & 1u], ((n + sb) >> 1) & 1u, abort_flag, err);
+                if (!ok) break;
                 jt::tc_fence_after();
-                const uint32_t acc = tmem_base + buf * kBN;
                 for (int kb = 0; kb < G; ++kb) {
                     if (!jt::mbar_wait(&bfull[bb], bphase, abort_flag, err)) {
                         ok = false;
                         break;
                     }
                     jt::tc_fence_after();
-                    const uint64_t dH = jt::umma_desc_sw128(jt::smem_u32(smem + (size_t)stage * kStage));
                     const uint64_t dW = jt::umma_desc_sw128(jt::smem_u32(bbuf + bb * kB16));
+                    for (uint32_t sb = 0; sb < nsub; ++sb) {
+                        const uint32_t acc = tmem_base + ((n + sb) & 1u) * kBN;
+                        const uint64_t dH =
+                            jt::umma_desc_sw128(jt::smem_u32(smem + (size_t)stage * kStage + sb * kX16));
 #pragma unroll
-                    for (int ks = 0; ks < 4; ++ks)
-                        mma_bf16(acc, dH + 2u * ks, dW + 2u * ks, idesc, (kb | ks) != 0 ? 1u : 0u);
+                        for (int ks = 0; ks < 4; ++ks)
+                            mma_bf16(acc, dH + 2u * ks, dW + 2u * ks, idesc, (kb | ks) != 0 ? 1u : 0u);
+                    }
                     jt::mma_commit(&empty[stage]);
                     jt::mma_commit(&bempty[bb]);
                     if (++stage == (uint32_t)S) {
@@ -267,7 +279,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_dn16(const __grid_constant_
                         bphase ^= 1u;
                     }
                 }
-                if (ok) jt::mma_commit(&tfull[buf]);
+                if (!ok) break;
+                for (uint32_t sb = 0; sb < nsub; ++sb) jt::mma_commit(&tfull[(n + sb) & 1u]);
+                n += nsub;
             }
             if (!ok) {  // already-issued MMAs retire before TMEM is released
                 jt::mma_commit(drain);
@@ -290,9 +304,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_dn16(const __grid_constant_
                     break;
                 }
                 const uint8_t *st = smem + (size_t)stage * kStage;
-                const __half sh = reinterpret_cast<const __half *>(st + kX16 + kPk)[r];
+                const __half sh = reinterpret_cast<const __half *>(st + kOffPk + kPk)[r];
                 const __nv_bfloat162 s2 = __bfloat162bfloat162(__float2bfloat16_rn(__half2float(sh)));
-                const uint4 *pk = reinterpret_cast<const uint4 *>(st + kX16 + r * 32);
+                const uint4 *pk = reinterpret_cast<const uint4 *>(st + kOffPk + r * 32);
                 const uint32_t row_addr = jt::smem_u32(bbuf + bb * kB16) + static_cast<uint32_t>(r) * 128u;
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {  // 32 codes -> 32 weights = chunks 4h .. 4h+3
@@ -331,17 +345,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_dn16(const __grid_constant_
             jt::mbar_arrive(&tempty[0]);
             jt::mbar_arrive(&tempty[1]);
         }
-        uint32_t tc = 0, ts = 0, tphase = 0;
+        uint32_t n = 0, ts = 0, tphase = 0;
         bool ok = true;
-        for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++tc) {
+        for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
             if (!jt::mbar_wait(&pfull[ts], tphase, abort_flag, err)) {
                 ok = false;
                 break;
             }
             const uint8_t *sl = slot_base + ts * kSlot;
             const int4 info = *reinterpret_cast<const int4 *>(sl);  // {e, row0, row_end, c0}
-            const float4 mt = reinterpret_cast<const float4 *>(sl + kOffMeta)[j];
-            const bool live = j < min(info.z - info.y, kBM);
+            const int rows = min(info.z - info.y, kTile);
+            const uint32_t nsub = rows > kBM ? 2u : 1u;
+            float4 mt[kSubs];
+#pragma unroll
+            for (int sb = 0; sb < kSubs; ++sb) mt[sb] = reinterpret_cast<const float4 *>(sl + kOffMeta)[sb * kBM + j];
             const bool cols = ch0 < p.d - info.w;  // this warp's channels exist (last tile of d % 256 == 128)
             __syncwarp();
             if (lane == 0) jt::mbar_arrive(&pempty[ts]);
@@ -349,42 +366,47 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_dn16(const __grid_constant_
                 ts = 0;
                 tphase ^= 1u;
             }
-            const uint32_t buf = tc & 1u;
-            if (!jt::mbar_wait(&tfull[buf], (tc >> 1) & 1u, abort_flag, err)) {
-                ok = false;
-                break;
-            }
-            jt::tc_fence_after();
-            const uint32_t acc = tq + buf * kBN + ch0;
-            float *dst = p.y + (size_t)__float_as_int(mt.z) * p.d + info.w + ch0;
-            const float wr = mt.y;
+            for (uint32_t sb = 0; sb < nsub && ok; ++sb, ++n) {
+                const bool live = (int)sb * kBM + j < rows;
+                const uint32_t buf = n & 1u;
+                if (!jt::mbar_wait(&tfull[buf], (n >> 1) & 1u, abort_flag, err)) {
+                    ok = false;
+                    break;
+                }
+                jt::tc_fence_after();
+                const uint32_t acc = tq + buf * kBN + ch0;
+                float *dst = p.y + (size_t)__float_as_int(mt[sb].z) * p.d + info.w + ch0;
+                const float wr = mt[sb].y;
 #pragma unroll 2
-            for (int c = 0; c < 128; c += 16) {
-                uint32_t a0[8], a1[8];
-                jt::tmem_ld8(acc + c, a0);
-                jt::tmem_ld8(acc + c + 8, a1);
-                jt::tmem_wait_ld8(a0);
-                jt::tmem_wait_ld8(a1);
-                if (live && cols) {
-                    float v[16];
+                for (int c = 0; c < 128; c += 16) {
+                    uint32_t a0[8], a1[8];
+                    jt::tmem_ld8(acc + c, a0);
+                    jt::tmem_ld8(acc + c + 8, a1);
+                    jt::tmem_wait_ld8(a0);
+                    jt::tmem_wait_ld8(a1);
+                    if (live && cols) {
+                        float v[16];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        v[i] = __fmul_rn(wr, __uint_as_float(a0[i]));
-                        v[8 + i] = __fmul_rn(wr, __uint_as_float(a1[i]));
-                    }
-                    if (p.y_accumulate) {
+                        for (int i = 0; i < 8; ++i) {
+                            v[i] = __fmul_rn(wr, __uint_as_float(a0[i]));
+                            v[8 + i] = __fmul_rn(wr, __uint_as_float(a1[i]));
+                        }
+                        if (p.y_accumulate) {
 #pragma unroll
-                        for (int i = 0; i < 16; i += 4) red_add_v4(dst + c + i, v[i], v[i + 1], v[i + 2], v[i + 3]);
-                    } else {
+                            for (int i = 0; i < 16; i += 4)
+                                red_add_v4(dst + c + i, v[i], v[i + 1], v[i + 2], v[i + 3]);
+                        } else {
 #pragma unroll
-                        for (int i = 0; i < 16; i += 4)
-                            *reinterpret_cast<float4 *>(dst + c + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                            for (int i = 0; i < 16; i += 4)
+                                *reinterpret_cast<float4 *>(dst + c + i) =
+                                    make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                        }
                     }
                 }
+                jt::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) jt::mbar_arrive(&tempty[buf]);
             }
-            jt::tc_fence_before();
-            __syncwarp();
-            if (lane == 0) jt::mbar_arrive(&tempty[buf]);
         }
     }
     __syncthreads();

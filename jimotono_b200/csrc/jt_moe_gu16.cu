@@ -13,7 +13,8 @@
 // (moe_layer.c:146-148, jt_swiglu.cuh), the routed down projection's input
 // (jt_moe_dn16.cu).
 //
-// Tile: 128 token rows of one expert (MMA M, TMEM lane = token row) x 128
+// Tile: 128 token rows of one expert (MMA M, TMEM lane = token row; an
+// entry of the 128-row tile table jtk_split_tiles derives) x 128
 // channels (MMA N = 256: the 128 gate rows, then the same 128 up rows), so
 // a thread of the epilogue holds the gate and up sums of its token for
 // the same channels and forms SwiGLU in registers.  One pipeline stage is one 64-K scale group: the token rows as
@@ -51,7 +52,7 @@
 
 namespace {
 
-constexpr int kBM = JT_TILE_ROWS;         // token rows per tile (MMA M)
+constexpr int kBM = JT_SUB_ROWS;          // token rows per tile (MMA M)
 constexpr int kCh = 128;                  // channels per tile
 constexpr int kBN = 2 * kCh;              // MMA N: gate rows, then up rows
 constexpr int kThreads = 576;             // 18 warps

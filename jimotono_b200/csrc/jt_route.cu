@@ -161,6 +161,42 @@ __global__ void k_build_tiles(const int32_t *__restrict__ off, const int32_t *__
     }
 }
 
+// The JT_SUB_ROWS-row tiles of the tile table, in order: entry i of the
+// table yields ceil(min(rows, JT_TILE_ROWS) / JT_SUB_ROWS) of them (a block
+// scan of those counts, 1024 entries at a time, gives their positions).
+__global__ void __launch_bounds__(1024) k_split_tiles(const int4 *__restrict__ tiles,
+                                                     const int32_t *__restrict__ ntiles,
+                                                     int4 *__restrict__ out, int32_t *__restrict__ nout) {
+    __shared__ int sm[1024];
+    __shared__ int carry;
+    const int n = *ntiles, tid = threadIdx.x;
+    if (tid == 0) carry = 0;
+    __syncthreads();
+    for (int b = 0; b < n; b += 1024) {
+        const int i = b + tid;
+        int4 te = make_int4(0, 0, 0, 0);
+        int ns = 0;
+        if (i < n) {
+            te = tiles[i];
+            ns = (min(te.z - te.y, JT_TILE_ROWS) + JT_SUB_ROWS - 1) / JT_SUB_ROWS;
+        }
+        sm[tid] = ns;
+        __syncthreads();
+        for (int o = 1; o < 1024; o <<= 1) {  // inclusive Hillis-Steele scan
+            const int v = tid >= o ? sm[tid - o] : 0;
+            __syncthreads();
+            sm[tid] += v;
+            __syncthreads();
+        }
+        const int pos = carry + sm[tid] - ns;
+        for (int j = 0; j < ns; ++j) out[pos + j] = make_int4(te.x, te.y + JT_SUB_ROWS * j, te.z, 0);
+        __syncthreads();  // every thread has read carry
+        if (tid == 1023) carry += sm[1023];
+        __syncthreads();
+    }
+    if (tid == 0) *nout = carry;
+}
+
 // One warp per chunk, pairs visited in q order 32 at a time; lanes routed
 // to the same expert are ranked by __match_any_sync, so placement is the
 // sequential scan of moe_layer.c:955-970.  Then renormalization of the
@@ -372,6 +408,12 @@ extern "C" int jtk_moe_sort(const int32_t *ids, const float *w_in, int T, int k,
     k_build_tiles<<<(E + 255) / 256, 256, 0, stream>>>(off, tile_off, E, tiles);
     k_sort_scatter<<<nch, 32, (size_t)E * sizeof(int32_t), stream>>>(
         ids, w_in, T, k, E, cap, gbase, hist, off, perm, pos, drop, w_out, err);
+    return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
+extern "C" int jtk_split_tiles(const int4 *tiles, const int32_t *ntiles, int4 *out, int32_t *nout,
+                               cudaStream_t stream) {
+    k_split_tiles<<<1, 1024, 0, stream>>>(tiles, ntiles, out, nout);
     return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 
