@@ -8,20 +8,21 @@
 // kernels:
 //
 //   k_dec_gateup  work units of 128 weight rows: 64 gate rows over the same
-//                 64 up rows of one expert.  Routed unit (slot, 64-channel
-//                 block): INT2 rows, one row per thread; each group's exact
+//                 64 up rows of one expert, four threads per row.  Routed
+//                 unit (slot, 64-channel block): INT2 rows; the four threads
+//                 of a row take interleaved groups, each group's exact
 //                 integer partials give its dot with the fp16 weights
 //                 fp16_rn(code * scale) of the batched kernel (jt_moe_gu16.cu),
-//                 folded in fp32 in group order; then SwiGLU
-//                 (moe_layer.c:146-148) and the per-64-channel requantization
-//                 of h.  Shared-expert unit
-//                 (expert, 64-channel block, K part): the int8 rows of a
-//                 shared expert are d bytes long, so ksplit CTAs each take a
-//                 K part of every row; their exact int32 partial dots meet
-//                 in a device accumulator through integer atomic adds, and
-//                 the CTA that arrives last (ticket counter, no waiting)
-//                 takes the totals - resetting the accumulator for the next
-//                 call - and finishes the unit.  Every CTA quantizes the
+//                 passed by shuffle so that the fold runs in fp32 in group
+//                 order; then SwiGLU (moe_layer.c:146-148), h in bf16.
+//                 Shared-expert unit (expert, 64-channel block, K part of up
+//                 to 1024 bytes, a quarter per thread): for d <= 1024 one CTA
+//                 takes the whole row and its quad sum is the dot; for longer
+//                 rows ksplit CTAs each take a K part, their exact int32
+//                 partial dots meet in a device accumulator through integer
+//                 atomic adds, and the CTA that arrives last (ticket counter,
+//                 no waiting) takes the totals - resetting the accumulator
+//                 for the next call - and finishes the unit.  Every CTA quantizes the
 //                 token itself (w8a8.c:688-747); routed CTAs route it first
 //                 (jt_topk.cuh), which only they need, and the token's
 //                 quantization runs while their weight loads are in flight.
@@ -62,9 +63,9 @@ namespace {
 constexpr int kMaxD = 4096;        // token width handled (d <= 4096)
 constexpr int kMaxF = 4096;        // expert ffn handled (f, fs <= 4096)
 constexpr int kMaxE = 4096;        // experts
-constexpr int kGuThreads = 128;    // one thread per weight row of a unit
-constexpr int kGroupsPerLoad = 8;  // 64-element groups per register batch (INT2: 16 B each)
-constexpr int kSharedPart = 256;   // bytes of one shared-expert row per K part
+constexpr int kGuThreads = 512;       // four threads per weight row of a unit
+constexpr int kSharedPartMax = 1024;  // bytes of one shared-expert row per K part (at most)
+constexpr int kSharedQuarter = kSharedPartMax / 4;  // of which one thread takes a quarter
 constexpr int kDnWarps = 8;        // output channels per down CTA
 constexpr size_t kDnSmemMax = 200 * 1024;
 
@@ -172,13 +173,16 @@ __device__ __forceinline__ void swiglu_bf16_64(const float (&gu)[2][64], uint16_
     reinterpret_cast<uint32_t *>(h)[lane] = *reinterpret_cast<const uint32_t *>(&v);
 }
 
-// grid n_routed_units + S * (fs/64) * ksplit, kGuThreads threads.
+// grid n_routed_units + S * (fs/64) * ksplit, kGuThreads threads: four
+// per weight row (thread t: row t / 4, quarter t % 4).
 //
 // The token row is read once, as float4 per thread, and kept in registers;
-// raw fp16 scales are kept until the fold; the weight rows of a shared
-// expert (which depend neither on the token nor on the routing) are loaded
-// before the wait for the previous kernel of the stream.
-__global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant__ DecParams p) {
+// the weight rows of a shared expert (which depend neither on the token nor
+// on the routing) are loaded before the wait for the previous kernel of the
+// stream.  At most 96 registers per thread (a few bytes spill), so that a
+// CTA of the down kernel, launched early as a programmatic dependent, fits
+// on the same SM: 16.4 us per token against 18.2 us at 128 registers.
+__global__ void __maxnreg__(96) k_dec_gateup(const __grid_constant__ DecParams p) {
     __shared__ __align__(16) int8_t sx[kMaxD];
     __shared__ __align__(16) uint32_t xp[kMaxD / 4];
     __shared__ int gsum[kMaxD / 64];
@@ -200,7 +204,8 @@ __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int d = p.d, ng = d / 64;
     const bool routed = (int)blockIdx.x < p.n_routed_units;
-    const int r = threadIdx.x;  // 0..63 gate rows, 64..127 up rows
+    const int r = threadIdx.x >> 2;  // 0..63 gate rows, 64..127 up rows
+    const int qd = threadIdx.x & 3;  // quarter of the row
     const bool up = r >= 64;
     int slot = 0, cb = 0, s = 0, kq = 0;
     if (routed) {
@@ -214,24 +219,23 @@ __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant
         cb = (u / p.ksplit) % nb;
         kq = u % p.ksplit;
     }
-    const int part_bytes = d / p.ksplit;  // shared units: bytes of the row's K part
+    // shared units: the row's K part [kq part_bytes, +part_bytes), a quarter
+    // of it per thread (qbytes = part_bytes / 4, 32..256 bytes)
+    const int part_bytes = d / p.ksplit, qbytes = part_bytes / 4;
     if (threadIdx.x == 0) {
         abort_flag = 0;
         jt::mbar_init(&wbar, 1);
         jt::fence_mbar_init();
     }
-    uint4 wv[2][kGroupsPerLoad];
+    uint4 wv[kSharedQuarter / 16];
     if (!routed) {
         const int c = cb * 64 + (r & 63);
         const uint4 *wrow = reinterpret_cast<const uint4 *>(
-            reinterpret_cast<const uint8_t *>((up ? p.wsu : p.wsg) + ((size_t)s * p.fs + c) * d) + kq * part_bytes);
+            reinterpret_cast<const uint8_t *>((up ? p.wsu : p.wsg) + ((size_t)s * p.fs + c) * d) + kq * part_bytes +
+            qd * qbytes);
 #pragma unroll
-        for (int b = 0; b < 2; ++b)
-#pragma unroll
-            for (int i = 0; i < kGroupsPerLoad; ++i) {
-                const int j = b * kGroupsPerLoad + i;
-                if (16 * j < part_bytes) wv[b][i] = __ldg(wrow + j);
-            }
+        for (int j = 0; j < kSharedQuarter / 16; ++j)
+            if (16 * j < qbytes) wv[j] = __ldg(wrow + j);
     }
     // this grid is itself launched as a dependent of the previous kernel of
     // the stream (the previous token's down kernel in a decode loop): wait
@@ -285,12 +289,11 @@ __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant
         wb[warp] = bad;
     }
     __syncthreads();
-    // ---- routed units: this thread's raw fp16 scales (coalesced over the
-    // block's 64 channels; groups past 16 are read in the fold), and its row
-    // when the rows do not come by tensor map
-    __half sv[16];
-    const uint4 *grow = nullptr;
+    // ---- routed units: the raw fp16 scales of this thread's groups
+    // g = qd + 4 i (coalesced over the block's 64 channels)
+    uint32_t sv[kMaxD / 256];
     const __half *srow = nullptr;
+    const uint4 *grow = nullptr;
     if (routed) {
         int e = sids[slot];
         e = (e < 0 || e >= p.E) ? 0 : e;
@@ -298,16 +301,9 @@ __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant
         srow = (up ? p.su : p.sg) + (size_t)e * ng * p.f + c;
         grow = reinterpret_cast<const uint4 *>((up ? p.wu : p.wg) + ((size_t)e * p.f + c) * (d / 4));
 #pragma unroll
-        for (int g = 0; g < 16; ++g)
-            if (g < ng) sv[g] = srow[(size_t)g * p.f];
-        if (!p.tma) {
-#pragma unroll
-            for (int b = 0; b < 2; ++b)
-#pragma unroll
-                for (int i = 0; i < kGroupsPerLoad; ++i) {
-                    const int g = b * kGroupsPerLoad + i;
-                    if (g < ng) wv[b][i] = __ldg(grow + g);
-                }
+        for (int i = 0; i < kMaxD / 256; ++i) {
+            const int g = qd + 4 * i;
+            sv[i] = g < ng ? (uint32_t)__half_as_ushort(srow[(size_t)g * p.f]) : 0u;
         }
     }
     // ---- quantize the token (w8a8.c:688-747) from the registers, in the
@@ -365,48 +361,37 @@ __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant
             gsum[g] = sm;
         }
         __syncthreads();
+        if (p.tma && !jt::mbar_wait(&wbar, 0, &abort_flag, p.err)) return;
+        // the four threads of a row take groups qd, qd + 4, ...: each group's
+        // exact integer partials, then the fold of every group in ascending
+        // order (all four lanes run it on the partials passed by shuffle;
+        // lane qd == 0 keeps the result).  Row rr of a weight box holds its
+        // 16-byte chunk c at chunk c ^ (rr % 8).
+        const int rr = r & 63, nbox = d / 512;
+        const uint8_t *rowb = wsm + (size_t)(up ? nbox : 0) * 8192 + (size_t)rr * 128;
         float acc = 0.0f;
-        if (p.tma) {
-            if (!jt::mbar_wait(&wbar, 0, &abort_flag, p.err)) return;
-            // fold the groups' dots with the fp16 weights in order; row
-            // rr of a box holds its 16-byte chunk c at chunk c ^ (rr % 8)
-            const int rr = r & 63, nbox = d / 512;
-            const uint8_t *rowb = wsm + (size_t)(up ? nbox : 0) * 8192 + (size_t)rr * 128;
-            for (int g0 = 0; g0 < ng; g0 += 16) {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int g = g0 + i;
-                    if (g < ng) {
-                        const uint4 w = *reinterpret_cast<const uint4 *>(rowb + (size_t)(g >> 3) * 8192 +
-                                                                          (((g & 7) ^ (rr & 7)) << 4));
-                        const __half sg = g0 == 0 ? sv[i] : srow[(size_t)g * p.f];
-                        acc = int2_fold(acc, int2_group(w, xp + 16 * g, gsum[g]), sg);
-                    }
-                }
+        for (int i = 0; i < kMaxD / 256; ++i) {
+            const int g0 = 4 * i;
+            if (g0 >= ng) break;  // uniform over the CTA
+            const int g = g0 + qd;
+            int2 pa = make_int2(0, 0);
+            if (g < ng) {
+                const uint4 w = p.tma ? *reinterpret_cast<const uint4 *>(rowb + (size_t)(g >> 3) * 8192 +
+                                                                         (((g & 7) ^ (rr & 7)) << 4))
+                                      : __ldg(grow + g);
+                pa = int2_group(w, xp + 16 * g, gsum[g]);
             }
-        } else {
-            // register path: groups in batches, the next batch loaded while
-            // the current one is folded
-            for (int g0 = 0; g0 < ng; g0 += 2 * kGroupsPerLoad) {
 #pragma unroll
-                for (int b = 0; b < 2; ++b) {
-#pragma unroll
-                    for (int i = 0; i < kGroupsPerLoad; ++i) {
-                        const int g = g0 + b * kGroupsPerLoad + i;
-                        if (g < ng) {
-                            const __half sg = g0 == 0 ? sv[b * kGroupsPerLoad + i] : srow[(size_t)g * p.f];
-                            acc = int2_fold(acc, int2_group(wv[b][i], xp + 16 * g, gsum[g]), sg);
-                        }
-                    }
-#pragma unroll
-                    for (int i = 0; i < kGroupsPerLoad; ++i) {
-                        const int g = g0 + (b + 2) * kGroupsPerLoad + i;
-                        if (g < ng) wv[b][i] = __ldg(grow + g);
-                    }
-                }
+            for (int j = 0; j < 4; ++j) {
+                const int src = (lane & ~3) | j;
+                const int P = __shfl_sync(0xffffffffu, pa.x, src);
+                const int A3 = __shfl_sync(0xffffffffu, pa.y, src);
+                const uint32_t sb = __shfl_sync(0xffffffffu, sv[i], src);
+                if (g0 + j < ng) acc = int2_fold(acc, make_int2(P, A3), __ushort_as_half((unsigned short)sb));
             }
         }
-        gu[up][r & 63] = __fmul_rn(acc, xs);
+        if (qd == 0) gu[up][rr] = __fmul_rn(acc, xs);
         __syncthreads();
         if (warp == 0) {
             const int row = slot_rank(sids, p.k, slot);
@@ -439,40 +424,42 @@ __global__ void __launch_bounds__(kGuThreads) k_dec_gateup(const __grid_constant
         }
         return;
     }
-    // ---- shared-expert unit: exact int32 partial dot over this K part
+    // ---- shared-expert unit: exact int32 partial dot over this K part, a
+    // quarter per thread, summed over the row's four lanes
     int dot = 0;
     {
-        const int8_t *xk = sx + kq * part_bytes;
+        const int8_t *xk = sx + kq * part_bytes + qd * qbytes;
 #pragma unroll
-        for (int b = 0; b < 2; ++b)
-#pragma unroll
-            for (int i = 0; i < kGroupsPerLoad; ++i) {
-                const int j = b * kGroupsPerLoad + i;
-                if (16 * j < part_bytes) {
-                    const int4 xk4 = *reinterpret_cast<const int4 *>(xk + 16 * j);
-                    dot = __dp4a((int)wv[b][i].x, xk4.x, dot);
-                    dot = __dp4a((int)wv[b][i].y, xk4.y, dot);
-                    dot = __dp4a((int)wv[b][i].z, xk4.z, dot);
-                    dot = __dp4a((int)wv[b][i].w, xk4.w, dot);
-                }
+        for (int j = 0; j < kSharedQuarter / 16; ++j) {
+            if (16 * j < qbytes) {
+                const int4 xk4 = *reinterpret_cast<const int4 *>(xk + 16 * j);
+                dot = __dp4a((int)wv[j].x, xk4.x, dot);
+                dot = __dp4a((int)wv[j].y, xk4.y, dot);
+                dot = __dp4a((int)wv[j].z, xk4.z, dot);
+                dot = __dp4a((int)wv[j].w, xk4.w, dot);
             }
+        }
+        dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+        dot += __shfl_xor_sync(0xffffffffu, dot, 2);
     }
     int32_t *acc = p.acc_s + ((size_t)s * 2 + up) * p.fs + cb * 64 + (r & 63);
     int total = dot;
     if (p.ksplit > 1) {
-        atomicAdd(acc, dot);
+        if (qd == 0) atomicAdd(acc, dot);
         __threadfence();
         __syncthreads();
         if (threadIdx.x == 0) ticket = atomicAdd(&p.cnt_s[s * (p.fs / 64) + cb], 1);
         __syncthreads();
         if (ticket != p.ksplit - 1) return;  // another CTA of the unit finishes it
         __threadfence();
-        total = atomicExch(acc, 0);  // the sum of every part; cleared for the next call
+        if (qd == 0) total = atomicExch(acc, 0);  // the sum of every part; cleared for the next call
         if (threadIdx.x == 0) p.cnt_s[s * (p.fs / 64) + cb] = 0;
     }
-    const int c = cb * 64 + (r & 63);
-    const float cs = (up ? p.ssu : p.ssg)[(size_t)s * p.fs + c];
-    gu[up][r & 63] = __fmul_rn(__fmul_rn(__int2float_rn(total), xs), cs);
+    if (qd == 0) {
+        const int c = cb * 64 + (r & 63);
+        const float cs = (up ? p.ssu : p.ssg)[(size_t)s * p.fs + c];
+        gu[up][r & 63] = __fmul_rn(__fmul_rn(__int2float_rn(total), xs), cs);
+    }
     __syncthreads();
     if (warp == 0)
         swiglu_bf16_64(gu, p.hb_s + (size_t)s * p.fs + cb * 64, p.err);
@@ -792,8 +779,12 @@ extern "C" int jtk_moe_decode(const float *x, const float *logits, const float *
     p.S = S;
     p.fs = fs_eff;
     p.n_routed_units = k * (f / 64);
-    // K parts of kSharedPart bytes (half that when d is an odd multiple of 128)
-    p.ksplit = d % kSharedPart == 0 ? d / kSharedPart : d / (kSharedPart / 2);
+    // K parts of the largest of 1024, 512, 256, 128 bytes that divides d
+    {
+        int part = kSharedPartMax;
+        while (d % part) part /= 2;
+        p.ksplit = d / part;
+    }
     p.acc_s = acc_s;
     p.cnt_s = cnt_s;
     p.xq = xq;
