@@ -505,6 +505,7 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constan
     __shared__ int32_t sids[64], ssel[64], srank[64];
     __shared__ float sw[64], sselv[64];
     __shared__ unsigned smax[8];  // shared h row maxima (float bits), S <= 8
+    __shared__ double terms[kDnWarps][64 + 8];  // combine terms [channel][k slots, then S shared experts]
     __shared__ int abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int d = p.d, f = p.f, fs = p.fs, k = p.k, S = p.S, gf = f / 64;
@@ -696,24 +697,34 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_dec_down(const __grid_constan
         }
     }
     __syncthreads();
-    // ---- one thread per output channel: the combine in double, routed rows
-    // in slot order (moe_layer.c:1443-1463), then the shared experts in s
-    // order (moe_layer.c:1549-1559), each ((float)acc * hs) * ssd[o] with its
-    // exact int32 dot summed over the groups
+    // ---- the combine in double (moe_layer.c:1443-1463, :1549-1559): first
+    // every term at once, one thread per (channel, term) - routed slot q:
+    // w_q * (the row's group dots added in group order); shared expert sh:
+    // ((float)acc * hs) * ssd[o] with its exact int32 dot summed over the
+    // groups - then one thread per output channel adds them, routed rows in
+    // slot order, then the shared experts in s order
+    const int nterm = k + S;
+    for (int it = threadIdx.x; it < kDnWarps * nterm; it += blockDim.x) {
+        const int jj = it / nterm, t = it % nterm;
+        double v;
+        if (t < k) {
+            float yp = 0.0f;
+            for (int g = 0; g < gf; ++g) yp += racc[(jj * k + t) * gf + g];
+            v = __dmul_rn((double)sw[t], (double)yp);
+        } else {
+            const int sh = t - k;
+            int acc = 0;
+            for (int g = 0; g < gs; ++g) acc += sp[(jj * S + sh) * gs + g];
+            v = (double)__fmul_rn(__fmul_rn((float)acc, hss[sh]), ssc[sh * kDnWarps + jj]);
+        }
+        terms[jj][t] = v;
+    }
+    __syncthreads();
     if (threadIdx.x >= kDnWarps) return;
     const int j = threadIdx.x, o = o0 + j;
     if (o >= d) return;
     double ya = 0.0;
-    for (int q = 0; q < k; ++q) {
-        float yp = 0.0f;  // the row's group dots in group order
-        for (int g = 0; g < gf; ++g) yp += racc[(j * k + q) * gf + g];
-        ya = __dadd_rn(ya, __dmul_rn((double)sw[q], (double)yp));
-    }
-    for (int sh = 0; sh < S; ++sh) {
-        int acc = 0;
-        for (int g = 0; g < gs; ++g) acc += sp[(j * S + sh) * gs + g];
-        ya = __dadd_rn(ya, (double)__fmul_rn(__fmul_rn((float)acc, hss[sh]), ssc[sh * kDnWarps + j]));
-    }
+    for (int t = 0; t < nterm; ++t) ya = __dadd_rn(ya, terms[j][t]);
     const float yv = (float)ya;
     if (p.y) p.y[o] = yv;
     if (p.y_bf16) p.y_bf16[o] = __bfloat16_as_ushort(__float2bfloat16_rn(yv));
