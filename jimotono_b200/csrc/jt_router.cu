@@ -12,8 +12,10 @@
 // FP64 path accumulates in another order): a 256-thread block computes 64
 // tokens x 64 experts, staging 32-element K chunks of both operands in
 // shared memory as doubles (converted once per element and block); each
-// thread holds 4 tokens x 4 experts x 4 lanes of accumulators and reads its
-// operands as 16-byte pairs, one shared-memory load per four DFMA.  Up to 32768
+// thread holds one lane's partial sums for 8 tokens x 8 experts and reads
+// its operands as 16-byte pairs, one shared-memory load per eight DFMA
+// (the shared-memory pipe, not the FP64 pipe, bounded a layout with four
+// lanes per thread).  Up to 32768
 // logits (decode) a chain kernel with one thread per (logit, lane) is used
 // instead.
 #include <cuda_runtime.h>
@@ -26,31 +28,34 @@ namespace {
 
 constexpr int kTT = 64;  // tokens per block
 constexpr int kTE = 64;  // experts per block
-constexpr int kKC = 32;  // K elements per chunk (a multiple of 4: lanes stay j mod 4)
-constexpr int kLd = kKC + 2;  // row stride in doubles: 16-byte loads of neighbouring rows hit other banks
+constexpr int kKC = 32;  // K elements per chunk (a multiple of 8: two per lane and load)
+constexpr int kLS = kKC / 4 + 2;  // lane stride in doubles (8 elements + pad)
+constexpr int kRS = 4 * kLS;      // row stride in doubles: [row][lane][element]
 
+// Thread t: lane l = t % 4 of the reference's accumulation (elements
+// j = l mod 4), tokens tu + 8m (tu = (t / 4) % 8) and experts ti + 8n
+// (ti = t / 32, the warp) of the block, m, n = 0..7.  The chunk lives in
+// shared memory lane-major (element k of row r at [r][k % 4][k / 4]), so
+// one 16-byte load gives a row's next two elements of one lane; per two
+// K steps a thread issues 16 such loads for 128 DFMA.  With the 10-double
+// lane pitch and token rows interleaved by 8, the eight 16-byte reads of a
+// load phase fall in distinct banks.
 __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__ x, const float *__restrict__ wg,
                                                        int T, int d, int E, float *__restrict__ logits, int *err) {
-    __shared__ __align__(16) double xs[kTT][kLd];
-    __shared__ __align__(16) double ws[kTE][kLd];
-    // experts tx + 16i, tokens ty + 16u; a warp covers 8 expert rows x 4
-    // token rows, so each of its 16-byte operand loads is one wavefront
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tx = (warp & 1) * 8 + (lane & 7), ty = (warp >> 1) * 4 + (lane >> 3);
+    __shared__ __align__(16) double xs[kTT * kRS];
+    __shared__ __align__(16) double ws[kTE * kRS];
+    const int l = threadIdx.x & 3, tu = (threadIdx.x >> 2) & 7, ti = threadIdx.x >> 5;
     const int t0 = blockIdx.y * kTT, e0 = blockIdx.x * kTE;
-    double acc[4][4][4];  // [token u][expert i][lane l]
+    double acc[8][8];  // [token m][expert n], lane l's partial sum
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
+    for (int m = 0; m < 8; ++m)
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int l = 0; l < 4; ++l) acc[u][i][l] = 0.0;
+        for (int n = 0; n < 8; ++n) acc[m][n] = 0.0;
 
-    // staging: each thread moves two 16-byte pieces of the activation tile
-    // and two of the weight tile per chunk (rows sr and sr + 32, elements
-    // sc .. sc+3); the next chunk is loaded into registers while the current
-    // one is multiplied
-    const int sr = threadIdx.x >> 3, sc = 4 * (threadIdx.x & 7);
+    // staging: each thread moves elements sc .. sc+3 of rows sr and sr + 32
+    // of both tiles per chunk; the next chunk is loaded into registers while
+    // the current one is multiplied
+    const int sr = threadIdx.x >> 3, sq = threadIdx.x & 7, sc = 4 * sq;
     const bool x0in = t0 + sr < T, x1in = t0 + sr + 32 < T, w0in = e0 + sr < E, w1in = e0 + sr + 32 < E;
     const float *xp0 = x + (size_t)(x0in ? t0 + sr : 0) * d + sc;
     const float *xp1 = x + (size_t)(x1in ? t0 + sr + 32 : 0) * d + sc;
@@ -61,15 +66,20 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
     float4 px1 = x1in ? __ldg(reinterpret_cast<const float4 *>(xp1)) : z4;
     float4 pw0 = w0in ? __ldg(reinterpret_cast<const float4 *>(wp0)) : z4;
     float4 pw1 = w1in ? __ldg(reinterpret_cast<const float4 *>(wp1)) : z4;
+    auto put = [&](double *base, int row, float4 v) {  // elements sc..sc+3 -> lanes 0..3, position sq
+        double *q = base + row * kRS + sq;
+        q[0] = v.x;
+        q[kLS] = v.y;
+        q[2 * kLS] = v.z;
+        q[3 * kLS] = v.w;
+    };
+    const double *xr = xs + tu * kRS + l * kLS;  // + 8m rows
+    const double *wr = ws + ti * kRS + l * kLS;  // + 8n rows
     for (int k0 = 0; k0 < d; k0 += kKC) {
-        *reinterpret_cast<double2 *>(&xs[sr][sc]) = make_double2(px0.x, px0.y);
-        *reinterpret_cast<double2 *>(&xs[sr][sc + 2]) = make_double2(px0.z, px0.w);
-        *reinterpret_cast<double2 *>(&xs[sr + 32][sc]) = make_double2(px1.x, px1.y);
-        *reinterpret_cast<double2 *>(&xs[sr + 32][sc + 2]) = make_double2(px1.z, px1.w);
-        *reinterpret_cast<double2 *>(&ws[sr][sc]) = make_double2(pw0.x, pw0.y);
-        *reinterpret_cast<double2 *>(&ws[sr][sc + 2]) = make_double2(pw0.z, pw0.w);
-        *reinterpret_cast<double2 *>(&ws[sr + 32][sc]) = make_double2(pw1.x, pw1.y);
-        *reinterpret_cast<double2 *>(&ws[sr + 32][sc + 2]) = make_double2(pw1.z, pw1.w);
+        put(xs, sr, px0);
+        put(xs, sr + 32, px1);
+        put(ws, sr, pw0);
+        put(ws, sr + 32, pw1);
         __syncthreads();
         if (k0 + kKC < d) {
             const int kn = k0 + kKC;
@@ -78,42 +88,37 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
             pw0 = w0in ? __ldg(reinterpret_cast<const float4 *>(wp0 + kn)) : z4;
             pw1 = w1in ? __ldg(reinterpret_cast<const float4 *>(wp1 + kn)) : z4;
         }
-        // four K elements (one per lane) per step, ascending j in every lane
+        // two of the lane's elements per step pair, ascending
 #pragma unroll 1
-        for (int j = 0; j < kKC; j += 4) {
-            double a[4][4], b[4][4];
+        for (int sp = 0; sp < kKC / 8; ++sp) {
+            double2 a[8];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const double2 lo = *reinterpret_cast<const double2 *>(&xs[ty + 16 * u][j]);
-                const double2 hi = *reinterpret_cast<const double2 *>(&xs[ty + 16 * u][j + 2]);
-                a[u][0] = lo.x, a[u][1] = lo.y, a[u][2] = hi.x, a[u][3] = hi.y;
+            for (int m = 0; m < 8; ++m) a[m] = *reinterpret_cast<const double2 *>(xr + 8 * m * kRS + 2 * sp);
+#pragma unroll
+            for (int n = 0; n < 8; ++n) {
+                const double2 b = *reinterpret_cast<const double2 *>(wr + 8 * n * kRS + 2 * sp);
+#pragma unroll
+                for (int m = 0; m < 8; ++m) acc[m][n] = __fma_rn(a[m].x, b.x, acc[m][n]);
+#pragma unroll
+                for (int m = 0; m < 8; ++m) acc[m][n] = __fma_rn(a[m].y, b.y, acc[m][n]);
             }
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const double2 lo = *reinterpret_cast<const double2 *>(&ws[tx + 16 * i][j]);
-                const double2 hi = *reinterpret_cast<const double2 *>(&ws[tx + 16 * i][j + 2]);
-                b[i][0] = lo.x, b[i][1] = lo.y, b[i][2] = hi.x, b[i][3] = hi.y;
-            }
-#pragma unroll
-            for (int l = 0; l < 4; ++l)
-#pragma unroll
-                for (int u = 0; u < 4; ++u)
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) acc[u][i][l] = __fma_rn(a[u][l], b[i][l], acc[u][i][l]);
         }
         __syncthreads();
     }
+    // the four lanes of a logit are neighbouring threads: (l0 + l1) + (l2 + l3)
     bool bad = false;
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-        const int t = t0 + ty + 16 * u;
+    for (int m = 0; m < 8; ++m) {
+        const int t = t0 + tu + 8 * m;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int e = e0 + tx + 16 * i;
-            const double s = __dadd_rn(__dadd_rn(acc[u][i][0], acc[u][i][1]), __dadd_rn(acc[u][i][2], acc[u][i][3]));
-            const float f = __double2float_rn(s);
-            if (t < T && e < E) {
-                bad |= !isfinite(s) || !isfinite(f);
+        for (int n = 0; n < 8; ++n) {
+            const int e = e0 + ti + 8 * n;
+            const double s01 = __dadd_rn(acc[m][n], __shfl_xor_sync(0xffffffffu, acc[m][n], 1));
+            const double s23 = __shfl_xor_sync(0xffffffffu, s01, 2);
+            const double sum = __dadd_rn(s01, s23);
+            const float f = __double2float_rn(sum);
+            if (l == 0 && t < T && e < E) {
+                bad |= !isfinite(sum) || !isfinite(f);
                 logits[(size_t)t * E + e] = f;
             }
         }
