@@ -161,16 +161,13 @@ __device__ __forceinline__ float int2_fold(float acc, int2 pa, __half sg) {
     return fmaf((float)pa.y, dt, fmaf((float)pa.x, s, acc));
 }
 
-// SwiGLU of the 64 channels staged in gu, rounded to bf16 into h[0..63]
-// (the routed experts' h).  Warp 0 only.
+// SwiGLU of the 64 channels staged in gu, rounded to bf16 into h[0..63].
+// Warps 0 and 1, one channel per thread (a single exp chain each).
 __device__ __forceinline__ void swiglu_bf16_64(const float (&gu)[2][64], uint16_t *h, int *err) {
-    const int lane = threadIdx.x & 31;
-    const float h0 = jt::swiglu(gu[0][2 * lane], gu[1][2 * lane]);
-    const float h1 = jt::swiglu(gu[0][2 * lane + 1], gu[1][2 * lane + 1]);
-    const bool bad = !isfinite(h0) || !isfinite(h1);
-    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicExch(err, JT_KERR_NONFINITE);
-    const __nv_bfloat162 v = __floats2bfloat162_rn(h0, h1);
-    reinterpret_cast<uint32_t *>(h)[lane] = *reinterpret_cast<const uint32_t *>(&v);
+    const int c = threadIdx.x;  // 0..63
+    const float hv = jt::swiglu(gu[0][c], gu[1][c]);
+    if (__any_sync(0xffffffffu, !isfinite(hv)) && (c & 31) == 0) atomicExch(err, JT_KERR_NONFINITE);
+    h[c] = __bfloat16_as_ushort(__float2bfloat16_rn(hv));
 }
 
 // grid n_routed_units + S * (fs/64) * ksplit, kGuThreads threads: four
@@ -393,7 +390,7 @@ __global__ void __maxnreg__(96) k_dec_gateup(const __grid_constant__ DecParams p
         }
         if (qd == 0) gu[up][rr] = __fmul_rn(acc, xs);
         __syncthreads();
-        if (warp == 0) {
+        if (warp < 2) {
             const int row = slot_rank(sids, p.k, slot);
             swiglu_bf16_64(gu, p.h + (size_t)row * p.f + cb * 64, p.err);
         }
@@ -461,8 +458,7 @@ __global__ void __maxnreg__(96) k_dec_gateup(const __grid_constant__ DecParams p
         gu[up][r & 63] = __fmul_rn(__fmul_rn(__int2float_rn(total), xs), cs);
     }
     __syncthreads();
-    if (warp == 0)
-        swiglu_bf16_64(gu, p.hb_s + (size_t)s * p.fs + cb * 64, p.err);
+    if (warp < 2) swiglu_bf16_64(gu, p.hb_s + (size_t)s * p.fs + cb * 64, p.err);
 }
 
 // Layout of the down kernel's dynamic shared memory (byte offsets).  Rows
