@@ -372,20 +372,28 @@ __global__ void __maxnreg__(96) k_dec_gateup(const __grid_constant__ DecParams p
             const int g0 = 4 * i;
             if (g0 >= ng) break;  // uniform over the CTA
             const int g = g0 + qd;
-            int2 pa = make_int2(0, 0);
+            // the group's owner converts once: its partials and the fold
+            // constants s and t - 3s of int2_fold
+            float pf = 0.0f, af = 0.0f, sf = 0.0f, dtf = 0.0f;
             if (g < ng) {
                 const uint4 w = p.tma ? *reinterpret_cast<const uint4 *>(rowb + (size_t)(g >> 3) * 8192 +
                                                                          (((g & 7) ^ (rr & 7)) << 4))
                                       : __ldg(grow + g);
-                pa = int2_group(w, xp + 16 * g, gsum[g]);
+                const int2 pa = int2_group(w, xp + 16 * g, gsum[g]);
+                pf = (float)pa.x;
+                af = (float)pa.y;
+                sf = __half2float(__ushort_as_half((unsigned short)sv[i]));
+                const float s3 = 3.0f * sf;
+                dtf = __half2float(__float2half_rn(s3)) - s3;
             }
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const int src = (lane & ~3) | j;
-                const int P = __shfl_sync(0xffffffffu, pa.x, src);
-                const int A3 = __shfl_sync(0xffffffffu, pa.y, src);
-                const uint32_t sb = __shfl_sync(0xffffffffu, sv[i], src);
-                if (g0 + j < ng) acc = int2_fold(acc, make_int2(P, A3), __ushort_as_half((unsigned short)sb));
+                const float P = __shfl_sync(0xffffffffu, pf, src);
+                const float A3 = __shfl_sync(0xffffffffu, af, src);
+                const float S = __shfl_sync(0xffffffffu, sf, src);
+                const float D = __shfl_sync(0xffffffffu, dtf, src);
+                if (g0 + j < ng) acc = fmaf(A3, D, fmaf(P, S, acc));  // int2_fold
             }
         }
         if (qd == 0) gu[up][rr] = __fmul_rn(acc, xs);
