@@ -428,7 +428,13 @@ extern "C" int jtk_quant_dispatch(const float *x, int T, int d, int k, const int
                                   const float *wfin, int8_t *xq, float *xs, uint16_t *xd,
                                   float4 *row_meta, float4 *sh_meta, cudaStream_t stream) {
     if (T <= 0 || d <= 0 || (d % 16) != 0 || k > 64) return -1;
-    k_quant_dispatch<<<T, 256, 0, stream>>>(x, T, d, k, pos, wfin, xq, xs, xd, row_meta, sh_meta,
+    // one thread per 16 codes of the row where that fits in 64..256 threads
+    // (every thread busy in the quantize-and-store phase); at least k
+    // threads, which write the row metadata
+    int thr = d / 16;
+    thr = thr < 64 ? 64 : (thr > 256 ? 256 : thr);
+    thr = (thr + 31) & ~31;
+    k_quant_dispatch<<<T, thr, 0, stream>>>(x, T, d, k, pos, wfin, xq, xs, xd, row_meta, sh_meta,
                                             jtk_error_word());
     return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
