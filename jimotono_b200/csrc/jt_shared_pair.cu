@@ -3,8 +3,8 @@
 // cta_group::2).  h leaves as bf16 with the running maximum of |h| of every
 // token row (the row's requantization scale, jt_shared.cu).
 //
-// Arithmetic (identical to the single-CTA form in jt_moe_gemm.cu, which is
-// the restatement of moe_layer.c:129-157 with the W8A8 projections of
+// Arithmetic (identical to the dense-GEMM form of jt_shared.cu used for
+// T < 256: moe_layer.c:129-157 with the W8A8 projections of
 // w8a8.c:1021-1072):
 //   g[t][c] = ((float)acc_gate[t][c] * xs[t]) * sg[c]     (xs[t] = meta[t].x)
 //   u[t][c] = ((float)acc_up[t][c]   * xs[t]) * su[c]
@@ -24,9 +24,10 @@
 //     their 32 channels of g or u for 32 tokens and store them to the
 //     chunk's [32 tokens][64 channels] fp32 block in shared memory;
 //   workers (warps 10-25, token half (w-10)/8): eight lanes per token form
-//     h over 8 channels each, reduce the 64-channel max-abs, requantize and
-//     store 64 codes and the group scale; warp w takes tokens 4((w-10)%8)
-//     .. +3 of every chunk of its half.
+//     h over 8 channels each, store them as bf16 (16 bytes per lane) and
+//     fold the 64-channel max of |bf16 h| into the row maximum with one
+//     atomic max per token; warp w takes tokens 4((w-10)%8) .. +3 of every
+//     chunk of its half.
 // The readers release the accumulator as soon as a tile is staged, so the
 // SwiGLU of one tile overlaps the TMEM reads of the next.
 #include <cuda.h>
