@@ -7,10 +7,12 @@
 //   r = 0; for g ascending: r = fmaf((float)P[n][g], s[n][g], r); y[n] = r * sa
 //
 // HBM-bound, every weight byte read once.  Two CTAs per SM, each with a
-// producer warp that streams chunks of consecutive rows (up to 10 KB of
-// codes and scales) into an 8-stage shared-memory ring with bulk
-// asynchronous copies, so up to 160 KB per SM are in flight; eight consumer
-// warps per CTA take the chunks in turn.  Launched with programmatic
+// producer warp that streams chunks of consecutive rows (up to 9 KB of
+// codes and scales) into a 7-stage shared-memory ring with bulk
+// asynchronous copies, so up to 129 KB per SM are in flight; seven consumer
+// warps per CTA take the chunks in turn and, on the K = 2048 path, release
+// a stage as soon as its codes and scales are copied out, so the refill
+// streams while they compute.  Launched with programmatic
 // dependent launch: a GEMV queued behind another kernel starts streaming its
 // weights while that kernel drains, and waits for it only before reading the
 // activations and writing y.  The weight and scale buffers must therefore
@@ -23,8 +25,8 @@
 // (INT4 high nibble), removed exactly by an arithmetic shift of its own
 // accumulator:
 //   P = 2 * sum(li * a) - (2^bits - 1) * sum(a)   (exact in int32).
-// The group partials go through shared memory so that the sequential fp32
-// fold runs lane-per-row.
+// The group partials go through shared memory (as exact fp32 on the
+// K = 2048 path) so that the sequential fp32 fold runs lane-per-row.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
