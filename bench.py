@@ -83,6 +83,7 @@ class ClockSampler:
         self.proc = None
 
     def __enter__(self):
+        self.first = []
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
@@ -90,6 +91,13 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
+        # nvidia-smi takes a moment to start: wait (at most 5 s) for its first
+        # sample so that the sampling covers the whole timed work that follows
+        if self.proc is not None:
+            import select
+            ready, _, _ = select.select([self.proc.stdout], [], [], 5.0)
+            if ready:
+                self.first.append(self.proc.stdout.readline())
         return self
 
     def __exit__(self, *a):
@@ -101,7 +109,7 @@ class ClockSampler:
             except Exception:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+            self.lines = [ln for ln in self.first + out.splitlines() if ln.strip()]
 
     def summary(self):
         sm, mx, reasons = [], 0.0, set()
@@ -551,7 +559,7 @@ def main_ep(torch, args, rank, world, local, hbm_peak, peak_kind):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-parts", action="store_true")
